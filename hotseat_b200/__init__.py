@@ -1,0 +1,385 @@
+"""hotseat_b200 — the hotseat token loop on B200 (sm_100a), behind a C ABI.
+
+This module is a thin ctypes binding of include/hotseat.h, shaped like the
+Rust API that hotseat's worker calls on hs-engine (crates/hs-engine/src):
+
+    Model.load(path, max_ctx)         model.rs:110   Model::load
+    model.cfg / .fingerprint / .eos   model.rs:62-78
+    model.scratch()                   model.rs:221   Model::scratch
+    model.forward(kv, tok, pos, s)    model.rs:240   Model::forward
+    model.kv(layout, page_size)       hs-track Region + kv.rs Kv::from_raw
+    kv.hash(n_pos)                    kv.rs:267      Kv::hash
+    Sampler(cfg).sample(s, history)   sampler.rs:100 Sampler::sample
+    argmax(s)                         sampler.rs:177 argmax
+    run_seq(...)                      hs-worker seq.rs:230 run
+
+All compute runs in libhotseat.so on the GPU. There is no CPU fallback: if the
+library is missing the import fails, and a call without a GPU raises.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libhotseat.so")
+
+HS_OK = 0
+HS_E_ARG, HS_E_IO, HS_E_CUDA, HS_E_STATE, HS_E_NOMEM, HS_E_UNSUPPORTED = -1, -2, -3, -4, -5, -6
+TOKEN_MAJOR, HEAD_MAJOR = 0, 1
+DONE_REASONS = {0: "", 1: "eos", 2: "max_tokens", 3: "context full"}
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is not built; run `python hotseat_b200/build.py` (needs nvcc)")
+_lib = C.CDLL(LIB_PATH)
+
+
+class HotseatError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+class Config(C.Structure):
+    _fields_ = [("n_layers", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32),
+                ("head_dim", C.c_uint32), ("d_model", C.c_uint32), ("d_ff", C.c_uint32), ("vocab", C.c_uint32),
+                ("eps", C.c_float), ("rope_base", C.c_float), ("train_ctx", C.c_uint32), ("max_ctx", C.c_uint32),
+                ("eos", C.c_uint32), ("fingerprint", C.c_uint64)]
+
+
+class KvSpec(C.Structure):
+    _fields_ = [("n_layers", C.c_uint32), ("n_kv_heads", C.c_uint32), ("head_dim", C.c_uint32),
+                ("max_ctx", C.c_uint32), ("layout", C.c_uint32)]
+
+
+class SamplerCfg(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_uint32),
+                ("repeat_penalty", C.c_float), ("repeat_last_n", C.c_uint32), ("seed", C.c_uint64)]
+
+    @classmethod
+    def default(cls, **kw):
+        c = cls()
+        _lib.hs_sampler_cfg_default(C.byref(c))
+        for k, v in kw.items():
+            setattr(c, k, v)
+        return c
+
+
+class Rng(C.Structure):
+    _fields_ = [("s", C.c_uint64 * 4), ("draws", C.c_uint64)]
+
+    @classmethod
+    def seed(cls, seed):
+        r = cls()
+        _lib.hs_rng_seed(C.c_uint64(seed), C.byref(r))
+        return r
+
+    def state(self):
+        return [int(x) for x in self.s], int(self.draws)
+
+
+class SeqState(C.Structure):
+    _fields_ = [("prompt_len", C.c_uint64), ("filled", C.c_uint64), ("max_tokens", C.c_uint64),
+                ("done", C.c_uint32), ("done_reason", C.c_uint32)]
+
+
+class SynthSpec(C.Structure):
+    _fields_ = [("n_layers", C.c_uint32), ("d_model", C.c_uint32), ("n_heads", C.c_uint32),
+                ("n_kv_heads", C.c_uint32), ("d_ff", C.c_uint32), ("vocab", C.c_uint32),
+                ("context_length", C.c_uint32), ("eos", C.c_uint32), ("eps", C.c_float), ("rope_base", C.c_float),
+                ("weight_std", C.c_float), ("bias_std", C.c_float), ("embd_type", C.c_uint32),
+                ("weight_type", C.c_uint32), ("tied", C.c_uint32), ("threads", C.c_uint32), ("seed", C.c_uint64)]
+
+
+_P = C.c_void_p
+_U64P = C.POINTER(C.c_uint64)
+_SIGS = {
+    "hs_last_error": (C.c_char_p, []),
+    "hs_model_load": (C.c_int, [C.c_char_p, C.c_uint32, C.c_int, C.POINTER(_P)]),
+    "hs_model_config": (C.c_int, [_P, C.POINTER(Config)]),
+    "hs_model_free": (None, [_P]),
+    "hs_model_tensor": (C.c_int, [_P, C.c_char_p, _P, C.c_uint64, C.POINTER(C.c_uint32)]),
+    "hs_kv_alloc": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.POINTER(_P)]),
+    "hs_kv_info": (C.c_int, [_P, C.POINTER(KvSpec), _U64P, C.POINTER(C.c_uint32), _U64P]),
+    "hs_kv_free": (None, [_P]),
+    "hs_kv_read": (C.c_int, [_P, C.c_uint64, C.c_uint64, _P]),
+    "hs_kv_write": (C.c_int, [_P, C.c_uint64, C.c_uint64, _P]),
+    "hs_kv_hash": (C.c_int, [_P, C.c_uint32, _U64P]),
+    "hs_kv_arm": (C.c_int, [_P]),
+    "hs_kv_harvest": (C.c_int, [_P, _P, C.c_uint64]),
+    "hs_kv_disarm": (C.c_int, [_P]),
+    "hs_kv_copy_runs": (C.c_int, [_P, _P, _P, C.c_uint64]),
+    "hs_kv_live_ranges_between": (C.c_uint64, [C.POINTER(KvSpec), C.c_uint32, C.c_uint32, _P, C.c_uint64]),
+    "hs_runs_to_byte_runs": (C.c_uint64, [_P, C.c_uint64, C.c_uint64, _P, C.c_uint64, _P, C.c_uint64]),
+    "hs_scratch_new": (C.c_int, [_P, C.POINTER(_P)]),
+    "hs_scratch_free": (None, [_P]),
+    "hs_forward": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P]),
+    "hs_scratch_logits": (C.c_int, [_P, _P, C.c_uint64]),
+    "hs_scratch_set_logits": (C.c_int, [_P, _P, C.c_uint64]),
+    "hs_sampler_cfg_default": (None, [C.POINTER(SamplerCfg)]),
+    "hs_rng_seed": (None, [C.c_uint64, C.POINTER(Rng)]),
+    "hs_sample": (C.c_int, [_P, C.POINTER(SamplerCfg), C.POINTER(Rng), _P, C.c_uint64, C.POINTER(C.c_uint32)]),
+    "hs_argmax": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "hs_seq_run": (C.c_int, [_P, _P, _P, _P, _U64P, C.c_uint64, C.POINTER(SeqState), C.POINTER(SamplerCfg),
+                             C.POINTER(Rng), C.c_uint64]),
+    "hs_seq_begin": (C.c_int, [_P, _P, _P, C.c_uint64, C.c_uint64, C.POINTER(SeqState), C.POINTER(SamplerCfg),
+                               C.POINTER(Rng), C.c_uint64]),
+    "hs_seq_step": (C.c_int, [_P, C.c_uint32]),
+    "hs_seq_end": (C.c_int, [_P, _P, _U64P, C.c_uint64, C.POINTER(SeqState), C.POINTER(Rng)]),
+    "hs_scratch_stream": (_P, [_P]),
+    "hs_seq_launches_per_step": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "hs_dequant_f16": (C.c_int, [C.c_uint32, _P, C.c_uint64, _P, _P]),
+    "hs_synth_write": (C.c_int, [C.c_char_p, C.POINTER(SynthSpec)]),
+}
+for _name, (_res, _args) in _SIGS.items():
+    _f = getattr(_lib, _name)
+    _f.restype = _res
+    _f.argtypes = _args
+
+EXPORTED = tuple(_SIGS)
+
+
+def _check(rc):
+    if rc != HS_OK:
+        raise HotseatError(rc, _lib.hs_last_error().decode(errors="replace"))
+
+
+def _ptr(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def lib():
+    return _lib
+
+
+class Model:
+    """A loaded model on one GPU (Model::load, model.rs:110-215)."""
+
+    def __init__(self, handle):
+        self._h = handle
+        self.cfg = Config()
+        _check(_lib.hs_model_config(handle, C.byref(self.cfg)))
+
+    @classmethod
+    def load(cls, path, max_ctx=2048, device=0):
+        h = C.c_void_p()
+        _check(_lib.hs_model_load(os.fsencode(path), max_ctx, device, C.byref(h)))
+        return cls(h)
+
+    @property
+    def fingerprint(self):
+        return int(self.cfg.fingerprint)
+
+    @property
+    def eos(self):
+        return int(self.cfg.eos)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.hs_model_free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def tensor(self, name):
+        """A loaded tensor copied back: f16 bits (uint16) or f32."""
+        dt = C.c_uint32()
+        _check(_lib.hs_model_tensor(self._h, name.encode(), None, 0, C.byref(dt)))
+        c = self.cfg
+        hd = c.head_dim
+        shapes = {
+            "token_embd.weight": c.vocab * c.d_model, "output.weight": c.vocab * c.d_model,
+            "output_norm.weight": c.d_model,
+        }
+        base = name.split(".", 2)[-1] if name.startswith("blk.") else name
+        per = {
+            "attn_norm.weight": c.d_model, "ffn_norm.weight": c.d_model,
+            "attn_q.weight": c.n_heads * hd * c.d_model, "attn_k.weight": c.n_kv_heads * hd * c.d_model,
+            "attn_v.weight": c.n_kv_heads * hd * c.d_model, "attn_output.weight": c.d_model * c.n_heads * hd,
+            "attn_q.bias": c.n_heads * hd, "attn_k.bias": c.n_kv_heads * hd, "attn_v.bias": c.n_kv_heads * hd,
+            "ffn_gate.weight": c.d_ff * c.d_model, "ffn_up.weight": c.d_ff * c.d_model,
+            "ffn_down.weight": c.d_model * c.d_ff,
+        }
+        count = shapes.get(name) if not name.startswith("blk.") else per[base]
+        out = np.zeros(count, dtype=np.uint16 if dt.value == 1 else np.float32)
+        _check(_lib.hs_model_tensor(self._h, name.encode(), _ptr(out), out.nbytes, None))
+        return out
+
+    def kv_spec(self, layout=TOKEN_MAJOR):
+        c = self.cfg
+        return KvSpec(c.n_layers, c.n_kv_heads, c.head_dim, c.max_ctx, layout)
+
+    def kv(self, layout=TOKEN_MAJOR, page_size=4096):
+        return Kv.alloc(self, layout, page_size)
+
+    def scratch(self):
+        return Scratch(self)
+
+    def forward(self, kv, token, pos, scratch):
+        """One token through every layer; appends its K/V to `kv`."""
+        _check(_lib.hs_forward(self._h, kv._h, token, pos, scratch._h))
+
+
+class Kv:
+    """Device KV region in the reference's byte layout, with a dirty-page bitmap."""
+
+    def __init__(self, handle, model):
+        self._h = handle
+        self.model = model
+        self.spec = KvSpec()
+        b, ps, npg = C.c_uint64(), C.c_uint32(), C.c_uint64()
+        _check(_lib.hs_kv_info(handle, C.byref(self.spec), C.byref(b), C.byref(ps), C.byref(npg)))
+        self.bytes, self.page_size, self.n_pages = b.value, ps.value, npg.value
+        self.n_words = (self.n_pages + 63) // 64
+
+    @classmethod
+    def alloc(cls, model, layout=TOKEN_MAJOR, page_size=4096):
+        h = C.c_void_p()
+        _check(_lib.hs_kv_alloc(model._h, layout, page_size, C.byref(h)))
+        return cls(h, model)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.hs_kv_free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def read(self, off, length):
+        out = np.zeros(length, dtype=np.uint8)
+        _check(_lib.hs_kv_read(self._h, off, length, _ptr(out)))
+        return out
+
+    def write(self, off, data):
+        data = np.ascontiguousarray(np.frombuffer(bytes(data), dtype=np.uint8))
+        _check(_lib.hs_kv_write(self._h, off, data.size, _ptr(data)))
+
+    def floats(self):
+        return self.read(0, self.bytes).view(np.float32)
+
+    def hash(self, n_pos):
+        out = C.c_uint64()
+        _check(_lib.hs_kv_hash(self._h, n_pos, C.byref(out)))
+        return out.value
+
+    def arm(self):
+        _check(_lib.hs_kv_arm(self._h))
+
+    def harvest(self):
+        w = np.zeros(self.n_words, dtype=np.uint64)
+        _check(_lib.hs_kv_harvest(self._h, _ptr(w), w.size))
+        return w
+
+    def disarm(self):
+        _check(_lib.hs_kv_disarm(self._h))
+
+    def copy_runs_to(self, dst, runs):
+        r = np.array([x for run in runs for x in run] or [0], dtype=np.uint64)
+        _check(_lib.hs_kv_copy_runs(self._h, dst._h, _ptr(r), len(runs)))
+
+
+def live_ranges_between(spec, a, b):
+    n = _lib.hs_kv_live_ranges_between(C.byref(spec), a, b, None, 0)
+    out = np.zeros(2 * max(n, 1), dtype=np.uint64)
+    _lib.hs_kv_live_ranges_between(C.byref(spec), a, b, _ptr(out), n)
+    return [(int(out[2 * i]), int(out[2 * i + 1])) for i in range(n)]
+
+
+def runs_to_byte_runs(words, n_pages, page_size, live):
+    w = np.ascontiguousarray(words, dtype=np.uint64)
+    lv = np.array([x for r in live for x in r] or [0], dtype=np.uint64)
+    n = _lib.hs_runs_to_byte_runs(_ptr(w), n_pages, page_size, _ptr(lv), len(live), None, 0)
+    out = np.zeros(2 * max(n, 1), dtype=np.uint64)
+    _lib.hs_runs_to_byte_runs(_ptr(w), n_pages, page_size, _ptr(lv), len(live), _ptr(out), n)
+    return [(int(out[2 * i]), int(out[2 * i + 1])) for i in range(n)]
+
+
+class Scratch:
+    """Per-decode-thread device state: activations, logits, stream, graphs."""
+
+    def __init__(self, model):
+        h = C.c_void_p()
+        _check(_lib.hs_scratch_new(model._h, C.byref(h)))
+        self._h = h
+        self.model = model
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.hs_scratch_free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    def logits(self):
+        out = np.zeros(self.model.cfg.vocab, dtype=np.float32)
+        _check(_lib.hs_scratch_logits(self._h, _ptr(out), out.size))
+        return out
+
+    def set_logits(self, logits):
+        a = np.ascontiguousarray(logits, dtype=np.float32)
+        _check(_lib.hs_scratch_set_logits(self._h, _ptr(a), a.size))
+
+    @property
+    def stream(self):
+        return _lib.hs_scratch_stream(self._h)
+
+    def launches_per_step(self):
+        n = C.c_uint32()
+        _check(_lib.hs_seq_launches_per_step(self._h, C.byref(n)))
+        return n.value
+
+
+class Sampler:
+    """Sampler{cfg, rng} (sampler.rs:85-167); sampling runs on the device."""
+
+    def __init__(self, cfg=None, rng=None):
+        self.cfg = cfg or SamplerCfg.default()
+        self.rng = rng or Rng.seed(self.cfg.seed)
+
+    def sample(self, scratch, history=()):
+        h = np.ascontiguousarray(history, dtype=np.uint32)
+        out = C.c_uint32()
+        _check(_lib.hs_sample(scratch._h, C.byref(self.cfg), C.byref(self.rng), _ptr(h) if h.size else None, h.size,
+                              C.byref(out)))
+        return out.value
+
+
+def argmax(scratch):
+    out = C.c_uint32()
+    _check(_lib.hs_argmax(scratch._h, C.byref(out)))
+    return out.value
+
+
+def run_seq(model, kv, scratch, tokens, prompt_len, max_tokens, cfg, rng, filled=0, stop_at_filled=0, done=0,
+            done_reason=0):
+    """The seq.rs decode loop on the device. Returns (tokens, SeqState, Rng)."""
+    cap = model.cfg.max_ctx + 1
+    buf = np.zeros(cap, dtype=np.uint32)
+    buf[: len(tokens)] = tokens
+    n = C.c_uint64(len(tokens))
+    st = SeqState(prompt_len, filled, max_tokens, done, done_reason)
+    _check(_lib.hs_seq_run(model._h, kv._h, scratch._h, _ptr(buf), C.byref(n), cap, C.byref(st), C.byref(cfg),
+                           C.byref(rng), stop_at_filled))
+    return buf[: n.value].copy(), st, rng
+
+
+def dequant_f16(ggml_type, src_dev_ptr, n, dst_dev_ptr, stream=None):
+    _check(_lib.hs_dequant_f16(ggml_type, C.c_void_p(src_dev_ptr), n, C.c_void_p(dst_dev_ptr),
+                               C.c_void_p(stream) if stream else None))
+
+
+QWEN05 = dict(n_layers=24, d_model=896, n_heads=14, n_kv_heads=2, d_ff=4864, vocab=151936)
+QWEN15 = dict(n_layers=28, d_model=1536, n_heads=12, n_kv_heads=2, d_ff=8960, vocab=151936)
+
+
+def write_synthetic_gguf(path, n_layers, d_model, n_heads, n_kv_heads, d_ff, vocab, seed, context_length=32768,
+                         eos=None, eps=1e-6, rope_base=1e6, weight_std=0.02, bias_std=0.02, embd_type=14,
+                         weight_type=12, tied=True, threads=0):
+    """Seeded random-init Qwen2-architecture GGUF (no counterpart in hs-engine)."""
+    if eos is None:
+        eos = 151643 if vocab > 151643 else vocab - 1
+    spec = SynthSpec(n_layers, d_model, n_heads, n_kv_heads, d_ff, vocab, context_length, eos, eps, rope_base,
+                     weight_std, bias_std, embd_type, weight_type, 1 if tied else 0, threads or (os.cpu_count() or 1),
+                     seed)
+    _check(_lib.hs_synth_write(os.fsencode(path), C.byref(spec)))
+    return path

@@ -1,0 +1,712 @@
+// Batch-1 token-loop kernels for sm_100a.
+//
+// Numerics are the reference's, operation for operation (hotseat
+// crates/hs-engine/src/model.rs:240-327 and math.rs): every dot product is
+// eight strided lanes acc[l] += w[8j+l]*x[8j+l] accumulated in order, folded as
+// ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)); no FMA anywhere. The GPU therefore
+// produces the same bits as the CPU reference for the same weights, which is
+// what lets a sequence move between the two.
+//
+// Performance shape (HBM-bound decode): each GEMV CTA owns a contiguous row
+// range, TMA-loads its weight rows (128B-swizzled 64-column slabs) into shared
+// memory *before* griddepcontrol.wait, so the weight stream of kernel k+1
+// overlaps the tail of kernel k under programmatic dependent launch; after the
+// wait it reads the activation and runs the fixed-order lanes out of shared
+// memory, one (row, lane-group) per thread.
+#include <cfloat>
+
+#include "common.h"
+#include "kernels.h"
+
+namespace hs {
+namespace {
+
+__device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) { return *(const volatile uint32_t*)p; }
+
+template <int L>
+struct HalfVec;
+template <>
+struct HalfVec<1> {
+    static __device__ __forceinline__ void load(const uint8_t* p, float* w) {
+        w[0] = h2f(*reinterpret_cast<const uint16_t*>(p));
+    }
+};
+template <>
+struct HalfVec<2> {
+    static __device__ __forceinline__ void load(const uint8_t* p, float* w) {
+        uint32_t v = *reinterpret_cast<const uint32_t*>(p);
+        w[0] = h2f((uint16_t)v);
+        w[1] = h2f((uint16_t)(v >> 16));
+    }
+};
+template <>
+struct HalfVec<4> {
+    static __device__ __forceinline__ void load(const uint8_t* p, float* w) {
+        uint2 v = *reinterpret_cast<const uint2*>(p);
+        w[0] = h2f((uint16_t)v.x);
+        w[1] = h2f((uint16_t)(v.x >> 16));
+        w[2] = h2f((uint16_t)v.y);
+        w[3] = h2f((uint16_t)(v.y >> 16));
+    }
+};
+template <>
+struct HalfVec<8> {
+    static __device__ __forceinline__ void load(const uint8_t* p, float* w) {
+        uint4 v = *reinterpret_cast<const uint4*>(p);
+        uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            w[2 * i] = h2f((uint16_t)u[i]);
+            w[2 * i + 1] = h2f((uint16_t)(u[i] >> 16));
+        }
+    }
+};
+
+// Fold this thread's L lanes with its row-mates' (8/L consecutive lanes of
+// the warp) into the reference's fold tree (math.rs:89-93). IEEE addition is
+// commutative, so each partner computing b+a instead of a+b is the same value.
+template <int L>
+__device__ __forceinline__ float fold_lanes(const float* a) {
+    const unsigned full = 0xffffffffu;
+    float v;
+    if (L == 8) {
+        v = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
+                      __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
+    } else if (L == 4) {
+        v = __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3]));
+        v = __fadd_rn(v, __shfl_xor_sync(full, v, 1));
+    } else if (L == 2) {
+        v = __fadd_rn(a[0], a[1]);
+        v = __fadd_rn(v, __shfl_xor_sync(full, v, 1));
+        v = __fadd_rn(v, __shfl_xor_sync(full, v, 2));
+    } else {
+        v = a[0];
+        v = __fadd_rn(v, __shfl_xor_sync(full, v, 1));
+        v = __fadd_rn(v, __shfl_xor_sync(full, v, 2));
+        v = __fadd_rn(v, __shfl_xor_sync(full, v, 4));
+    }
+    return v;
+}
+
+// ------------------------------------------------------------------ GEMV
+// y[r] = fold8(W[r] . x) for the CTA's rows, with the prologue/epilogue that
+// model.rs fuses around each matvec: rmsnorm (math.rs:200-207) of the
+// residual stream (or of the embedding row, model.rs:247-250) on the way in;
+// bias (model.rs:255-257), residual add (308-310, 319-321) or SiLU gate
+// (315-317) on the way out.
+template <int OUT, int L>
+__global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMap tm0,
+                                              const __grid_constant__ CUtensorMap tm1, const GemvArgs a,
+                                              const int in_mode) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int NMAT = OUT == OUT_SILU ? 2 : 1;
+    const uint32_t kslabs = a.n / 64;
+    const uint32_t mat_bytes = kslabs * a.slab_stride;
+    const uint32_t stage_bytes = NMAT * mat_bytes;
+    uint8_t* stages = smem;
+    float* xs = reinterpret_cast<float*>(smem + a.nst * stage_bytes);
+    float* outs = xs + a.n;
+    float* red = outs + 2 * a.rt;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + 32);
+    const uint32_t tid = threadIdx.x;
+
+    uint32_t r0, r1;
+    split_range(a.rows, gridDim.x, blockIdx.x, &r0, &r1);
+    const uint32_t mine = r1 - r0;
+    const uint32_t ntiles = (mine + a.rt - 1) / a.rt;
+    const uint32_t tx_bytes = NMAT * kslabs * a.rt * 128;
+
+    if (tid == 0) {
+        for (uint32_t s = 0; s < a.nst; s++) mbar_init(&bars[s], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    auto issue = [&](uint32_t t) {
+        uint32_t s = t % a.nst;
+        uint8_t* st = stages + s * stage_bytes;
+        mbar_expect_tx(&bars[s], tx_bytes);
+        int y = (int)(r0 + t * a.rt);
+        for (int m = 0; m < NMAT; m++)
+            for (uint32_t k = 0; k < kslabs; k++)
+                tma_load_2d(st + m * mat_bytes + k * a.slab_stride, m ? &tm1 : &tm0, (int)(k * 64), y, &bars[s]);
+    };
+    const uint32_t npre = ntiles < a.nst ? ntiles : a.nst;
+    // Weights never change: fetch them before waiting on the previous kernel.
+    if (tid == 0)
+        for (uint32_t t = 0; t < npre; t++) issue(t);
+    pdl_launch_dependents();
+    pdl_wait();
+
+    DevCtl* ctl = a.ctl;
+    bool run = ld_volatile(&ctl->active) != 0;
+    uint32_t token = 0;
+    if (run && in_mode == IN_EMBED_NORM) {
+        token = ld_volatile(&ctl->token);
+        if (token >= ctl->vocab) {
+            if (tid == 0 && blockIdx.x == 0) atomicOr(&ctl->err, ERR_TOKEN);
+            run = false;
+        }
+    }
+    if (!run) {
+        // Never leave with bulk copies in flight into this CTA's shared memory.
+        for (uint32_t t = 0; t < npre; t++) mbar_wait_bounded(&bars[t], 0);
+        return;
+    }
+
+    // ---- activation prologue
+    const uint32_t n = a.n;
+    if (in_mode == IN_EMBED_NORM) {
+        const uint16_t* row = a.embd + (size_t)token * n;
+        for (uint32_t i = tid; i < n; i += blockDim.x) {
+            float v = h2f(row[i]);
+            xs[i] = v;
+            if (blockIdx.x == 0) a.x_out[i] = v;
+        }
+    } else {
+        const float4* s4 = reinterpret_cast<const float4*>(a.src);
+        float4* x4 = reinterpret_cast<float4*>(xs);
+        for (uint32_t i = tid; i < n / 4; i += blockDim.x) x4[i] = s4[i];
+    }
+    __syncthreads();
+    if (in_mode != IN_PLAIN) {
+        // rmsnorm: ss = dot_f32(x, x) in the 8-lane shape; scale = 1/sqrt(ss/n + eps);
+        // out[i] = x[i] * scale * g[i].
+        if (tid < 32) {
+            float acc = 0.0f;
+            if (tid < 8)
+                for (uint32_t j = 0; j < n / 8; j++) {
+                    float v = xs[8 * j + tid];
+                    acc = __fadd_rn(acc, __fmul_rn(v, v));
+                }
+            float v = acc;
+            v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+            v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+            v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+            if (tid == 0) red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(v, (float)n), a.eps)));
+        }
+        __syncthreads();
+        const float scale = red[0];
+        for (uint32_t i = tid; i < n; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], scale), a.norm_g[i]);
+        __syncthreads();
+    }
+
+    // ---- fixed-order lanes out of shared memory
+    constexpr uint32_t TPR = 8 / L;  // threads per row
+    const uint32_t vr = tid / TPR, g = tid % TPR;
+    const bool lane_active = vr < NMAT * a.rt;
+    const uint32_t m = lane_active ? vr / a.rt : 0, r = lane_active ? vr % a.rt : 0;
+    for (uint32_t t = 0; t < ntiles; t++) {
+        const uint32_t s = t % a.nst;
+        if (!mbar_wait_bounded(&bars[s], (t / a.nst) & 1)) {
+            if (tid == 0) atomicOr(&ctl->err, ERR_TIMEOUT);
+            return;
+        }
+        float acc[L];
+#pragma unroll
+        for (int i = 0; i < L; i++) acc[i] = 0.0f;
+        if (lane_active) {
+            const uint8_t* base = stages + s * stage_bytes + m * mat_bytes + r * 128;
+            const uint32_t sw = r & 7;
+            for (uint32_t k = 0; k < kslabs; k++) {
+                const uint8_t* sb = base + k * a.slab_stride;
+                const float* xk = xs + k * 64 + g * L;
+#pragma unroll
+                for (uint32_t c = 0; c < 8; c++) {
+                    float w[L];
+                    HalfVec<L>::load(sb + (((c ^ sw) << 4) | (g * L * 2)), w);
+#pragma unroll
+                    for (int i = 0; i < L; i++) acc[i] = __fadd_rn(acc[i], __fmul_rn(w[i], xk[c * 8 + i]));
+                }
+            }
+        }
+        const float v = fold_lanes<L>(acc);
+        const uint32_t rr = t * a.rt + r;  // row index inside this CTA's range
+        if (OUT == OUT_SILU) {
+            if (lane_active && g == 0) outs[m * a.rt + r] = v;
+            __syncthreads();
+            if (tid < a.rt && t * a.rt + tid < mine) {
+                const float gv = outs[tid], uv = outs[a.rt + tid];
+                a.dst[r0 + t * a.rt + tid] = __fmul_rn(ref_silu(gv), uv);
+            }
+        } else if (lane_active && g == 0 && rr < mine) {
+            const uint32_t row = r0 + rr;
+            if (OUT == OUT_STORE) a.dst[row] = a.bias ? __fadd_rn(v, a.bias[row]) : v;
+            else a.dst[row] = __fadd_rn(a.dst[row], v);
+        }
+        __syncthreads();
+        if (tid == 0 && t + a.nst < ntiles) {
+            fence_proxy_async_smem();
+            issue(t + a.nst);
+        }
+    }
+}
+
+// ------------------------------------------------------------ attention
+// One CTA per query head (model.rs:259-305): RoPE on q and k from the cached
+// tables (rope_apply, model.rs:365-373); the head group's first CTA appends
+// k, v at `pos` (model.rs:268-275) and marks the touched pages in the dirty
+// bitmap; scores p in [0, pos] = dot_f32(q, k_p) * (1/sqrt(hd)); softmax with
+// exp_f32, sequential sum and 1/sum (math.rs:210-226); out = sum_p sc[p]*v_p in
+// position order (axpy, math.rs:185-190).
+template <int HD>
+__global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    constexpr int CH = 8192 / HD;  // positions staged per chunk
+    constexpr int RS = HD + 4;     // padded row stride (floats): conflict-free row reads
+    constexpr int HALF = HD / 2;
+    float* q = sm;
+    float* kc = q + HD;
+    float* vc = kc + HD;
+    float* red = vc + HD;
+    float* buf = red + 64;
+    float* sc = buf + CH * RS;
+    const uint32_t tid = threadIdx.x;
+    pdl_launch_dependents();
+    pdl_wait();
+    DevCtl* ctl = a.ctl;
+    if (!ld_volatile(&ctl->active)) return;
+    const uint32_t pos = ld_volatile(&ctl->pos);
+    if (pos >= a.max_ctx) {
+        if (tid == 0 && blockIdx.x == 0) atomicOr(&ctl->err, ERR_POS);
+        return;
+    }
+    const uint32_t h = blockIdx.x, groups = a.nh / a.nkv, kvh = h / groups;
+    if (tid < HD) {
+        q[tid] = a.qkv[h * HD + tid];
+        kc[tid] = a.qkv[a.nh * HD + kvh * HD + tid];
+        vc[tid] = a.qkv[(a.nh + a.nkv) * HD + kvh * HD + tid];
+    }
+    __syncthreads();
+    if (tid < HALF) {
+        const float c = a.rope_cos[(size_t)pos * HALF + tid], s = a.rope_sin[(size_t)pos * HALF + tid];
+        float x0 = q[tid], x1 = q[tid + HALF];
+        q[tid] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        q[tid + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        x0 = kc[tid];
+        x1 = kc[tid + HALF];
+        kc[tid] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        kc[tid + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    }
+    __syncthreads();
+
+    const uint64_t plane = (uint64_t)a.max_ctx * a.nkv * HD;
+    const uint64_t lbase = (uint64_t)a.layer * 2 * plane;
+    auto row_off = [&](uint32_t p, uint32_t is_v) -> uint64_t {
+        uint64_t within = a.layout == 0 ? ((uint64_t)p * a.nkv + kvh) * HD : ((uint64_t)kvh * a.max_ctx + p) * HD;
+        return lbase + (is_v ? plane : 0) + within;
+    };
+    if (h % groups == 0) {
+        if (tid < HD) {
+            a.kv[row_off(pos, 0) + tid] = kc[tid];
+            a.kv[row_off(pos, 1) + tid] = vc[tid];
+        }
+        // Data first, then the mark: a harvester that sees the page dirty
+        // also sees the bytes that dirtied it.
+        __syncthreads();
+        if (tid < 2 && ld_volatile(a.tracking)) {
+            __threadfence();
+            const uint64_t off = row_off(pos, tid) * 4, last = off + HD * 4 - 1;
+            for (uint64_t pg = off >> a.page_shift; pg <= (last >> a.page_shift); pg++)
+                atomicOr(reinterpret_cast<unsigned long long*>(&a.dirty[pg >> 6]), 1ull << (pg & 63));
+        }
+    }
+
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+    const uint32_t n = pos + 1;
+    // pass 1: scores
+    for (uint32_t c0 = 0; c0 < n; c0 += CH) {
+        const uint32_t cnt = min((uint32_t)CH, n - c0);
+        for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += blockDim.x) {
+            const uint32_t rr = idx / (HD / 4), c4 = idx % (HD / 4), p = c0 + rr;
+            float4 v = p == pos ? reinterpret_cast<const float4*>(kc)[c4]
+                                : *reinterpret_cast<const float4*>(a.kv + row_off(p, 0) + 4 * c4);
+            *reinterpret_cast<float4*>(buf + rr * RS + 4 * c4) = v;
+        }
+        __syncthreads();
+        if (tid < cnt) {
+            const float* kr = buf + tid * RS;
+            float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll 4
+            for (int j = 0; j < HD / 8; j++)
+#pragma unroll
+                for (int l = 0; l < 8; l++) acc[l] = __fadd_rn(acc[l], __fmul_rn(q[8 * j + l], kr[8 * j + l]));
+            const float d = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3])),
+                                      __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7])));
+            sc[c0 + tid] = __fmul_rn(d, scale);
+        }
+        __syncthreads();
+    }
+    // softmax: max (order-free), exp, sequential sum, scale by 1/sum
+    float mx = -FLT_MAX * 2.0f;  // -inf
+    for (uint32_t p = tid; p < n; p += blockDim.x) mx = fmaxf(mx, sc[p]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float m2 = red[0];
+        for (uint32_t w = 1; w < blockDim.x / 32; w++) m2 = fmaxf(m2, red[w]);
+        red[32] = m2;
+    }
+    __syncthreads();
+    mx = red[32];
+    for (uint32_t p = tid; p < n; p += blockDim.x) sc[p] = ref_exp(__fsub_rn(sc[p], mx));
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.0f;
+        for (uint32_t p = 0; p < n; p++) sum = __fadd_rn(sum, sc[p]);
+        red[33] = __fdiv_rn(1.0f, sum);
+    }
+    __syncthreads();
+    const float inv = red[33];
+    for (uint32_t p = tid; p < n; p += blockDim.x) sc[p] = __fmul_rn(sc[p], inv);
+    __syncthreads();
+    // pass 2: out[d] = sum over p, in order, of sc[p] * v_p[d]
+    float out = 0.0f;
+    for (uint32_t c0 = 0; c0 < n; c0 += CH) {
+        const uint32_t cnt = min((uint32_t)CH, n - c0);
+        for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += blockDim.x) {
+            const uint32_t rr = idx / (HD / 4), c4 = idx % (HD / 4), p = c0 + rr;
+            float4 v = p == pos ? reinterpret_cast<const float4*>(vc)[c4]
+                                : *reinterpret_cast<const float4*>(a.kv + row_off(p, 1) + 4 * c4);
+            *reinterpret_cast<float4*>(buf + rr * RS + 4 * c4) = v;
+        }
+        __syncthreads();
+        if (tid < HD)
+            for (uint32_t t = 0; t < cnt; t++) out = __fadd_rn(out, __fmul_rn(sc[c0 + t], buf[t * RS + tid]));
+        __syncthreads();
+    }
+    if (tid < HD) a.att[h * HD + tid] = out;
+}
+
+// -------------------------------------------------------------- sampler
+// Stage 1: each CTA takes 1024 logits, applies the repetition penalty to the
+// history tokens in its slice (sampler.rs:103-111; one token can be penalised
+// several times, in history order), then either finds its first maximum
+// (greedy, sampler.rs:177-187) or sorts its slice under cmp_desc and keeps the
+// best kmax keys.
+__device__ __forceinline__ bool seq_needs_sample(const DevCtl* c) {
+    if (c->mode == 1) return true;
+    return ld_volatile(&c->active) && c->filled + 1 == c->n_tokens;
+}
+
+__global__ void __launch_bounds__(256) k_sample_cand(const SampleArgs a) {
+    __shared__ float vals[kSampleSlice];
+    __shared__ uint64_t keys[kSampleSlice];
+    __shared__ float bv_s[256];
+    __shared__ uint32_t bi_s[256];
+    const uint32_t tid = threadIdx.x;
+    pdl_launch_dependents();
+    pdl_wait();
+    const DevCtl* c = a.ctl;
+    if (!seq_needs_sample(c)) return;
+    const uint32_t base = blockIdx.x * kSampleSlice;
+    for (uint32_t i = tid; i < kSampleSlice; i += blockDim.x)
+        vals[i] = base + i < a.vocab ? a.logits[base + i] : 0.0f;
+    __syncthreads();
+    if (tid == 0 && c->repeat_penalty != 1.0f && c->repeat_last_n > 0) {
+        const uint64_t nt = c->n_tokens;
+        const uint64_t nw = c->repeat_last_n < nt ? c->repeat_last_n : nt;
+        for (uint64_t i = nt - nw; i < nt; i++) {
+            const uint32_t t = a.tokens[i];
+            if (t >= base && t < base + kSampleSlice && t < a.vocab) {
+                const float l = vals[t - base];
+                vals[t - base] = l > 0.0f ? __fdiv_rn(l, c->repeat_penalty) : __fmul_rn(l, c->repeat_penalty);
+            }
+        }
+    }
+    __syncthreads();
+    if (c->temperature <= 0.0f) {
+        float bv = __int_as_float(0xff800000);  // -inf
+        uint32_t bi = 0xffffffffu;
+        for (uint32_t i = tid * 4; i < tid * 4 + 4; i++)
+            if (base + i < a.vocab && vals[i] > bv) {
+                bv = vals[i];
+                bi = base + i;
+            }
+        bv_s[tid] = bv;
+        bi_s[tid] = bi;
+        __syncthreads();
+        if (tid == 0) {
+            float v = bv_s[0];
+            uint32_t ix = bi_s[0];
+            for (uint32_t t = 1; t < blockDim.x; t++)
+                if (bi_s[t] != 0xffffffffu && (ix == 0xffffffffu || bv_s[t] > v)) {
+                    v = bv_s[t];
+                    ix = bi_s[t];
+                }
+            a.argbuf[blockIdx.x] = ((uint64_t)__float_as_uint(v) << 32) | ix;
+        }
+        return;
+    }
+    for (uint32_t i = tid; i < kSampleSlice; i += blockDim.x)
+        keys[i] = base + i < a.vocab ? cand_key(vals[i], base + i) : ~0ull;
+    __syncthreads();
+    for (uint32_t k = 2; k <= kSampleSlice; k <<= 1)
+        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+            for (uint32_t i = tid; i < kSampleSlice; i += blockDim.x) {
+                const uint32_t ixj = i ^ j;
+                if (ixj > i) {
+                    const uint64_t x = keys[i], y = keys[ixj];
+                    if ((x > y) == ((i & k) == 0)) {
+                        keys[i] = y;
+                        keys[ixj] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    for (uint32_t i = tid; i < a.kmax; i += blockDim.x) a.cand[(size_t)blockIdx.x * a.kmax + i] = keys[i];
+}
+
+// Stage 2 (one CTA): merge the per-CTA lists (already sorted) by a warp
+// tournament into the global top-k, then run the reference's serial tail on
+// one thread: temperature softmax with exp_f32, nucleus cut, one next_f32
+// draw (sampler.rs:134-166). In sequence mode, then commit the step exactly as
+// seq.rs:273-312 does and arm the next one.
+constexpr int kMaxListsPerLane = 8;
+
+__global__ void __launch_bounds__(256) k_sample_final(const SampleArgs a) {
+    extern __shared__ uint64_t lists[];  // n_cta * kmax keys, then the merged top-k
+    __shared__ float pk[1024];
+    __shared__ uint32_t tok_s;
+    const uint32_t tid = threadIdx.x;
+    pdl_launch_dependents();
+    pdl_wait();
+    DevCtl* c = a.ctl;
+    const bool seq = c->mode == 0;
+    if (seq && !ld_volatile(&c->active)) return;
+    const bool need = seq_needs_sample(c);
+    if (tid == 0) tok_s = 0;
+    if (need) {
+        if (c->temperature <= 0.0f) {
+            if (tid == 0) {
+                float v = 0.0f;
+                uint32_t ix = 0xffffffffu;
+                for (uint32_t i = 0; i < a.n_cta; i++) {
+                    const uint64_t e = a.argbuf[i];
+                    const uint32_t ei = (uint32_t)e;
+                    const float ev = __uint_as_float((uint32_t)(e >> 32));
+                    if (ei != 0xffffffffu && (ix == 0xffffffffu || ev > v)) {
+                        v = ev;
+                        ix = ei;
+                    }
+                }
+                tok_s = ix == 0xffffffffu ? 0u : ix;
+            }
+        } else {
+            const uint32_t total = a.n_cta * a.kmax;
+            for (uint32_t i = tid; i < total; i += blockDim.x) lists[i] = a.cand[i];
+            __syncthreads();
+            const uint32_t k = c->top_k == 0 ? a.vocab : min(c->top_k, a.vocab);
+            uint64_t* merged = lists + total;
+            if (tid < 32) {
+                uint32_t ptr[kMaxListsPerLane];
+                uint64_t head[kMaxListsPerLane];
+#pragma unroll
+                for (int s = 0; s < kMaxListsPerLane; s++) {
+                    const uint32_t li = tid + 32 * s;
+                    ptr[s] = 0;
+                    head[s] = li < a.n_cta ? lists[li * a.kmax] : ~0ull;
+                }
+                for (uint32_t round = 0; round < k; round++) {
+                    uint64_t best = ~0ull;
+                    int bs = -1;
+#pragma unroll
+                    for (int s = 0; s < kMaxListsPerLane; s++)
+                        if (head[s] < best) {
+                            best = head[s];
+                            bs = s;
+                        }
+                    uint64_t wm = best;
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const uint64_t other = __shfl_xor_sync(0xffffffffu, wm, o);
+                        wm = other < wm ? other : wm;
+                    }
+                    if (bs >= 0 && best == wm) {
+                        merged[round] = wm;
+#pragma unroll
+                        for (int s = 0; s < kMaxListsPerLane; s++)
+                            if (s == bs) {
+                                ptr[s]++;
+                                const uint32_t li = tid + 32 * s;
+                                head[s] = ptr[s] < a.kmax ? lists[li * a.kmax + ptr[s]] : ~0ull;
+                            }
+                    }
+                    __syncwarp();
+                }
+            }
+            __syncthreads();
+            if (tid == 0) {
+                const float inv_t = __fdiv_rn(1.0f, c->temperature);
+                const float mx = key_value(merged[0]);
+                float sum = 0.0f;
+                for (uint32_t i = 0; i < k; i++) {
+                    pk[i] = ref_exp(__fmul_rn(__fsub_rn(key_value(merged[i]), mx), inv_t));
+                    sum = __fadd_rn(sum, pk[i]);
+                }
+                uint32_t cut = k;
+                if (c->top_p < 1.0f) {
+                    const float target = __fmul_rn(c->top_p, sum);
+                    float acc = 0.0f;
+                    for (uint32_t i = 0; i < k; i++) {
+                        acc = __fadd_rn(acc, pk[i]);
+                        if (acc >= target) {
+                            cut = i + 1;
+                            break;
+                        }
+                    }
+                    sum = 0.0f;
+                    for (uint32_t i = 0; i < cut; i++) sum = __fadd_rn(sum, pk[i]);
+                }
+                uint64_t s4[4] = {c->rng[0], c->rng[1], c->rng[2], c->rng[3]};
+                const float u = __fmul_rn((float)(rng_next(s4) >> 40), 1.0f / 16777216.0f);
+                for (int i = 0; i < 4; i++) c->rng[i] = s4[i];
+                c->draws += 1;
+                const float r = __fmul_rn(u, sum);
+                uint32_t pick = (uint32_t)merged[cut - 1];
+                float acc = 0.0f;
+                for (uint32_t i = 0; i < cut; i++) {
+                    acc = __fadd_rn(acc, pk[i]);
+                    if (r < acc) {
+                        pick = (uint32_t)merged[i];
+                        break;
+                    }
+                }
+                tok_s = pick;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid != 0) return;
+    if (!seq) {
+        c->out_token = tok_s;
+        return;
+    }
+    // seq.rs:273-312 commit, then arm the next step (seq.rs:239-268).
+    const uint64_t filled = c->filled + 1;
+    c->filled = filled;
+    if (filled == c->n_tokens) {
+        const uint32_t next = tok_s;
+        const uint64_t generated = c->n_tokens - c->prompt_len;
+        if (next == c->eos) {
+            c->done = 1;
+            c->done_reason = 1;
+        } else if (generated >= c->max_tokens) {
+            c->done = 1;
+            c->done_reason = 2;
+        } else if (c->n_tokens + 1 >= c->max_ctx) {
+            c->done = 1;
+            c->done_reason = 3;
+        } else if (c->n_tokens >= c->cap) {
+            c->done = 1;
+            atomicOr(&c->err, ERR_CAP);
+        } else {
+            a.tokens_w[c->n_tokens] = next;
+            c->n_tokens += 1;
+        }
+    }
+    uint32_t active = 0;
+    if (!c->done) {
+        if (filled >= c->n_tokens) {
+            c->done = 1;
+            atomicOr(&c->err, ERR_INVARIANT);
+        } else if (!(c->stop_at && filled >= c->stop_at)) {
+            active = 1;
+            c->token = a.tokens_w[filled];
+            c->pos = (uint32_t)filled;
+        }
+    }
+    c->active = active;
+}
+
+template <int OUT, int L>
+cudaError_t launch_gemv_t(const GemvPlan& p, const GemvArgs& a, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(p.threads);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_gemv<OUT, L>, p.tm0, p.tm1, a, p.in_mode);
+}
+
+template <typename K, typename A>
+cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, const A& args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args);
+}
+
+}  // namespace
+
+cudaError_t gemv_set_smem_limits() {
+    const int lim = 232448;
+#define HS_SET(O, L)                                                                                   \
+    {                                                                                                  \
+        cudaError_t e = cudaFuncSetAttribute(k_gemv<O, L>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim); \
+        if (e != cudaSuccess) return e;                                                                \
+    }
+    HS_SET(OUT_STORE, 1) HS_SET(OUT_STORE, 2) HS_SET(OUT_STORE, 4) HS_SET(OUT_STORE, 8)
+    HS_SET(OUT_RESID, 1) HS_SET(OUT_RESID, 2) HS_SET(OUT_RESID, 4) HS_SET(OUT_RESID, 8)
+    HS_SET(OUT_SILU, 1) HS_SET(OUT_SILU, 2) HS_SET(OUT_SILU, 4) HS_SET(OUT_SILU, 8)
+#undef HS_SET
+    cudaError_t e = cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_sample_final, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    return e;
+}
+
+cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_t st) {
+    switch (p.out_mode * 16 + p.lanes) {
+        case OUT_STORE * 16 + 1: return launch_gemv_t<OUT_STORE, 1>(p, a, st);
+        case OUT_STORE * 16 + 2: return launch_gemv_t<OUT_STORE, 2>(p, a, st);
+        case OUT_STORE * 16 + 4: return launch_gemv_t<OUT_STORE, 4>(p, a, st);
+        case OUT_STORE * 16 + 8: return launch_gemv_t<OUT_STORE, 8>(p, a, st);
+        case OUT_RESID * 16 + 1: return launch_gemv_t<OUT_RESID, 1>(p, a, st);
+        case OUT_RESID * 16 + 2: return launch_gemv_t<OUT_RESID, 2>(p, a, st);
+        case OUT_RESID * 16 + 4: return launch_gemv_t<OUT_RESID, 4>(p, a, st);
+        case OUT_RESID * 16 + 8: return launch_gemv_t<OUT_RESID, 8>(p, a, st);
+        case OUT_SILU * 16 + 1: return launch_gemv_t<OUT_SILU, 1>(p, a, st);
+        case OUT_SILU * 16 + 2: return launch_gemv_t<OUT_SILU, 2>(p, a, st);
+        case OUT_SILU * 16 + 4: return launch_gemv_t<OUT_SILU, 4>(p, a, st);
+        case OUT_SILU * 16 + 8: return launch_gemv_t<OUT_SILU, 8>(p, a, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+size_t attention_smem(uint32_t head_dim, uint32_t max_ctx) {
+    const size_t ch = 8192 / head_dim, rs = head_dim + 4;
+    return (3 * head_dim + 64 + ch * rs + max_ctx) * sizeof(float);
+}
+
+cudaError_t launch_attention(uint32_t head_dim, uint32_t nh, size_t smem, const AttnArgs& a, cudaStream_t st) {
+    if (head_dim == 64) return launch_pdl(k_attention<64>, dim3(nh), dim3(256), smem, st, a);
+    if (head_dim == 128) return launch_pdl(k_attention<128>, dim3(nh), dim3(256), smem, st, a);
+    return cudaErrorInvalidValue;
+}
+
+size_t sample_final_smem(uint32_t n_cta, uint32_t kmax) {
+    const size_t k_merge = kmax > 1024 ? 1024 : kmax;
+    return ((size_t)n_cta * kmax + k_merge + 1024) * sizeof(uint64_t);
+}
+
+cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st) {
+    cudaError_t e = launch_pdl(k_sample_cand, dim3(a.n_cta), dim3(256), 0, st, a);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_sample_final, dim3(1), dim3(256), sample_final_smem(a.n_cta, a.kmax), st, a);
+}
+
+}  // namespace hs

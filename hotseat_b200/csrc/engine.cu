@@ -1,0 +1,1131 @@
+// Host side of libhotseat: model load, KV regions, the per-thread scratch with
+// its captured CUDA graphs, and the C ABI declared in include/hotseat.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "gguf.h"
+#include "kernels.h"
+
+namespace hs {
+
+void rope_tables(uint32_t head_dim, uint32_t max_ctx, float rope_base, std::vector<float>* cos_t,
+                 std::vector<float>* sin_t);
+
+namespace {
+thread_local std::string g_err;
+}
+void set_error(const std::string& msg) { g_err = msg; }
+int fail(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+
+namespace {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library loads on hosts without a CUDA driver (it then fails at first use).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+int make_weight_map(CUtensorMap* map, const uint16_t* w, uint32_t n, uint32_t rows, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(HS_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {n, rows};
+    cuuint64_t strides[1] = {(cuuint64_t)n * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t*>(w), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(HS_E_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return HS_OK;
+}
+
+uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
+
+// Choose tile height, stages and lanes for one GEMV so the CTA's working set
+// fits in shared memory; prefer keeping a CTA's whole row range resident
+// (one stage, loaded before the PDL wait), else stream tiles through 2-3 stages.
+int plan_gemv(GemvPlan* p, int in_mode, int out_mode, uint32_t rows, uint32_t n, const uint16_t* w0,
+              const uint16_t* w1, int n_sm, size_t smem_cap) {
+    if (n % 64) return fail(HS_E_UNSUPPORTED, "row length must be a multiple of 64, got " + std::to_string(n));
+    const uint32_t nmat = out_mode == OUT_SILU ? 2 : 1, kslabs = n / 64;
+    p->in_mode = in_mode;
+    p->out_mode = out_mode;
+    p->n = n;
+    p->rows = rows;
+    p->grid = std::min<uint32_t>(rows, (uint32_t)n_sm);
+    const uint32_t per = (rows + p->grid - 1) / p->grid;
+    auto need = [&](uint32_t rt, uint32_t nst) -> size_t {
+        size_t slab = round_up(rt * 128, 1024);
+        return 1024 + (size_t)nst * nmat * kslabs * slab + (size_t)n * 4 + 2 * rt * 4 + 128 + nst * 8;
+    };
+    uint32_t rt = 0, nst = 0;
+    if (per * nmat <= 256 && need(per, 1) <= smem_cap) {
+        rt = per;
+        nst = 1;
+    } else {
+        for (uint32_t s : {3u, 2u}) {
+            for (uint32_t r = std::min<uint32_t>(per, 256 / nmat); r >= 1; r--) {
+                if (r < per && r > 8 && r % 8) continue;  // whole swizzle atoms when streaming
+                if (need(r, s) <= smem_cap) {
+                    rt = r;
+                    break;
+                }
+            }
+            if (rt) {
+                nst = s;
+                break;
+            }
+        }
+    }
+    if (!rt) return fail(HS_E_UNSUPPORTED, "GEMV tile does not fit in shared memory");
+    p->rt = rt;
+    p->nst = nst;
+    p->slab_stride = round_up(rt * 128, 1024);
+    const uint32_t vrows = rt * nmat;
+    p->lanes = vrows <= 32 ? 1 : vrows <= 64 ? 2 : vrows <= 128 ? 4 : 8;
+    p->threads = 256;
+    p->smem = need(rt, nst);
+    int rc = make_weight_map(&p->tm0, w0, n, rows, rt);
+    if (rc == HS_OK && w1) rc = make_weight_map(&p->tm1, w1, n, rows, rt);
+    return rc;
+}
+
+struct TensorRef {
+    void* ptr;
+    uint64_t count;
+    uint32_t dtype;  // 1 = f16, 0 = f32
+};
+
+}  // namespace
+}  // namespace hs
+
+using namespace hs;
+
+struct LayerDev {
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *bqkv = nullptr;
+    uint16_t *wqkv = nullptr, *wo = nullptr, *wgate = nullptr, *wup = nullptr, *wdown = nullptr;
+    GemvPlan qkv, o, gu, down;
+};
+
+struct hs_model {
+    hs_config cfg{};
+    int device = 0, n_sm = 0;
+    size_t smem_cap = 0;
+    uint16_t *embd = nullptr, *out_w = nullptr;
+    float *out_norm = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    std::vector<LayerDev> layers;
+    GemvPlan head;
+    size_t attn_smem = 0;
+    std::map<std::string, TensorRef> tensors;
+    std::vector<void*> allocs;
+    ~hs_model() {
+        if (!allocs.empty()) cudaSetDevice(device);
+        for (void* p : allocs) cudaFree(p);
+    }
+};
+
+struct hs_kv {
+    hs_kv_spec spec{};
+    int device = 0;
+    uint64_t bytes = 0, n_pages = 0, n_words = 0;
+    uint32_t page_size = 0, page_shift = 0;
+    float* base = nullptr;
+    uint64_t* dirty = nullptr;
+    uint64_t* harvest_buf = nullptr;
+    uint32_t* tracking = nullptr;
+    uint64_t fingerprint = 0;
+    cudaStream_t st = nullptr;
+    ~hs_kv() {
+        cudaSetDevice(device);
+        if (st) cudaStreamDestroy(st);
+        cudaFree(base);
+        cudaFree(dirty);
+        cudaFree(harvest_buf);
+        cudaFree(tracking);
+    }
+};
+
+struct hs_scratch {
+    const hs_model* m = nullptr;
+    cudaStream_t st = nullptr;
+    DevCtl* ctl = nullptr;       // device
+    DevCtl* ctl_h = nullptr;     // pinned host mirror
+    float *x = nullptr, *qkv = nullptr, *att = nullptr, *hb = nullptr, *logits = nullptr;
+    uint32_t* tokens = nullptr;
+    uint64_t cap = 0;
+    uint64_t *cand = nullptr, *argbuf = nullptr;
+    uint32_t n_cta = 0, kmax = 0;
+    cudaGraphExec_t g_fwd = nullptr, g_step = nullptr;
+    const hs_kv* graph_kv = nullptr;
+    uint32_t graph_kmax = 0;
+    uint32_t launches_fwd = 0;
+    ~hs_scratch() {
+        cudaSetDevice(m->device);
+        if (g_fwd) cudaGraphExecDestroy(g_fwd);
+        if (g_step) cudaGraphExecDestroy(g_step);
+        if (st) cudaStreamDestroy(st);
+        cudaFree(ctl);
+        cudaFreeHost(ctl_h);
+        for (void* p : {(void*)x, (void*)qkv, (void*)att, (void*)hb, (void*)logits, (void*)tokens, (void*)cand,
+                        (void*)argbuf})
+            cudaFree(p);
+    }
+};
+
+namespace hs {
+namespace {
+
+template <typename T>
+int dev_alloc(hs_model* m, T** p, uint64_t count) {
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, std::max<uint64_t>(count, 1) * sizeof(T));
+    if (e != cudaSuccess) return fail(HS_E_NOMEM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+    m->allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return HS_OK;
+}
+
+// Dequantise one GGUF tensor to f16 on the device at `dst` (model.rs:375-396).
+int load_f16(hs_model* m, const Gguf& g, const std::string& name, uint16_t* dst, uint64_t expect, uint8_t* staging,
+             cudaStream_t st) {
+    const GgufTensor* t = g.tensor(name);
+    if (!t) return fail(HS_E_IO, "missing tensor \"" + name + "\"");
+    if (t->elems() != expect)
+        return fail(HS_E_IO, "tensor \"" + name + "\" has " + std::to_string(t->elems()) + " elements, expected " +
+                                 std::to_string(expect));
+    HS_CUDA_TRY(cudaMemcpyAsync(staging, g.data() + t->off, t->len, cudaMemcpyHostToDevice, st));
+    int rc = launch_dequant(t->type, staging, t->elems(), dst, st, m->n_sm);
+    if (rc) return rc;
+    HS_CUDA_TRY(cudaStreamSynchronize(st));
+    m->tensors[name] = TensorRef{dst, expect, 1};
+    return HS_OK;
+}
+
+// model.rs:398-413: F32 tensors as stored, anything else through f16.
+int load_f32(hs_model* m, const Gguf& g, const std::string& name, float* dst, uint64_t expect) {
+    const GgufTensor* t = g.tensor(name);
+    if (!t) return fail(HS_E_IO, "missing tensor \"" + name + "\"");
+    if (t->elems() != expect)
+        return fail(HS_E_IO, "tensor \"" + name + "\" has " + std::to_string(t->elems()) + " elements, expected " +
+                                 std::to_string(expect));
+    std::vector<float> host(expect);
+    if (t->type == 0) {
+        std::memcpy(host.data(), g.data() + t->off, expect * 4);
+    } else {
+        // Rare (norms and biases are F32 in practice): dequantise on the device.
+        uint8_t* raw = nullptr;
+        uint16_t* h16 = nullptr;
+        HS_CUDA_TRY(cudaMalloc(&raw, t->len));
+        HS_CUDA_TRY(cudaMalloc(&h16, expect * 2));
+        cudaMemcpy(raw, g.data() + t->off, t->len, cudaMemcpyHostToDevice);
+        int rc = launch_dequant(t->type, raw, expect, h16, nullptr, m->n_sm);
+        std::vector<uint16_t> hh(expect);
+        if (rc == HS_OK) cudaMemcpy(hh.data(), h16, expect * 2, cudaMemcpyDeviceToHost);
+        cudaFree(raw);
+        cudaFree(h16);
+        if (rc) return rc;
+        for (uint64_t i = 0; i < expect; i++) host[i] = h2f_host(hh[i]);
+    }
+    HS_CUDA_TRY(cudaMemcpy(dst, host.data(), expect * 4, cudaMemcpyHostToDevice));
+    m->tensors[name] = TensorRef{dst, expect, 0};
+    return HS_OK;
+}
+
+// Kernel-side FNV-1a of the tensor table (model.rs:145-156). `t.ty as u32`
+// there is the Rust enum's declaration index, not the ggml id.
+uint64_t fingerprint_of(const Gguf& g) {
+    auto enum_index = [](uint32_t ty) -> uint32_t {
+        switch (ty) {
+            case 0: return 0;
+            case 1: return 1;
+            case 6: return 2;
+            case 8: return 3;
+            case 12: return 4;
+            case 13: return 5;
+            case 14: return 6;
+        }
+        return 0xffffffffu;
+    };
+    uint64_t h = 0xcbf29ce484222325ull;
+    auto put = [&](const void* p, size_t n) {
+        const uint8_t* b = static_cast<const uint8_t*>(p);
+        for (size_t i = 0; i < n; i++) h = (h ^ b[i]) * 0x100000001b3ull;
+    };
+    uint64_t len = g.size();
+    put(&len, 8);
+    for (const auto& name : g.order()) {
+        const GgufTensor* t = g.tensor(name);
+        put(name.data(), name.size());
+        uint32_t e = enum_index(t->type);
+        put(&e, 4);
+        uint64_t off = t->off, l = t->len;
+        put(&off, 8);
+        put(&l, 8);
+    }
+    return h;
+}
+
+int check_kv(const hs_model* m, const hs_kv* kv) {
+    const hs_config& c = m->cfg;
+    if (kv->spec.n_layers != c.n_layers || kv->spec.n_kv_heads != c.n_kv_heads || kv->spec.head_dim != c.head_dim ||
+        kv->spec.max_ctx != c.max_ctx)
+        return fail(HS_E_ARG, "KV cache shape does not match the model");
+    if (kv->device != m->device) return fail(HS_E_ARG, "KV cache lives on another device than the model");
+    return HS_OK;
+}
+
+// Enqueue one forward pass (the 5 kernels per layer + final norm/LM head).
+int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
+    const hs_model* m = s->m;
+    const hs_config& c = m->cfg;
+    cudaStream_t st = s->st;
+    for (uint32_t l = 0; l < c.n_layers; l++) {
+        const LayerDev& L = m->layers[l];
+        GemvArgs a{};
+        a.ctl = s->ctl;
+        a.eps = c.eps;
+        // rmsnorm + fused QKV (+bias); layer 0 also reads the embedding row.
+        a.src = s->x;
+        a.embd = m->embd;
+        a.x_out = s->x;
+        a.norm_g = L.attn_norm;
+        a.bias = L.bqkv;
+        a.dst = s->qkv;
+        a.n = L.qkv.n;
+        a.rows = L.qkv.rows;
+        a.rt = L.qkv.rt;
+        a.nst = L.qkv.nst;
+        a.slab_stride = L.qkv.slab_stride;
+        a.lanes = L.qkv.lanes;
+        GemvPlan pq = L.qkv;
+        pq.in_mode = l == 0 ? IN_EMBED_NORM : IN_NORM;
+        HS_CUDA_TRY(launch_gemv(pq, a, st));
+        AttnArgs at{};
+        at.qkv = s->qkv;
+        at.kv = kv->base;
+        at.dirty = kv->dirty;
+        at.tracking = kv->tracking;
+        at.rope_cos = m->rope_cos;
+        at.rope_sin = m->rope_sin;
+        at.att = s->att;
+        at.ctl = s->ctl;
+        at.layer = l;
+        at.nh = c.n_heads;
+        at.nkv = c.n_kv_heads;
+        at.max_ctx = c.max_ctx;
+        at.layout = kv->spec.layout;
+        at.page_shift = kv->page_shift;
+        HS_CUDA_TRY(launch_attention(c.head_dim, c.n_heads, m->attn_smem, at, st));
+        GemvArgs o{};
+        o.ctl = s->ctl;
+        o.src = s->att;
+        o.dst = s->x;
+        o.n = L.o.n;
+        o.rows = L.o.rows;
+        o.rt = L.o.rt;
+        o.nst = L.o.nst;
+        o.slab_stride = L.o.slab_stride;
+        o.lanes = L.o.lanes;
+        HS_CUDA_TRY(launch_gemv(L.o, o, st));
+        GemvArgs gu{};
+        gu.ctl = s->ctl;
+        gu.eps = c.eps;
+        gu.src = s->x;
+        gu.norm_g = L.ffn_norm;
+        gu.dst = s->hb;
+        gu.n = L.gu.n;
+        gu.rows = L.gu.rows;
+        gu.rt = L.gu.rt;
+        gu.nst = L.gu.nst;
+        gu.slab_stride = L.gu.slab_stride;
+        gu.lanes = L.gu.lanes;
+        HS_CUDA_TRY(launch_gemv(L.gu, gu, st));
+        GemvArgs dn{};
+        dn.ctl = s->ctl;
+        dn.src = s->hb;
+        dn.dst = s->x;
+        dn.n = L.down.n;
+        dn.rows = L.down.rows;
+        dn.rt = L.down.rt;
+        dn.nst = L.down.nst;
+        dn.slab_stride = L.down.slab_stride;
+        dn.lanes = L.down.lanes;
+        HS_CUDA_TRY(launch_gemv(L.down, dn, st));
+    }
+    GemvArgs h{};
+    h.ctl = s->ctl;
+    h.eps = c.eps;
+    h.src = s->x;
+    h.norm_g = m->out_norm;
+    h.dst = s->logits;
+    h.n = m->head.n;
+    h.rows = m->head.rows;
+    h.rt = m->head.rt;
+    h.nst = m->head.nst;
+    h.slab_stride = m->head.slab_stride;
+    h.lanes = m->head.lanes;
+    HS_CUDA_TRY(launch_gemv(m->head, h, st));
+    return HS_OK;
+}
+
+SampleArgs sample_args(hs_scratch* s) {
+    SampleArgs a{};
+    a.logits = s->logits;
+    a.tokens = s->tokens;
+    a.tokens_w = s->tokens;
+    a.cand = s->cand;
+    a.argbuf = s->argbuf;
+    a.ctl = s->ctl;
+    a.vocab = s->m->cfg.vocab;
+    a.n_cta = s->n_cta;
+    a.kmax = s->kmax;
+    return a;
+}
+
+int capture(hs_scratch* s, const hs_kv* kv, bool with_sampler, cudaGraphExec_t* out) {
+    cudaGraph_t g = nullptr;
+    HS_CUDA_TRY(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_forward(s, kv);
+    if (rc == HS_OK && with_sampler) {
+        cudaError_t e = launch_sample(sample_args(s), s->st);
+        if (e != cudaSuccess) rc = fail(HS_E_CUDA, std::string("sampler launch: ") + cudaGetErrorString(e));
+    }
+    cudaError_t e = cudaStreamEndCapture(s->st, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    return HS_OK;
+}
+
+// (Re)build the graphs for this KV region and sampler width.
+int ensure_graphs(hs_scratch* s, const hs_kv* kv, uint32_t kmax) {
+    if (s->graph_kv == kv && s->graph_kmax == kmax && s->g_fwd && s->g_step) return HS_OK;
+    if (s->g_fwd) cudaGraphExecDestroy(s->g_fwd);
+    if (s->g_step) cudaGraphExecDestroy(s->g_step);
+    s->g_fwd = s->g_step = nullptr;
+    s->kmax = kmax;
+    int rc = capture(s, kv, false, &s->g_fwd);
+    if (rc == HS_OK) rc = capture(s, kv, true, &s->g_step);
+    if (rc) return rc;
+    s->graph_kv = kv;
+    s->graph_kmax = kmax;
+    return HS_OK;
+}
+
+int check_ctl_err(hs_scratch* s) {
+    uint32_t err = s->ctl_h->err;
+    if (!err) return HS_OK;
+    std::string why;
+    if (err & ERR_TIMEOUT) why += " bounded-wait-timeout";
+    if (err & ERR_TOKEN) why += " token-out-of-range";
+    if (err & ERR_POS) why += " position-past-max_ctx";
+    if (err & ERR_CAP) why += " token-buffer-full";
+    if (err & ERR_INVARIANT) why += " nothing-to-feed-at-token-boundary";
+    int code = (err & (ERR_INVARIANT | ERR_CAP)) ? HS_E_STATE : (err & ERR_TIMEOUT) ? HS_E_CUDA : HS_E_ARG;
+    return fail(code, "device reported:" + why);
+}
+
+int sync_ctl(hs_scratch* s) {
+    HS_CUDA_TRY(cudaMemcpyAsync(s->ctl_h, s->ctl, sizeof(DevCtl), cudaMemcpyDeviceToHost, s->st));
+    HS_CUDA_TRY(cudaStreamSynchronize(s->st));
+    return HS_OK;
+}
+
+int validate_cfg(const hs_scratch* s, const hs_sampler_cfg* cfg, uint32_t* kmax) {
+    const uint32_t vocab = s->m->cfg.vocab;
+    uint32_t k = cfg->top_k == 0 ? vocab : std::min(cfg->top_k, vocab);
+    if (cfg->temperature > 0.0f) {
+        if (k > kSampleSlice || (s->n_cta > 1 && k > kMaxTopK))
+            return fail(HS_E_UNSUPPORTED, "device sampler supports top_k <= " + std::to_string(kMaxTopK) +
+                                              " (or any top_k when vocab <= " + std::to_string(kSampleSlice) + ")");
+    }
+    *kmax = s->n_cta > 1 ? kMaxTopK : kSampleSlice;
+    if (*kmax > vocab) *kmax = std::min<uint32_t>(kSampleSlice, vocab);
+    return HS_OK;
+}
+
+}  // namespace
+}  // namespace hs
+
+extern "C" {
+
+const char* hs_last_error(void) { return g_err.c_str(); }
+
+int hs_model_load(const char* path, uint32_t max_ctx, int device, hs_model** out) {
+    if (!path || !out) return fail(HS_E_ARG, "null argument");
+    if (max_ctx == 0) return fail(HS_E_ARG, "max_ctx must be positive");
+    *out = nullptr;
+    Gguf g;
+    int rc = g.open(path);
+    if (rc) return rc;
+    std::string arch;
+    if ((rc = g.get_str("general.architecture", &arch))) return rc;
+    if (arch != "qwen2") return fail(HS_E_IO, "general.architecture = \"" + arch + "\"; only qwen2 is implemented");
+    auto k = [&](const char* s) { return arch + "." + s; };
+    uint32_t n_layers, d_model, d_ff, n_heads, n_kv, train_ctx, eos;
+    float eps, rope_base;
+    if ((rc = g.get_u32(k("block_count"), &n_layers)) || (rc = g.get_u32(k("embedding_length"), &d_model)) ||
+        (rc = g.get_u32(k("feed_forward_length"), &d_ff)) || (rc = g.get_u32(k("attention.head_count"), &n_heads)) ||
+        (rc = g.get_u32(k("attention.head_count_kv"), &n_kv)) ||
+        (rc = g.get_f32(k("attention.layer_norm_rms_epsilon"), &eps)))
+        return rc;
+    if (g.get_f32(k("rope.freq_base"), &rope_base) != HS_OK) rope_base = 10000.0f;  // model.rs:127
+    if ((rc = g.get_u32(k("context_length"), &train_ctx))) return rc;
+    uint64_t vocab = 0, n_merges = 0;
+    if ((rc = g.get_str_array_len("tokenizer.ggml.tokens", &vocab)) ||
+        (rc = g.get_str_array_len("tokenizer.ggml.merges", &n_merges)) ||
+        (rc = g.get_u32("tokenizer.ggml.eos_token_id", &eos)))
+        return rc;
+    if (!n_heads || !n_kv || d_model % n_heads || n_heads % n_kv)
+        return fail(HS_E_IO, "inconsistent attention shape");
+    const uint32_t hd = d_model / n_heads;
+    if (hd != 64 && hd != 128) return fail(HS_E_UNSUPPORTED, "head_dim must be 64 or 128");
+    if (d_model % 64 || d_ff % 64) return fail(HS_E_UNSUPPORTED, "d_model and d_ff must be multiples of 64");
+
+    auto m = std::make_unique<hs_model>();
+    m->device = device;
+    HS_CUDA_TRY(cudaSetDevice(device));
+    HS_CUDA_TRY(cudaDeviceGetAttribute(&m->n_sm, cudaDevAttrMultiProcessorCount, device));
+    int optin = 0;
+    HS_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    m->smem_cap = (size_t)optin;
+    HS_CUDA_TRY(gemv_set_smem_limits());
+    hs_config& c = m->cfg;
+    c.n_layers = n_layers;
+    c.n_heads = n_heads;
+    c.n_kv_heads = n_kv;
+    c.head_dim = hd;
+    c.d_model = d_model;
+    c.d_ff = d_ff;
+    c.vocab = (uint32_t)vocab;
+    c.eps = eps;
+    c.rope_base = rope_base;
+    c.train_ctx = train_ctx;
+    c.max_ctx = max_ctx;
+    c.eos = eos;
+    c.fingerprint = fingerprint_of(g);
+    m->attn_smem = attention_smem(hd, max_ctx);
+    if (m->attn_smem > m->smem_cap) return fail(HS_E_UNSUPPORTED, "max_ctx too large for the attention kernel");
+
+    // Staging buffer for the largest quantised tensor.
+    uint64_t max_raw = 0;
+    for (const auto& name : g.order()) max_raw = std::max(max_raw, g.tensor(name)->len);
+    uint8_t* staging = nullptr;
+    HS_CUDA_TRY(cudaMalloc(&staging, max_raw + 16));
+    cudaStream_t st = nullptr;
+    HS_CUDA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    struct Cleanup {
+        uint8_t* p;
+        cudaStream_t s;
+        ~Cleanup() {
+            cudaFree(p);
+            cudaStreamDestroy(s);
+        }
+    } cleanup{staging, st};
+
+    const uint64_t qrows = (uint64_t)(n_heads + 2 * n_kv) * hd;
+    if ((rc = dev_alloc(m.get(), &m->embd, (uint64_t)vocab * d_model)) ||
+        (rc = load_f16(m.get(), g, "token_embd.weight", m->embd, (uint64_t)vocab * d_model, staging, st)) ||
+        (rc = dev_alloc(m.get(), &m->out_norm, d_model)) ||
+        (rc = load_f32(m.get(), g, "output_norm.weight", m->out_norm, d_model)))
+        return rc;
+    const uint16_t* head_w = m->embd;  // tied to the embedding unless output.weight exists (model.rs:163-166)
+    if (g.tensor("output.weight")) {
+        if ((rc = dev_alloc(m.get(), &m->out_w, (uint64_t)vocab * d_model)) ||
+            (rc = load_f16(m.get(), g, "output.weight", m->out_w, (uint64_t)vocab * d_model, staging, st)))
+            return rc;
+        head_w = m->out_w;
+    }
+    m->layers.resize(n_layers);
+    for (uint32_t i = 0; i < n_layers; i++) {
+        LayerDev& L = m->layers[i];
+        std::string p = "blk." + std::to_string(i) + ".";
+        const uint64_t dq = (uint64_t)n_heads * hd * d_model, dk = (uint64_t)n_kv * hd * d_model;
+        if ((rc = dev_alloc(m.get(), &L.attn_norm, d_model)) || (rc = dev_alloc(m.get(), &L.ffn_norm, d_model)) ||
+            (rc = dev_alloc(m.get(), &L.bqkv, qrows)) || (rc = dev_alloc(m.get(), &L.wqkv, qrows * d_model)) ||
+            (rc = dev_alloc(m.get(), &L.wo, (uint64_t)d_model * n_heads * hd)) ||
+            (rc = dev_alloc(m.get(), &L.wgate, (uint64_t)d_ff * d_model)) ||
+            (rc = dev_alloc(m.get(), &L.wup, (uint64_t)d_ff * d_model)) ||
+            (rc = dev_alloc(m.get(), &L.wdown, (uint64_t)d_model * d_ff)))
+            return rc;
+        // Wq, Wk, Wv stacked row-wise into one matrix, biases likewise.
+        if ((rc = load_f32(m.get(), g, p + "attn_norm.weight", L.attn_norm, d_model)) ||
+            (rc = load_f16(m.get(), g, p + "attn_q.weight", L.wqkv, dq, staging, st)) ||
+            (rc = load_f32(m.get(), g, p + "attn_q.bias", L.bqkv, (uint64_t)n_heads * hd)) ||
+            (rc = load_f16(m.get(), g, p + "attn_k.weight", L.wqkv + dq, dk, staging, st)) ||
+            (rc = load_f32(m.get(), g, p + "attn_k.bias", L.bqkv + n_heads * hd, (uint64_t)n_kv * hd)) ||
+            (rc = load_f16(m.get(), g, p + "attn_v.weight", L.wqkv + dq + dk, dk, staging, st)) ||
+            (rc = load_f32(m.get(), g, p + "attn_v.bias", L.bqkv + (n_heads + n_kv) * hd, (uint64_t)n_kv * hd)) ||
+            (rc = load_f16(m.get(), g, p + "attn_output.weight", L.wo, (uint64_t)d_model * n_heads * hd, staging, st)) ||
+            (rc = load_f32(m.get(), g, p + "ffn_norm.weight", L.ffn_norm, d_model)) ||
+            (rc = load_f16(m.get(), g, p + "ffn_gate.weight", L.wgate, (uint64_t)d_ff * d_model, staging, st)) ||
+            (rc = load_f16(m.get(), g, p + "ffn_up.weight", L.wup, (uint64_t)d_ff * d_model, staging, st)) ||
+            (rc = load_f16(m.get(), g, p + "ffn_down.weight", L.wdown, (uint64_t)d_model * d_ff, staging, st)))
+            return rc;
+        if ((rc = plan_gemv(&L.qkv, IN_NORM, OUT_STORE, (uint32_t)qrows, d_model, L.wqkv, nullptr, m->n_sm,
+                            m->smem_cap)) ||
+            (rc = plan_gemv(&L.o, IN_PLAIN, OUT_RESID, d_model, n_heads * hd, L.wo, nullptr, m->n_sm, m->smem_cap)) ||
+            (rc = plan_gemv(&L.gu, IN_NORM, OUT_SILU, d_ff, d_model, L.wgate, L.wup, m->n_sm, m->smem_cap)) ||
+            (rc = plan_gemv(&L.down, IN_PLAIN, OUT_RESID, d_model, d_ff, L.wdown, nullptr, m->n_sm, m->smem_cap)))
+            return rc;
+    }
+    if ((rc = plan_gemv(&m->head, IN_NORM, OUT_STORE, (uint32_t)vocab, d_model, head_w, nullptr, m->n_sm,
+                        m->smem_cap)))
+        return rc;
+    std::vector<float> cs, sn;
+    rope_tables(hd, max_ctx, rope_base, &cs, &sn);
+    if ((rc = dev_alloc(m.get(), &m->rope_cos, cs.size())) || (rc = dev_alloc(m.get(), &m->rope_sin, sn.size())))
+        return rc;
+    HS_CUDA_TRY(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    HS_CUDA_TRY(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    *out = m.release();
+    return HS_OK;
+}
+
+int hs_model_config(const hs_model* m, hs_config* out) {
+    if (!m || !out) return fail(HS_E_ARG, "null argument");
+    *out = m->cfg;
+    return HS_OK;
+}
+
+void hs_model_free(hs_model* m) { delete m; }
+
+int hs_model_tensor(const hs_model* m, const char* name, void* host, uint64_t bytes, uint32_t* dtype_out) {
+    if (!m || !name) return fail(HS_E_ARG, "null argument");
+    auto it = m->tensors.find(name);
+    if (it == m->tensors.end()) return fail(HS_E_ARG, std::string("no tensor \"") + name + "\"");
+    const TensorRef& t = it->second;
+    uint64_t need = t.count * (t.dtype == 1 ? 2 : 4);
+    if (dtype_out) *dtype_out = t.dtype;
+    if (!host) return bytes == 0 ? (int)HS_OK : fail(HS_E_ARG, "null buffer");
+    if (bytes < need) return fail(HS_E_ARG, "buffer too small: need " + std::to_string(need) + " bytes");
+    HS_CUDA_TRY(cudaSetDevice(m->device));
+    HS_CUDA_TRY(cudaMemcpy(host, t.ptr, need, cudaMemcpyDeviceToHost));
+    return HS_OK;
+}
+
+// ---------------------------------------------------------------- KV cache
+
+int hs_kv_alloc(const hs_model* m, uint32_t layout, uint32_t page_size, hs_kv** out) {
+    if (!m || !out) return fail(HS_E_ARG, "null argument");
+    if (layout > 1) return fail(HS_E_ARG, "unknown KV layout");
+    if (page_size < 256 || (page_size & (page_size - 1))) return fail(HS_E_ARG, "page_size must be a power of two >= 256");
+    HS_CUDA_TRY(cudaSetDevice(m->device));
+    auto kv = std::make_unique<hs_kv>();
+    kv->device = m->device;
+    kv->spec = hs_kv_spec{m->cfg.n_layers, m->cfg.n_kv_heads, m->cfg.head_dim, m->cfg.max_ctx, layout};
+    kv->bytes = (uint64_t)kv->spec.n_layers * 2 * kv->spec.max_ctx * kv->spec.n_kv_heads * kv->spec.head_dim * 4;
+    kv->page_size = page_size;
+    kv->page_shift = (uint32_t)__builtin_ctz(page_size);
+    kv->n_pages = (kv->bytes + page_size - 1) / page_size;
+    kv->n_words = (kv->n_pages + 63) / 64;
+    kv->fingerprint = m->cfg.fingerprint;
+    HS_CUDA_TRY(cudaStreamCreateWithFlags(&kv->st, cudaStreamNonBlocking));
+    HS_CUDA_TRY(cudaMalloc(&kv->base, kv->bytes));
+    HS_CUDA_TRY(cudaMemset(kv->base, 0, kv->bytes));
+    HS_CUDA_TRY(cudaMalloc(&kv->dirty, kv->n_words * 8));
+    HS_CUDA_TRY(cudaMemset(kv->dirty, 0, kv->n_words * 8));
+    HS_CUDA_TRY(cudaMalloc(&kv->harvest_buf, kv->n_words * 8));
+    HS_CUDA_TRY(cudaMalloc(&kv->tracking, 4));
+    HS_CUDA_TRY(cudaMemset(kv->tracking, 0, 4));
+    *out = kv.release();
+    return HS_OK;
+}
+
+int hs_kv_info(const hs_kv* kv, hs_kv_spec* spec, uint64_t* bytes, uint32_t* page_size, uint64_t* n_pages) {
+    if (!kv) return fail(HS_E_ARG, "null argument");
+    if (spec) *spec = kv->spec;
+    if (bytes) *bytes = kv->bytes;
+    if (page_size) *page_size = kv->page_size;
+    if (n_pages) *n_pages = kv->n_pages;
+    return HS_OK;
+}
+
+void hs_kv_free(hs_kv* kv) { delete kv; }
+
+int hs_kv_read(hs_kv* kv, uint64_t off, uint64_t len, void* host) {
+    if (!kv || (!host && len)) return fail(HS_E_ARG, "null argument");
+    if (off > kv->bytes || len > kv->bytes - off) return fail(HS_E_ARG, "range outside the KV region");
+    HS_CUDA_TRY(cudaSetDevice(kv->device));
+    HS_CUDA_TRY(cudaMemcpy(host, reinterpret_cast<uint8_t*>(kv->base) + off, len, cudaMemcpyDeviceToHost));
+    return HS_OK;
+}
+
+int hs_kv_write(hs_kv* kv, uint64_t off, uint64_t len, const void* host) {
+    if (!kv || (!host && len)) return fail(HS_E_ARG, "null argument");
+    if (off > kv->bytes || len > kv->bytes - off) return fail(HS_E_ARG, "range outside the KV region");
+    HS_CUDA_TRY(cudaSetDevice(kv->device));
+    HS_CUDA_TRY(cudaMemcpy(reinterpret_cast<uint8_t*>(kv->base) + off, host, len, cudaMemcpyHostToDevice));
+    return HS_OK;
+}
+
+uint64_t hs_kv_live_ranges_between(const hs_kv_spec* s, uint32_t from, uint32_t to, uint64_t* out, uint64_t cap) {
+    // kv.rs:150-175
+    if (!s || to <= from) return 0;
+    const uint64_t plane = (uint64_t)s->max_ctx * s->n_kv_heads * s->head_dim, n = to - from;
+    uint64_t count = 0;
+    auto push = [&](uint64_t off, uint64_t len) {
+        if (out && count < cap) {
+            out[2 * count] = off;
+            out[2 * count + 1] = len;
+        }
+        count++;
+    };
+    for (uint64_t layer = 0; layer < s->n_layers; layer++)
+        for (int is_v = 0; is_v < 2; is_v++) {
+            const uint64_t plane_off = (layer * 2 * plane + (is_v ? plane : 0)) * 4;
+            if (s->layout == 0) {
+                const uint64_t w = (uint64_t)s->n_kv_heads * s->head_dim * 4;
+                push(plane_off + from * w, n * w);
+            } else {
+                const uint64_t w = (uint64_t)s->head_dim * 4;
+                for (uint64_t h = 0; h < s->n_kv_heads; h++) push(plane_off + (h * s->max_ctx + from) * w, n * w);
+            }
+        }
+    return count;
+}
+
+int hs_kv_hash(hs_kv* kv, uint32_t n_pos, uint64_t* out) {
+    // kv.rs:267-274 with hash::Wide (hash.rs:63-126), over bytes staged to the host.
+    if (!kv || !out) return fail(HS_E_ARG, "null argument");
+    if (n_pos > kv->spec.max_ctx) return fail(HS_E_ARG, "n_pos past max_ctx");
+    const uint64_t nr = hs_kv_live_ranges_between(&kv->spec, 0, n_pos, nullptr, 0);
+    std::vector<uint64_t> r(2 * nr);
+    hs_kv_live_ranges_between(&kv->spec, 0, n_pos, r.data(), nr);
+    uint64_t lanes[4] = {0x243f6a8885a308d3ull, 0x13198a2e03707344ull, 0xa4093822299f31d0ull, 0x082efa98ec4e6c89ull};
+    uint64_t total = 0;
+    const uint64_t P = 0x00000100000001b3ull;
+    std::vector<uint8_t> buf;
+    HS_CUDA_TRY(cudaSetDevice(kv->device));
+    for (uint64_t i = 0; i < nr; i++) {
+        const uint64_t off = r[2 * i], len = r[2 * i + 1];
+        buf.resize(len);
+        HS_CUDA_TRY(cudaMemcpy(buf.data(), reinterpret_cast<uint8_t*>(kv->base) + off, len, cudaMemcpyDeviceToHost));
+        total += len;
+        const uint64_t full = len / 32 * 32;
+        for (uint64_t c = 0; c < full; c += 32)
+            for (int k = 0; k < 4; k++) {
+                uint64_t w;
+                std::memcpy(&w, buf.data() + c + 8 * k, 8);
+                lanes[k] = (lanes[k] ^ w) * P;
+                lanes[k] ^= lanes[k] >> 29;
+            }
+        for (uint64_t j = 0; j < len - full; j++) lanes[j % 4] = (lanes[j % 4] ^ buf[full + j]) * P;
+    }
+    auto rotl = [](uint64_t x, int k) { return (x << k) | (x >> (64 - k)); };
+    uint64_t h = lanes[0] ^ rotl(lanes[1], 17) ^ rotl(lanes[2], 34) ^ rotl(lanes[3], 51);
+    h += total;
+    h ^= h >> 33;
+    h *= 0xff51afd7ed558ccdull;
+    h ^= h >> 33;
+    *out = h;
+    return HS_OK;
+}
+
+uint64_t hs_runs_to_byte_runs(const uint64_t* words, uint64_t n_pages, uint64_t page_size, const uint64_t* live,
+                              uint64_t n_live, uint64_t* out, uint64_t cap) {
+    // hs-track pageset.rs:79-113 (runs of set bits) clipped to the live byte
+    // ranges and merged (hs-wire lib.rs:418-446).
+    std::vector<std::pair<uint64_t, uint64_t>> acc;
+    auto merge = [](std::vector<std::pair<uint64_t, uint64_t>>& v, uint64_t off, uint64_t len) {
+        if (!v.empty() && v.back().first + v.back().second >= off) {
+            uint64_t end = std::max(v.back().first + v.back().second, off + len);
+            v.back().second = end - v.back().first;
+            return;
+        }
+        v.push_back({off, len});
+    };
+    uint64_t p = 0;
+    while (p < n_pages) {
+        if (!((words[p >> 6] >> (p & 63)) & 1)) {
+            p++;
+            continue;
+        }
+        uint64_t q = p;
+        while (q < n_pages && ((words[q >> 6] >> (q & 63)) & 1)) q++;
+        const uint64_t a = p * page_size, b = q * page_size;
+        for (uint64_t i = 0; i < n_live; i++) {
+            const uint64_t lo = live[2 * i], hi = lo + live[2 * i + 1];
+            const uint64_t c = std::max(a, lo), d = std::min(b, hi);
+            if (c < d) merge(acc, c, d - c);
+        }
+        p = q;
+    }
+    std::stable_sort(acc.begin(), acc.end(), [](const auto& x, const auto& y) { return x.first < y.first; });
+    std::vector<std::pair<uint64_t, uint64_t>> merged;
+    for (auto& r : acc) merge(merged, r.first, r.second);
+    for (uint64_t i = 0; i < merged.size() && i < cap && out; i++) {
+        out[2 * i] = merged[i].first;
+        out[2 * i + 1] = merged[i].second;
+    }
+    return merged.size();
+}
+
+int hs_kv_copy_runs(hs_kv* src, hs_kv* dst, const uint64_t* runs, uint64_t n_runs) {
+    if (!src || !dst || (!runs && n_runs)) return fail(HS_E_ARG, "null argument");
+    if (std::memcmp(&src->spec, &dst->spec, sizeof(hs_kv_spec)) != 0)
+        return fail(HS_E_ARG, "KV specs differ between source and destination");
+    for (uint64_t i = 0; i < n_runs; i++)
+        if (runs[2 * i] > src->bytes || runs[2 * i + 1] > src->bytes - runs[2 * i])
+            return fail(HS_E_ARG, "run outside the KV region");
+    HS_CUDA_TRY(cudaSetDevice(dst->device));
+    if (src->device != dst->device) {
+        int can = 0;
+        HS_CUDA_TRY(cudaDeviceCanAccessPeer(&can, dst->device, src->device));
+        if (can) {
+            cudaError_t e = cudaDeviceEnablePeerAccess(src->device, 0);
+            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+                return fail(HS_E_CUDA, std::string("enable peer access: ") + cudaGetErrorString(e));
+            cudaGetLastError();
+        }
+    }
+    for (uint64_t i = 0; i < n_runs; i++) {
+        uint8_t* s = reinterpret_cast<uint8_t*>(src->base) + runs[2 * i];
+        uint8_t* d = reinterpret_cast<uint8_t*>(dst->base) + runs[2 * i];
+        if (src->device == dst->device)
+            HS_CUDA_TRY(cudaMemcpyAsync(d, s, runs[2 * i + 1], cudaMemcpyDeviceToDevice, dst->st));
+        else
+            HS_CUDA_TRY(cudaMemcpyPeerAsync(d, dst->device, s, src->device, runs[2 * i + 1], dst->st));
+    }
+    HS_CUDA_TRY(cudaStreamSynchronize(dst->st));
+    return HS_OK;
+}
+
+// ---------------------------------------------------------------- scratch
+
+int hs_scratch_new(const hs_model* m, hs_scratch** out) {
+    if (!m || !out) return fail(HS_E_ARG, "null argument");
+    HS_CUDA_TRY(cudaSetDevice(m->device));
+    auto s = std::make_unique<hs_scratch>();
+    s->m = m;
+    const hs_config& c = m->cfg;
+    HS_CUDA_TRY(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    HS_CUDA_TRY(cudaMalloc(&s->ctl, sizeof(DevCtl)));
+    HS_CUDA_TRY(cudaMemset(s->ctl, 0, sizeof(DevCtl)));
+    HS_CUDA_TRY(cudaMallocHost(&s->ctl_h, sizeof(DevCtl)));
+    std::memset(s->ctl_h, 0, sizeof(DevCtl));
+    HS_CUDA_TRY(cudaMalloc(&s->x, c.d_model * 4));
+    HS_CUDA_TRY(cudaMalloc(&s->qkv, (size_t)(c.n_heads + 2 * c.n_kv_heads) * c.head_dim * 4));
+    HS_CUDA_TRY(cudaMalloc(&s->att, (size_t)c.n_heads * c.head_dim * 4));
+    HS_CUDA_TRY(cudaMalloc(&s->hb, (size_t)c.d_ff * 4));
+    HS_CUDA_TRY(cudaMalloc(&s->logits, (size_t)c.vocab * 4));
+    s->cap = (uint64_t)c.max_ctx + 1;
+    HS_CUDA_TRY(cudaMalloc(&s->tokens, s->cap * 4));
+    s->n_cta = (c.vocab + kSampleSlice - 1) / kSampleSlice;
+    if (s->n_cta > 256) return fail(HS_E_UNSUPPORTED, "vocab too large for the device sampler");
+    HS_CUDA_TRY(cudaMalloc(&s->cand, (size_t)s->n_cta * kSampleSlice * 8));
+    HS_CUDA_TRY(cudaMalloc(&s->argbuf, (size_t)s->n_cta * 8));
+    s->launches_fwd = c.n_layers * 5 + 1;
+    *out = s.release();
+    return HS_OK;
+}
+
+void hs_scratch_free(hs_scratch* s) { delete s; }
+
+void* hs_scratch_stream(hs_scratch* s) { return s ? (void*)s->st : nullptr; }
+
+int hs_seq_launches_per_step(hs_scratch* s, uint32_t* out) {
+    if (!s || !out) return fail(HS_E_ARG, "null argument");
+    *out = s->launches_fwd + 2;
+    return HS_OK;
+}
+
+int hs_forward(const hs_model* m, hs_kv* kv, uint32_t token, uint32_t pos, hs_scratch* s) {
+    if (!m || !kv || !s || s->m != m) return fail(HS_E_ARG, "null or mismatched argument");
+    int rc = check_kv(m, kv);
+    if (rc) return rc;
+    if (pos >= m->cfg.max_ctx)
+        return fail(HS_E_ARG, "position " + std::to_string(pos) + " past max_ctx " + std::to_string(m->cfg.max_ctx));
+    if (token >= m->cfg.vocab) return fail(HS_E_ARG, "token " + std::to_string(token) + " out of range");
+    HS_CUDA_TRY(cudaSetDevice(m->device));
+    if ((rc = ensure_graphs(s, kv, s->kmax ? s->kmax : kMaxTopK))) return rc;
+    DevCtl& h = *s->ctl_h;
+    std::memset(&h, 0, sizeof(DevCtl));
+    h.token = token;
+    h.pos = pos;
+    h.active = 1;
+    h.mode = 0;
+    h.vocab = m->cfg.vocab;
+    h.max_ctx = m->cfg.max_ctx;
+    HS_CUDA_TRY(cudaMemcpyAsync(s->ctl, &h, sizeof(DevCtl), cudaMemcpyHostToDevice, s->st));
+    HS_CUDA_TRY(cudaGraphLaunch(s->g_fwd, s->st));
+    if ((rc = sync_ctl(s))) return rc;
+    return check_ctl_err(s);
+}
+
+int hs_scratch_logits(hs_scratch* s, float* host, uint64_t n) {
+    if (!s || !host) return fail(HS_E_ARG, "null argument");
+    if (n > s->m->cfg.vocab) return fail(HS_E_ARG, "more logits requested than the vocabulary has");
+    HS_CUDA_TRY(cudaSetDevice(s->m->device));
+    HS_CUDA_TRY(cudaMemcpyAsync(host, s->logits, n * 4, cudaMemcpyDeviceToHost, s->st));
+    HS_CUDA_TRY(cudaStreamSynchronize(s->st));
+    return HS_OK;
+}
+
+int hs_scratch_set_logits(hs_scratch* s, const float* host, uint64_t n) {
+    if (!s || !host) return fail(HS_E_ARG, "null argument");
+    if (n != s->m->cfg.vocab) return fail(HS_E_ARG, "expected exactly vocab logits");
+    HS_CUDA_TRY(cudaSetDevice(s->m->device));
+    HS_CUDA_TRY(cudaMemcpyAsync(s->logits, host, n * 4, cudaMemcpyHostToDevice, s->st));
+    HS_CUDA_TRY(cudaStreamSynchronize(s->st));
+    return HS_OK;
+}
+
+void hs_sampler_cfg_default(hs_sampler_cfg* c) {
+    if (!c) return;
+    c->temperature = 0.8f;
+    c->top_p = 0.95f;
+    c->top_k = 40;
+    c->repeat_penalty = 1.1f;
+    c->repeat_last_n = 64;
+    c->seed = 0xC0FFEE0012345678ull;
+}
+
+void hs_rng_seed(uint64_t seed, hs_rng* r) {
+    // sampler.rs:47-58
+    if (!r) return;
+    uint64_t z = seed;
+    for (int i = 0; i < 4; i++) {
+        z += 0x9E3779B97F4A7C15ull;
+        uint64_t x = z;
+        x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+        x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+        r->s[i] = x ^ (x >> 31);
+    }
+    r->draws = 0;
+}
+
+static void fill_cfg(DevCtl& h, const hs_sampler_cfg* cfg, const hs_rng* rng) {
+    h.temperature = cfg->temperature;
+    h.top_p = cfg->top_p;
+    h.top_k = cfg->top_k;
+    h.repeat_penalty = cfg->repeat_penalty;
+    h.repeat_last_n = cfg->repeat_last_n;
+    for (int i = 0; i < 4; i++) h.rng[i] = rng->s[i];
+    h.draws = rng->draws;
+}
+
+int hs_sample(hs_scratch* s, const hs_sampler_cfg* cfg, hs_rng* rng, const uint32_t* hist, uint64_t n_hist,
+              uint32_t* out) {
+    if (!s || !cfg || !rng || !out || (!hist && n_hist)) return fail(HS_E_ARG, "null argument");
+    if (n_hist > s->cap) return fail(HS_E_ARG, "history longer than the scratch's token buffer");
+    uint32_t kmax;
+    int rc = validate_cfg(s, cfg, &kmax);
+    if (rc) return rc;
+    const hs_model* m = s->m;
+    for (uint64_t i = 0; i < n_hist; i++)
+        if (hist[i] >= m->cfg.vocab) return fail(HS_E_ARG, "history token out of range");
+    HS_CUDA_TRY(cudaSetDevice(m->device));
+    s->kmax = kmax;
+    DevCtl& h = *s->ctl_h;
+    std::memset(&h, 0, sizeof(DevCtl));
+    h.mode = 1;
+    h.n_tokens = n_hist;
+    h.vocab = m->cfg.vocab;
+    h.max_ctx = m->cfg.max_ctx;
+    fill_cfg(h, cfg, rng);
+    if (n_hist) HS_CUDA_TRY(cudaMemcpyAsync(s->tokens, hist, n_hist * 4, cudaMemcpyHostToDevice, s->st));
+    HS_CUDA_TRY(cudaMemcpyAsync(s->ctl, &h, sizeof(DevCtl), cudaMemcpyHostToDevice, s->st));
+    cudaError_t e = launch_sample(sample_args(s), s->st);
+    if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("sampler launch: ") + cudaGetErrorString(e));
+    if ((rc = sync_ctl(s))) return rc;
+    if ((rc = check_ctl_err(s))) return rc;
+    *out = s->ctl_h->out_token;
+    for (int i = 0; i < 4; i++) rng->s[i] = s->ctl_h->rng[i];
+    rng->draws = s->ctl_h->draws;
+    return HS_OK;
+}
+
+int hs_argmax(hs_scratch* s, uint32_t* out) {
+    hs_sampler_cfg cfg{};
+    cfg.temperature = 0.0f;
+    cfg.top_p = 1.0f;
+    cfg.top_k = 1;
+    cfg.repeat_penalty = 1.0f;
+    hs_rng r{};
+    return hs_sample(s, &cfg, &r, nullptr, 0, out);
+}
+
+// ---------------------------------------------------------------- the loop
+
+int hs_seq_begin(hs_scratch* s, hs_kv* kv, const uint32_t* tokens, uint64_t n_tokens, uint64_t cap,
+                 const hs_seq_state* st, const hs_sampler_cfg* cfg, const hs_rng* rng, uint64_t stop_at_filled) {
+    if (!s || !kv || !tokens || !st || !cfg || !rng) return fail(HS_E_ARG, "null argument");
+    const hs_model* m = s->m;
+    int rc = check_kv(m, kv);
+    if (rc) return rc;
+    if (n_tokens == 0 || st->filled > n_tokens || st->prompt_len > n_tokens)
+        return fail(HS_E_ARG, "inconsistent sequence state");
+    if (n_tokens > s->cap) return fail(HS_E_ARG, "history longer than max_ctx");
+    for (uint64_t i = 0; i < n_tokens; i++)
+        if (tokens[i] >= m->cfg.vocab) return fail(HS_E_ARG, "token " + std::to_string(tokens[i]) + " out of range");
+    uint32_t kmax;
+    if ((rc = validate_cfg(s, cfg, &kmax))) return rc;
+    HS_CUDA_TRY(cudaSetDevice(m->device));
+    if ((rc = ensure_graphs(s, kv, kmax))) return rc;
+    DevCtl& h = *s->ctl_h;
+    std::memset(&h, 0, sizeof(DevCtl));
+    h.mode = 0;
+    h.n_tokens = n_tokens;
+    h.filled = st->filled;
+    h.prompt_len = st->prompt_len;
+    h.max_tokens = st->max_tokens;
+    h.cap = std::min<uint64_t>(cap, s->cap);
+    h.stop_at = stop_at_filled;
+    h.done = st->done;
+    h.done_reason = st->done_reason;
+    h.eos = m->cfg.eos;
+    h.max_ctx = m->cfg.max_ctx;
+    h.vocab = m->cfg.vocab;
+    fill_cfg(h, cfg, rng);
+    const bool runnable = !st->done && st->filled < n_tokens && !(stop_at_filled && st->filled >= stop_at_filled);
+    if (!st->done && st->filled >= n_tokens) return fail(HS_E_STATE, "internal: nothing to feed at the token boundary");
+    if (runnable && st->filled >= m->cfg.max_ctx) return fail(HS_E_ARG, "position past max_ctx");
+    h.active = runnable ? 1 : 0;
+    h.token = runnable ? tokens[st->filled] : 0;
+    h.pos = (uint32_t)st->filled;
+    HS_CUDA_TRY(cudaMemcpyAsync(s->tokens, tokens, n_tokens * 4, cudaMemcpyHostToDevice, s->st));
+    HS_CUDA_TRY(cudaMemcpyAsync(s->ctl, &h, sizeof(DevCtl), cudaMemcpyHostToDevice, s->st));
+    return HS_OK;
+}
+
+int hs_seq_step(hs_scratch* s, uint32_t n_steps) {
+    if (!s || !s->g_step) return fail(HS_E_ARG, "hs_seq_begin has not been called");
+    HS_CUDA_TRY(cudaSetDevice(s->m->device));
+    for (uint32_t i = 0; i < n_steps; i++) HS_CUDA_TRY(cudaGraphLaunch(s->g_step, s->st));
+    return HS_OK;
+}
+
+int hs_seq_end(hs_scratch* s, uint32_t* tokens, uint64_t* n_tokens, uint64_t cap, hs_seq_state* st, hs_rng* rng) {
+    if (!s) return fail(HS_E_ARG, "null argument");
+    HS_CUDA_TRY(cudaSetDevice(s->m->device));
+    int rc = sync_ctl(s);
+    if (rc) return rc;
+    const DevCtl& h = *s->ctl_h;
+    if (tokens && n_tokens) {
+        if (h.n_tokens > cap) return fail(HS_E_ARG, "token buffer too small");
+        HS_CUDA_TRY(cudaMemcpy(tokens, s->tokens, h.n_tokens * 4, cudaMemcpyDeviceToHost));
+        *n_tokens = h.n_tokens;
+    }
+    if (st) {
+        st->filled = h.filled;
+        st->done = h.done;
+        st->done_reason = h.done_reason;
+    }
+    if (rng) {
+        for (int i = 0; i < 4; i++) rng->s[i] = h.rng[i];
+        rng->draws = h.draws;
+    }
+    return check_ctl_err(s);
+}
+
+int hs_seq_run(const hs_model* m, hs_kv* kv, hs_scratch* s, uint32_t* tokens, uint64_t* n_tokens, uint64_t cap,
+               hs_seq_state* st, const hs_sampler_cfg* cfg, hs_rng* rng, uint64_t stop_at_filled) {
+    if (!m || !s || s->m != m || !n_tokens) return fail(HS_E_ARG, "null or mismatched argument");
+    int rc = hs_seq_begin(s, kv, tokens, *n_tokens, cap, st, cfg, rng, stop_at_filled);
+    if (rc) return rc;
+    // Every chunk advances `filled` by at least one unless the sequence
+    // stopped, so max_ctx chunks is a hard upper bound.
+    for (uint32_t guard = 0;; guard++) {
+        const DevCtl& h = *s->ctl_h;
+        if (h.done || !h.active) break;
+        if (guard > m->cfg.max_ctx) return fail(HS_E_STATE, "decode loop made no progress");
+        // Forwards still possible before the sequence must stop on its own:
+        // the rest of the prompt, then one per token still allowed.
+        const uint64_t pre = h.n_tokens - h.filled;
+        const uint64_t gen = h.n_tokens - h.prompt_len;
+        uint64_t bound = pre + (h.max_tokens > gen ? h.max_tokens - gen : 0);
+        if (h.stop_at && h.stop_at > h.filled) bound = std::min<uint64_t>(bound, h.stop_at - h.filled);
+        bound = std::max<uint64_t>(1, std::min<uint64_t>(bound, 256));
+        if ((rc = hs_seq_step(s, (uint32_t)bound))) return rc;
+        if ((rc = sync_ctl(s))) return rc;
+        if ((rc = check_ctl_err(s))) return rc;
+    }
+    return hs_seq_end(s, tokens, n_tokens, cap, st, rng);
+}
+
+int hs_dequant_f16(uint32_t ggml_type, const void* src, uint64_t n, void* dst, void* stream) {
+    if ((!src || !dst) && n) return fail(HS_E_ARG, "null argument");
+    int dev = 0, n_sm = 0;
+    HS_CUDA_TRY(cudaGetDevice(&dev));
+    HS_CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+    return launch_dequant(ggml_type, src, n, dst, static_cast<cudaStream_t>(stream), n_sm);
+}
+
+}  // extern "C"
+
+namespace hs {
+namespace {
+// Take-and-clear of the dirty bitmap: a concurrent atomicOr from the
+// KV-append kernel lands either in this harvest or in the next one
+// (the swap of PageSet::drain_into, hs-track pageset.rs:64-72).
+__global__ void k_harvest(unsigned long long* words, unsigned long long* out, uint64_t n) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        out[i] = atomicExch(&words[i], 0ull);
+}
+}  // namespace
+}  // namespace hs
+
+extern "C" {
+
+int hs_kv_harvest(hs_kv* kv, uint64_t* words, uint64_t n_words) {
+    if (!kv || !words) return fail(HS_E_ARG, "null argument");
+    if (n_words < kv->n_words) return fail(HS_E_ARG, "need " + std::to_string(kv->n_words) + " words");
+    HS_CUDA_TRY(cudaSetDevice(kv->device));
+    const unsigned grid = (unsigned)std::min<uint64_t>((kv->n_words + 255) / 256, 1024);
+    hs::k_harvest<<<grid, 256, 0, kv->st>>>(reinterpret_cast<unsigned long long*>(kv->dirty),
+                                            reinterpret_cast<unsigned long long*>(kv->harvest_buf), kv->n_words);
+    HS_CUDA_TRY(cudaGetLastError());
+    HS_CUDA_TRY(cudaMemcpyAsync(words, kv->harvest_buf, kv->n_words * 8, cudaMemcpyDeviceToHost, kv->st));
+    HS_CUDA_TRY(cudaStreamSynchronize(kv->st));
+    for (uint64_t i = kv->n_words; i < n_words; i++) words[i] = 0;
+    return HS_OK;
+}
+
+int hs_kv_arm(hs_kv* kv) {
+    if (!kv) return fail(HS_E_ARG, "null argument");
+    HS_CUDA_TRY(cudaSetDevice(kv->device));
+    HS_CUDA_TRY(cudaMemset(kv->dirty, 0, kv->n_words * 8));
+    const uint32_t one = 1;
+    HS_CUDA_TRY(cudaMemcpy(kv->tracking, &one, 4, cudaMemcpyHostToDevice));
+    return HS_OK;
+}
+
+int hs_kv_disarm(hs_kv* kv) {
+    if (!kv) return fail(HS_E_ARG, "null argument");
+    HS_CUDA_TRY(cudaSetDevice(kv->device));
+    const uint32_t zero = 0;
+    HS_CUDA_TRY(cudaMemcpy(kv->tracking, &zero, 4, cudaMemcpyHostToDevice));
+    HS_CUDA_TRY(cudaMemset(kv->dirty, 0, kv->n_words * 8));
+    return HS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,195 @@
+/*
+ * hotseat.h — C ABI of the B200 token loop (libhotseat.so).
+ *
+ * This replaces the Rust API that hotseat's hs-worker and hs-wire call on
+ * hs-engine (crates/hs-engine/src). Each entry point names the reference
+ * interface it stands in for. Conventions:
+ *   - every call returns an int status: HS_OK (0) or a negative HS_E_* code;
+ *     hs_last_error() gives the message of the calling thread's last failure;
+ *   - no exception or abort crosses the ABI: conditions on which the reference
+ *     panics (pos >= max_ctx, model.rs:242; a KV shape mismatch, model.rs:243)
+ *     return HS_E_ARG instead;
+ *   - plain pointers and sizes only; host buffers are owned by the caller;
+ *   - an hs_kv / hs_scratch is used by one thread at a time (the reference's
+ *     one decode thread per sequence, hs-worker seq.rs:223-318).
+ */
+#ifndef HOTSEAT_H
+#define HOTSEAT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HS_OK 0
+#define HS_E_ARG (-1)         /* bad argument, out-of-range pos/token, shape mismatch */
+#define HS_E_IO (-2)          /* file or GGUF format error (gguf.rs Error variants) */
+#define HS_E_CUDA (-3)        /* CUDA error, no device, or a kernel reported a fault */
+#define HS_E_STATE (-4)       /* sequence invariant broken (seq.rs:258-266) */
+#define HS_E_NOMEM (-5)       /* device or host allocation failed */
+#define HS_E_UNSUPPORTED (-6) /* shape or option this build does not implement */
+
+/* Message for the calling thread's most recent failing call. */
+const char* hs_last_error(void);
+
+/* KV layouts (kv.rs:29-33). */
+#define HS_LAYOUT_TOKEN_MAJOR 0u
+#define HS_LAYOUT_HEAD_MAJOR 1u
+
+/* Model configuration plus the load-time facts the worker needs
+ * (model.rs:21-33 Config, model.rs:62-68 fingerprint, tok.rs eos). */
+typedef struct {
+    uint32_t n_layers, n_heads, n_kv_heads, head_dim, d_model, d_ff, vocab;
+    float eps, rope_base;
+    uint32_t train_ctx, max_ctx, eos;
+    uint64_t fingerprint;
+} hs_config;
+
+typedef struct hs_model hs_model;
+typedef struct hs_kv hs_kv;
+typedef struct hs_scratch hs_scratch;
+
+/* ---- model (replaces Model::load, model.rs:110-215) ------------------------ */
+
+/* Parse the GGUF, copy the quantised tensors to `device` and dequantise them
+ * there to f16 (Q4_K/Q6_K/Q5_K/Q5_0/Q8_0/F16/F32, quant.rs:18-206), build the
+ * RoPE tables with the reference's own exp/ln/sincos (model.rs:187-201). */
+int hs_model_load(const char* path, uint32_t max_ctx, int device, hs_model** out);
+/* Model{cfg, fingerprint} and tok.eos (model.rs:62-78). */
+int hs_model_config(const hs_model* m, hs_config* out);
+void hs_model_free(hs_model* m);
+/* Copy one loaded tensor back to the host: f16 bits for 2-D weights (as
+ * Layer::wq etc. hold them, model.rs:47-60), f32 for norms and biases.
+ * *dtype_out = 1 (f16) or 0 (f32). For parity checks. */
+int hs_model_tensor(const hs_model* m, const char* name, void* host, uint64_t bytes, uint32_t* dtype_out);
+
+/* ---- KV cache (replaces hs-track Region + Kv::from_raw, kv.rs:196-274) ---- */
+
+typedef struct {
+    uint32_t n_layers, n_kv_heads, head_dim, max_ctx, layout;
+} hs_kv_spec;
+
+/* Device KV region with the reference's exact byte layout (KvSpec::row_off,
+ * kv.rs:96-104) and a device dirty-page bitmap of `page_size`-byte pages in
+ * PageSet's word/bit format (hs-track pageset.rs:10-34). */
+int hs_kv_alloc(const hs_model* m, uint32_t layout, uint32_t page_size, hs_kv** out);
+int hs_kv_info(const hs_kv* kv, hs_kv_spec* spec, uint64_t* bytes, uint32_t* page_size, uint64_t* n_pages);
+void hs_kv_free(hs_kv* kv);
+/* Byte-range staging between the device region and host memory (the hs-wire
+ * send_page_bytes / recv_page_bytes path, hs-wire lib.rs:339-396). */
+int hs_kv_read(hs_kv* kv, uint64_t off, uint64_t len, void* host);
+int hs_kv_write(hs_kv* kv, uint64_t off, uint64_t len, const void* host);
+/* Kv::hash (kv.rs:267-274): hash::Wide over live_ranges(n_pos). */
+int hs_kv_hash(hs_kv* kv, uint32_t n_pos, uint64_t* out);
+/* Dirty-page tracking (Tracker::arm/harvest/disarm, hs-track lib.rs:75-170).
+ * The KV-append kernel marks pages as it stores; harvest atomically takes and
+ * clears the set into `words` (ceil(n_pages/64) u64 words). */
+int hs_kv_arm(hs_kv* kv);
+int hs_kv_harvest(hs_kv* kv, uint64_t* words, uint64_t n_words);
+int hs_kv_disarm(hs_kv* kv);
+/* Copy byte runs (off, len pairs) from one KV region to another, over
+ * NVLink when the two live on different GPUs (the pre-copy data path of
+ * hs-worker migrate.rs:234-473 without the TCP hop). Specs must match. */
+int hs_kv_copy_runs(hs_kv* src, hs_kv* dst, const uint64_t* runs, uint64_t n_runs);
+
+/* Host-only mirrors of the reference's range logic (no device needed).
+ * Output is (off, len) pairs; return value is the number of pairs, which may
+ * exceed `cap` (then only cap pairs were written). */
+uint64_t hs_kv_live_ranges_between(const hs_kv_spec* s, uint32_t from, uint32_t to, uint64_t* out, uint64_t cap);
+uint64_t hs_runs_to_byte_runs(const uint64_t* words, uint64_t n_pages, uint64_t page_size, const uint64_t* live,
+                              uint64_t n_live, uint64_t* out, uint64_t cap);
+
+/* ---- forward (replaces Model::scratch / Model::forward, model.rs:221-327) - */
+
+int hs_scratch_new(const hs_model* m, hs_scratch** out);
+void hs_scratch_free(hs_scratch* s);
+/* One token at `pos`: appends its K/V to `kv` (marking dirty pages) and
+ * leaves the next-token logits on the device. Blocks until done. */
+int hs_forward(const hs_model* m, hs_kv* kv, uint32_t token, uint32_t pos, hs_scratch* s);
+/* Scratch::logits (model.rs:341) copied to the host. */
+int hs_scratch_logits(hs_scratch* s, float* host, uint64_t n);
+/* Overwrite Scratch::logits from the host (the field is public in the
+ * reference, so a caller may sample from logits it supplies). */
+int hs_scratch_set_logits(hs_scratch* s, const float* host, uint64_t n);
+
+/* ---- sampling (replaces sampler.rs:12-187, seq.rs:321-330) ------------- */
+
+typedef struct {
+    float temperature, top_p;
+    uint32_t top_k;
+    float repeat_penalty;
+    uint32_t repeat_last_n;
+    uint64_t seed;
+} hs_sampler_cfg;
+
+typedef struct {
+    uint64_t s[4];
+    uint64_t draws;
+} hs_rng;
+
+void hs_sampler_cfg_default(hs_sampler_cfg* cfg); /* SamplerCfg::default, sampler.rs:22-33 */
+void hs_rng_seed(uint64_t seed, hs_rng* r);        /* Rng::seed, sampler.rs:47-58 */
+/* Sampler::sample over the scratch's logits on the device: penalty, top-k
+ * by (value desc, id asc), temperature softmax, nucleus, one RNG draw
+ * (none at temperature <= 0). `rng` is read and written back. */
+int hs_sample(hs_scratch* s, const hs_sampler_cfg* cfg, hs_rng* rng, const uint32_t* hist, uint64_t n_hist,
+              uint32_t* out);
+/* argmax (sampler.rs:177-187) of the scratch's logits. */
+int hs_argmax(hs_scratch* s, uint32_t* out);
+
+/* ---- the decode loop (replaces hs-worker seq.rs:230-318 `run`) ---------- */
+
+/* SeqState fields that a handover carries (seq.rs:35-61, hs-wire FinalState).
+ * done_reason: 0 running, 1 eos, 2 max_tokens, 3 context full. */
+typedef struct {
+    uint64_t prompt_len, filled, max_tokens;
+    uint32_t done, done_reason;
+} hs_seq_state;
+
+/* Run the sequence until it stops or `filled` reaches stop_at_filled (0 =
+ * never), entirely on the device: forward, commit, sample and the stop
+ * checks of seq.rs:273-312 run as kernels, with no host round trip per
+ * token. tokens[0..*n_tokens) is the history on entry (prompt plus anything
+ * generated before a handover); on return it holds the full history. */
+int hs_seq_run(const hs_model* m, hs_kv* kv, hs_scratch* s, uint32_t* tokens, uint64_t* n_tokens, uint64_t cap,
+               hs_seq_state* st, const hs_sampler_cfg* cfg, hs_rng* rng, uint64_t stop_at_filled);
+
+/* The same loop split into its stream-ordered parts, for callers that keep
+ * the history resident on the device between calls (and for timing):
+ * begin uploads the state, step enqueues n forward+commit steps without
+ * synchronising, end downloads the state. */
+int hs_seq_begin(hs_scratch* s, hs_kv* kv, const uint32_t* tokens, uint64_t n_tokens, uint64_t cap,
+                 const hs_seq_state* st, const hs_sampler_cfg* cfg, const hs_rng* rng, uint64_t stop_at_filled);
+int hs_seq_step(hs_scratch* s, uint32_t n_steps);
+int hs_seq_end(hs_scratch* s, uint32_t* tokens, uint64_t* n_tokens, uint64_t cap, hs_seq_state* st, hs_rng* rng);
+/* The scratch's CUDA stream (cudaStream_t), for event timing. */
+void* hs_scratch_stream(hs_scratch* s);
+/* Kernel launches one hs_seq_step(s, 1) enqueues. */
+int hs_seq_launches_per_step(hs_scratch* s, uint32_t* out);
+
+/* ---- load-time dequantisation as a standalone op (quant.rs:18-38) ------ */
+
+/* Dequantise n elements of ggml type `ggml_type` from device memory `src`
+ * into f16 bits at device memory `dst`, on `stream` (cudaStream_t or NULL). */
+int hs_dequant_f16(uint32_t ggml_type, const void* src, uint64_t n, void* dst, void* stream);
+
+/* ---- seeded synthetic GGUF (fixture writer; no counterpart in hs-engine) -- */
+
+typedef struct {
+    uint32_t n_layers, d_model, n_heads, n_kv_heads, d_ff, vocab, context_length, eos;
+    float eps, rope_base, weight_std, bias_std;
+    uint32_t embd_type;   /* ggml type of token_embd.weight (14 = Q6_K) */
+    uint32_t weight_type; /* ggml type of the other 2-D weights (12 = Q4_K) */
+    uint32_t tied;        /* 1: no output.weight (tied LM head) */
+    uint32_t threads;
+    uint64_t seed;
+} hs_synth_spec;
+
+int hs_synth_write(const char* path, const hs_synth_spec* spec);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,132 @@
+"""The on-device sampler against Sampler::sample (sampler.rs:100-187): same
+token and same RNG state for the same logits, history and configuration."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import hotseat_b200 as hs
+from oracle import ffi
+
+from conftest import TINY
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tiny_scratch(tiny_gguf):
+    m = hs.Model.load(tiny_gguf, max_ctx=64)
+    return m, m.scratch()
+
+
+@pytest.fixture(scope="module")
+def big_scratch(q05_gguf):
+    m = hs.Model.load(q05_gguf, max_ctx=64)
+    return m, m.scratch()
+
+
+def oracle_sample(cfg, rng_state, logits, hist):
+    ocfg = ffi.SamplerCfg(cfg.temperature, cfg.top_p, cfg.top_k, cfg.repeat_penalty, cfg.repeat_last_n, cfg.seed)
+    r = ffi.Rng()
+    r.s[:] = list(rng_state.s)
+    r.draws = rng_state.draws
+    l = logits.copy()
+    h = np.ascontiguousarray(hist, dtype=np.uint32)
+    tok = ffi.lib().hso_sample(C.byref(ocfg), C.byref(r), ffi.ptr(l), l.size, ffi.ptr(h) if h.size else None, h.size)
+    return tok, list(r.s), r.draws
+
+
+def device_sample(scratch, cfg, rng, logits, hist):
+    scratch.set_logits(logits)
+    smp = hs.Sampler(cfg, hs.Rng())
+    smp.rng.s[:] = list(rng.s)
+    smp.rng.draws = rng.draws
+    tok = smp.sample(scratch, hist)
+    return tok, list(smp.rng.s), smp.rng.draws
+
+
+def check(scratch, cfg, logits, hist, seed=5):
+    rng = hs.Rng.seed(seed)
+    got = device_sample(scratch, cfg, rng, logits, hist)
+    want = oracle_sample(cfg, rng, logits, hist)
+    assert got == want
+
+
+def test_reference_cases_on_the_device(tiny_scratch):
+    m, s = tiny_scratch
+    v = TINY["vocab"]
+    # greedy_sampling_ignores_the_rng (sampler.rs:235-242)
+    l = np.full(v, -10.0, dtype=np.float32)
+    l[:4] = [0.1, 5.0, -3.0, 4.9]
+    cfg = hs.SamplerCfg.default(temperature=0.0)
+    smp = hs.Sampler(cfg)
+    s.set_logits(l)
+    assert smp.sample(s, []) == 1 and smp.rng.draws == 0
+    # top_k_one_is_greedy_even_with_temperature (244-258)
+    cfg = hs.SamplerCfg.default(temperature=2.0, top_k=1, top_p=1.0, repeat_penalty=1.0)
+    smp = hs.Sampler(cfg)
+    for _ in range(20):
+        assert smp.sample(s, []) == 1
+    # repetition_penalty_pushes_logits_down (275-284)
+    l2 = np.full(v, -10.0, dtype=np.float32)
+    l2[:4] = [0.0, 10.0, 9.0, 0.0]
+    s.set_logits(l2)
+    cfg = hs.SamplerCfg.default(temperature=0.0, repeat_penalty=2.0, repeat_last_n=8)
+    assert hs.Sampler(cfg).sample(s, [1]) == 2
+
+
+def test_same_state_gives_the_same_token_on_the_device(tiny_scratch):
+    m, s = tiny_scratch
+    logits = np.array([((i * 37 % 91) / 13.0) for i in range(TINY["vocab"])], dtype=np.float32)
+    cfg = hs.SamplerCfg.default(temperature=1.0, top_k=0, top_p=1.0, repeat_penalty=1.0)
+    s.set_logits(logits)
+    a = hs.Sampler(cfg)
+    for _ in range(20):
+        a.sample(s)
+    b = hs.Sampler(cfg, hs.Rng())
+    b.rng.s[:] = list(a.rng.s)
+    b.rng.draws = a.rng.draws
+    assert a.sample(s) == b.sample(s)
+
+
+@pytest.mark.parametrize("trial", range(12))
+def test_random_configs_match_the_oracle_tiny(tiny_scratch, trial):
+    m, s = tiny_scratch
+    rng = np.random.default_rng(trial)
+    v = TINY["vocab"]
+    logits = (rng.standard_normal(v) * rng.choice([0.3, 1.0, 4.0])).astype(np.float32)
+    if trial % 3 == 0:  # exact ties: the id must break them
+        logits[rng.integers(0, v, 50)] = logits.max()
+    hist = rng.integers(0, v, size=int(rng.integers(0, 100))).astype(np.uint32)
+    cfg = hs.SamplerCfg.default(temperature=float(rng.choice([0.0, 0.3, 0.8, 1.5])),
+                                top_p=float(rng.choice([0.5, 0.9, 0.95, 1.0])),
+                                top_k=int(rng.choice([0, 1, 5, 40, 64, 200])),
+                                repeat_penalty=float(rng.choice([1.0, 1.1, 1.3])),
+                                repeat_last_n=int(rng.choice([0, 8, 64])))
+    for seed in range(3):
+        check(s, cfg, logits, hist, seed)
+
+
+@pytest.mark.parametrize("trial", range(8))
+def test_random_configs_match_the_oracle_full_vocab(big_scratch, trial):
+    m, s = big_scratch
+    rng = np.random.default_rng(100 + trial)
+    v = hs.QWEN05["vocab"]
+    logits = (rng.standard_normal(v) * 0.6).astype(np.float32)
+    if trial % 2 == 0:
+        logits[rng.integers(0, v, 200)] = np.float32(np.sort(logits)[-30])
+    hist = rng.integers(0, v, size=int(rng.integers(1, 300))).astype(np.uint32)
+    hist[-5:] = np.argsort(logits)[-5:]
+    cfg = hs.SamplerCfg.default(temperature=float(rng.choice([0.0, 0.8, 1.2])),
+                                top_k=int(rng.choice([1, 20, 40, 64])),
+                                top_p=float(rng.choice([0.8, 0.95, 1.0])))
+    for seed in range(3):
+        check(s, cfg, logits, hist, seed)
+
+
+def test_unsupported_top_k_is_an_error(big_scratch):
+    m, s = big_scratch
+    cfg = hs.SamplerCfg.default(top_k=0)
+    with pytest.raises(hs.HotseatError) as e:
+        hs.Sampler(cfg).sample(s, [])
+    assert e.value.code == hs.HS_E_UNSUPPORTED
