@@ -163,6 +163,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="hotseat", choices=["hotseat", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="prefill, then run one decode token inside the NVTX range 'decode_step' and exit")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -216,6 +218,20 @@ def main():
         return out[: n.value], sst
 
     n_steps = PROMPT_LEN + GEN - snap_state[1]  # forwards in the decode phase
+    if args.profile_step:
+        for _ in range(3):
+            begin()
+            hs._check(lib.hs_seq_step(s._h, 1))
+            end_check()
+        begin()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_step")
+        hs._check(lib.hs_seq_step(s._h, 1))
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        end_check()
+        print(json.dumps({"profile_step": "done", "launches": s.launches_per_step()}))
+        return
     for _ in range(args.warmup):
         begin()
         hs._check(lib.hs_seq_step(s._h, n_steps))

@@ -94,6 +94,9 @@ __device__ __forceinline__ float fold_lanes(const float* a) {
 // residual stream (or of the embedding row, model.rs:247-250) on the way in;
 // bias (model.rs:255-257), residual add (308-310, 319-321) or SiLU gate
 // (315-317) on the way out.
+//
+// Shared memory: [nst weight stages][xs: n f32][gs: n f32 norm gain]
+// [xe: n f16 embedding row][outs: 2*rt][bias_s: rt][red: 32][bars: nst+1].
 template <int OUT, int L>
 __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMap tm0,
                                               const __grid_constant__ CUtensorMap tm1, const GemvArgs a,
@@ -101,14 +104,19 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int NMAT = OUT == OUT_SILU ? 2 : 1;
-    const uint32_t kslabs = a.n / 64;
+    const uint32_t n = a.n;
+    const uint32_t kslabs = n / 64;
     const uint32_t mat_bytes = kslabs * a.slab_stride;
     const uint32_t stage_bytes = NMAT * mat_bytes;
     uint8_t* stages = smem;
     float* xs = reinterpret_cast<float*>(smem + a.nst * stage_bytes);
-    float* outs = xs + a.n;
-    float* red = outs + 2 * a.rt;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(red + 32);
+    float* gs = xs + n;
+    uint16_t* xe = reinterpret_cast<uint16_t*>(gs + n);
+    float* outs = reinterpret_cast<float*>(xe + n);
+    float* bias_s = outs + 2 * a.rt;
+    float* red = bias_s + a.rt;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + 32 + ((a.rt & 1) ? 1 : 0));
+    uint64_t* xbar = bars + a.nst;
     const uint32_t tid = threadIdx.x;
 
     uint32_t r0, r1;
@@ -118,7 +126,7 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
     const uint32_t tx_bytes = NMAT * kslabs * a.rt * 128;
 
     if (tid == 0) {
-        for (uint32_t s = 0; s < a.nst; s++) mbar_init(&bars[s], 1);
+        for (uint32_t s = 0; s <= a.nst; s++) mbar_init(&bars[s], 1);
         mbar_init_fence();
     }
     __syncthreads();
@@ -132,9 +140,17 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
                 tma_load_2d(st + m * mat_bytes + k * a.slab_stride, m ? &tm1 : &tm0, (int)(k * 64), y, &bars[s]);
     };
     const uint32_t npre = ntiles < a.nst ? ntiles : a.nst;
-    // Weights never change: fetch them before waiting on the previous kernel.
+    // Everything constant is fetched before waiting on the previous kernel:
+    // the weight tiles, the norm gain, the first tile's bias.
     if (tid == 0)
         for (uint32_t t = 0; t < npre; t++) issue(t);
+    if (in_mode != IN_PLAIN) {
+        const float4* g4 = reinterpret_cast<const float4*>(a.norm_g);
+        float4* s4 = reinterpret_cast<float4*>(gs);
+#pragma unroll 4
+        for (uint32_t i = tid; i < n / 4; i += blockDim.x) s4[i] = g4[i];
+    }
+    if (OUT == OUT_STORE && a.bias && tid < a.rt && tid < mine) bias_s[tid] = a.bias[r0 + tid];
     pdl_launch_dependents();
     pdl_wait();
 
@@ -154,31 +170,42 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
         return;
     }
 
-    // ---- activation prologue
-    const uint32_t n = a.n;
+    // ---- activation: one bulk copy (it was just written; it is in L2)
+    if (tid == 0) {
+        if (in_mode == IN_EMBED_NORM) {
+            mbar_expect_tx(xbar, n * 2);
+            bulk_load_1d(xe, a.embd + (size_t)token * n, n * 2, xbar);
+        } else {
+            mbar_expect_tx(xbar, n * 4);
+            bulk_load_1d(xs, a.src, n * 4, xbar);
+        }
+    }
+    if (!mbar_wait_bounded(xbar, 0)) {
+        if (tid == 0) atomicOr(&ctl->err, ERR_TIMEOUT);
+        for (uint32_t t = 0; t < npre; t++) mbar_wait_bounded(&bars[t], 0);
+        return;
+    }
     if (in_mode == IN_EMBED_NORM) {
-        const uint16_t* row = a.embd + (size_t)token * n;
         for (uint32_t i = tid; i < n; i += blockDim.x) {
-            float v = h2f(row[i]);
+            const float v = h2f(xe[i]);
             xs[i] = v;
             if (blockIdx.x == 0) a.x_out[i] = v;
         }
-    } else {
-        const float4* s4 = reinterpret_cast<const float4*>(a.src);
-        float4* x4 = reinterpret_cast<float4*>(xs);
-        for (uint32_t i = tid; i < n / 4; i += blockDim.x) x4[i] = s4[i];
+        __syncthreads();
     }
-    __syncthreads();
     if (in_mode != IN_PLAIN) {
         // rmsnorm: ss = dot_f32(x, x) in the 8-lane shape; scale = 1/sqrt(ss/n + eps);
         // out[i] = x[i] * scale * g[i].
         if (tid < 32) {
             float acc = 0.0f;
-            if (tid < 8)
-                for (uint32_t j = 0; j < n / 8; j++) {
-                    float v = xs[8 * j + tid];
+            if (tid < 8) {
+                const uint32_t nj = n / 8;
+#pragma unroll 16
+                for (uint32_t j = 0; j < nj; j++) {
+                    const float v = xs[8 * j + tid];
                     acc = __fadd_rn(acc, __fmul_rn(v, v));
                 }
+            }
             float v = acc;
             v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
             v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
@@ -187,7 +214,7 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
         }
         __syncthreads();
         const float scale = red[0];
-        for (uint32_t i = tid; i < n; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], scale), a.norm_g[i]);
+        for (uint32_t i = tid; i < n; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], scale), gs[i]);
         __syncthreads();
     }
 
@@ -208,6 +235,7 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
         if (lane_active) {
             const uint8_t* base = stages + s * stage_bytes + m * mat_bytes + r * 128;
             const uint32_t sw = r & 7;
+#pragma unroll 2
             for (uint32_t k = 0; k < kslabs; k++) {
                 const uint8_t* sb = base + k * a.slab_stride;
                 const float* xk = xs + k * 64 + g * L;
@@ -231,8 +259,12 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
             }
         } else if (lane_active && g == 0 && rr < mine) {
             const uint32_t row = r0 + rr;
-            if (OUT == OUT_STORE) a.dst[row] = a.bias ? __fadd_rn(v, a.bias[row]) : v;
-            else a.dst[row] = __fadd_rn(a.dst[row], v);
+            if (OUT == OUT_STORE) {
+                if (a.bias) a.dst[row] = __fadd_rn(v, t == 0 ? bias_s[r] : a.bias[row]);
+                else a.dst[row] = v;
+            } else {
+                a.dst[row] = __fadd_rn(a.dst[row], v);
+            }
         }
         __syncthreads();
         if (tid == 0 && t + a.nst < ntiles) {
@@ -249,29 +281,57 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
 // bitmap; scores p in [0, pos] = dot_f32(q, k_p) * (1/sqrt(hd)); softmax with
 // exp_f32, sequential sum and 1/sum (math.rs:210-226); out = sum_p sc[p]*v_p in
 // position order (axpy, math.rs:185-190).
+//
+// Rows p < pos were written by earlier tokens, so up to kAttnPre of them are
+// copied into shared memory before griddepcontrol.wait, overlapping the QKV
+// kernel; longer contexts stream the remainder in chunks after the wait.
+template <int HD>
+struct AttnShape {
+    static constexpr int RS = HD + 4;          // padded row stride (floats): conflict-free row reads
+    static constexpr int PRE = 12288 / HD;     // rows of K and of V prefetched (192 at hd 64)
+    static constexpr int CH = 4096 / HD;       // rows per streamed chunk beyond PRE
+};
+
 template <int HD>
 __global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
     extern __shared__ __align__(16) float sm[];
-    constexpr int CH = 8192 / HD;  // positions staged per chunk
-    constexpr int RS = HD + 4;     // padded row stride (floats): conflict-free row reads
-    constexpr int HALF = HD / 2;
+    using S = AttnShape<HD>;
+    constexpr int RS = S::RS, PRE = S::PRE, CH = S::CH, HALF = HD / 2;
     float* q = sm;
     float* kc = q + HD;
     float* vc = kc + HD;
     float* red = vc + HD;
-    float* buf = red + 64;
-    float* sc = buf + CH * RS;
+    float* kb = red + 64;       // [PRE][RS]
+    float* vb = kb + PRE * RS;  // [PRE][RS]
+    float* cb = vb + PRE * RS;  // [CH][RS]
+    float* sc = cb + CH * RS;   // [max_ctx]
     const uint32_t tid = threadIdx.x;
+    DevCtl* ctl = a.ctl;
+    const uint32_t h = blockIdx.x, groups = a.nh / a.nkv, kvh = h / groups;
+    const uint64_t plane = (uint64_t)a.max_ctx * a.nkv * HD;
+    const uint64_t lbase = (uint64_t)a.layer * 2 * plane;
+    auto row_off = [&](uint32_t p, uint32_t is_v) -> uint64_t {
+        uint64_t within = a.layout == 0 ? ((uint64_t)p * a.nkv + kvh) * HD : ((uint64_t)kvh * a.max_ctx + p) * HD;
+        return lbase + (is_v ? plane : 0) + within;
+    };
+    // `active` and `pos` were set before this graph launch began (by the host
+    // or by the previous step's commit kernel), so they are stable here.
+    const bool run = ld_volatile(&ctl->active) != 0;
+    const uint32_t pos = ld_volatile(&ctl->pos);
+    const bool pos_ok = pos < a.max_ctx;
+    const uint32_t npre = run && pos_ok ? min(pos, (uint32_t)PRE) : 0;
+    for (uint32_t idx = tid; idx < npre * (HD / 4); idx += blockDim.x) {
+        const uint32_t p = idx / (HD / 4), c4 = idx % (HD / 4);
+        cp_async16(kb + p * RS + 4 * c4, a.kv + row_off(p, 0) + 4 * c4);
+        cp_async16(vb + p * RS + 4 * c4, a.kv + row_off(p, 1) + 4 * c4);
+    }
     pdl_launch_dependents();
     pdl_wait();
-    DevCtl* ctl = a.ctl;
-    if (!ld_volatile(&ctl->active)) return;
-    const uint32_t pos = ld_volatile(&ctl->pos);
-    if (pos >= a.max_ctx) {
-        if (tid == 0 && blockIdx.x == 0) atomicOr(&ctl->err, ERR_POS);
+    if (!run || !pos_ok) {
+        cp_async_wait_all();
+        if (run && tid == 0 && blockIdx.x == 0) atomicOr(&ctl->err, ERR_POS);
         return;
     }
-    const uint32_t h = blockIdx.x, groups = a.nh / a.nkv, kvh = h / groups;
     if (tid < HD) {
         q[tid] = a.qkv[h * HD + tid];
         kc[tid] = a.qkv[a.nh * HD + kvh * HD + tid];
@@ -289,13 +349,6 @@ __global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
         kc[tid + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
     }
     __syncthreads();
-
-    const uint64_t plane = (uint64_t)a.max_ctx * a.nkv * HD;
-    const uint64_t lbase = (uint64_t)a.layer * 2 * plane;
-    auto row_off = [&](uint32_t p, uint32_t is_v) -> uint64_t {
-        uint64_t within = a.layout == 0 ? ((uint64_t)p * a.nkv + kvh) * HD : ((uint64_t)kvh * a.max_ctx + p) * HD;
-        return lbase + (is_v ? plane : 0) + within;
-    };
     if (h % groups == 0) {
         if (tid < HD) {
             a.kv[row_off(pos, 0) + tid] = kc[tid];
@@ -311,49 +364,49 @@ __global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
                 atomicOr(reinterpret_cast<unsigned long long*>(&a.dirty[pg >> 6]), 1ull << (pg & 63));
         }
     }
+    cp_async_wait_all();
+    __syncthreads();
 
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
     const uint32_t n = pos + 1;
-    // pass 1: scores
-    for (uint32_t c0 = 0; c0 < n; c0 += CH) {
-        const uint32_t cnt = min((uint32_t)CH, n - c0);
-        for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += blockDim.x) {
-            const uint32_t rr = idx / (HD / 4), c4 = idx % (HD / 4), p = c0 + rr;
-            float4 v = p == pos ? reinterpret_cast<const float4*>(kc)[c4]
-                                : *reinterpret_cast<const float4*>(a.kv + row_off(p, 0) + 4 * c4);
-            *reinterpret_cast<float4*>(buf + rr * RS + 4 * c4) = v;
-        }
-        __syncthreads();
-        if (tid < cnt) {
-            const float* kr = buf + tid * RS;
-            float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll 4
-            for (int j = 0; j < HD / 8; j++)
+    auto score = [&](const float* kr) -> float {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
-                for (int l = 0; l < 8; l++) acc[l] = __fadd_rn(acc[l], __fmul_rn(q[8 * j + l], kr[8 * j + l]));
-            const float d = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3])),
-                                      __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7])));
-            sc[c0 + tid] = __fmul_rn(d, scale);
+        for (int j = 0; j < HD / 8; j++)
+#pragma unroll
+            for (int l = 0; l < 8; l++) acc[l] = __fadd_rn(acc[l], __fmul_rn(q[8 * j + l], kr[8 * j + l]));
+        const float d = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3])),
+                                  __fadd_rn(__fadd_rn(acc[4], acc[5]), __fadd_rn(acc[6], acc[7])));
+        return __fmul_rn(d, scale);
+    };
+    // scores: prefetched rows, the current row, then any streamed remainder
+    for (uint32_t p = tid; p < npre; p += blockDim.x) sc[p] = score(kb + p * RS);
+    if (tid == 0) sc[pos] = score(kc);
+    for (uint32_t c0 = npre; c0 < pos; c0 += CH) {
+        const uint32_t cnt = min((uint32_t)CH, pos - c0);
+        __syncthreads();
+        for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += blockDim.x) {
+            const uint32_t rr = idx / (HD / 4), c4 = idx % (HD / 4);
+            *reinterpret_cast<float4*>(cb + rr * RS + 4 * c4) =
+                *reinterpret_cast<const float4*>(a.kv + row_off(c0 + rr, 0) + 4 * c4);
         }
         __syncthreads();
+        if (tid < cnt) sc[c0 + tid] = score(cb + tid * RS);
     }
+    __syncthreads();
     // softmax: max (order-free), exp, sequential sum, scale by 1/sum
-    float mx = -FLT_MAX * 2.0f;  // -inf
+    float mx = __int_as_float(0xff800000);
     for (uint32_t p = tid; p < n; p += blockDim.x) mx = fmaxf(mx, sc[p]);
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if ((tid & 31) == 0) red[tid >> 5] = mx;
     __syncthreads();
-    if (tid == 0) {
-        float m2 = red[0];
-        for (uint32_t w = 1; w < blockDim.x / 32; w++) m2 = fmaxf(m2, red[w]);
-        red[32] = m2;
-    }
-    __syncthreads();
-    mx = red[32];
+    mx = red[0];
+    for (uint32_t w = 1; w < blockDim.x / 32; w++) mx = fmaxf(mx, red[w]);
     for (uint32_t p = tid; p < n; p += blockDim.x) sc[p] = ref_exp(__fsub_rn(sc[p], mx));
     __syncthreads();
     if (tid == 0) {
         float sum = 0.0f;
+#pragma unroll 8
         for (uint32_t p = 0; p < n; p++) sum = __fadd_rn(sum, sc[p]);
         red[33] = __fdiv_rn(1.0f, sum);
     }
@@ -361,116 +414,199 @@ __global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
     const float inv = red[33];
     for (uint32_t p = tid; p < n; p += blockDim.x) sc[p] = __fmul_rn(sc[p], inv);
     __syncthreads();
-    // pass 2: out[d] = sum over p, in order, of sc[p] * v_p[d]
+    // out[d] = sum over p, in order, of sc[p] * v_p[d]
     float out = 0.0f;
-    for (uint32_t c0 = 0; c0 < n; c0 += CH) {
-        const uint32_t cnt = min((uint32_t)CH, n - c0);
+    if (tid < HD) {
+#pragma unroll 8
+        for (uint32_t p = 0; p < npre; p++) out = __fadd_rn(out, __fmul_rn(sc[p], vb[p * RS + tid]));
+    }
+    for (uint32_t c0 = npre; c0 < pos; c0 += CH) {
+        const uint32_t cnt = min((uint32_t)CH, pos - c0);
+        __syncthreads();
         for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += blockDim.x) {
-            const uint32_t rr = idx / (HD / 4), c4 = idx % (HD / 4), p = c0 + rr;
-            float4 v = p == pos ? reinterpret_cast<const float4*>(vc)[c4]
-                                : *reinterpret_cast<const float4*>(a.kv + row_off(p, 1) + 4 * c4);
-            *reinterpret_cast<float4*>(buf + rr * RS + 4 * c4) = v;
+            const uint32_t rr = idx / (HD / 4), c4 = idx % (HD / 4);
+            *reinterpret_cast<float4*>(cb + rr * RS + 4 * c4) =
+                *reinterpret_cast<const float4*>(a.kv + row_off(c0 + rr, 1) + 4 * c4);
         }
         __syncthreads();
         if (tid < HD)
-            for (uint32_t t = 0; t < cnt; t++) out = __fadd_rn(out, __fmul_rn(sc[c0 + t], buf[t * RS + tid]));
-        __syncthreads();
+#pragma unroll 8
+            for (uint32_t t = 0; t < cnt; t++) out = __fadd_rn(out, __fmul_rn(sc[c0 + t], cb[t * RS + tid]));
     }
-    if (tid < HD) a.att[h * HD + tid] = out;
+    if (tid < HD) {
+        out = __fadd_rn(out, __fmul_rn(sc[pos], vc[tid]));
+        a.att[h * HD + tid] = out;
+    }
 }
 
 // -------------------------------------------------------------- sampler
-// Stage 1: each CTA takes 1024 logits, applies the repetition penalty to the
-// history tokens in its slice (sampler.rs:103-111; one token can be penalised
-// several times, in history order), then either finds its first maximum
-// (greedy, sampler.rs:177-187) or sorts its slice under cmp_desc and keeps the
-// best kmax keys.
+// Stage 1 (k_sample_cand): each CTA takes 1024 logits (8 warps x 128),
+// applies the repetition penalty to the history tokens in its slice
+// (sampler.rs:103-111: a token is penalised once per occurrence, in history
+// order), then either finds its first maximum (greedy, sampler.rs:177-187)
+// or orders its slice under cmp_desc and keeps the best kmax keys.
+// Stage 2 (k_sample_final): merges the per-CTA lists into the global top-k
+// and runs the reference's serial tail on one thread: temperature softmax
+// with exp_f32, nucleus cut, one next_f32 draw (sampler.rs:134-166); in
+// sequence mode it then commits the step exactly as seq.rs:273-312 does.
 __device__ __forceinline__ bool seq_needs_sample(const DevCtl* c) {
     if (c->mode == 1) return true;
     return ld_volatile(&c->active) && c->filled + 1 == c->n_tokens;
 }
 
+// (value, index) "better" for greedy: larger value, then smaller index; an
+// invalid index (0xffffffff) never wins and NaN never compares larger.
+__device__ __forceinline__ bool arg_better(float v2, uint32_t i2, float v1, uint32_t i1) {
+    if (i2 == 0xffffffffu) return false;
+    if (i1 == 0xffffffffu) return true;
+    return v2 > v1 || (v2 == v1 && i2 < i1);
+}
+
+__device__ __forceinline__ void warp_argbest(float* v, uint32_t* i) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, *v, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, *i, o);
+        if (arg_better(ov, oi, *v, *i)) {
+            *v = ov;
+            *i = oi;
+        }
+    }
+}
+
+// Ascending bitonic sort of 128 keys held as k[i] = element i*32 + lane.
+__device__ __forceinline__ void warp_sort128(uint64_t k[4], int lane) {
+#pragma unroll
+    for (int size = 2; size <= 128; size <<= 1) {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int e = i * 32 + lane;
+                const bool up = (e & size) == 0;
+                if (j >= 32) {
+                    const int ii = i ^ (j >> 5);
+                    if (ii > i) {
+                        const uint64_t x = k[i], y = k[ii];
+                        if ((x > y) == up) {
+                            k[i] = y;
+                            k[ii] = x;
+                        }
+                    }
+                } else {
+                    const uint64_t o = __shfl_xor_sync(0xffffffffu, k[i], j);
+                    const bool lower = (e & j) == 0;
+                    k[i] = (lower == up) ? (o < k[i] ? o : k[i]) : (o > k[i] ? o : k[i]);
+                }
+            }
+        }
+    }
+}
+
+// Number of keys in sorted list[0..len) smaller than `key`.
+__device__ __forceinline__ uint32_t lower_bound_u64(const uint64_t* list, uint32_t len, uint64_t key) {
+    uint32_t lo = 0, hi = len;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (list[mid] < key) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
 __global__ void __launch_bounds__(256) k_sample_cand(const SampleArgs a) {
-    __shared__ float vals[kSampleSlice];
-    __shared__ uint64_t keys[kSampleSlice];
-    __shared__ float bv_s[256];
-    __shared__ uint32_t bi_s[256];
-    const uint32_t tid = threadIdx.x;
+    __shared__ uint64_t lists[8][128];
+    __shared__ uint32_t win[256];
+    __shared__ float bv_s[8];
+    __shared__ uint32_t bi_s[8];
+    const uint32_t tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     pdl_launch_dependents();
     pdl_wait();
     const DevCtl* c = a.ctl;
     if (!seq_needs_sample(c)) return;
-    const uint32_t base = blockIdx.x * kSampleSlice;
-    for (uint32_t i = tid; i < kSampleSlice; i += blockDim.x)
-        vals[i] = base + i < a.vocab ? a.logits[base + i] : 0.0f;
-    __syncthreads();
-    if (tid == 0 && c->repeat_penalty != 1.0f && c->repeat_last_n > 0) {
-        const uint64_t nt = c->n_tokens;
-        const uint64_t nw = c->repeat_last_n < nt ? c->repeat_last_n : nt;
-        for (uint64_t i = nt - nw; i < nt; i++) {
-            const uint32_t t = a.tokens[i];
-            if (t >= base && t < base + kSampleSlice && t < a.vocab) {
-                const float l = vals[t - base];
-                vals[t - base] = l > 0.0f ? __fdiv_rn(l, c->repeat_penalty) : __fmul_rn(l, c->repeat_penalty);
-            }
+    const uint32_t base = blockIdx.x * kSampleSlice + w * 128;
+    float v[4];
+    uint32_t e[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        e[i] = base + i * 32 + lane;
+        v[i] = e[i] < a.vocab ? a.logits[e[i]] : 0.0f;
+    }
+    const float pen = c->repeat_penalty;
+    const uint64_t nt = c->n_tokens;
+    const uint64_t nw = (pen != 1.0f && c->repeat_last_n > 0) ? (c->repeat_last_n < nt ? c->repeat_last_n : nt) : 0;
+    for (uint64_t w0 = nt - nw; w0 < nt; w0 += 256) {
+        const uint32_t cnt = (uint32_t)min((uint64_t)256, nt - w0);
+        __syncthreads();
+        if (tid < cnt) win[tid] = a.tokens[w0 + tid];
+        __syncthreads();
+        for (uint32_t j = 0; j < cnt; j++) {
+            const uint32_t t = win[j];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                if (t == e[i]) v[i] = v[i] > 0.0f ? __fdiv_rn(v[i], pen) : __fmul_rn(v[i], pen);
         }
     }
-    __syncthreads();
     if (c->temperature <= 0.0f) {
-        float bv = __int_as_float(0xff800000);  // -inf
+        float bv = 0.0f;
         uint32_t bi = 0xffffffffu;
-        for (uint32_t i = tid * 4; i < tid * 4 + 4; i++)
-            if (base + i < a.vocab && vals[i] > bv) {
-                bv = vals[i];
-                bi = base + i;
+#pragma unroll
+        for (int i = 0; i < 4; i++)  // index order within the thread
+            if (e[i] < a.vocab && !(v[i] != v[i]) && v[i] > __int_as_float(0xff800000) && arg_better(v[i], e[i], bv, bi)) {
+                bv = v[i];
+                bi = e[i];
             }
-        bv_s[tid] = bv;
-        bi_s[tid] = bi;
+        warp_argbest(&bv, &bi);
+        if (lane == 0) {
+            bv_s[w] = bv;
+            bi_s[w] = bi;
+        }
         __syncthreads();
         if (tid == 0) {
-            float v = bv_s[0];
-            uint32_t ix = bi_s[0];
-            for (uint32_t t = 1; t < blockDim.x; t++)
-                if (bi_s[t] != 0xffffffffu && (ix == 0xffffffffu || bv_s[t] > v)) {
-                    v = bv_s[t];
-                    ix = bi_s[t];
+            float fv = bv_s[0];
+            uint32_t fi = bi_s[0];
+            for (int k = 1; k < 8; k++)
+                if (arg_better(bv_s[k], bi_s[k], fv, fi)) {
+                    fv = bv_s[k];
+                    fi = bi_s[k];
                 }
-            a.argbuf[blockIdx.x] = ((uint64_t)__float_as_uint(v) << 32) | ix;
+            a.argbuf[blockIdx.x] = ((uint64_t)__float_as_uint(fv) << 32) | fi;
         }
         return;
     }
-    for (uint32_t i = tid; i < kSampleSlice; i += blockDim.x)
-        keys[i] = base + i < a.vocab ? cand_key(vals[i], base + i) : ~0ull;
+    uint64_t k[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) k[i] = e[i] < a.vocab ? cand_key(v[i], e[i]) : ~0ull - e[i];
+    warp_sort128(k, (int)lane);
+#pragma unroll
+    for (int i = 0; i < 4; i++) lists[w][i * 32 + lane] = k[i];
     __syncthreads();
-    for (uint32_t k = 2; k <= kSampleSlice; k <<= 1)
-        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
-            for (uint32_t i = tid; i < kSampleSlice; i += blockDim.x) {
-                const uint32_t ixj = i ^ j;
-                if (ixj > i) {
-                    const uint64_t x = keys[i], y = keys[ixj];
-                    if ((x > y) == ((i & k) == 0)) {
-                        keys[i] = y;
-                        keys[ixj] = x;
-                    }
-                }
-            }
-            __syncthreads();
-        }
-    for (uint32_t i = tid; i < a.kmax; i += blockDim.x) a.cand[(size_t)blockIdx.x * a.kmax + i] = keys[i];
+    // Rank-based merge of the 8 sorted lists: element j of list l has rank
+    // j + (keys smaller than it in the other lists); keep ranks < kmax.
+    const uint32_t J = a.kmax < 128 ? a.kmax : 128;
+    for (uint32_t idx = tid; idx < 8 * J; idx += blockDim.x) {
+        const uint32_t l = idx / J, j = idx % J;
+        const uint64_t key = lists[l][j];
+        uint32_t rank = j;
+#pragma unroll
+        for (uint32_t o = 0; o < 8; o++)
+            if (o != l) rank += lower_bound_u64(lists[o], J, key);
+        if (rank < a.kmax) a.cand[(size_t)blockIdx.x * a.kmax + rank] = key;
+    }
 }
 
-// Stage 2 (one CTA): merge the per-CTA lists (already sorted) by a warp
-// tournament into the global top-k, then run the reference's serial tail on
-// one thread: temperature softmax with exp_f32, nucleus cut, one next_f32
-// draw (sampler.rs:134-166). In sequence mode, then commit the step exactly as
-// seq.rs:273-312 does and arm the next one.
-constexpr int kMaxListsPerLane = 8;
+constexpr uint32_t kFinalThreads = 256;
 
-__global__ void __launch_bounds__(256) k_sample_final(const SampleArgs a) {
-    extern __shared__ uint64_t lists[];  // n_cta * kmax keys, then the merged top-k
+__global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs a) {
+    extern __shared__ uint64_t sel_lists[];  // [n_sel][kmax]
+    __shared__ uint64_t heads[256];
+    __shared__ uint32_t sel[64];
+    __shared__ uint64_t merged[1024];
     __shared__ float pk[1024];
+    __shared__ float bv_s[8];
+    __shared__ uint32_t bi_s[8];
     __shared__ uint32_t tok_s;
-    const uint32_t tid = threadIdx.x;
+    const uint32_t tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     pdl_launch_dependents();
     pdl_wait();
     DevCtl* c = a.ctl;
@@ -478,103 +614,115 @@ __global__ void __launch_bounds__(256) k_sample_final(const SampleArgs a) {
     if (seq && !ld_volatile(&c->active)) return;
     const bool need = seq_needs_sample(c);
     if (tid == 0) tok_s = 0;
-    if (need) {
-        if (c->temperature <= 0.0f) {
-            if (tid == 0) {
-                float v = 0.0f;
-                uint32_t ix = 0xffffffffu;
-                for (uint32_t i = 0; i < a.n_cta; i++) {
-                    const uint64_t e = a.argbuf[i];
-                    const uint32_t ei = (uint32_t)e;
-                    const float ev = __uint_as_float((uint32_t)(e >> 32));
-                    if (ei != 0xffffffffu && (ix == 0xffffffffu || ev > v)) {
-                        v = ev;
-                        ix = ei;
-                    }
+    if (need && c->temperature <= 0.0f) {
+        float bv = 0.0f;
+        uint32_t bi = 0xffffffffu;
+        if (tid < a.n_cta) {
+            const uint64_t ent = a.argbuf[tid];
+            bv = __uint_as_float((uint32_t)(ent >> 32));
+            bi = (uint32_t)ent;
+        }
+        warp_argbest(&bv, &bi);
+        if (lane == 0) {
+            bv_s[w] = bv;
+            bi_s[w] = bi;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float fv = bv_s[0];
+            uint32_t fi = bi_s[0];
+            for (uint32_t k = 1; k < kFinalThreads / 32; k++)
+                if (arg_better(bv_s[k], bi_s[k], fv, fi)) {
+                    fv = bv_s[k];
+                    fi = bi_s[k];
                 }
-                tok_s = ix == 0xffffffffu ? 0u : ix;
-            }
+            tok_s = fi == 0xffffffffu ? 0u : fi;
+        }
+    } else if (need) {
+        const uint32_t k = c->top_k == 0 ? a.vocab : min(c->top_k, a.vocab);
+        if (a.n_cta == 1) {
+            for (uint32_t i = tid; i < k; i += blockDim.x) merged[i] = a.cand[i];
         } else {
-            const uint32_t total = a.n_cta * a.kmax;
-            for (uint32_t i = tid; i < total; i += blockDim.x) lists[i] = a.cand[i];
+            // Only lists whose best key is among the k best heads can hold a
+            // global top-k key (the k best heads are k keys).
+            if (tid < a.n_cta) heads[tid] = a.cand[(size_t)tid * a.kmax];
             __syncthreads();
-            const uint32_t k = c->top_k == 0 ? a.vocab : min(c->top_k, a.vocab);
-            uint64_t* merged = lists + total;
-            if (tid < 32) {
-                uint32_t ptr[kMaxListsPerLane];
-                uint64_t head[kMaxListsPerLane];
-#pragma unroll
-                for (int s = 0; s < kMaxListsPerLane; s++) {
-                    const uint32_t li = tid + 32 * s;
-                    ptr[s] = 0;
-                    head[s] = li < a.n_cta ? lists[li * a.kmax] : ~0ull;
-                }
-                for (uint32_t round = 0; round < k; round++) {
-                    uint64_t best = ~0ull;
-                    int bs = -1;
-#pragma unroll
-                    for (int s = 0; s < kMaxListsPerLane; s++)
-                        if (head[s] < best) {
-                            best = head[s];
-                            bs = s;
-                        }
-                    uint64_t wm = best;
-                    for (int o = 16; o > 0; o >>= 1) {
-                        const uint64_t other = __shfl_xor_sync(0xffffffffu, wm, o);
-                        wm = other < wm ? other : wm;
-                    }
-                    if (bs >= 0 && best == wm) {
-                        merged[round] = wm;
-#pragma unroll
-                        for (int s = 0; s < kMaxListsPerLane; s++)
-                            if (s == bs) {
-                                ptr[s]++;
-                                const uint32_t li = tid + 32 * s;
-                                head[s] = ptr[s] < a.kmax ? lists[li * a.kmax + ptr[s]] : ~0ull;
-                            }
-                    }
-                    __syncwarp();
-                }
+            if (tid < a.n_cta) {
+                const uint64_t hk = heads[tid];
+                uint32_t rank = 0;
+                for (uint32_t o = 0; o < a.n_cta; o++) rank += heads[o] < hk;
+                if (rank < k) sel[rank] = tid;
             }
             __syncthreads();
-            if (tid == 0) {
-                const float inv_t = __fdiv_rn(1.0f, c->temperature);
-                const float mx = key_value(merged[0]);
-                float sum = 0.0f;
-                for (uint32_t i = 0; i < k; i++) {
-                    pk[i] = ref_exp(__fmul_rn(__fsub_rn(key_value(merged[i]), mx), inv_t));
-                    sum = __fadd_rn(sum, pk[i]);
-                }
-                uint32_t cut = k;
-                if (c->top_p < 1.0f) {
-                    const float target = __fmul_rn(c->top_p, sum);
-                    float acc = 0.0f;
-                    for (uint32_t i = 0; i < k; i++) {
-                        acc = __fadd_rn(acc, pk[i]);
-                        if (acc >= target) {
-                            cut = i + 1;
-                            break;
+            const uint32_t n_sel = min(k, a.n_cta);
+            for (uint32_t idx = tid; idx < n_sel * k; idx += blockDim.x) {
+                const uint32_t s = idx / k, j = idx % k;
+                sel_lists[s * k + j] = a.cand[(size_t)sel[s] * a.kmax + j];
+            }
+            __syncthreads();
+            if (w == 0) {
+                // Warp tournament: lane l owns selected lists l and l + 32.
+                uint32_t ptr0 = 0, ptr1 = 0;
+                uint64_t h0 = lane < n_sel ? sel_lists[lane * k] : ~0ull;
+                uint64_t h1 = lane + 32 < n_sel ? sel_lists[(lane + 32) * k] : ~0ull;
+                for (uint32_t round = 0; round < k; round++) {
+                    const bool first = h0 <= h1;
+                    const uint64_t best = first ? h0 : h1;
+                    const uint32_t hi = (uint32_t)(best >> 32), lo = (uint32_t)best;
+                    const uint32_t mhi = __reduce_min_sync(0xffffffffu, hi);
+                    const uint32_t mlo = __reduce_min_sync(0xffffffffu, hi == mhi ? lo : 0xffffffffu);
+                    const unsigned winners = __ballot_sync(0xffffffffu, hi == mhi && lo == mlo);
+                    if (lane == (uint32_t)(__ffs(winners) - 1)) {
+                        merged[round] = best;
+                        if (first) {
+                            ptr0++;
+                            h0 = ptr0 < k ? sel_lists[lane * k + ptr0] : ~0ull;
+                        } else {
+                            ptr1++;
+                            h1 = ptr1 < k ? sel_lists[(lane + 32) * k + ptr1] : ~0ull;
                         }
                     }
-                    sum = 0.0f;
-                    for (uint32_t i = 0; i < cut; i++) sum = __fadd_rn(sum, pk[i]);
                 }
-                uint64_t s4[4] = {c->rng[0], c->rng[1], c->rng[2], c->rng[3]};
-                const float u = __fmul_rn((float)(rng_next(s4) >> 40), 1.0f / 16777216.0f);
-                for (int i = 0; i < 4; i++) c->rng[i] = s4[i];
-                c->draws += 1;
-                const float r = __fmul_rn(u, sum);
-                uint32_t pick = (uint32_t)merged[cut - 1];
+            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const float inv_t = __fdiv_rn(1.0f, c->temperature);
+            const float mx = key_value(merged[0]);
+            float sum = 0.0f;
+            for (uint32_t i = 0; i < k; i++) {
+                pk[i] = ref_exp(__fmul_rn(__fsub_rn(key_value(merged[i]), mx), inv_t));
+                sum = __fadd_rn(sum, pk[i]);
+            }
+            uint32_t cut = k;
+            if (c->top_p < 1.0f) {
+                const float target = __fmul_rn(c->top_p, sum);
                 float acc = 0.0f;
-                for (uint32_t i = 0; i < cut; i++) {
+                for (uint32_t i = 0; i < k; i++) {
                     acc = __fadd_rn(acc, pk[i]);
-                    if (r < acc) {
-                        pick = (uint32_t)merged[i];
+                    if (acc >= target) {
+                        cut = i + 1;
                         break;
                     }
                 }
-                tok_s = pick;
+                sum = 0.0f;
+                for (uint32_t i = 0; i < cut; i++) sum = __fadd_rn(sum, pk[i]);
             }
+            uint64_t s4[4] = {c->rng[0], c->rng[1], c->rng[2], c->rng[3]};
+            const float u = __fmul_rn((float)(rng_next(s4) >> 40), 1.0f / 16777216.0f);
+            for (int i = 0; i < 4; i++) c->rng[i] = s4[i];
+            c->draws += 1;
+            const float r = __fmul_rn(u, sum);
+            uint32_t pick = (uint32_t)merged[cut - 1];
+            float acc = 0.0f;
+            for (uint32_t i = 0; i < cut; i++) {
+                acc = __fadd_rn(acc, pk[i]);
+                if (r < acc) {
+                    pick = (uint32_t)merged[i];
+                    break;
+                }
+            }
+            tok_s = pick;
         }
     }
     __syncthreads();
@@ -652,20 +800,30 @@ cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_
 
 }  // namespace
 
-cudaError_t gemv_set_smem_limits() {
-    const int lim = 232448;
-#define HS_SET(O, L)                                                                                   \
-    {                                                                                                  \
-        cudaError_t e = cudaFuncSetAttribute(k_gemv<O, L>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim); \
-        if (e != cudaSuccess) return e;                                                                \
-    }
+// Allow each kernel the device's opt-in shared memory minus its static part.
+template <typename K>
+cudaError_t allow_smem(K kernel, int optin) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+    if (e != cudaSuccess) return e;
+    // One carveout for every kernel, so a kernel launched early under PDL
+    // never waits for an SM to switch its L1/shared split.
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+}
+
+cudaError_t gemv_set_smem_limits(int optin) {
+    cudaError_t e = cudaSuccess;
+#define HS_SET(O, L) \
+    if (e == cudaSuccess) e = allow_smem(k_gemv<O, L>, optin);
     HS_SET(OUT_STORE, 1) HS_SET(OUT_STORE, 2) HS_SET(OUT_STORE, 4) HS_SET(OUT_STORE, 8)
     HS_SET(OUT_RESID, 1) HS_SET(OUT_RESID, 2) HS_SET(OUT_RESID, 4) HS_SET(OUT_RESID, 8)
     HS_SET(OUT_SILU, 1) HS_SET(OUT_SILU, 2) HS_SET(OUT_SILU, 4) HS_SET(OUT_SILU, 8)
 #undef HS_SET
-    cudaError_t e = cudaFuncSetAttribute(k_attention<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_sample_final, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if (e == cudaSuccess) e = allow_smem(k_attention<64>, optin);
+    if (e == cudaSuccess) e = allow_smem(k_attention<128>, optin);
+    if (e == cudaSuccess) e = allow_smem(k_sample_final, optin);
     return e;
 }
 
@@ -688,8 +846,8 @@ cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_t st) {
 }
 
 size_t attention_smem(uint32_t head_dim, uint32_t max_ctx) {
-    const size_t ch = 8192 / head_dim, rs = head_dim + 4;
-    return (3 * head_dim + 64 + ch * rs + max_ctx) * sizeof(float);
+    const size_t rs = head_dim + 4, pre = 12288 / head_dim, ch = 4096 / head_dim;
+    return (3 * head_dim + 64 + (2 * pre + ch) * rs + max_ctx) * sizeof(float);
 }
 
 cudaError_t launch_attention(uint32_t head_dim, uint32_t nh, size_t smem, const AttnArgs& a, cudaStream_t st) {
@@ -699,14 +857,15 @@ cudaError_t launch_attention(uint32_t head_dim, uint32_t nh, size_t smem, const 
 }
 
 size_t sample_final_smem(uint32_t n_cta, uint32_t kmax) {
-    const size_t k_merge = kmax > 1024 ? 1024 : kmax;
-    return ((size_t)n_cta * kmax + k_merge + 1024) * sizeof(uint64_t);
+    // Selected lists: at most 64 lists of at most 64 keys (top_k <= 64) when
+    // there are several CTAs; none with one CTA.
+    return n_cta > 1 ? (size_t)64 * 64 * sizeof(uint64_t) : 16;
 }
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st) {
     cudaError_t e = launch_pdl(k_sample_cand, dim3(a.n_cta), dim3(256), 0, st, a);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k_sample_final, dim3(1), dim3(256), sample_final_smem(a.n_cta, a.kmax), st, a);
+    return launch_pdl(k_sample_final, dim3(1), dim3(kFinalThreads), sample_final_smem(a.n_cta, a.kmax), st, a);
 }
 
 }  // namespace hs

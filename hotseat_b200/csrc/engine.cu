@@ -77,9 +77,10 @@ int plan_gemv(GemvPlan* p, int in_mode, int out_mode, uint32_t rows, uint32_t n,
     p->rows = rows;
     p->grid = std::min<uint32_t>(rows, (uint32_t)n_sm);
     const uint32_t per = (rows + p->grid - 1) / p->grid;
+    // Mirrors the kernel's shared-memory carve-up (decode.cu k_gemv).
     auto need = [&](uint32_t rt, uint32_t nst) -> size_t {
         size_t slab = round_up(rt * 128, 1024);
-        return 1024 + (size_t)nst * nmat * kslabs * slab + (size_t)n * 4 + 2 * rt * 4 + 128 + nst * 8;
+        return 1024 + (size_t)nst * nmat * kslabs * slab + (size_t)n * 10 + 3 * rt * 4 + 4 + 128 + (nst + 1) * 8;
     };
     uint32_t rt = 0, nst = 0;
     if (per * nmat <= 256 && need(per, 1) <= smem_cap) {
@@ -517,7 +518,7 @@ int hs_model_load(const char* path, uint32_t max_ctx, int device, hs_model** out
     int optin = 0;
     HS_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
     m->smem_cap = (size_t)optin;
-    HS_CUDA_TRY(gemv_set_smem_limits());
+    HS_CUDA_TRY(gemv_set_smem_limits(optin));
     hs_config& c = m->cfg;
     c.n_layers = n_layers;
     c.n_heads = n_heads;
@@ -936,11 +937,17 @@ static void fill_cfg(DevCtl& h, const hs_sampler_cfg* cfg, const hs_rng* rng) {
 int hs_sample(hs_scratch* s, const hs_sampler_cfg* cfg, hs_rng* rng, const uint32_t* hist, uint64_t n_hist,
               uint32_t* out) {
     if (!s || !cfg || !rng || !out || (!hist && n_hist)) return fail(HS_E_ARG, "null argument");
-    if (n_hist > s->cap) return fail(HS_E_ARG, "history longer than the scratch's token buffer");
     uint32_t kmax;
     int rc = validate_cfg(s, cfg, &kmax);
     if (rc) return rc;
     const hs_model* m = s->m;
+    // Only the tail the penalty reads matters (sampler.rs:103-111).
+    const uint64_t win = (cfg->repeat_penalty != 1.0f && cfg->repeat_last_n > 0)
+                             ? std::min<uint64_t>(cfg->repeat_last_n, n_hist)
+                             : 0;
+    if (win > s->cap) return fail(HS_E_UNSUPPORTED, "repeat_last_n longer than max_ctx");
+    hist += n_hist - win;
+    n_hist = win;
     for (uint64_t i = 0; i < n_hist; i++)
         if (hist[i] >= m->cfg.vocab) return fail(HS_E_ARG, "history token out of range");
     HS_CUDA_TRY(cudaSetDevice(m->device));

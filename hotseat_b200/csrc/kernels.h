@@ -69,7 +69,7 @@ cudaError_t launch_attention(uint32_t head_dim, uint32_t nh, size_t smem, const 
 size_t attention_smem(uint32_t head_dim, uint32_t max_ctx);
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st);
 size_t sample_final_smem(uint32_t n_cta, uint32_t kmax);
-cudaError_t gemv_set_smem_limits();
+cudaError_t gemv_set_smem_limits(int optin);
 
 constexpr uint32_t kSampleSlice = 1024;  // logits per CTA of the candidate kernel
 constexpr uint32_t kMaxTopK = 64;        // top_k supported by the device sampler
