@@ -128,6 +128,7 @@ _SIGS = {
     "hs_seq_end": (C.c_int, [_P, _P, _U64P, C.c_uint64, C.POINTER(SeqState), C.POINTER(Rng)]),
     "hs_scratch_stream": (_P, [_P]),
     "hs_seq_launches_per_step": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "hs_scratch_trace": (C.c_int, [_P, _P, C.c_uint64, _U64P]),
     "hs_dequant_f16": (C.c_int, [C.c_uint32, _P, C.c_uint64, _P, _P]),
     "hs_synth_write": (C.c_int, [C.c_char_p, C.POINTER(SynthSpec)]),
 }
@@ -322,6 +323,15 @@ class Scratch:
     @property
     def stream(self):
         return _lib.hs_scratch_stream(self._h)
+
+    def trace(self):
+        """Launch timeline of the last decode step (needs HS_TRACE=1 at creation):
+        array [slots, 8]: entry, past-wait, exit, last entry, checkpoints 1-4 (ns)."""
+        used = C.c_uint64()
+        _check(_lib.hs_scratch_trace(self._h, None, 0, C.byref(used)))
+        out = np.zeros((used.value, 8), dtype=np.uint64)
+        _check(_lib.hs_scratch_trace(self._h, _ptr(out), used.value, C.byref(used)))
+        return out
 
     def launches_per_step(self):
         n = C.c_uint32()

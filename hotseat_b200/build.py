@@ -51,7 +51,19 @@ def _compile(src, verbose):
     return obj, True
 
 
+def up_to_date():
+    """True when libhotseat.so is newer than every source and header."""
+    if not os.path.exists(LIB):
+        return False
+    t = os.path.getmtime(LIB)
+    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS] + [os.path.join(HERE, "..", "include", "hotseat.h"),
+                                                                   os.path.abspath(__file__)]
+    return all(os.path.getmtime(p) <= t for p in deps)
+
+
 def build(force=False, verbose=False):
+    if not force and not verbose and up_to_date():
+        return LIB
     os.makedirs(BUILD, exist_ok=True)
     srcs = [os.path.join(CSRC, s) for s in SOURCES]
     if force:

@@ -23,44 +23,31 @@ namespace {
 
 __device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) { return *(const volatile uint32_t*)p; }
 
+// L consecutive f16 weights of one row (one per dot lane), widened to f32.
 template <int L>
-struct HalfVec;
-template <>
-struct HalfVec<1> {
-    static __device__ __forceinline__ void load(const uint8_t* p, float* w) {
+__device__ __forceinline__ void load_w(const uint8_t* p, float* w) {
+    if (L == 1) {
         w[0] = h2f(*reinterpret_cast<const uint16_t*>(p));
-    }
-};
-template <>
-struct HalfVec<2> {
-    static __device__ __forceinline__ void load(const uint8_t* p, float* w) {
-        uint32_t v = *reinterpret_cast<const uint32_t*>(p);
+    } else if (L == 2) {
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(p);
         w[0] = h2f((uint16_t)v);
         w[1] = h2f((uint16_t)(v >> 16));
-    }
-};
-template <>
-struct HalfVec<4> {
-    static __device__ __forceinline__ void load(const uint8_t* p, float* w) {
-        uint2 v = *reinterpret_cast<const uint2*>(p);
+    } else if (L == 4) {
+        const uint2 v = *reinterpret_cast<const uint2*>(p);
         w[0] = h2f((uint16_t)v.x);
         w[1] = h2f((uint16_t)(v.x >> 16));
         w[2] = h2f((uint16_t)v.y);
         w[3] = h2f((uint16_t)(v.y >> 16));
-    }
-};
-template <>
-struct HalfVec<8> {
-    static __device__ __forceinline__ void load(const uint8_t* p, float* w) {
-        uint4 v = *reinterpret_cast<const uint4*>(p);
-        uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    } else {
+        const uint4 v = *reinterpret_cast<const uint4*>(p);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             w[2 * i] = h2f((uint16_t)u[i]);
             w[2 * i + 1] = h2f((uint16_t)(u[i] >> 16));
         }
     }
-};
+}
 
 // Fold this thread's L lanes with its row-mates' (8/L consecutive lanes of
 // the warp) into the reference's fold tree (math.rs:89-93). IEEE addition is
@@ -98,11 +85,13 @@ __device__ __forceinline__ float fold_lanes(const float* a) {
 // Shared memory: [nst weight stages][xs: n f32][gs: n f32 norm gain]
 // [xe: n f16 embedding row][outs: 2*rt][bias_s: rt][red: 32][bars: nst+1].
 template <int OUT, int L>
-__global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMap tm0,
+__global__ void __launch_bounds__(512) k_gemv(const __grid_constant__ CUtensorMap tm0,
                                               const __grid_constant__ CUtensorMap tm1, const GemvArgs a,
                                               const int in_mode) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    // Align by offsetting the shared array itself, so every access below
+    // stays a shared-space access.
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     constexpr int NMAT = OUT == OUT_SILU ? 2 : 1;
     const uint32_t n = a.n;
     const uint32_t kslabs = n / 64;
@@ -118,6 +107,8 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
     uint64_t* bars = reinterpret_cast<uint64_t*>(red + 32 + ((a.rt & 1) ? 1 : 0));
     uint64_t* xbar = bars + a.nst;
     const uint32_t tid = threadIdx.x;
+    const KTrace tr(a.trace, a.trace_slot);
+    tr.enter();
 
     uint32_t r0, r1;
     split_range(a.rows, gridDim.x, blockIdx.x, &r0, &r1);
@@ -151,9 +142,8 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
         for (uint32_t i = tid; i < n / 4; i += blockDim.x) s4[i] = g4[i];
     }
     if (OUT == OUT_STORE && a.bias && tid < a.rt && tid < mine) bias_s[tid] = a.bias[r0 + tid];
-    pdl_launch_dependents();
-    pdl_wait();
-
+    // `active` and `token` are set before the graph launch (by the host or the
+    // previous step's commit kernel) and stay fixed during it.
     DevCtl* ctl = a.ctl;
     bool run = ld_volatile(&ctl->active) != 0;
     uint32_t token = 0;
@@ -164,6 +154,9 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
             run = false;
         }
     }
+    pdl_launch_dependents();
+    pdl_wait();
+    tr.waited();
     if (!run) {
         // Never leave with bulk copies in flight into this CTA's shared memory.
         for (uint32_t t = 0; t < npre; t++) mbar_wait_bounded(&bars[t], 0);
@@ -185,6 +178,7 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
         for (uint32_t t = 0; t < npre; t++) mbar_wait_bounded(&bars[t], 0);
         return;
     }
+    tr.mark(1);
     if (in_mode == IN_EMBED_NORM) {
         for (uint32_t i = tid; i < n; i += blockDim.x) {
             const float v = h2f(xe[i]);
@@ -197,19 +191,20 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
         // rmsnorm: ss = dot_f32(x, x) in the 8-lane shape; scale = 1/sqrt(ss/n + eps);
         // out[i] = x[i] * scale * g[i].
         if (tid < 32) {
-            float acc = 0.0f;
-            if (tid < 8) {
+            // Thread t < 4 runs lanes 2t and 2t+1 of the 8-lane sum of squares.
+            float a0 = 0.0f, a1 = 0.0f;
+            if (tid < 4) {
                 const uint32_t nj = n / 8;
+                const uint64_t* x2 = reinterpret_cast<const uint64_t*>(xs) + tid;
 #pragma unroll 16
                 for (uint32_t j = 0; j < nj; j++) {
-                    const float v = xs[8 * j + tid];
-                    acc = __fadd_rn(acc, __fmul_rn(v, v));
+                    const uint64_t v = x2[4 * j];
+                    mul_add_pair(&a0, &a1, v, v);
                 }
             }
-            float v = acc;
+            float v = __fadd_rn(a0, a1);
             v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
             v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
-            v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
             if (tid == 0) red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(v, (float)n), a.eps)));
         }
         __syncthreads();
@@ -217,6 +212,7 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
         for (uint32_t i = tid; i < n; i += blockDim.x) xs[i] = __fmul_rn(__fmul_rn(xs[i], scale), gs[i]);
         __syncthreads();
     }
+    tr.mark(2);
 
     // ---- fixed-order lanes out of shared memory
     constexpr uint32_t TPR = 8 / L;  // threads per row
@@ -229,26 +225,43 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
             if (tid == 0) atomicOr(&ctl->err, ERR_TIMEOUT);
             return;
         }
+        if (t == 0) tr.mark(3);
         float acc[L];
 #pragma unroll
         for (int i = 0; i < L; i++) acc[i] = 0.0f;
         if (lane_active) {
             const uint8_t* base = stages + s * stage_bytes + m * mat_bytes + r * 128;
             const uint32_t sw = r & 7;
+            if (L == 1) {
 #pragma unroll 2
-            for (uint32_t k = 0; k < kslabs; k++) {
-                const uint8_t* sb = base + k * a.slab_stride;
-                const float* xk = xs + k * 64 + g * L;
+                for (uint32_t k = 0; k < kslabs; k++) {
+                    const uint8_t* sb = base + k * a.slab_stride;
+                    const float* xk = xs + k * 64 + g;
 #pragma unroll
-                for (uint32_t c = 0; c < 8; c++) {
-                    float w[L];
-                    HalfVec<L>::load(sb + (((c ^ sw) << 4) | (g * L * 2)), w);
+                    for (uint32_t c = 0; c < 8; c++) {
+                        float w[1];
+                        load_w<1>(sb + (((c ^ sw) << 4) | (g * 2)), w);
+                        acc[0] = __fadd_rn(acc[0], __fmul_rn(w[0], xk[c * 8]));
+                    }
+                }
+            } else {
+#pragma unroll 2
+                for (uint32_t k = 0; k < kslabs; k++) {
+                    const uint8_t* sb = base + k * a.slab_stride;
+                    const uint64_t* xk = reinterpret_cast<const uint64_t*>(xs + k * 64 + g * L);
 #pragma unroll
-                    for (int i = 0; i < L; i++) acc[i] = __fadd_rn(acc[i], __fmul_rn(w[i], xk[c * 8 + i]));
+                    for (uint32_t c = 0; c < 8; c++) {
+                        float w[L];
+                        load_w<L>(sb + (((c ^ sw) << 4) | (g * L * 2)), w);
+#pragma unroll
+                        for (int i = 0; i < L / 2; i++)
+                            mul_add_pair(&acc[2 * i], &acc[2 * i + 1], pack2(w[2 * i], w[2 * i + 1]), xk[c * 4 + i]);
+                    }
                 }
             }
         }
         const float v = fold_lanes<L>(acc);
+        if (t == 0) tr.mark(4);
         const uint32_t rr = t * a.rt + r;  // row index inside this CTA's range
         if (OUT == OUT_SILU) {
             if (lane_active && g == 0) outs[m * a.rt + r] = v;
@@ -272,6 +285,7 @@ __global__ void __launch_bounds__(256) k_gemv(const __grid_constant__ CUtensorMa
             issue(t + a.nst);
         }
     }
+    tr.exit();
 }
 
 // ------------------------------------------------------------ attention
@@ -306,6 +320,8 @@ __global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
     float* cb = vb + PRE * RS;  // [CH][RS]
     float* sc = cb + CH * RS;   // [max_ctx]
     const uint32_t tid = threadIdx.x;
+    const KTrace tr(a.trace, a.trace_slot);
+    tr.enter();
     DevCtl* ctl = a.ctl;
     const uint32_t h = blockIdx.x, groups = a.nh / a.nkv, kvh = h / groups;
     const uint64_t plane = (uint64_t)a.max_ctx * a.nkv * HD;
@@ -327,6 +343,7 @@ __global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
     }
     pdl_launch_dependents();
     pdl_wait();
+    tr.waited();
     if (!run || !pos_ok) {
         cp_async_wait_all();
         if (run && tid == 0 && blockIdx.x == 0) atomicOr(&ctl->err, ERR_POS);
@@ -364,8 +381,10 @@ __global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
                 atomicOr(reinterpret_cast<unsigned long long*>(&a.dirty[pg >> 6]), 1ull << (pg & 63));
         }
     }
+    tr.mark(1);
     cp_async_wait_all();
     __syncthreads();
+    tr.mark(2);
 
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
     const uint32_t n = pos + 1;
@@ -414,6 +433,7 @@ __global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
     const float inv = red[33];
     for (uint32_t p = tid; p < n; p += blockDim.x) sc[p] = __fmul_rn(sc[p], inv);
     __syncthreads();
+    tr.mark(3);
     // out[d] = sum over p, in order, of sc[p] * v_p[d]
     float out = 0.0f;
     if (tid < HD) {
@@ -437,6 +457,7 @@ __global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
         out = __fadd_rn(out, __fmul_rn(sc[pos], vc[tid]));
         a.att[h * HD + tid] = out;
     }
+    tr.exit();
 }
 
 // -------------------------------------------------------------- sampler
@@ -451,7 +472,18 @@ __global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
 // sequence mode it then commits the step exactly as seq.rs:273-312 does.
 __device__ __forceinline__ bool seq_needs_sample(const DevCtl* c) {
     if (c->mode == 1) return true;
-    return ld_volatile(&c->active) && c->filled + 1 == c->n_tokens;
+    return c->active && c->filled + 1 == c->n_tokens;
+}
+
+// Copy the control block into shared memory with one parallel batch of loads.
+// Nothing launched in the same step writes it before the commit kernel, so
+// both sampler kernels take this snapshot before waiting on their predecessor.
+__device__ __forceinline__ void load_ctl(DevCtl* dst, const DevCtl* src) {
+    constexpr uint32_t words = sizeof(DevCtl) / 4;
+    static_assert(sizeof(DevCtl) % 4 == 0, "DevCtl is copied as 32-bit words");
+    if (threadIdx.x < words)
+        reinterpret_cast<uint32_t*>(dst)[threadIdx.x] =
+            __ldcg(reinterpret_cast<const unsigned int*>(src) + threadIdx.x);
 }
 
 // (value, index) "better" for greedy: larger value, then smaller index; an
@@ -504,47 +536,65 @@ __device__ __forceinline__ void warp_sort128(uint64_t k[4], int lane) {
 }
 
 // Number of keys in sorted list[0..len) smaller than `key`.
+// len must be a power of two; fixed step count, no data-dependent loop, so
+// several searches interleave.
 __device__ __forceinline__ uint32_t lower_bound_u64(const uint64_t* list, uint32_t len, uint64_t key) {
-    uint32_t lo = 0, hi = len;
-    while (lo < hi) {
-        const uint32_t mid = (lo + hi) >> 1;
-        if (list[mid] < key) lo = mid + 1;
-        else hi = mid;
-    }
-    return lo;
+    uint32_t idx = 0;
+#pragma unroll
+    for (uint32_t step = 128; step > 0; step >>= 1)
+        if (step <= len && idx + step <= len && list[idx + step - 1] < key) idx += step;
+    return idx;
 }
 
 __global__ void __launch_bounds__(256) k_sample_cand(const SampleArgs a) {
     __shared__ uint64_t lists[8][128];
-    __shared__ uint32_t win[256];
+    __shared__ uint32_t win_cnt[kSampleSlice];
     __shared__ float bv_s[8];
     __shared__ uint32_t bi_s[8];
+    __shared__ DevCtl cs;
     const uint32_t tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const KTrace tr(a.trace, a.trace_slot);
+    tr.enter();
+    load_ctl(&cs, a.ctl);
+    __syncthreads();
+    const DevCtl* c = &cs;
+    // The history window is also fixed until the commit: count it now.
+    const float pen = c->repeat_penalty;
+    const uint64_t nt = c->n_tokens;
+    const uint64_t nw = (pen != 1.0f && c->repeat_last_n > 0) ? (c->repeat_last_n < nt ? c->repeat_last_n : nt) : 0;
+    const uint32_t cta_base = blockIdx.x * kSampleSlice;
+    const bool need = seq_needs_sample(c);
+    if (need && nw) {
+        for (uint32_t i = tid; i < kSampleSlice; i += blockDim.x) win_cnt[i] = 0;
+        __syncthreads();
+        for (uint64_t i = nt - nw + tid; i < nt; i += blockDim.x) {
+            const uint32_t t = __ldcg(a.tokens + i);
+            if (t >= cta_base && t < cta_base + kSampleSlice) atomicAdd(&win_cnt[t - cta_base], 1u);
+        }
+    }
     pdl_launch_dependents();
     pdl_wait();
-    const DevCtl* c = a.ctl;
-    if (!seq_needs_sample(c)) return;
+    tr.waited();
+    if (!need) return;
+    __syncthreads();
     const uint32_t base = blockIdx.x * kSampleSlice + w * 128;
     float v[4];
     uint32_t e[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         e[i] = base + i * 32 + lane;
-        v[i] = e[i] < a.vocab ? a.logits[e[i]] : 0.0f;
+        v[i] = e[i] < a.vocab ? __ldcg(a.logits + e[i]) : 0.0f;
     }
-    const float pen = c->repeat_penalty;
-    const uint64_t nt = c->n_tokens;
-    const uint64_t nw = (pen != 1.0f && c->repeat_last_n > 0) ? (c->repeat_last_n < nt ? c->repeat_last_n : nt) : 0;
-    for (uint64_t w0 = nt - nw; w0 < nt; w0 += 256) {
-        const uint32_t cnt = (uint32_t)min((uint64_t)256, nt - w0);
-        __syncthreads();
-        if (tid < cnt) win[tid] = a.tokens[w0 + tid];
-        __syncthreads();
-        for (uint32_t j = 0; j < cnt; j++) {
-            const uint32_t t = win[j];
+    tr.mark(1);
+    // Penalty: each slice token's occurrences in the history window were
+    // counted above; apply the reference's update that many times. Every
+    // occurrence applies the same operation to the same logit, so this is the
+    // sequential loop of sampler.rs:105-110 with the loop order factored out.
+    if (nw) {
 #pragma unroll
-            for (int i = 0; i < 4; i++)
-                if (t == e[i]) v[i] = v[i] > 0.0f ? __fdiv_rn(v[i], pen) : __fmul_rn(v[i], pen);
+        for (int i = 0; i < 4; i++) {
+            uint32_t times = win_cnt[e[i] - cta_base];
+            while (times--) v[i] = v[i] > 0.0f ? __fdiv_rn(v[i], pen) : __fmul_rn(v[i], pen);
         }
     }
     if (c->temperature <= 0.0f) {
@@ -574,10 +624,12 @@ __global__ void __launch_bounds__(256) k_sample_cand(const SampleArgs a) {
         }
         return;
     }
+    tr.mark(2);
     uint64_t k[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) k[i] = e[i] < a.vocab ? cand_key(v[i], e[i]) : ~0ull - e[i];
     warp_sort128(k, (int)lane);
+    tr.mark(3);
 #pragma unroll
     for (int i = 0; i < 4; i++) lists[w][i * 32 + lane] = k[i];
     __syncthreads();
@@ -593,6 +645,7 @@ __global__ void __launch_bounds__(256) k_sample_cand(const SampleArgs a) {
             if (o != l) rank += lower_bound_u64(lists[o], J, key);
         if (rank < a.kmax) a.cand[(size_t)blockIdx.x * a.kmax + rank] = key;
     }
+    tr.exit();
 }
 
 constexpr uint32_t kFinalThreads = 256;
@@ -606,12 +659,18 @@ __global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs
     __shared__ float bv_s[8];
     __shared__ uint32_t bi_s[8];
     __shared__ uint32_t tok_s;
+    __shared__ DevCtl cs;
     const uint32_t tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const KTrace tr(a.trace, a.trace_slot + 1);
+    tr.enter();
+    load_ctl(&cs, a.ctl);
     pdl_launch_dependents();
     pdl_wait();
-    DevCtl* c = a.ctl;
+    tr.waited();
+    __syncthreads();
+    DevCtl* c = &cs;
     const bool seq = c->mode == 0;
-    if (seq && !ld_volatile(&c->active)) return;
+    if (seq && !c->active) return;
     const bool need = seq_needs_sample(c);
     if (tid == 0) tok_s = 0;
     if (need && c->temperature <= 0.0f) {
@@ -710,8 +769,9 @@ __global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs
             }
             uint64_t s4[4] = {c->rng[0], c->rng[1], c->rng[2], c->rng[3]};
             const float u = __fmul_rn((float)(rng_next(s4) >> 40), 1.0f / 16777216.0f);
-            for (int i = 0; i < 4; i++) c->rng[i] = s4[i];
+            for (int i = 0; i < 4; i++) c->rng[i] = a.ctl->rng[i] = s4[i];
             c->draws += 1;
+            a.ctl->draws = c->draws;
             const float r = __fmul_rn(u, sum);
             uint32_t pick = (uint32_t)merged[cut - 1];
             float acc = 0.0f;
@@ -727,45 +787,61 @@ __global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs
     }
     __syncthreads();
     if (tid != 0) return;
+    DevCtl* g = a.ctl;
     if (!seq) {
-        c->out_token = tok_s;
+        g->out_token = tok_s;
         return;
     }
-    // seq.rs:273-312 commit, then arm the next step (seq.rs:239-268).
+    // seq.rs:273-312 commit, then arm the next step (seq.rs:239-268); the
+    // decisions use the snapshot, and only the changed fields are stored.
     const uint64_t filled = c->filled + 1;
-    c->filled = filled;
-    if (filled == c->n_tokens) {
+    uint64_t n_tokens = c->n_tokens;
+    uint32_t done = c->done, reason = c->done_reason, err = 0;
+    uint32_t next_token = 0;
+    if (filled == n_tokens) {
         const uint32_t next = tok_s;
-        const uint64_t generated = c->n_tokens - c->prompt_len;
+        const uint64_t generated = n_tokens - c->prompt_len;
         if (next == c->eos) {
-            c->done = 1;
-            c->done_reason = 1;
+            done = 1;
+            reason = 1;
         } else if (generated >= c->max_tokens) {
-            c->done = 1;
-            c->done_reason = 2;
-        } else if (c->n_tokens + 1 >= c->max_ctx) {
-            c->done = 1;
-            c->done_reason = 3;
-        } else if (c->n_tokens >= c->cap) {
-            c->done = 1;
-            atomicOr(&c->err, ERR_CAP);
+            done = 1;
+            reason = 2;
+        } else if (n_tokens + 1 >= c->max_ctx) {
+            done = 1;
+            reason = 3;
+        } else if (n_tokens >= c->cap) {
+            done = 1;
+            err |= ERR_CAP;
         } else {
-            a.tokens_w[c->n_tokens] = next;
-            c->n_tokens += 1;
+            a.tokens_w[n_tokens] = next;
+            n_tokens += 1;
+            if (filled == n_tokens - 1) next_token = next;
         }
     }
     uint32_t active = 0;
-    if (!c->done) {
-        if (filled >= c->n_tokens) {
-            c->done = 1;
-            atomicOr(&c->err, ERR_INVARIANT);
+    if (!done) {
+        if (filled >= n_tokens) {
+            done = 1;
+            err |= ERR_INVARIANT;
         } else if (!(c->stop_at && filled >= c->stop_at)) {
             active = 1;
-            c->token = a.tokens_w[filled];
-            c->pos = (uint32_t)filled;
+            // The token at `filled` is the one just appended, or a prompt token
+            // already in the history.
+            c->token = filled == n_tokens - 1 && n_tokens != c->n_tokens ? next_token : __ldcg(a.tokens + filled);
         }
     }
-    c->active = active;
+    g->filled = filled;
+    g->n_tokens = n_tokens;
+    g->done = done;
+    g->done_reason = reason;
+    if (err) atomicOr(&g->err, err);
+    if (active) {
+        g->token = c->token;
+        g->pos = (uint32_t)filled;
+    }
+    g->active = active;
+    tr.exit();
 }
 
 template <int OUT, int L>

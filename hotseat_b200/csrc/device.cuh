@@ -158,6 +158,57 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Optional launch timeline (trace mode): per launch slot, 8 u64 of
+// %globaltimer ns: [first CTA entry (min), CTA 0 past the PDL wait,
+// last CTA exit (max), last CTA entry (max), checkpoints 1-4 (max over CTAs)].
+__device__ __forceinline__ uint64_t gtime() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+struct KTrace {
+    uint64_t* p;
+    __device__ __forceinline__ KTrace(uint64_t* base, uint32_t slot) : p(base ? base + 8 * slot : nullptr) {}
+    __device__ __forceinline__ void enter() const {
+        if (p && threadIdx.x == 0) {
+            const unsigned long long t = gtime();
+            atomicMin(reinterpret_cast<unsigned long long*>(p), t);
+            atomicMax(reinterpret_cast<unsigned long long*>(p + 3), t);
+        }
+    }
+    __device__ __forceinline__ void waited() const {
+        if (p && threadIdx.x == 0 && blockIdx.x == 0) p[1] = gtime();
+    }
+    __device__ __forceinline__ void mark(int i) const {
+        if (p && threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned long long*>(p + 3 + i), (unsigned long long)gtime());
+    }
+    __device__ __forceinline__ void exit() const {
+        if (p && threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned long long*>(p + 2), (unsigned long long)gtime());
+    }
+};
+
+// Packed pairs of f32 (sm_100 f32x2 ALU ops). The packed multiply is exact
+// lane-wise IEEE; the adds stay scalar add.rn, which is never contracted, so
+// `acc + w*x` keeps its two roundings. (A packed multiply feeding only a
+// packed add can be fused into a packed FMA by the assembler, which would
+// change the bits; this form avoids it.)
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float* a, float* b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(*a), "=f"(*b) : "l"(v));
+}
+__device__ __forceinline__ void mul_add_pair(float* acc0, float* acc1, uint64_t w, uint64_t x) {
+    uint64_t p;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(w), "l"(x));
+    float p0, p1;
+    unpack2(p, &p0, &p1);
+    *acc0 = __fadd_rn(*acc0, p0);
+    *acc1 = __fadd_rn(*acc1, p1);
+}
+
 // pool.rs:139-145 split: contiguous balanced ranges.
 __device__ __forceinline__ void split_range(uint32_t rows, uint32_t n, uint32_t tid, uint32_t* a, uint32_t* b) {
     uint32_t per = rows / n, rem = rows % n;

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -105,9 +106,23 @@ int plan_gemv(GemvPlan* p, int in_mode, int out_mode, uint32_t rows, uint32_t n,
     p->rt = rt;
     p->nst = nst;
     p->slab_stride = round_up(rt * 128, 1024);
+    // Lanes per thread: the fewest per-SMSP instructions for one tile pass,
+    // counting ~7/9/10/19 instructions per step at 1/2/4/8 lanes and the
+    // warps an SMSP must issue in turn.
     const uint32_t vrows = rt * nmat;
-    p->lanes = vrows <= 32 ? 1 : vrows <= 64 ? 2 : vrows <= 128 ? 4 : 8;
-    p->threads = 256;
+    const uint32_t instr[4] = {7, 7, 10, 19};
+    uint64_t best = ~0ull;
+    for (uint32_t li = 0; li < 4; li++) {
+        const uint32_t L = 1u << li, threads = vrows * (8 / L);
+        if (threads > 512) continue;
+        const uint32_t warps = (threads + 31) / 32;
+        const uint64_t cost = (uint64_t)((warps + 3) / 4) * instr[li];
+        if (cost < best) {
+            best = cost;
+            p->lanes = L;
+            p->threads = std::max<uint32_t>(128, (threads + 31) / 32 * 32);
+        }
+    }
     p->smem = need(rt, nst);
     int rc = make_weight_map(&p->tm0, w0, n, rows, rt);
     if (rc == HS_OK && w1) rc = make_weight_map(&p->tm1, w1, n, rows, rt);
@@ -183,6 +198,9 @@ struct hs_scratch {
     const hs_kv* graph_kv = nullptr;
     uint32_t graph_kmax = 0;
     uint32_t launches_fwd = 0;
+    uint64_t* trace = nullptr;      // device, 4 u64 per launch slot (trace mode only)
+    uint64_t* trace_init = nullptr; // pinned host template: start=~0, rest 0
+    uint32_t trace_slots = 0;
     ~hs_scratch() {
         cudaSetDevice(m->device);
         if (g_fwd) cudaGraphExecDestroy(g_fwd);
@@ -190,6 +208,8 @@ struct hs_scratch {
         if (st) cudaStreamDestroy(st);
         cudaFree(ctl);
         cudaFreeHost(ctl_h);
+        cudaFree(trace);
+        cudaFreeHost(trace_init);
         for (void* p : {(void*)x, (void*)qkv, (void*)att, (void*)hb, (void*)logits, (void*)tokens, (void*)cand,
                         (void*)argbuf})
             cudaFree(p);
@@ -303,6 +323,7 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
     const hs_model* m = s->m;
     const hs_config& c = m->cfg;
     cudaStream_t st = s->st;
+    uint32_t slot = 0;
     for (uint32_t l = 0; l < c.n_layers; l++) {
         const LayerDev& L = m->layers[l];
         GemvArgs a{};
@@ -323,6 +344,8 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         a.lanes = L.qkv.lanes;
         GemvPlan pq = L.qkv;
         pq.in_mode = l == 0 ? IN_EMBED_NORM : IN_NORM;
+        a.trace = s->trace;
+        a.trace_slot = slot++;
         HS_CUDA_TRY(launch_gemv(pq, a, st));
         AttnArgs at{};
         at.qkv = s->qkv;
@@ -339,6 +362,8 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         at.max_ctx = c.max_ctx;
         at.layout = kv->spec.layout;
         at.page_shift = kv->page_shift;
+        at.trace = s->trace;
+        at.trace_slot = slot++;
         HS_CUDA_TRY(launch_attention(c.head_dim, c.n_heads, m->attn_smem, at, st));
         GemvArgs o{};
         o.ctl = s->ctl;
@@ -350,6 +375,8 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         o.nst = L.o.nst;
         o.slab_stride = L.o.slab_stride;
         o.lanes = L.o.lanes;
+        o.trace = s->trace;
+        o.trace_slot = slot++;
         HS_CUDA_TRY(launch_gemv(L.o, o, st));
         GemvArgs gu{};
         gu.ctl = s->ctl;
@@ -363,6 +390,8 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         gu.nst = L.gu.nst;
         gu.slab_stride = L.gu.slab_stride;
         gu.lanes = L.gu.lanes;
+        gu.trace = s->trace;
+        gu.trace_slot = slot++;
         HS_CUDA_TRY(launch_gemv(L.gu, gu, st));
         GemvArgs dn{};
         dn.ctl = s->ctl;
@@ -374,6 +403,8 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         dn.nst = L.down.nst;
         dn.slab_stride = L.down.slab_stride;
         dn.lanes = L.down.lanes;
+        dn.trace = s->trace;
+        dn.trace_slot = slot++;
         HS_CUDA_TRY(launch_gemv(L.down, dn, st));
     }
     GemvArgs h{};
@@ -388,6 +419,8 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
     h.nst = m->head.nst;
     h.slab_stride = m->head.slab_stride;
     h.lanes = m->head.lanes;
+    h.trace = s->trace;
+    h.trace_slot = slot++;
     HS_CUDA_TRY(launch_gemv(m->head, h, st));
     return HS_OK;
 }
@@ -403,6 +436,8 @@ SampleArgs sample_args(hs_scratch* s) {
     a.vocab = s->m->cfg.vocab;
     a.n_cta = s->n_cta;
     a.kmax = s->kmax;
+    a.trace = s->trace;
+    a.trace_slot = s->launches_fwd;  // and launches_fwd + 1 for the second kernel
     return a;
 }
 
@@ -845,6 +880,16 @@ int hs_scratch_new(const hs_model* m, hs_scratch** out) {
     HS_CUDA_TRY(cudaMalloc(&s->cand, (size_t)s->n_cta * kSampleSlice * 8));
     HS_CUDA_TRY(cudaMalloc(&s->argbuf, (size_t)s->n_cta * 8));
     s->launches_fwd = c.n_layers * 5 + 1;
+    const char* tenv = getenv("HS_TRACE");
+    if (tenv && tenv[0] == '1') {
+        s->trace_slots = s->launches_fwd + 2;
+        HS_CUDA_TRY(cudaMalloc(&s->trace, (size_t)s->trace_slots * 8 * 8));
+        HS_CUDA_TRY(cudaMallocHost(&s->trace_init, (size_t)s->trace_slots * 8 * 8));
+        for (uint32_t i = 0; i < s->trace_slots; i++) {
+            s->trace_init[8 * i] = ~0ull;
+            for (int j = 1; j < 8; j++) s->trace_init[8 * i + j] = 0;
+        }
+    }
     *out = s.release();
     return HS_OK;
 }
@@ -852,6 +897,17 @@ int hs_scratch_new(const hs_model* m, hs_scratch** out) {
 void hs_scratch_free(hs_scratch* s) { delete s; }
 
 void* hs_scratch_stream(hs_scratch* s) { return s ? (void*)s->st : nullptr; }
+
+int hs_scratch_trace(hs_scratch* s, uint64_t* out, uint64_t n_slots, uint64_t* used) {
+    if (!s || !used) return fail(HS_E_ARG, "null argument");
+    *used = s->trace_slots;
+    if (!s->trace) return fail(HS_E_STATE, "tracing is off (set HS_TRACE=1 before creating the scratch)");
+    if (!out) return HS_OK;
+    HS_CUDA_TRY(cudaSetDevice(s->m->device));
+    HS_CUDA_TRY(cudaStreamSynchronize(s->st));
+    HS_CUDA_TRY(cudaMemcpy(out, s->trace, std::min<uint64_t>(n_slots, s->trace_slots) * 64, cudaMemcpyDeviceToHost));
+    return HS_OK;
+}
 
 int hs_seq_launches_per_step(hs_scratch* s, uint32_t* out) {
     if (!s || !out) return fail(HS_E_ARG, "null argument");
@@ -1027,7 +1083,12 @@ int hs_seq_begin(hs_scratch* s, hs_kv* kv, const uint32_t* tokens, uint64_t n_to
 int hs_seq_step(hs_scratch* s, uint32_t n_steps) {
     if (!s || !s->g_step) return fail(HS_E_ARG, "hs_seq_begin has not been called");
     HS_CUDA_TRY(cudaSetDevice(s->m->device));
-    for (uint32_t i = 0; i < n_steps; i++) HS_CUDA_TRY(cudaGraphLaunch(s->g_step, s->st));
+    for (uint32_t i = 0; i < n_steps; i++) {
+        if (s->trace)
+            HS_CUDA_TRY(cudaMemcpyAsync(s->trace, s->trace_init, (size_t)s->trace_slots * 64, cudaMemcpyHostToDevice,
+                                        s->st));
+        HS_CUDA_TRY(cudaGraphLaunch(s->g_step, s->st));
+    }
     return HS_OK;
 }
 

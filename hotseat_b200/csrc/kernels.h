@@ -29,6 +29,8 @@ struct GemvArgs {
     uint32_t nst;           // pipeline stages
     uint32_t slab_stride;   // bytes between 64-column slabs of one tile (multiple of 1024)
     uint32_t lanes;         // dot lanes per thread (1, 2, 4, 8)
+    uint64_t* trace;        // optional per-launch timestamps (see KTrace)
+    uint32_t trace_slot;
 };
 
 // One planned GEMV launch (shapes fixed at load).
@@ -49,6 +51,8 @@ struct AttnArgs {
     float* att;              // [nh*hd]
     DevCtl* ctl;
     uint32_t layer, nh, nkv, max_ctx, layout, page_shift;
+    uint64_t* trace;
+    uint32_t trace_slot;
 };
 
 struct SampleArgs {
@@ -59,6 +63,8 @@ struct SampleArgs {
     uint64_t* argbuf;        // per-CTA (value bits, index) for greedy
     DevCtl* ctl;
     uint32_t vocab, n_cta, kmax;
+    uint64_t* trace;
+    uint32_t trace_slot;
 };
 
 int launch_dequant(uint32_t ty, const void* src, uint64_t n, void* dst, cudaStream_t st, int n_sm);

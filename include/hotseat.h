@@ -168,6 +168,12 @@ int hs_seq_end(hs_scratch* s, uint32_t* tokens, uint64_t* n_tokens, uint64_t cap
 void* hs_scratch_stream(hs_scratch* s);
 /* Kernel launches one hs_seq_step(s, 1) enqueues. */
 int hs_seq_launches_per_step(hs_scratch* s, uint32_t* out);
+/* Launch timeline of the last hs_seq_step (profiling; enabled by HS_TRACE=1
+ * in the environment when the scratch is created): 8 u64 per launch, in
+ * launch order, %globaltimer ns: first CTA entry, CTA 0 past its wait on the
+ * previous kernel, last CTA exit, last CTA entry, then four kernel-specific
+ * checkpoints (latest CTA). *used = number of launch slots. */
+int hs_scratch_trace(hs_scratch* s, uint64_t* out, uint64_t n_slots, uint64_t* used);
 
 /* ---- load-time dequantisation as a standalone op (quant.rs:18-38) ------ */
 
