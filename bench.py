@@ -163,6 +163,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="hotseat", choices=["hotseat", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--numeric", default="fast", choices=["fast", "reference"],
+                    help="fast: GPU-native reduction order (logits within 1e-2 of the CPU path); "
+                         "reference: bit-identical to the CPU reference")
     ap.add_argument("--profile-step", action="store_true",
                     help="prefill, then run one decode token inside the NVTX range 'decode_step' and exit")
     args = ap.parse_args()
@@ -188,7 +191,8 @@ def main():
     td = tempfile.mkdtemp(prefix="hsbench")
     path = os.path.join(td, "qwen05.gguf")
     make_model(path)
-    m = hs.Model.load(path, max_ctx=MAX_CTX, device=local)
+    numeric = hs.NUMERIC_FAST if args.numeric == "fast" else hs.NUMERIC_REFERENCE
+    m = hs.Model.load(path, max_ctx=MAX_CTX, device=local, numeric=numeric)
     kv, s = m.kv(), m.scratch()
     cfg = hs.SamplerCfg.default(temperature=TEMP, seed=SEED)
     prompt = prompt_tokens()
@@ -315,7 +319,8 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 (f16 weights)", "data": "synthetic",
-            "config": dict(workload_config(), parallelism=f"replicas x{world}" if world > 1 else "1 GPU"),
+            "config": dict(workload_config(), parallelism=f"replicas x{world}" if world > 1 else "1 GPU",
+                           numeric=args.numeric),
             "roofline": {"bound": "hbm", "kernel": "decode step (k_gemv x121, k_attention x24, sampler x2)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": peak_src, "traffic": traffic,

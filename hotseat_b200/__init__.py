@@ -27,6 +27,7 @@ LIB_PATH = os.path.join(_HERE, "libhotseat.so")
 HS_OK = 0
 HS_E_ARG, HS_E_IO, HS_E_CUDA, HS_E_STATE, HS_E_NOMEM, HS_E_UNSUPPORTED = -1, -2, -3, -4, -5, -6
 TOKEN_MAJOR, HEAD_MAJOR = 0, 1
+NUMERIC_REFERENCE, NUMERIC_FAST = 0, 1
 DONE_REASONS = {0: "", 1: "eos", 2: "max_tokens", 3: "context full"}
 
 if not os.path.exists(LIB_PATH):
@@ -44,7 +45,7 @@ class Config(C.Structure):
     _fields_ = [("n_layers", C.c_uint32), ("n_heads", C.c_uint32), ("n_kv_heads", C.c_uint32),
                 ("head_dim", C.c_uint32), ("d_model", C.c_uint32), ("d_ff", C.c_uint32), ("vocab", C.c_uint32),
                 ("eps", C.c_float), ("rope_base", C.c_float), ("train_ctx", C.c_uint32), ("max_ctx", C.c_uint32),
-                ("eos", C.c_uint32), ("fingerprint", C.c_uint64)]
+                ("eos", C.c_uint32), ("fingerprint", C.c_uint64), ("numeric", C.c_uint32)]
 
 
 class KvSpec(C.Structure):
@@ -96,6 +97,7 @@ _U64P = C.POINTER(C.c_uint64)
 _SIGS = {
     "hs_last_error": (C.c_char_p, []),
     "hs_model_load": (C.c_int, [C.c_char_p, C.c_uint32, C.c_int, C.POINTER(_P)]),
+    "hs_model_load_ex": (C.c_int, [C.c_char_p, C.c_uint32, C.c_int, C.c_uint32, C.POINTER(_P)]),
     "hs_model_config": (C.c_int, [_P, C.POINTER(Config)]),
     "hs_model_free": (None, [_P]),
     "hs_model_tensor": (C.c_int, [_P, C.c_char_p, _P, C.c_uint64, C.POINTER(C.c_uint32)]),
@@ -162,9 +164,11 @@ class Model:
         _check(_lib.hs_model_config(handle, C.byref(self.cfg)))
 
     @classmethod
-    def load(cls, path, max_ctx=2048, device=0):
+    def load(cls, path, max_ctx=2048, device=0, numeric=NUMERIC_REFERENCE):
+        """numeric: NUMERIC_REFERENCE (bit-identical to the CPU reference) or
+        NUMERIC_FAST (GPU-native reduction order, deterministic across GPUs)."""
         h = C.c_void_p()
-        _check(_lib.hs_model_load(os.fsencode(path), max_ctx, device, C.byref(h)))
+        _check(_lib.hs_model_load_ex(os.fsencode(path), max_ctx, device, numeric, C.byref(h)))
         return cls(h)
 
     @property

@@ -129,6 +129,65 @@ int plan_gemv(GemvPlan* p, int in_mode, int out_mode, uint32_t rows, uint32_t n,
     return rc;
 }
 
+// Fast path: threads per row T from the row length alone (a power of two
+// with at most 6 chunks of 8 elements per thread), 256 threads per CTA.
+int plan_gemv_fast(GemvPlan* p, int in_mode, int out_mode, uint32_t rows, uint32_t n, const uint16_t* w0,
+                   const uint16_t* w1, int n_sm, size_t smem_cap) {
+    if (n % 64) return fail(HS_E_UNSUPPORTED, "row length must be a multiple of 64, got " + std::to_string(n));
+    const uint32_t nmat = out_mode == OUT_SILU ? 2 : 1, kslabs = n / 64, nchunks = n / 8;
+    uint32_t T = 32;
+    while (T < 256 && (nchunks + T - 1) / T > 6) T *= 2;
+    const uint32_t cmax = fast_cmax_for((nchunks + T - 1) / T);
+    if (!cmax) return fail(HS_E_UNSUPPORTED, "row too long for the fast GEMV");
+    p->fast = true;
+    p->cmax = cmax;
+    p->lanes = T;
+    p->threads = 256;
+    p->in_mode = in_mode;
+    p->out_mode = out_mode;
+    p->n = n;
+    p->rows = rows;
+    p->grid = std::min<uint32_t>(rows, (uint32_t)n_sm);
+    const uint32_t per = (rows + p->grid - 1) / p->grid;
+    // Mirrors the kernel's shared-memory carve-up (decode_fast.cu k_gemv_fast).
+    auto need = [&](uint32_t rt, uint32_t nst) -> size_t {
+        size_t slab = round_up(rt * 128, 1024);
+        return 1024 + (size_t)nst * nmat * kslabs * slab + (size_t)n * 10 + 2 * rt * 8 * 4 + rt * 4 + 4 + 128 +
+               (nst + 1) * 8;
+    };
+    uint32_t rt = 0, nst = 0;
+    if (per <= 256 / nmat && need(per, 1) <= smem_cap) {
+        rt = per;
+        nst = 1;
+    } else {
+        for (uint32_t s : {3u, 2u}) {
+            for (uint32_t r = std::min<uint32_t>(per, 256 / nmat); r >= 1; r--) {
+                if (r < per && r > 8 && r % 8) continue;
+                if (need(r, s) <= smem_cap) {
+                    rt = r;
+                    break;
+                }
+            }
+            if (rt) {
+                nst = s;
+                break;
+            }
+        }
+    }
+    if (!rt) return fail(HS_E_UNSUPPORTED, "GEMV tile does not fit in shared memory");
+    p->rt = rt;
+    p->nst = nst;
+    p->slab_stride = round_up(rt * 128, 1024);
+    p->smem = need(rt, nst);
+    int rc = make_weight_map(&p->tm0, w0, n, rows, rt);
+    if (rc == HS_OK && w1) rc = make_weight_map(&p->tm1, w1, n, rows, rt);
+    return rc;
+}
+
+cudaError_t launch_plan(const GemvPlan& p, const GemvArgs& a, cudaStream_t st) {
+    return p.fast ? launch_gemv_fast(p, a, st) : launch_gemv(p, a, st);
+}
+
 struct TensorRef {
     void* ptr;
     uint64_t count;
@@ -155,6 +214,7 @@ struct hs_model {
     std::vector<LayerDev> layers;
     GemvPlan head;
     size_t attn_smem = 0;
+    uint32_t numeric = HS_NUMERIC_REFERENCE;
     std::map<std::string, TensorRef> tensors;
     std::vector<void*> allocs;
     ~hs_model() {
@@ -346,7 +406,7 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         pq.in_mode = l == 0 ? IN_EMBED_NORM : IN_NORM;
         a.trace = s->trace;
         a.trace_slot = slot++;
-        HS_CUDA_TRY(launch_gemv(pq, a, st));
+        HS_CUDA_TRY(launch_plan(pq, a, st));
         AttnArgs at{};
         at.qkv = s->qkv;
         at.kv = kv->base;
@@ -364,7 +424,10 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         at.page_shift = kv->page_shift;
         at.trace = s->trace;
         at.trace_slot = slot++;
-        HS_CUDA_TRY(launch_attention(c.head_dim, c.n_heads, m->attn_smem, at, st));
+        if (m->numeric == HS_NUMERIC_FAST)
+            HS_CUDA_TRY(launch_attention_fast(c.head_dim, c.n_heads, m->attn_smem, at, st));
+        else
+            HS_CUDA_TRY(launch_attention(c.head_dim, c.n_heads, m->attn_smem, at, st));
         GemvArgs o{};
         o.ctl = s->ctl;
         o.src = s->att;
@@ -377,7 +440,7 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         o.lanes = L.o.lanes;
         o.trace = s->trace;
         o.trace_slot = slot++;
-        HS_CUDA_TRY(launch_gemv(L.o, o, st));
+        HS_CUDA_TRY(launch_plan(L.o, o, st));
         GemvArgs gu{};
         gu.ctl = s->ctl;
         gu.eps = c.eps;
@@ -392,7 +455,7 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         gu.lanes = L.gu.lanes;
         gu.trace = s->trace;
         gu.trace_slot = slot++;
-        HS_CUDA_TRY(launch_gemv(L.gu, gu, st));
+        HS_CUDA_TRY(launch_plan(L.gu, gu, st));
         GemvArgs dn{};
         dn.ctl = s->ctl;
         dn.src = s->hb;
@@ -405,7 +468,7 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         dn.lanes = L.down.lanes;
         dn.trace = s->trace;
         dn.trace_slot = slot++;
-        HS_CUDA_TRY(launch_gemv(L.down, dn, st));
+        HS_CUDA_TRY(launch_plan(L.down, dn, st));
     }
     GemvArgs h{};
     h.ctl = s->ctl;
@@ -421,7 +484,7 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
     h.lanes = m->head.lanes;
     h.trace = s->trace;
     h.trace_slot = slot++;
-    HS_CUDA_TRY(launch_gemv(m->head, h, st));
+    HS_CUDA_TRY(launch_plan(m->head, h, st));
     return HS_OK;
 }
 
@@ -516,7 +579,12 @@ extern "C" {
 const char* hs_last_error(void) { return g_err.c_str(); }
 
 int hs_model_load(const char* path, uint32_t max_ctx, int device, hs_model** out) {
+    return hs_model_load_ex(path, max_ctx, device, HS_NUMERIC_REFERENCE, out);
+}
+
+int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t numeric, hs_model** out) {
     if (!path || !out) return fail(HS_E_ARG, "null argument");
+    if (numeric > HS_NUMERIC_FAST) return fail(HS_E_ARG, "unknown numeric path");
     if (max_ctx == 0) return fail(HS_E_ARG, "max_ctx must be positive");
     *out = nullptr;
     Gguf g;
@@ -554,6 +622,9 @@ int hs_model_load(const char* path, uint32_t max_ctx, int device, hs_model** out
     HS_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
     m->smem_cap = (size_t)optin;
     HS_CUDA_TRY(gemv_set_smem_limits(optin));
+    HS_CUDA_TRY(fast_set_smem_limits(optin));
+    m->numeric = numeric;
+    const bool fast = numeric == HS_NUMERIC_FAST;
     hs_config& c = m->cfg;
     c.n_layers = n_layers;
     c.n_heads = n_heads;
@@ -568,7 +639,14 @@ int hs_model_load(const char* path, uint32_t max_ctx, int device, hs_model** out
     c.max_ctx = max_ctx;
     c.eos = eos;
     c.fingerprint = fingerprint_of(g);
-    m->attn_smem = attention_smem(hd, max_ctx);
+    c.numeric = numeric;
+    if (fast) {
+        // Mix the path into the fingerprint: a reference-order worker and a
+        // fast worker must not hand sequences to each other.
+        const char tag[] = "hotseat-b200 numeric=fast";
+        for (const char* q = tag; *q; q++) c.fingerprint = (c.fingerprint ^ (uint8_t)*q) * 0x100000001b3ull;
+    }
+    m->attn_smem = fast ? attention_fast_smem(hd, max_ctx) : attention_smem(hd, max_ctx);
     if (m->attn_smem > m->smem_cap) return fail(HS_E_UNSUPPORTED, "max_ctx too large for the attention kernel");
 
     // Staging buffer for the largest quantised tensor.
@@ -626,15 +704,15 @@ int hs_model_load(const char* path, uint32_t max_ctx, int device, hs_model** out
             (rc = load_f16(m.get(), g, p + "ffn_up.weight", L.wup, (uint64_t)d_ff * d_model, staging, st)) ||
             (rc = load_f16(m.get(), g, p + "ffn_down.weight", L.wdown, (uint64_t)d_model * d_ff, staging, st)))
             return rc;
-        if ((rc = plan_gemv(&L.qkv, IN_NORM, OUT_STORE, (uint32_t)qrows, d_model, L.wqkv, nullptr, m->n_sm,
-                            m->smem_cap)) ||
-            (rc = plan_gemv(&L.o, IN_PLAIN, OUT_RESID, d_model, n_heads * hd, L.wo, nullptr, m->n_sm, m->smem_cap)) ||
-            (rc = plan_gemv(&L.gu, IN_NORM, OUT_SILU, d_ff, d_model, L.wgate, L.wup, m->n_sm, m->smem_cap)) ||
-            (rc = plan_gemv(&L.down, IN_PLAIN, OUT_RESID, d_model, d_ff, L.wdown, nullptr, m->n_sm, m->smem_cap)))
+        auto plan = fast ? plan_gemv_fast : plan_gemv;
+        if ((rc = plan(&L.qkv, IN_NORM, OUT_STORE, (uint32_t)qrows, d_model, L.wqkv, nullptr, m->n_sm, m->smem_cap)) ||
+            (rc = plan(&L.o, IN_PLAIN, OUT_RESID, d_model, n_heads * hd, L.wo, nullptr, m->n_sm, m->smem_cap)) ||
+            (rc = plan(&L.gu, IN_NORM, OUT_SILU, d_ff, d_model, L.wgate, L.wup, m->n_sm, m->smem_cap)) ||
+            (rc = plan(&L.down, IN_PLAIN, OUT_RESID, d_model, d_ff, L.wdown, nullptr, m->n_sm, m->smem_cap)))
             return rc;
     }
-    if ((rc = plan_gemv(&m->head, IN_NORM, OUT_STORE, (uint32_t)vocab, d_model, head_w, nullptr, m->n_sm,
-                        m->smem_cap)))
+    if ((rc = (fast ? plan_gemv_fast : plan_gemv)(&m->head, IN_NORM, OUT_STORE, (uint32_t)vocab, d_model, head_w,
+                                                   nullptr, m->n_sm, m->smem_cap)))
         return rc;
     std::vector<float> cs, sn;
     rope_tables(hd, max_ctx, rope_base, &cs, &sn);

@@ -36,6 +36,8 @@ struct GemvArgs {
 // One planned GEMV launch (shapes fixed at load).
 struct GemvPlan {
     int in_mode = IN_PLAIN, out_mode = OUT_STORE;
+    bool fast = false;      // GPU-native order (decode_fast.cu); `lanes` then holds threads per row
+    uint32_t cmax = 0;      // fast: 16-byte chunks per thread (template width)
     uint32_t n = 0, rows = 0, rt = 0, nst = 1, slab_stride = 0, lanes = 1, grid = 0, threads = 256;
     size_t smem = 0;
     CUtensorMap tm0{}, tm1{};
@@ -76,6 +78,13 @@ size_t attention_smem(uint32_t head_dim, uint32_t max_ctx);
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st);
 size_t sample_final_smem(uint32_t n_cta, uint32_t kmax);
 cudaError_t gemv_set_smem_limits(int optin);
+
+// GPU-native numeric order (decode_fast.cu).
+uint32_t fast_cmax_for(uint32_t chunks_per_thread);
+cudaError_t fast_set_smem_limits(int optin);
+cudaError_t launch_gemv_fast(const GemvPlan& p, const GemvArgs& a, cudaStream_t st);
+size_t attention_fast_smem(uint32_t head_dim, uint32_t max_ctx);
+cudaError_t launch_attention_fast(uint32_t head_dim, uint32_t nh, size_t smem, const AttnArgs& a, cudaStream_t st);
 
 constexpr uint32_t kSampleSlice = 1024;  // logits per CTA of the candidate kernel
 constexpr uint32_t kMaxTopK = 64;        // top_k supported by the device sampler

@@ -45,7 +45,20 @@ typedef struct {
     float eps, rope_base;
     uint32_t train_ctx, max_ctx, eos;
     uint64_t fingerprint;
+    uint32_t numeric; /* HS_NUMERIC_* the model was loaded with */
 } hs_config;
+
+/* Numeric paths. A sequence must use one path for its whole life; the path is
+ * part of the fingerprint, so workers on different paths refuse a handover
+ * exactly as the reference refuses different weights (migrate.rs:497-505).
+ *   REFERENCE: every reduction in hs-engine's order (eight serial lanes and
+ *              one fold, no FMA): bit-identical to the CPU reference, and the
+ *              fingerprint equals the reference's (model.rs:145-156).
+ *   FAST:      fixed GPU-native reduction shapes (warp trees, packed FMA):
+ *              bit-identical across B200s and migrations, logits within 1e-2
+ *              of the CPU reference. */
+#define HS_NUMERIC_REFERENCE 0u
+#define HS_NUMERIC_FAST 1u
 
 typedef struct hs_model hs_model;
 typedef struct hs_kv hs_kv;
@@ -57,6 +70,8 @@ typedef struct hs_scratch hs_scratch;
  * there to f16 (Q4_K/Q6_K/Q5_K/Q5_0/Q8_0/F16/F32, quant.rs:18-206), build the
  * RoPE tables with the reference's own exp/ln/sincos (model.rs:187-201). */
 int hs_model_load(const char* path, uint32_t max_ctx, int device, hs_model** out);
+/* hs_model_load with an explicit numeric path (hs_model_load uses REFERENCE). */
+int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t numeric, hs_model** out);
 /* Model{cfg, fingerprint} and tok.eos (model.rs:62-78). */
 int hs_model_config(const hs_model* m, hs_config* out);
 void hs_model_free(hs_model* m);
