@@ -122,6 +122,8 @@ _SIGS = {
     "hs_rng_seed": (None, [C.c_uint64, C.POINTER(Rng)]),
     "hs_sample": (C.c_int, [_P, C.POINTER(SamplerCfg), C.POINTER(Rng), _P, C.c_uint64, C.POINTER(C.c_uint32)]),
     "hs_argmax": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "hs_sample_noalloc": (C.c_int, [C.c_int, _P, C.c_uint32, C.POINTER(SamplerCfg), C.POINTER(Rng), _P, C.c_uint64,
+                                    _P, C.POINTER(C.c_uint32)]),
     "hs_seq_run": (C.c_int, [_P, _P, _P, _P, _U64P, C.c_uint64, C.POINTER(SeqState), C.POINTER(SamplerCfg),
                              C.POINTER(Rng), C.c_uint64]),
     "hs_seq_begin": (C.c_int, [_P, _P, _P, C.c_uint64, C.c_uint64, C.POINTER(SeqState), C.POINTER(SamplerCfg),

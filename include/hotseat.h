@@ -153,6 +153,18 @@ int hs_sample(hs_scratch* s, const hs_sampler_cfg* cfg, hs_rng* rng, const uint3
               uint32_t* out);
 /* argmax (sampler.rs:177-187) of the scratch's logits. */
 int hs_argmax(hs_scratch* s, uint32_t* out);
+/* hs_sample over `vocab` f32 logits in the caller's device memory on
+ * `device`, with no allocation: its working memory is one fixed array per
+ * device inside this library. No counterpart in the reference (its sampler
+ * reads host logits); it serves callers that cannot allocate device memory
+ * where they sample. Limits: vocab <= 262144; penalty window (min of
+ * repeat_last_n and n_hist, when the penalty is on) <= 4096 tokens; larger
+ * inputs return HS_E_ARG. The first call on a device does the set-up and must
+ * come before any stream capture; each call waits for its result on `stream`
+ * (cudaStream_t or NULL). Overlapping calls on one device race: serialise
+ * them. Same tokens and RNG state as hs_sample on the same logits. */
+int hs_sample_noalloc(int device, const float* logits, uint32_t vocab, const hs_sampler_cfg* cfg, hs_rng* rng,
+                      const uint32_t* hist, uint64_t n_hist, void* stream, uint32_t* out);
 
 /* ---- the decode loop (replaces hs-worker seq.rs:230-318 `run`) ---------- */
 
