@@ -302,11 +302,13 @@ def main():
         bpt = bytes_per_token_avg()
         achieved = bpt * (tokens_per_step / (ms_per_step / 1000.0)) / 1e9
         traffic = None
-        tp = os.path.join(ROOT, "profiles", "decode_step_traffic.json")
+        tp = os.path.join(ROOT, "profiles", "decode_step_traffic.txt")
         if os.path.exists(tp):
             try:
-                traffic = json.load(open(tp)).get("dram_bytes_per_token")
-            except (OSError, ValueError):
+                for ln in open(tp):
+                    if ln.startswith("dram_bytes_per_token"):
+                        traffic = float(ln.split()[1])
+            except (OSError, ValueError, IndexError):
                 traffic = None
         cpu = None
         if not args.no_cpu_baseline:
