@@ -27,7 +27,7 @@ LIB_PATH = os.path.join(_HERE, "libhotseat.so")
 HS_OK = 0
 HS_E_ARG, HS_E_IO, HS_E_CUDA, HS_E_STATE, HS_E_NOMEM, HS_E_UNSUPPORTED = -1, -2, -3, -4, -5, -6
 TOKEN_MAJOR, HEAD_MAJOR = 0, 1
-NUMERIC_REFERENCE, NUMERIC_FAST = 0, 1
+NUMERIC_REFERENCE, NUMERIC_FAST, NUMERIC_TC = 0, 1, 2
 DONE_REASONS = {0: "", 1: "eos", 2: "max_tokens", 3: "context full"}
 
 if not os.path.exists(LIB_PATH):
@@ -135,6 +135,18 @@ _SIGS = {
     "hs_scratch_trace": (C.c_int, [_P, _P, C.c_uint64, _U64P]),
     "hs_dequant_f16": (C.c_int, [C.c_uint32, _P, C.c_uint64, _P, _P]),
     "hs_synth_write": (C.c_int, [C.c_char_p, C.POINTER(SynthSpec)]),
+    "hs_batch_new": (C.c_int, [_P, C.c_uint32, C.POINTER(_P)]),
+    "hs_batch_free": (None, [_P]),
+    "hs_forward_batch": (C.c_int, [_P, _P, _P, _P, C.c_uint32, _P]),
+    "hs_batch_logits": (C.c_int, [_P, C.c_uint32, _P, C.c_uint64]),
+    "hs_batch_seq_run": (C.c_int, [_P, _P, _P, C.c_uint32, _P, _U64P, C.c_uint64, C.POINTER(SeqState),
+                                   C.POINTER(SamplerCfg), C.POINTER(Rng), C.c_uint64]),
+    "hs_batch_seq_begin": (C.c_int, [_P, _P, C.c_uint32, _P, _U64P, C.c_uint64, C.POINTER(SeqState),
+                                     C.POINTER(SamplerCfg), C.POINTER(Rng), C.c_uint64]),
+    "hs_batch_seq_step": (C.c_int, [_P, C.c_uint32]),
+    "hs_batch_seq_end": (C.c_int, [_P, _P, _U64P, C.c_uint64, C.POINTER(SeqState), C.POINTER(Rng)]),
+    "hs_batch_stream": (_P, [_P]),
+    "hs_batch_launches_per_step": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _f = getattr(_lib, _name)
@@ -377,6 +389,85 @@ def run_seq(model, kv, scratch, tokens, prompt_len, max_tokens, cfg, rng, filled
     _check(_lib.hs_seq_run(model._h, kv._h, scratch._h, _ptr(buf), C.byref(n), cap, C.byref(st), C.byref(cfg),
                            C.byref(rng), stop_at_filled))
     return buf[: n.value].copy(), st, rng
+
+
+class Batch:
+    """Working memory for decoding up to `max_seqs` sequences together
+    (models loaded with NUMERIC_TC)."""
+
+    def __init__(self, model, max_seqs):
+        h = C.c_void_p()
+        _check(_lib.hs_batch_new(model._h, max_seqs, C.byref(h)))
+        self._h = h
+        self.model = model
+        self.max_seqs = max_seqs
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.hs_batch_free(self._h)
+            self._h = None
+
+    __del__ = close
+
+    @staticmethod
+    def _kv_table(kvs):
+        return (C.c_void_p * len(kvs))(*[k._h.value for k in kvs])
+
+    def forward(self, kvs, tokens, pos):
+        """One forward per sequence: tokens[i] at pos[i] into kvs[i]."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(pos, dtype=np.uint32)
+        _check(_lib.hs_forward_batch(self.model._h, self._kv_table(kvs), _ptr(t), _ptr(p), len(kvs), self._h))
+
+    def logits(self, slot):
+        out = np.zeros(self.model.cfg.vocab, dtype=np.float32)
+        _check(_lib.hs_batch_logits(self._h, slot, _ptr(out), out.size))
+        return out
+
+    @property
+    def stream(self):
+        return _lib.hs_batch_stream(self._h)
+
+    def launches_per_step(self):
+        n = C.c_uint32()
+        _check(_lib.hs_batch_launches_per_step(self._h, C.byref(n)))
+        return n.value
+
+    def _state(self, seqs, stop_at_filled):
+        """seqs: list of dicts with tokens, prompt_len, max_tokens, cfg, rng, filled, done, done_reason."""
+        n = len(seqs)
+        cap = self.model.cfg.max_ctx + 1
+        bufs = [np.zeros(cap, dtype=np.uint32) for _ in range(n)]
+        for b, q in zip(bufs, seqs):
+            b[: len(q["tokens"])] = q["tokens"]
+        tabs = (C.c_void_p * n)(*[b.ctypes.data for b in bufs])
+        nt = (C.c_uint64 * n)(*[len(q["tokens"]) for q in seqs])
+        st = (SeqState * n)(*[SeqState(q["prompt_len"], q.get("filled", 0), q["max_tokens"], q.get("done", 0),
+                                       q.get("done_reason", 0)) for q in seqs])
+        cfg = (SamplerCfg * n)(*[q["cfg"] for q in seqs])
+        rng = (Rng * n)(*[q["rng"] for q in seqs])
+        return bufs, tabs, nt, st, cfg, rng, cap
+
+    def run_seqs(self, kvs, seqs, stop_at_filled=0):
+        """hs_batch_seq_run: every sequence to its stop. Returns [(tokens, SeqState, Rng)]."""
+        bufs, tabs, nt, st, cfg, rng, cap = self._state(seqs, stop_at_filled)
+        _check(_lib.hs_batch_seq_run(self.model._h, self._kv_table(kvs), self._h, len(seqs), tabs, nt, cap, st, cfg,
+                                     rng, stop_at_filled))
+        return [(bufs[i][: nt[i]].copy(), st[i], rng[i]) for i in range(len(seqs))]
+
+    def begin(self, kvs, seqs, stop_at_filled=0):
+        self._pending = self._state(seqs, stop_at_filled)
+        bufs, tabs, nt, st, cfg, rng, cap = self._pending
+        _check(_lib.hs_batch_seq_begin(self._h, self._kv_table(kvs), len(seqs), tabs, nt, cap, st, cfg, rng,
+                                       stop_at_filled))
+
+    def step(self, n_steps):
+        _check(_lib.hs_batch_seq_step(self._h, n_steps))
+
+    def end(self):
+        bufs, tabs, nt, st, cfg, rng, cap = self._pending
+        _check(_lib.hs_batch_seq_end(self._h, tabs, nt, cap, st, rng))
+        return [(bufs[i][: nt[i]].copy(), st[i], rng[i]) for i in range(len(bufs))]
 
 
 def dequant_f16(ggml_type, src_dev_ptr, n, dst_dev_ptr, stream=None):

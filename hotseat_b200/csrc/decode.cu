@@ -546,7 +546,26 @@ __device__ __forceinline__ uint32_t lower_bound_u64(const uint64_t* list, uint32
     return idx;
 }
 
-__global__ void __launch_bounds__(256) k_sample_cand(const SampleArgs a) {
+// Slot blockIdx.y of a batched launch: its logits, candidate lists, greedy
+// entries, control block and history buffer.
+__device__ __forceinline__ SampleArgs slot_args(const SampleArgs& a0) {
+    SampleArgs a = a0;
+    const uint32_t s = blockIdx.y;
+    if (s) {
+        a.logits += s * a0.logits_stride;
+        a.cand += s * a0.cand_stride;
+        a.argbuf += s * a0.n_cta;
+        a.ctl += s;
+    }
+    if (a0.tok_tab) {
+        a.tokens = a0.tok_tab[s];
+        a.tokens_w = a0.tok_tab[s];
+    }
+    return a;
+}
+
+__global__ void __launch_bounds__(256) k_sample_cand(const SampleArgs a0) {
+    const SampleArgs a = slot_args(a0);
     __shared__ uint64_t lists[8][128];
     __shared__ uint32_t win_cnt[kSampleSlice];
     __shared__ float bv_s[8];
@@ -650,7 +669,8 @@ __global__ void __launch_bounds__(256) k_sample_cand(const SampleArgs a) {
 
 constexpr uint32_t kFinalThreads = 256;
 
-__global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs a) {
+__global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs a0) {
+    const SampleArgs a = slot_args(a0);
     extern __shared__ uint64_t sel_lists[];  // [n_sel][kmax]
     __shared__ uint64_t heads[256];
     __shared__ uint32_t sel[64];
@@ -939,9 +959,10 @@ size_t sample_final_smem(uint32_t n_cta, uint32_t kmax) {
 }
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st) {
-    cudaError_t e = launch_pdl(k_sample_cand, dim3(a.n_cta), dim3(256), 0, st, a);
+    const uint32_t slots = a.slots ? a.slots : 1;
+    cudaError_t e = launch_pdl(k_sample_cand, dim3(a.n_cta, slots), dim3(256), 0, st, a);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k_sample_final, dim3(1), dim3(kFinalThreads), sample_final_smem(a.n_cta, a.kmax), st, a);
+    return launch_pdl(k_sample_final, dim3(1, slots), dim3(kFinalThreads), sample_final_smem(a.n_cta, a.kmax), st, a);
 }
 
 }  // namespace hs

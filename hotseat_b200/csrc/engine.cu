@@ -203,6 +203,7 @@ struct LayerDev {
     float *attn_norm = nullptr, *ffn_norm = nullptr, *bqkv = nullptr;
     uint16_t *wqkv = nullptr, *wo = nullptr, *wgate = nullptr, *wup = nullptr, *wdown = nullptr;
     GemvPlan qkv, o, gu, down;
+    TcGemmPlan tq, to, tgu, tdown;  // tensor-core path
 };
 
 struct hs_model {
@@ -215,6 +216,9 @@ struct hs_model {
     GemvPlan head;
     size_t attn_smem = 0;
     uint32_t numeric = HS_NUMERIC_REFERENCE;
+    TcGemmPlan thead;             // tensor-core LM head
+    uint64_t tc_part_per_slot = 0;  // max over split-K GEMMs of splits * rows
+    const uint16_t* head_w = nullptr;
     std::map<std::string, TensorRef> tensors;
     std::vector<void*> allocs;
     ~hs_model() {
@@ -378,6 +382,58 @@ int check_kv(const hs_model* m, const hs_kv* kv) {
     return HS_OK;
 }
 
+// Tensor-core GEMM plan: weight-row tile, K splits and pipeline depth so
+// that about one work unit lands on each SM.
+//   TC_SILU : gate+up rows of one tile per CTA, no split (the SiLU needs
+//             whole sums);
+//   TC_STORE: tiles of up to 256 rows, CTAs loop over tiles (LM head);
+//   TC_PART : 64/128-row tiles, K split so tiles x splits ~ SM count; the
+//             consumer adds the split partials in split order.
+int plan_tc(TcGemmPlan* p, int epi, uint32_t rows, uint32_t K, const uint16_t* w0, const uint16_t* w1, int n_sm,
+            size_t smem_cap) {
+    if (K % 64) return fail(HS_E_UNSUPPORTED, "GEMM reduction length must be a multiple of 64");
+    const bool silu = epi == TC_SILU;
+    const uint32_t kt_n = K / 64, sm = (uint32_t)n_sm;
+    p->epi = epi;
+    p->K = K;
+    p->rows = rows;
+    p->splits = 1;
+    if (silu) {
+        uint32_t nt = 8;
+        while (nt < 128 && (rows + nt - 1) / nt > sm) nt += 8;
+        p->n_tile = nt;
+    } else if (epi == TC_STORE) {
+        uint64_t best = ~0ull;
+        for (uint32_t nt = 16; nt <= 256; nt += 16) {
+            const uint64_t tiles = (rows + nt - 1) / nt, per = (tiles + sm - 1) / sm;
+            const uint64_t cost = per * nt;
+            if (cost < best || (cost == best && nt > p->n_tile)) {
+                best = cost;
+                p->n_tile = nt;
+            }
+        }
+    } else {
+        uint32_t nt = K >= 2048 ? 128 : 64;
+        while (nt > 16 && nt / 2 >= rows) nt /= 2;
+        p->n_tile = nt;
+        const uint32_t tiles = (rows + nt - 1) / nt;
+        p->splits = std::max<uint32_t>(1, std::min<uint32_t>(kt_n, sm / std::max<uint32_t>(tiles, 1)));
+    }
+    p->n_tiles = (rows + p->n_tile - 1) / p->n_tile;
+    const uint32_t units = p->n_tiles * p->splits;
+    p->grid = std::min<uint32_t>(units, sm);
+    p->m_tiles = 1;
+    const uint32_t per_cta = (units + p->grid - 1) / p->grid * ((kt_n + p->splits - 1) / p->splits);
+    uint32_t nst = std::min<uint32_t>(16, per_cta);
+    while (nst > 1 && tc_gemm_smem(p->n_tile, nst, silu) > smem_cap) nst--;
+    p->nst = nst;
+    p->smem = tc_gemm_smem(p->n_tile, nst, silu);
+    if (p->smem > smem_cap || !tc_tile_ok(p->n_tile, silu)) return fail(HS_E_UNSUPPORTED, "tensor-core GEMM tile does not fit");
+    int rc = make_weight_map(&p->tm0, w0, K, rows, p->n_tile);
+    if (rc == HS_OK) rc = make_weight_map(&p->tm1, w1 ? w1 : w0, K, rows, p->n_tile);
+    return rc;
+}
+
 // Enqueue one forward pass (the 5 kernels per layer + final norm/LM head).
 int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
     const hs_model* m = s->m;
@@ -539,8 +595,7 @@ int ensure_graphs(hs_scratch* s, const hs_kv* kv, uint32_t kmax) {
     return HS_OK;
 }
 
-int check_ctl_err(hs_scratch* s) {
-    uint32_t err = s->ctl_h->err;
+int ctl_err(uint32_t err) {
     if (!err) return HS_OK;
     std::string why;
     if (err & ERR_TIMEOUT) why += " bounded-wait-timeout";
@@ -551,6 +606,8 @@ int check_ctl_err(hs_scratch* s) {
     int code = (err & (ERR_INVARIANT | ERR_CAP)) ? HS_E_STATE : (err & ERR_TIMEOUT) ? HS_E_CUDA : HS_E_ARG;
     return fail(code, "device reported:" + why);
 }
+
+int check_ctl_err(hs_scratch* s) { return ctl_err(s->ctl_h->err); }
 
 int sync_ctl(hs_scratch* s) {
     HS_CUDA_TRY(cudaMemcpyAsync(s->ctl_h, s->ctl, sizeof(DevCtl), cudaMemcpyDeviceToHost, s->st));
@@ -584,7 +641,7 @@ int hs_model_load(const char* path, uint32_t max_ctx, int device, hs_model** out
 
 int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t numeric, hs_model** out) {
     if (!path || !out) return fail(HS_E_ARG, "null argument");
-    if (numeric > HS_NUMERIC_FAST) return fail(HS_E_ARG, "unknown numeric path");
+    if (numeric > HS_NUMERIC_TC) return fail(HS_E_ARG, "unknown numeric path");
     if (max_ctx == 0) return fail(HS_E_ARG, "max_ctx must be positive");
     *out = nullptr;
     Gguf g;
@@ -623,8 +680,10 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
     m->smem_cap = (size_t)optin;
     HS_CUDA_TRY(gemv_set_smem_limits(optin));
     HS_CUDA_TRY(fast_set_smem_limits(optin));
+    HS_CUDA_TRY(tc_set_smem_limits(optin));
+    HS_CUDA_TRY(tc_ops_set_smem_limits(optin));
     m->numeric = numeric;
-    const bool fast = numeric == HS_NUMERIC_FAST;
+    const bool fast = numeric == HS_NUMERIC_FAST, tc = numeric == HS_NUMERIC_TC;
     hs_config& c = m->cfg;
     c.n_layers = n_layers;
     c.n_heads = n_heads;
@@ -640,13 +699,16 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
     c.eos = eos;
     c.fingerprint = fingerprint_of(g);
     c.numeric = numeric;
-    if (fast) {
-        // Mix the path into the fingerprint: a reference-order worker and a
-        // fast worker must not hand sequences to each other.
-        const char tag[] = "hotseat-b200 numeric=fast";
+    if (fast || tc) {
+        // Mix the path into the fingerprint: workers on different numeric
+        // paths must not hand sequences to each other.
+        const char* tag = fast ? "hotseat-b200 numeric=fast" : "hotseat-b200 numeric=tc";
         for (const char* q = tag; *q; q++) c.fingerprint = (c.fingerprint ^ (uint8_t)*q) * 0x100000001b3ull;
     }
-    m->attn_smem = fast ? attention_fast_smem(hd, max_ctx) : attention_smem(hd, max_ctx);
+    if (tc && n_heads / n_kv > 8) return fail(HS_E_UNSUPPORTED, "tensor-core path supports up to 8 query heads per KV head");
+    if (tc && d_model > 2048) return fail(HS_E_UNSUPPORTED, "tensor-core path supports d_model up to 2048");
+    m->attn_smem = tc ? tc_attention_smem(hd, n_heads / n_kv, max_ctx)
+                      : fast ? attention_fast_smem(hd, max_ctx) : attention_smem(hd, max_ctx);
     if (m->attn_smem > m->smem_cap) return fail(HS_E_UNSUPPORTED, "max_ctx too large for the attention kernel");
 
     // Staging buffer for the largest quantised tensor.
@@ -704,6 +766,16 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
             (rc = load_f16(m.get(), g, p + "ffn_up.weight", L.wup, (uint64_t)d_ff * d_model, staging, st)) ||
             (rc = load_f16(m.get(), g, p + "ffn_down.weight", L.wdown, (uint64_t)d_model * d_ff, staging, st)))
             return rc;
+        if (tc) {
+            if ((rc = plan_tc(&L.tq, TC_PART, (uint32_t)qrows, d_model, L.wqkv, nullptr, m->n_sm, m->smem_cap)) ||
+                (rc = plan_tc(&L.to, TC_PART, d_model, n_heads * hd, L.wo, nullptr, m->n_sm, m->smem_cap)) ||
+                (rc = plan_tc(&L.tgu, TC_SILU, d_ff, d_model, L.wgate, L.wup, m->n_sm, m->smem_cap)) ||
+                (rc = plan_tc(&L.tdown, TC_PART, d_model, d_ff, L.wdown, nullptr, m->n_sm, m->smem_cap)))
+                return rc;
+            for (const TcGemmPlan* q : {&L.tq, &L.to, &L.tdown})
+                m->tc_part_per_slot = std::max<uint64_t>(m->tc_part_per_slot, (uint64_t)q->splits * q->rows);
+            continue;
+        }
         auto plan = fast ? plan_gemv_fast : plan_gemv;
         if ((rc = plan(&L.qkv, IN_NORM, OUT_STORE, (uint32_t)qrows, d_model, L.wqkv, nullptr, m->n_sm, m->smem_cap)) ||
             (rc = plan(&L.o, IN_PLAIN, OUT_RESID, d_model, n_heads * hd, L.wo, nullptr, m->n_sm, m->smem_cap)) ||
@@ -711,9 +783,14 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
             (rc = plan(&L.down, IN_PLAIN, OUT_RESID, d_model, d_ff, L.wdown, nullptr, m->n_sm, m->smem_cap)))
             return rc;
     }
-    if ((rc = (fast ? plan_gemv_fast : plan_gemv)(&m->head, IN_NORM, OUT_STORE, (uint32_t)vocab, d_model, head_w,
-                                                   nullptr, m->n_sm, m->smem_cap)))
+    m->head_w = head_w;
+    if (tc) {
+        if ((rc = plan_tc(&m->thead, TC_STORE, (uint32_t)vocab, d_model, head_w, nullptr, m->n_sm, m->smem_cap)))
+            return rc;
+    } else if ((rc = (fast ? plan_gemv_fast : plan_gemv)(&m->head, IN_NORM, OUT_STORE, (uint32_t)vocab, d_model, head_w,
+                                                          nullptr, m->n_sm, m->smem_cap))) {
         return rc;
+    }
     std::vector<float> cs, sn;
     rope_tables(hd, max_ctx, rope_base, &cs, &sn);
     if ((rc = dev_alloc(m.get(), &m->rope_cos, cs.size())) || (rc = dev_alloc(m.get(), &m->rope_sin, sn.size())))
@@ -937,6 +1014,8 @@ int hs_kv_copy_runs(hs_kv* src, hs_kv* dst, const uint64_t* runs, uint64_t n_run
 
 int hs_scratch_new(const hs_model* m, hs_scratch** out) {
     if (!m || !out) return fail(HS_E_ARG, "null argument");
+    if (m->numeric == HS_NUMERIC_TC)
+        return fail(HS_E_UNSUPPORTED, "a tensor-core model decodes through hs_batch_* (a batch of one is fine)");
     HS_CUDA_TRY(cudaSetDevice(m->device));
     auto s = std::make_unique<hs_scratch>();
     s->m = m;
@@ -1272,6 +1351,454 @@ int hs_kv_disarm(hs_kv* kv) {
     HS_CUDA_TRY(cudaMemcpy(kv->tracking, &zero, 4, cudaMemcpyHostToDevice));
     HS_CUDA_TRY(cudaMemset(kv->dirty, 0, kv->n_words * 8));
     return HS_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- batched decode
+
+struct hs_batch {
+    const hs_model* m = nullptr;
+    uint32_t cap_slots = 0;       // slot capacity, a multiple of 64
+    cudaStream_t st = nullptr;
+    float *x = nullptr, *part = nullptr, *logits = nullptr;
+    uint16_t *xn_hi = nullptr, *xn_lo = nullptr, *att_hi = nullptr, *att_lo = nullptr, *hb_hi = nullptr,
+             *hb_lo = nullptr;
+    DevCtl* ctl = nullptr;        // device [cap_slots]
+    DevCtl* ctl_h = nullptr;      // pinned host mirror
+    uint32_t* tokens = nullptr;   // device [cap_slots][tok_cap] histories
+    uint64_t tok_cap = 0;
+    uint32_t** tok_tab = nullptr;  // device [cap_slots] -> tokens rows
+    float** kv_tab = nullptr;      // device per-slot KV regions, dirty bitmaps, tracking flags
+    uint64_t** dirty_tab = nullptr;
+    uint32_t** track_tab = nullptr;
+    void** tab_h = nullptr;        // pinned staging for the three tables
+    uint64_t *cand = nullptr, *argbuf = nullptr;
+    uint32_t n_cta = 0, kmax_alloc = 0;
+    uint32_t* err = nullptr;       // GEMM error word (device)
+    uint32_t err_h = 0;
+    uint32_t layout = 0, page_shift = 0;
+    // Graphs by (slots, sampler width, KV layout, page shift); forward-only
+    // graphs use sampler width 0. Value: the graph and its kernel count.
+    std::map<uint64_t, std::pair<cudaGraphExec_t, uint32_t>> graphs;
+    cudaGraphExec_t g_step = nullptr;
+    uint32_t step_n = 0, launches = 0;
+    ~hs_batch() {
+        cudaSetDevice(m->device);
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second.first);
+        if (st) cudaStreamDestroy(st);
+        cudaFreeHost(ctl_h);
+        cudaFreeHost(tab_h);
+        for (void* p : {(void*)x, (void*)part, (void*)logits, (void*)xn_hi, (void*)xn_lo, (void*)att_hi, (void*)att_lo,
+                        (void*)hb_hi, (void*)hb_lo, (void*)ctl, (void*)tokens, (void*)tok_tab, (void*)kv_tab,
+                        (void*)dirty_tab, (void*)track_tab, (void*)cand, (void*)argbuf, (void*)err})
+            cudaFree(p);
+    }
+};
+
+namespace hs {
+namespace {
+
+// Activation operand map: rows = the live slots (rows past them read as
+// zeros), box 64 columns x 64 slots.
+int act_map(CUtensorMap* mp, const uint16_t* base, uint32_t cols, uint32_t slots) {
+    return make_weight_map(mp, base, cols, slots, 64);
+}
+
+int batch_gemm(hs_batch* b, const TcGemmPlan& p, const uint16_t* a_hi, const uint16_t* a_lo, uint32_t n, float* out,
+               uint16_t* out_hi, uint16_t* out_lo, uint32_t ld, uint32_t* launches) {
+    CUtensorMap mh, ml;
+    int rc = act_map(&mh, a_hi, p.K, n);
+    if (rc == HS_OK) rc = act_map(&ml, a_lo, p.K, n);
+    if (rc) return rc;
+    TcGemmPlan q = p;
+    q.m_tiles = (n + 63) / 64;
+    TcGemmArgs a{};
+    a.K = p.K;
+    a.rows = p.rows;
+    a.n_tile = p.n_tile;
+    a.n_tiles = p.n_tiles;
+    a.splits = p.splits;
+    a.slots = n;
+    a.nst = p.nst;
+    a.ld = ld;
+    a.part_stride = (uint64_t)b->cap_slots * p.rows;
+    a.out = out;
+    a.out_hi = out_hi;
+    a.out_lo = out_lo;
+    a.err = b->err;
+    cudaError_t e = launch_tc_gemm(q, mh, ml, a, b->st);
+    if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("tensor-core GEMM launch: ") + cudaGetErrorString(e));
+    (*launches)++;
+    return HS_OK;
+}
+
+// One batched forward for slots [0, n): 7 launches per layer + final norm + LM head.
+int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches) {
+    const hs_model* m = b->m;
+    const hs_config& c = m->cfg;
+    const uint32_t d = c.d_model, hd = c.head_dim, qrows = (c.n_heads + 2 * c.n_kv_heads) * hd;
+    int rc;
+    const TcGemmPlan* prev_down = nullptr;
+    auto norm = [&](const float* g, const TcGemmPlan* part_of, bool embed) -> int {
+        TcNormArgs a{};
+        a.x = b->x;
+        a.part = part_of ? b->part : nullptr;
+        a.n_part = part_of ? part_of->splits : 0;
+        a.part_stride = part_of ? (uint64_t)b->cap_slots * part_of->rows : 0;
+        a.embd = embed ? m->embd : nullptr;
+        a.g = g;
+        a.out_hi = b->xn_hi;
+        a.out_lo = b->xn_lo;
+        a.ctl = b->ctl;
+        a.d = d;
+        a.vocab = c.vocab;
+        a.eps = c.eps;
+        cudaError_t e = launch_tc_norm(a, n, b->st);
+        if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("norm launch: ") + cudaGetErrorString(e));
+        (*launches)++;
+        return HS_OK;
+    };
+    for (uint32_t l = 0; l < c.n_layers; l++) {
+        const LayerDev& L = m->layers[l];
+        if ((rc = norm(L.attn_norm, prev_down, l == 0))) return rc;
+        if ((rc = batch_gemm(b, L.tq, b->xn_hi, b->xn_lo, n, b->part, nullptr, nullptr, qrows, launches))) return rc;
+        TcAttnArgs at{};
+        at.qkv_part = b->part;
+        at.n_part = L.tq.splits;
+        at.part_stride = (uint64_t)b->cap_slots * L.tq.rows;
+        at.bias = L.bqkv;
+        at.qkv_rows = qrows;
+        at.kv = b->kv_tab;
+        at.dirty = b->dirty_tab;
+        at.tracking = b->track_tab;
+        at.rope_cos = m->rope_cos;
+        at.rope_sin = m->rope_sin;
+        at.att_hi = b->att_hi;
+        at.att_lo = b->att_lo;
+        at.ctl = b->ctl;
+        at.layer = l;
+        at.nh = c.n_heads;
+        at.nkv = c.n_kv_heads;
+        at.max_ctx = c.max_ctx;
+        at.layout = b->layout;
+        at.page_shift = b->page_shift;
+        cudaError_t e = launch_tc_attention(hd, at, n, m->attn_smem, b->st);
+        if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
+        (*launches)++;
+        if ((rc = batch_gemm(b, L.to, b->att_hi, b->att_lo, n, b->part, nullptr, nullptr, d, launches))) return rc;
+        if ((rc = norm(L.ffn_norm, &L.to, false))) return rc;
+        if ((rc = batch_gemm(b, L.tgu, b->xn_hi, b->xn_lo, n, nullptr, b->hb_hi, b->hb_lo, c.d_ff, launches))) return rc;
+        if ((rc = batch_gemm(b, L.tdown, b->hb_hi, b->hb_lo, n, b->part, nullptr, nullptr, d, launches))) return rc;
+        prev_down = &L.tdown;
+    }
+    if ((rc = norm(m->out_norm, prev_down, false))) return rc;
+    return batch_gemm(b, m->thead, b->xn_hi, b->xn_lo, n, b->logits, nullptr, nullptr, c.vocab, launches);
+}
+
+SampleArgs batch_sample_args(hs_batch* b, uint32_t n, uint32_t kmax) {
+    SampleArgs a{};
+    a.logits = b->logits;
+    a.tokens = b->tokens;
+    a.tokens_w = b->tokens;
+    a.cand = b->cand;
+    a.argbuf = b->argbuf;
+    a.ctl = b->ctl;
+    a.vocab = b->m->cfg.vocab;
+    a.n_cta = b->n_cta;
+    a.kmax = kmax;
+    a.slots = n;
+    a.logits_stride = b->m->cfg.vocab;
+    a.cand_stride = (uint64_t)b->n_cta * kmax;
+    a.tok_tab = b->tok_tab;
+    return a;
+}
+
+int batch_graph(hs_batch* b, uint32_t n, uint32_t kmax, cudaGraphExec_t* out, uint32_t* launches) {
+    const uint64_t key = (uint64_t)n | (uint64_t)kmax << 16 | (uint64_t)b->layout << 32 | (uint64_t)b->page_shift << 40;
+    auto it = b->graphs.find(key);
+    if (it != b->graphs.end()) {
+        *out = it->second.first;
+        *launches = it->second.second;
+        return HS_OK;
+    }
+    *launches = 0;
+    cudaGraph_t g = nullptr;
+    HS_CUDA_TRY(cudaStreamBeginCapture(b->st, cudaStreamCaptureModeThreadLocal));
+    int rc = batch_enqueue_forward(b, n, launches);
+    if (rc == HS_OK && kmax) {
+        cudaError_t e = launch_sample(batch_sample_args(b, n, kmax), b->st);
+        if (e != cudaSuccess) rc = fail(HS_E_CUDA, std::string("sampler launch: ") + cudaGetErrorString(e));
+        *launches += 2;
+    }
+    cudaError_t e = cudaStreamEndCapture(b->st, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    cudaGraphExec_t ex = nullptr;
+    e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    b->graphs[key] = std::make_pair(ex, *launches);
+    *out = ex;
+    return HS_OK;
+}
+
+// Per-slot KV tables (all regions must share layout and page size).
+int batch_kv_tables(hs_batch* b, hs_kv* const* kvs, uint32_t n) {
+    const hs_model* m = b->m;
+    for (uint32_t i = 0; i < n; i++) {
+        if (!kvs[i]) return fail(HS_E_ARG, "null KV region");
+        int rc = check_kv(m, kvs[i]);
+        if (rc) return rc;
+        if (kvs[i]->spec.layout != kvs[0]->spec.layout || kvs[i]->page_shift != kvs[0]->page_shift)
+            return fail(HS_E_ARG, "KV regions of one batch must share layout and page size");
+        for (uint32_t j = 0; j < i; j++)
+            if (kvs[j] == kvs[i]) return fail(HS_E_ARG, "a KV region appears twice in one batch");
+    }
+    b->layout = kvs[0]->spec.layout;
+    b->page_shift = kvs[0]->page_shift;
+    void** h = b->tab_h;
+    const uint32_t C = b->cap_slots;
+    for (uint32_t i = 0; i < n; i++) {
+        h[i] = kvs[i]->base;
+        h[C + i] = kvs[i]->dirty;
+        h[2 * C + i] = kvs[i]->tracking;
+    }
+    HS_CUDA_TRY(cudaMemcpyAsync(b->kv_tab, h, n * sizeof(void*), cudaMemcpyHostToDevice, b->st));
+    HS_CUDA_TRY(cudaMemcpyAsync(b->dirty_tab, h + C, n * sizeof(void*), cudaMemcpyHostToDevice, b->st));
+    HS_CUDA_TRY(cudaMemcpyAsync(b->track_tab, h + 2 * C, n * sizeof(void*), cudaMemcpyHostToDevice, b->st));
+    return HS_OK;
+}
+
+int batch_sync(hs_batch* b, uint32_t n) {
+    HS_CUDA_TRY(cudaMemcpyAsync(b->ctl_h, b->ctl, (size_t)n * sizeof(DevCtl), cudaMemcpyDeviceToHost, b->st));
+    HS_CUDA_TRY(cudaMemcpyAsync(&b->err_h, b->err, 4, cudaMemcpyDeviceToHost, b->st));
+    HS_CUDA_TRY(cudaStreamSynchronize(b->st));
+    if (b->err_h) return fail(HS_E_CUDA, "tensor-core GEMM reported a bounded-wait timeout");
+    for (uint32_t i = 0; i < n; i++) {
+        int rc = ctl_err(b->ctl_h[i].err);
+        if (rc) return fail(rc, "sequence " + std::to_string(i) + ": " + hs_last_error());
+    }
+    return HS_OK;
+}
+
+}  // namespace
+}  // namespace hs
+
+extern "C" {
+
+int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out) {
+    if (!m || !out) return fail(HS_E_ARG, "null argument");
+    if (m->numeric != HS_NUMERIC_TC) return fail(HS_E_UNSUPPORTED, "hs_batch needs a model loaded with HS_NUMERIC_TC");
+    if (max_seqs == 0 || max_seqs > 128) return fail(HS_E_ARG, "max_seqs must be 1..128");
+    HS_CUDA_TRY(cudaSetDevice(m->device));
+    auto b = std::make_unique<hs_batch>();
+    b->m = m;
+    const hs_config& c = m->cfg;
+    const uint32_t C = (max_seqs + 63) / 64 * 64;
+    b->cap_slots = C;
+    const uint32_t qrows = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+    HS_CUDA_TRY(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking));
+    auto alloc = [&](auto** p, uint64_t count) -> int {
+        using T = std::remove_reference_t<decltype(**p)>;
+        cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), std::max<uint64_t>(count, 1) * sizeof(T));
+        if (e != cudaSuccess) return fail(HS_E_NOMEM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+        e = cudaMemset(*p, 0, std::max<uint64_t>(count, 1) * sizeof(T));
+        return e == cudaSuccess ? (int)HS_OK : fail(HS_E_CUDA, cudaGetErrorString(e));
+    };
+    b->tok_cap = (uint64_t)c.max_ctx + 1;
+    b->n_cta = (c.vocab + kSampleSlice - 1) / kSampleSlice;
+    if (b->n_cta > 256) return fail(HS_E_UNSUPPORTED, "vocab too large for the device sampler");
+    b->kmax_alloc = b->n_cta > 1 ? kMaxTopK : kSampleSlice;
+    int rc;
+    if ((rc = alloc(&b->x, (uint64_t)C * c.d_model)) ||
+        (rc = alloc(&b->part, (uint64_t)C * std::max<uint64_t>(m->tc_part_per_slot, qrows))) ||
+        (rc = alloc(&b->logits, (uint64_t)C * c.vocab)) || (rc = alloc(&b->xn_hi, (uint64_t)C * c.d_model)) ||
+        (rc = alloc(&b->xn_lo, (uint64_t)C * c.d_model)) ||
+        (rc = alloc(&b->att_hi, (uint64_t)C * c.n_heads * c.head_dim)) ||
+        (rc = alloc(&b->att_lo, (uint64_t)C * c.n_heads * c.head_dim)) ||
+        (rc = alloc(&b->hb_hi, (uint64_t)C * c.d_ff)) || (rc = alloc(&b->hb_lo, (uint64_t)C * c.d_ff)) ||
+        (rc = alloc(&b->ctl, C)) || (rc = alloc(&b->tokens, (uint64_t)C * b->tok_cap)) ||
+        (rc = alloc(&b->tok_tab, C)) || (rc = alloc(&b->kv_tab, C)) || (rc = alloc(&b->dirty_tab, C)) ||
+        (rc = alloc(&b->track_tab, C)) || (rc = alloc(&b->cand, (uint64_t)C * b->n_cta * b->kmax_alloc)) ||
+        (rc = alloc(&b->argbuf, (uint64_t)C * b->n_cta)) || (rc = alloc(&b->err, 1)))
+        return rc;
+    HS_CUDA_TRY(cudaMallocHost(&b->ctl_h, (size_t)C * sizeof(DevCtl)));
+    std::memset(b->ctl_h, 0, (size_t)C * sizeof(DevCtl));
+    HS_CUDA_TRY(cudaMallocHost(&b->tab_h, (size_t)3 * C * sizeof(void*)));
+    std::vector<uint32_t*> rows(C);
+    for (uint32_t i = 0; i < C; i++) rows[i] = b->tokens + (uint64_t)i * b->tok_cap;
+    HS_CUDA_TRY(cudaMemcpy(b->tok_tab, rows.data(), C * sizeof(uint32_t*), cudaMemcpyHostToDevice));
+    *out = b.release();
+    return HS_OK;
+}
+
+void hs_batch_free(hs_batch* b) { delete b; }
+
+void* hs_batch_stream(hs_batch* b) { return b ? (void*)b->st : nullptr; }
+
+int hs_batch_launches_per_step(hs_batch* b, uint32_t* out) {
+    if (!b || !out) return fail(HS_E_ARG, "null argument");
+    if (!b->g_step) return fail(HS_E_ARG, "hs_batch_seq_begin has not been called");
+    *out = b->launches;
+    return HS_OK;
+}
+
+int hs_forward_batch(const hs_model* m, hs_kv* const* kvs, const uint32_t* tokens, const uint32_t* pos, uint32_t n,
+                     hs_batch* b) {
+    if (!m || !b || b->m != m || !kvs || !tokens || !pos) return fail(HS_E_ARG, "null or mismatched argument");
+    if (n == 0 || n > b->cap_slots) return fail(HS_E_ARG, "sequence count outside the batch capacity");
+    for (uint32_t i = 0; i < n; i++) {
+        if (pos[i] >= m->cfg.max_ctx) return fail(HS_E_ARG, "position past max_ctx");
+        if (tokens[i] >= m->cfg.vocab) return fail(HS_E_ARG, "token " + std::to_string(tokens[i]) + " out of range");
+    }
+    HS_CUDA_TRY(cudaSetDevice(m->device));
+    int rc = batch_kv_tables(b, kvs, n);
+    if (rc) return rc;
+    for (uint32_t i = 0; i < n; i++) {
+        DevCtl& h = b->ctl_h[i];
+        std::memset(&h, 0, sizeof(DevCtl));
+        h.token = tokens[i];
+        h.pos = pos[i];
+        h.active = 1;
+        h.mode = 1;
+        h.vocab = m->cfg.vocab;
+        h.max_ctx = m->cfg.max_ctx;
+    }
+    HS_CUDA_TRY(cudaMemcpyAsync(b->ctl, b->ctl_h, (size_t)n * sizeof(DevCtl), cudaMemcpyHostToDevice, b->st));
+    cudaGraphExec_t g = nullptr;
+    uint32_t launches = 0;
+    if ((rc = batch_graph(b, n, 0, &g, &launches))) return rc;
+    HS_CUDA_TRY(cudaGraphLaunch(g, b->st));
+    return batch_sync(b, n);
+}
+
+int hs_batch_logits(hs_batch* b, uint32_t slot, float* host, uint64_t n) {
+    if (!b || !host) return fail(HS_E_ARG, "null argument");
+    if (slot >= b->cap_slots) return fail(HS_E_ARG, "slot outside the batch capacity");
+    if (n > b->m->cfg.vocab) return fail(HS_E_ARG, "more logits than the vocabulary");
+    HS_CUDA_TRY(cudaSetDevice(b->m->device));
+    HS_CUDA_TRY(cudaMemcpy(host, b->logits + (uint64_t)slot * b->m->cfg.vocab, n * 4, cudaMemcpyDeviceToHost));
+    return HS_OK;
+}
+
+int hs_batch_seq_begin(hs_batch* b, hs_kv* const* kvs, uint32_t n, uint32_t* const* tokens, const uint64_t* n_tokens,
+                       uint64_t cap, const hs_seq_state* st, const hs_sampler_cfg* cfg, const hs_rng* rng,
+                       uint64_t stop_at_filled) {
+    if (!b || !kvs || !tokens || !n_tokens || !st || !cfg || !rng) return fail(HS_E_ARG, "null argument");
+    if (n == 0 || n > b->cap_slots) return fail(HS_E_ARG, "sequence count outside the batch capacity");
+    const hs_model* m = b->m;
+    const uint32_t vocab = m->cfg.vocab;
+    uint32_t kmax = b->n_cta > 1 ? kMaxTopK : std::min<uint32_t>(kSampleSlice, vocab);
+    for (uint32_t i = 0; i < n; i++) {
+        const std::string who = "sequence " + std::to_string(i) + ": ";
+        if (!tokens[i]) return fail(HS_E_ARG, who + "null token buffer");
+        if (n_tokens[i] == 0 || st[i].filled > n_tokens[i] || st[i].prompt_len > n_tokens[i])
+            return fail(HS_E_ARG, who + "inconsistent sequence state");
+        if (n_tokens[i] > b->tok_cap) return fail(HS_E_ARG, who + "history longer than max_ctx");
+        for (uint64_t j = 0; j < n_tokens[i]; j++)
+            if (tokens[i][j] >= vocab) return fail(HS_E_ARG, who + "token out of range");
+        const uint32_t k = cfg[i].top_k == 0 ? vocab : std::min(cfg[i].top_k, vocab);
+        if (cfg[i].temperature > 0.0f && (k > kSampleSlice || (b->n_cta > 1 && k > kMaxTopK)))
+            return fail(HS_E_UNSUPPORTED, who + "device sampler supports top_k <= " + std::to_string(kMaxTopK));
+        if (!st[i].done && st[i].filled >= n_tokens[i])
+            return fail(HS_E_STATE, who + "nothing to feed at the token boundary");
+    }
+    HS_CUDA_TRY(cudaSetDevice(m->device));
+    int rc = batch_kv_tables(b, kvs, n);
+    if (rc) return rc;
+    for (uint32_t i = 0; i < n; i++) {
+        DevCtl& h = b->ctl_h[i];
+        std::memset(&h, 0, sizeof(DevCtl));
+        h.mode = 0;
+        h.n_tokens = n_tokens[i];
+        h.filled = st[i].filled;
+        h.prompt_len = st[i].prompt_len;
+        h.max_tokens = st[i].max_tokens;
+        h.cap = std::min<uint64_t>(cap, b->tok_cap);
+        h.stop_at = stop_at_filled;
+        h.done = st[i].done;
+        h.done_reason = st[i].done_reason;
+        h.eos = m->cfg.eos;
+        h.max_ctx = m->cfg.max_ctx;
+        h.vocab = vocab;
+        fill_cfg(h, &cfg[i], &rng[i]);
+        const bool runnable =
+            !st[i].done && st[i].filled < n_tokens[i] && !(stop_at_filled && st[i].filled >= stop_at_filled);
+        if (runnable && st[i].filled >= m->cfg.max_ctx) return fail(HS_E_ARG, "position past max_ctx");
+        h.active = runnable ? 1 : 0;
+        h.token = runnable ? tokens[i][st[i].filled] : 0;
+        h.pos = (uint32_t)st[i].filled;
+        HS_CUDA_TRY(cudaMemcpyAsync(b->tokens + (uint64_t)i * b->tok_cap, tokens[i], n_tokens[i] * 4,
+                                    cudaMemcpyHostToDevice, b->st));
+    }
+    HS_CUDA_TRY(cudaMemcpyAsync(b->ctl, b->ctl_h, (size_t)n * sizeof(DevCtl), cudaMemcpyHostToDevice, b->st));
+    if ((rc = batch_graph(b, n, kmax, &b->g_step, &b->launches))) return rc;
+    b->step_n = n;
+    return HS_OK;
+}
+
+int hs_batch_seq_step(hs_batch* b, uint32_t n_steps) {
+    if (!b || !b->g_step) return fail(HS_E_ARG, "hs_batch_seq_begin has not been called");
+    HS_CUDA_TRY(cudaSetDevice(b->m->device));
+    for (uint32_t i = 0; i < n_steps; i++) HS_CUDA_TRY(cudaGraphLaunch(b->g_step, b->st));
+    return HS_OK;
+}
+
+int hs_batch_seq_end(hs_batch* b, uint32_t* const* tokens, uint64_t* n_tokens, uint64_t cap, hs_seq_state* st,
+                     hs_rng* rng) {
+    if (!b || !b->g_step) return fail(HS_E_ARG, "hs_batch_seq_begin has not been called");
+    HS_CUDA_TRY(cudaSetDevice(b->m->device));
+    const uint32_t n = b->step_n;
+    int rc = batch_sync(b, n);
+    if (rc) return rc;
+    for (uint32_t i = 0; i < n; i++) {
+        const DevCtl& h = b->ctl_h[i];
+        if (tokens && n_tokens && tokens[i]) {
+            if (h.n_tokens > cap) return fail(HS_E_ARG, "token buffer too small");
+            HS_CUDA_TRY(cudaMemcpy(tokens[i], b->tokens + (uint64_t)i * b->tok_cap, h.n_tokens * 4,
+                                   cudaMemcpyDeviceToHost));
+            n_tokens[i] = h.n_tokens;
+        }
+        if (st) {
+            st[i].filled = h.filled;
+            st[i].done = h.done;
+            st[i].done_reason = h.done_reason;
+        }
+        if (rng) {
+            for (int k = 0; k < 4; k++) rng[i].s[k] = h.rng[k];
+            rng[i].draws = h.draws;
+        }
+    }
+    return HS_OK;
+}
+
+int hs_batch_seq_run(const hs_model* m, hs_kv* const* kvs, hs_batch* b, uint32_t n, uint32_t* const* tokens,
+                     uint64_t* n_tokens, uint64_t cap, hs_seq_state* st, const hs_sampler_cfg* cfg, hs_rng* rng,
+                     uint64_t stop_at_filled) {
+    if (!m || !b || b->m != m || !n_tokens) return fail(HS_E_ARG, "null or mismatched argument");
+    int rc = hs_batch_seq_begin(b, kvs, n, tokens, n_tokens, cap, st, cfg, rng, stop_at_filled);
+    if (rc) return rc;
+    // Each chunk advances every running sequence; max_ctx chunks bound the loop.
+    for (uint32_t guard = 0;; guard++) {
+        uint64_t bound = 0;
+        for (uint32_t i = 0; i < n; i++) {
+            const DevCtl& h = b->ctl_h[i];
+            if (h.done || !h.active) continue;
+            const uint64_t pre = h.n_tokens - h.filled, gen = h.n_tokens - h.prompt_len;
+            uint64_t bi = pre + (h.max_tokens > gen ? h.max_tokens - gen : 0);
+            if (h.stop_at && h.stop_at > h.filled) bi = std::min<uint64_t>(bi, h.stop_at - h.filled);
+            bound = std::max<uint64_t>(bound, std::max<uint64_t>(1, bi));
+        }
+        if (bound == 0) break;
+        if (guard > m->cfg.max_ctx) return fail(HS_E_STATE, "decode loop made no progress");
+        if ((rc = hs_batch_seq_step(b, (uint32_t)std::min<uint64_t>(bound, 256)))) return rc;
+        if ((rc = batch_sync(b, n))) return rc;
+    }
+    return hs_batch_seq_end(b, tokens, n_tokens, cap, st, rng);
 }
 
 }  // extern "C"

@@ -67,6 +67,12 @@ struct SampleArgs {
     uint32_t vocab, n_cta, kmax;
     uint64_t* trace;
     uint32_t trace_slot;
+    // Batched launch (gridDim.y = slots; 0 or 1 = the single-slot layout):
+    // slot s uses logits + s*logits_stride, cand + s*cand_stride,
+    // argbuf + s*n_cta, ctl + s, and history buffer tok_tab[s] when set.
+    uint32_t slots;
+    uint64_t logits_stride, cand_stride;
+    uint32_t* const* tok_tab;
 };
 
 int launch_dequant(uint32_t ty, const void* src, uint64_t n, void* dst, cudaStream_t st, int n_sm);
@@ -85,6 +91,80 @@ cudaError_t fast_set_smem_limits(int optin);
 cudaError_t launch_gemv_fast(const GemvPlan& p, const GemvArgs& a, cudaStream_t st);
 size_t attention_fast_smem(uint32_t head_dim, uint32_t max_ctx);
 cudaError_t launch_attention_fast(uint32_t head_dim, uint32_t nh, size_t smem, const AttnArgs& a, cudaStream_t st);
+
+// Tensor-core path (batch_tc.cu).
+enum TcEpi : int { TC_STORE = 0, TC_PART = 1, TC_SILU = 2 };
+
+struct TcGemmArgs {
+    uint32_t K;              // reduction length (multiple of 64)
+    uint32_t rows;           // weight rows = output features
+    uint32_t n_tile;         // weight rows per tile (multiple of 8; SiLU: gate + up rows <= 256)
+    uint32_t n_tiles;        // ceil(rows / n_tile)
+    uint32_t splits;         // K splits per tile (TC_PART: partial sums per split)
+    uint32_t slots;          // live activation rows (groups of 64 along gridDim.y)
+    uint32_t nst;            // shared-memory pipeline stages
+    uint32_t ld;             // row stride (elements) of the outputs
+    uint64_t part_stride;    // TC_PART: elements between splits
+    float* out;              // TC_STORE: out = D; TC_PART: out[split] = partial D
+    uint16_t* out_hi;        // TC_SILU: f16 pair of silu(gate) * up
+    uint16_t* out_lo;
+    uint32_t* err;           // error bits (ERR_TIMEOUT)
+    uint64_t* trace;
+    uint32_t trace_slot;
+};
+
+struct TcGemmPlan {
+    int epi = TC_STORE;
+    uint32_t K = 0, rows = 0, n_tile = 0, n_tiles = 0, splits = 1, nst = 0, grid = 0, m_tiles = 1;
+    size_t smem = 0;
+    CUtensorMap tm0{}, tm1{};  // weight boxes {64 columns, n_tile rows}
+};
+
+size_t tc_gemm_smem(uint32_t n_tile, uint32_t nst, bool silu);
+bool tc_tile_ok(uint32_t n_tile, bool silu);
+cudaError_t tc_set_smem_limits(int optin);
+cudaError_t launch_tc_gemm(const TcGemmPlan& p, const CUtensorMap& ahi, const CUtensorMap& alo, const TcGemmArgs& a,
+                           cudaStream_t st);
+
+struct TcNormArgs {
+    float* x;                // [slots][d] residual stream (updated when embd or n_part)
+    const float* part;       // split-K partials [n_part][slots][d] added before the norm
+    uint32_t n_part;
+    uint64_t part_stride;    // elements between splits
+    const uint16_t* embd;    // non-null: x = embedding row of the slot's token (layer 0)
+    const float* g;          // RMSNorm gain [d]
+    uint16_t* out_hi;        // [slots][d] f16 pair of the normed row
+    uint16_t* out_lo;
+    DevCtl* ctl;             // per-slot control blocks
+    uint32_t d, vocab;
+    float eps;
+    uint64_t* trace;
+    uint32_t trace_slot;
+};
+
+struct TcAttnArgs {
+    const float* qkv_part;   // split-K partials [n_part][slots][qkv_rows] of the QKV product
+    uint32_t n_part;
+    uint64_t part_stride;
+    const float* bias;       // [qkv_rows]
+    uint32_t qkv_rows;
+    float* const* kv;        // per-slot KV regions
+    uint64_t* const* dirty;  // per-slot page bitmaps
+    const uint32_t* const* tracking;
+    const float* rope_cos;   // [max_ctx][hd/2]
+    const float* rope_sin;
+    uint16_t* att_hi;        // [slots][nh*hd] f16 pair of the attention output
+    uint16_t* att_lo;
+    DevCtl* ctl;
+    uint32_t layer, nh, nkv, max_ctx, layout, page_shift;
+    uint64_t* trace;
+    uint32_t trace_slot;
+};
+
+size_t tc_attention_smem(uint32_t head_dim, uint32_t groups, uint32_t max_ctx);
+cudaError_t tc_ops_set_smem_limits(int optin);
+cudaError_t launch_tc_norm(const TcNormArgs& a, uint32_t slots, cudaStream_t st);
+cudaError_t launch_tc_attention(uint32_t head_dim, const TcAttnArgs& a, uint32_t slots, size_t smem, cudaStream_t st);
 
 constexpr uint32_t kSampleSlice = 1024;  // logits per CTA of the candidate kernel
 constexpr uint32_t kMaxTopK = 64;        // top_k supported by the device sampler

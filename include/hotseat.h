@@ -59,6 +59,11 @@ typedef struct {
  *              of the CPU reference. */
 #define HS_NUMERIC_REFERENCE 0u
 #define HS_NUMERIC_FAST 1u
+/* Tensor-core path: every matrix product runs as a tcgen05 GEMM over a batch
+ * of sequences (activations carried as f16 hi/lo pairs, f32 accumulation).
+ * Same tolerance contract as FAST; a sequence's bits do not depend on the
+ * batch it runs in. Models loaded with it decode through hs_batch_*. */
+#define HS_NUMERIC_TC 2u
 
 typedef struct hs_model hs_model;
 typedef struct hs_kv hs_kv;
@@ -191,6 +196,39 @@ int hs_seq_begin(hs_scratch* s, hs_kv* kv, const uint32_t* tokens, uint64_t n_to
                  const hs_seq_state* st, const hs_sampler_cfg* cfg, const hs_rng* rng, uint64_t stop_at_filled);
 int hs_seq_step(hs_scratch* s, uint32_t n_steps);
 int hs_seq_end(hs_scratch* s, uint32_t* tokens, uint64_t* n_tokens, uint64_t cap, hs_seq_state* st, hs_rng* rng);
+/* ---- batched decode (HS_NUMERIC_TC models; one worker, many sequences) --
+ * The reference decodes each Seq on its own thread (seq.rs:223-318); a B200
+ * worker keeps up to 128 sequences in one hs_batch and advances them together,
+ * one token each per step, with the same per-sequence semantics: own KV
+ * region, history, SeqState, sampler config and RNG. No counterpart type in
+ * the reference. */
+typedef struct hs_batch hs_batch;
+int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out);
+void hs_batch_free(hs_batch* b);
+/* One Model::forward for each of n sequences: tokens[i] at pos[i], appending
+ * to kvs[i] (all regions of one layout and page size). Blocks until done. */
+int hs_forward_batch(const hs_model* m, hs_kv* const* kvs, const uint32_t* tokens, const uint32_t* pos, uint32_t n,
+                     hs_batch* b);
+/* Logits of sequence `slot` from the last hs_forward_batch. */
+int hs_batch_logits(hs_batch* b, uint32_t slot, float* host, uint64_t n);
+/* hs_seq_run for n sequences at once: sequence i uses kvs[i], its history
+ * tokens[i] (n_tokens[i] valid, capacity cap each), st[i], cfg[i], rng[i];
+ * all advance until each stops (or reaches stop_at_filled, 0 = never). */
+int hs_batch_seq_run(const hs_model* m, hs_kv* const* kvs, hs_batch* b, uint32_t n, uint32_t* const* tokens,
+                     uint64_t* n_tokens, uint64_t cap, hs_seq_state* st, const hs_sampler_cfg* cfg, hs_rng* rng,
+                     uint64_t stop_at_filled);
+/* The same in parts (device-resident stepping, for timing): begin uploads the
+ * state, step enqueues n_steps batched decode steps, end syncs and reads back. */
+int hs_batch_seq_begin(hs_batch* b, hs_kv* const* kvs, uint32_t n, uint32_t* const* tokens, const uint64_t* n_tokens,
+                       uint64_t cap, const hs_seq_state* st, const hs_sampler_cfg* cfg, const hs_rng* rng,
+                       uint64_t stop_at_filled);
+int hs_batch_seq_step(hs_batch* b, uint32_t n_steps);
+int hs_batch_seq_end(hs_batch* b, uint32_t* const* tokens, uint64_t* n_tokens, uint64_t cap, hs_seq_state* st,
+                     hs_rng* rng);
+/* The batch's CUDA stream (cudaStream_t), and kernels launched per step. */
+void* hs_batch_stream(hs_batch* b);
+int hs_batch_launches_per_step(hs_batch* b, uint32_t* out);
+
 /* The scratch's CUDA stream (cudaStream_t), for event timing. */
 void* hs_scratch_stream(hs_scratch* s);
 /* Kernel launches one hs_seq_step(s, 1) enqueues. */
