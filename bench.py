@@ -1,19 +1,25 @@
 """Decode throughput of the hotseat token loop on B200.
 
-Workload (the batch-1 configuration the metric is quoted on): the seeded
+Headline workload (the batch-64 configuration of the metric): the seeded
 random-init Qwen2.5-0.5B-shape GGUF (24 layers, d 896, 14/2 heads, ff 4864,
-vocab 151936, Q6_K embedding, Q4_K weights, f32 norms/biases), a 36-token
-uniform-random prompt, temperature 0.8, seed 99, 120 generated tokens, f32 KV.
+vocab 151936, Q6_K embedding, Q4_K weights, f32 norms/biases), 64 independent
+sequences, each with a 128-token uniform-random prompt, 256 generated tokens
+at temperature 0.8 with seed 99+i, f32 KV, decoded together on the
+tensor-core path (HS_NUMERIC_TC). One step = the 256-token decode phase of
+all 64 sequences (16,384 tokens: batched forward, device sampling and
+seq.rs commit per token) from their post-prompt state, restored before
+each step. `value` is decode tok/s with that state already in HBM; `e2e` is
+the same through hs_batch_seq_run with host token buffers.
 
-One step = the 120-token decode phase of that sequence (forward + device
-sampling + seq.rs commit per token) from its post-prefill state, which is
-restored before each step. `value` is decode tok/s with the state already in
-HBM; `e2e` is the same through hs_seq_run with host token buffers.
+The batch-1 configuration of the metric (36-token prompt, 120 tokens,
+temperature 0.8, seed 99, GPU-native numeric path) is measured in the same
+run and reported under "batch1".
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Under torchrun each rank runs its own sequence on its own GPU (independent
-sequences shard with no collective); value = all ranks' tokens / max time.
+Under torchrun each rank decodes its own 64 sequences on its own GPU
+(independent sequences shard with no collective); value = all ranks' tokens
+/ max time over ranks.
 """
 import argparse
 import json
@@ -22,7 +28,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 
 import numpy as np
@@ -32,26 +37,37 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s per GPU, Qwen2.5-0.5B-shape, batch 1/64; % of HBM roofline"
 UNIT = "tok/s"
-PROMPT_LEN, GEN, SEED, TEMP, MAX_CTX = 36, 120, 99, 0.8, 2048
 MODEL_SEED = 1234
-CTL_BYTES = 160  # sizeof(DevCtl), the device control block hs_seq_* copies each way
+SEED, TEMP = 99, 0.8
+B64_SEQS, B64_PROMPT, B64_GEN, B64_CTX = 64, 128, 256, 512
+B1_PROMPT, B1_GEN, B1_CTX = 36, 120, 2048
+CTL_BYTES = 160  # sizeof(DevCtl), the device control block copied each way per sequence
+D, FF, NH, NKV, HD, L, V = 896, 4864, 14, 2, 64, 24, 151936
+KV_ROW = L * 2 * NKV * HD * 4  # bytes of K and V one position adds across the layers (24,576)
+WEIGHT_BYTES = L * 2 * ((NH + 2 * NKV) * HD * D + D * NH * HD + 3 * FF * D) + V * D * 2
+SMALL_BYTES = L * 4 * (2 * D + (NH + 2 * NKV) * HD) + D * 4
 
 
 def workload_config():
-    return {"workload": "qwen2.5-0.5b-shape decode, batch 1, prompt 36, gen 120, temp 0.8, seed 99, f32 KV",
+    return {"workload": "qwen2.5-0.5b-shape batched decode: 64 sequences, prompt 128, gen 256, temp 0.8, "
+                        "seed 99+i, f32 KV",
             "model_shape": "24L d896 14/2h hd64 ff4864 vocab151936 Q6_K-embd Q4_K-weights",
-            "max_ctx": MAX_CTX, "l2": "weights 0.99 GB stream per token > 126 MB L2 (no flush needed)"}
+            "global_batch": B64_SEQS, "max_ctx": B64_CTX,
+            "l2": "weights 0.99 GB stream per decode step > 126 MB L2 (no flush needed)"}
 
 
-def bytes_per_token_avg():
-    """Algorithmic HBM bytes per decode token, averaged over positions 36..155:
-    f16 weights + f32 norms/biases + KV read (pos+1 rows) + KV write."""
-    d, ff, nh, nkv, hd, L, V = 896, 4864, 14, 2, 64, 24, 151936
-    w = L * 2 * ((nh + 2 * nkv) * hd * d + d * nh * hd + 3 * ff * d) + V * d * 2
-    small = L * 4 * (2 * d + (nh + 2 * nkv) * hd) + d * 4
-    kv_row = L * 2 * nkv * hd * 4
-    kv = np.mean([(p + 1) * kv_row + kv_row for p in range(PROMPT_LEN, PROMPT_LEN + GEN)])
-    return w + small + kv
+def b64_bytes_per_step():
+    """Algorithmic HBM bytes of one batched decode step (64 tokens), averaged
+    over the decode phase: f16 weights + norms/biases once, each sequence's KV
+    read (pos+1 rows) and write, and the logits written and read back."""
+    kv = np.mean([B64_SEQS * ((p + 1) * KV_ROW + KV_ROW) for p in range(B64_PROMPT, B64_PROMPT + B64_GEN)])
+    logits = B64_SEQS * V * 4 * 2
+    return WEIGHT_BYTES + SMALL_BYTES + kv + logits
+
+
+def b1_bytes_per_token():
+    kv = np.mean([(p + 1) * KV_ROW + KV_ROW for p in range(B1_PROMPT, B1_PROMPT + B1_GEN)])
+    return WEIGHT_BYTES + SMALL_BYTES + kv
 
 
 def make_model(path):
@@ -59,9 +75,12 @@ def make_model(path):
     hs.write_synthetic_gguf(path, seed=MODEL_SEED, **hs.QWEN05)
 
 
-def prompt_tokens():
-    rng = np.random.default_rng(36)
-    return [int(t) for t in rng.integers(0, 151936, size=PROMPT_LEN)]
+def b64_prompts():
+    return [[int(t) for t in np.random.default_rng(128 + i).integers(0, V, size=B64_PROMPT)] for i in range(B64_SEQS)]
+
+
+def b1_prompt():
+    return [int(t) for t in np.random.default_rng(36).integers(0, V, size=B1_PROMPT)]
 
 
 class ClockSampler:
@@ -112,48 +131,225 @@ class ClockSampler:
                 "samples": len(loaded), "power_w_max": max(r[2] for r in rows), "reasons": reasons}
 
 
-def cpu_baseline(path, n_decode, threads):
+def cpu_sample(path, prompt, max_ctx, n_decode, threads):
     """The CPU restatement of the reference path (oracle/, test infrastructure
-    used here only as the baseline): prefill untimed, `n_decode` tokens timed."""
+    used here only as the baseline): prompt forwarded untimed, then `n_decode`
+    tokens timed. The reference decodes each sequence on its own thread over
+    one shared pool, so its throughput with many sequences is this rate."""
     from oracle import ffi
-    o = ffi.Model(path, max_ctx=MAX_CTX, threads=threads)
+    o = ffi.Model(path, max_ctx=max_ctx, threads=threads)
     kv = o.new_kv()
     cfg = ffi.default_cfg(temperature=TEMP, seed=SEED)
     rng = ffi.seeded_rng(SEED)
-    prompt = prompt_tokens()
-    toks, st, rng = o.run_seq(kv, prompt, GEN, cfg, rng, stop_at_filled=PROMPT_LEN)
+    toks, st, rng = o.run_seq(kv, prompt, 10 ** 6, cfg, rng, stop_at_filled=len(prompt))
     t0 = time.perf_counter()
-    toks, st, rng = o.run_seq(kv, toks, GEN, cfg, rng, state=st, stop_at_filled=PROMPT_LEN + n_decode)
-    dt = time.perf_counter() - t0
-    return n_decode / dt, toks
+    o.run_seq(kv, toks, 10 ** 6, cfg, rng, state=st, stop_at_filled=len(prompt) + n_decode)
+    return n_decode / (time.perf_counter() - t0)
+
+
+CPU_SAMPLE = "12 decode tokens of sequence 0 (128-token prompt forwarded untimed) on all host threads"
 
 
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU algorithm (its C++ restatement;
-    rustc is not available to build the Rust original) on the host cores."""
+    rustc is not available to build the Rust original) on the host cores,
+    on a bounded sample of the batch-64 workload."""
     if rank != 0:
         return
     from oracle import ffi
     ffi.build()
     threads = os.cpu_count() or 1
-    sample = 12
     with tempfile.TemporaryDirectory() as td:
         path = os.path.join(td, "qwen05.gguf")
         make_model(path)
+        prompt = b64_prompts()[0]
         vals = []
         for i in range(args.warmup + args.steps):
-            v, _ = cpu_baseline(path, sample, threads)
+            v = cpu_sample(path, prompt, B64_CTX, 12, threads)
             if i >= args.warmup:
                 vals.append(v)
     value = float(np.mean(vals))
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sample / value,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * 12 / value,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f16 weights)",
             "data": "synthetic", "config": workload_config(),
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"{sample} decode tokens per step after an untimed 36-token prefill"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": CPU_SAMPLE},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def max_over_ranks(x, world, torch, dist):
+    if world == 1:
+        return x
+    t = torch.tensor([x], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _copy_rng(hs, r):
+    c = hs.Rng()
+    c.s[:] = list(r.s)
+    c.draws = r.draws
+    return c
+
+
+def bench_batch64(hs, torch, dist, path, local, world, args):
+    m = hs.Model.load(path, max_ctx=B64_CTX, device=local, numeric=hs.NUMERIC_TC)
+    b = hs.Batch(m, B64_SEQS)
+    kvs = [m.kv() for _ in range(B64_SEQS)]
+    cfg = hs.SamplerCfg.default(temperature=TEMP, seed=SEED)
+    seqs = [dict(tokens=p, prompt_len=B64_PROMPT, max_tokens=B64_GEN, cfg=cfg, rng=hs.Rng.seed(SEED + i))
+            for i, p in enumerate(b64_prompts())]
+    # Prompt (untimed): the post-prompt state is every step's starting point.
+    pre = b.run_seqs(kvs, seqs, stop_at_filled=B64_PROMPT)
+    snap = [dict(tokens=list(t), prompt_len=B64_PROMPT, max_tokens=B64_GEN, cfg=cfg, rng=_copy_rng(hs, r),
+                 filled=st.filled) for t, st, r in pre]
+    n_steps = B64_PROMPT + B64_GEN - min(q["filled"] for q in snap)
+    stream = torch.cuda.ExternalStream(b.stream)
+
+    def fresh():
+        return [dict(q, rng=_copy_rng(hs, q["rng"])) for q in snap]
+
+    if args.profile_step:
+        for _ in range(3):
+            b.begin(kvs, fresh())
+            b.step(1)
+            b.end()
+        b.begin(kvs, fresh())
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_step")
+        b.step(1)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        b.end()
+        print(json.dumps({"profile_step": "done", "workload": "batch64", "launches": b.launches_per_step()}))
+        return None
+
+    def one(ev=None):
+        b.begin(kvs, fresh())
+        if ev:
+            ev[0].record(stream)
+        b.step(n_steps)
+        if ev:
+            ev[1].record(stream)
+        return b.end()
+
+    for _ in range(args.warmup):
+        ref = one()
+    gen_tokens = sum(len(t) for t, _, _ in ref) - sum(len(q["tokens"]) for q in snap)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        outs = [one(evs[i]) for i in range(args.steps)]
+        torch.cuda.synchronize()
+    for o in outs:
+        assert all(list(x[0]) == list(y[0]) for x, y in zip(o, ref)), "batched decode is not deterministic"
+    total_ms = max_over_ranks(float(sum(a.elapsed_time(z) for a, z in evs)), world, torch, dist)
+    if world > 1:
+        dist.barrier()
+    ms_per_step = total_ms / args.steps
+    value = world * gen_tokens * args.steps / (total_ms / 1000.0)
+
+    # end to end through hs_batch_seq_run with host buffers
+    e2e_ms = []
+    for _ in range(args.steps):
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        out = b.run_seqs(kvs, fresh())
+        z.record(stream)
+        z.synchronize()
+        e2e_ms.append(a.elapsed_time(z))
+        assert all(list(x[0]) == list(y[0]) for x, y in zip(out, ref))
+    e2e_total = max_over_ranks(float(sum(e2e_ms)), world, torch, dist)
+    e2e_value = world * gen_tokens * args.steps / (e2e_total / 1000.0)
+    h2d = sum(len(q["tokens"]) * 4 + CTL_BYTES for q in snap)
+    d2h = sum(len(t) * 4 + 2 * CTL_BYTES for t, _, _ in ref)
+    launches = b.launches_per_step()
+    res = dict(value=value, ms_per_step=ms_per_step, gen_tokens=gen_tokens, n_steps=n_steps, e2e_value=e2e_value,
+               h2d=h2d, d2h=d2h, gpu_launches=launches * n_steps * args.steps, launches_per_decode_step=launches,
+               clocks=clk.summary())
+    b.close()
+    m.close()
+    return res
+
+
+def bench_batch1(hs, torch, dist, path, local, world, args):
+    import ctypes as C
+    m = hs.Model.load(path, max_ctx=B1_CTX, device=local, numeric=hs.NUMERIC_FAST)
+    kv, s = m.kv(), m.scratch()
+    cfg = hs.SamplerCfg.default(temperature=TEMP, seed=SEED)
+    toks, st, rng = hs.run_seq(m, kv, s, b1_prompt(), B1_PROMPT, B1_GEN, cfg, hs.Rng.seed(SEED),
+                               stop_at_filled=B1_PROMPT)
+    snap_toks, snap_rng = np.array(toks, dtype=np.uint32), _copy_rng(hs, rng)
+    snap_state = (st.prompt_len, st.filled, st.max_tokens)
+    stream = torch.cuda.ExternalStream(s.stream)
+    lib = hs.lib()
+
+    def begin():
+        r = _copy_rng(hs, snap_rng)
+        sst = hs.SeqState(*snap_state, 0, 0)
+        hs._check(lib.hs_seq_begin(s._h, kv._h, hs._ptr(snap_toks), len(snap_toks), B1_CTX + 1, C.byref(sst),
+                                   C.byref(cfg), C.byref(r), 0))
+
+    def end():
+        out = np.zeros(B1_CTX + 1, dtype=np.uint32)
+        n = C.c_uint64()
+        sst, r = hs.SeqState(), hs.Rng()
+        hs._check(lib.hs_seq_end(s._h, hs._ptr(out), C.byref(n), out.size, C.byref(sst), C.byref(r)))
+        return out[: n.value]
+
+    n_steps = B1_PROMPT + B1_GEN - snap_state[1]
+    if args.profile_step:
+        for _ in range(3):
+            begin()
+            hs._check(lib.hs_seq_step(s._h, 1))
+            end()
+        begin()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_step")
+        hs._check(lib.hs_seq_step(s._h, 1))
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        end()
+        print(json.dumps({"profile_step": "done", "workload": "batch1", "launches": s.launches_per_step()}))
+        return None
+    for _ in range(args.warmup):
+        begin()
+        hs._check(lib.hs_seq_step(s._h, n_steps))
+        ref = end()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        begin()
+        evs[i][0].record(stream)
+        hs._check(lib.hs_seq_step(s._h, n_steps))
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    assert list(end()) == list(ref), "decode is not deterministic across steps"
+    total_ms = max_over_ranks(float(sum(a.elapsed_time(z) for a, z in evs)), world, torch, dist)
+    value = world * B1_GEN * args.steps / (total_ms / 1000.0)
+    e2e_ms = []
+    for _ in range(args.steps):
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        out, _, _ = hs.run_seq(m, kv, s, snap_toks, snap_state[0], snap_state[2], cfg, _copy_rng(hs, snap_rng),
+                               filled=snap_state[1])
+        z.record(stream)
+        z.synchronize()
+        e2e_ms.append(a.elapsed_time(z))
+        assert list(out) == list(ref)
+    e2e_total = max_over_ranks(float(sum(e2e_ms)), world, torch, dist)
+    res = dict(value=value, ms_per_step=total_ms / args.steps,
+               e2e_value=world * B1_GEN * args.steps / (e2e_total / 1000.0),
+               gpu_launches=s.launches_per_step() * n_steps * args.steps)
+    for o in (s, kv):
+        o.close()
+    m.close()
+    return res
 
 
 def main():
@@ -163,11 +359,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="hotseat", choices=["hotseat", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--numeric", default="fast", choices=["fast", "reference"],
-                    help="fast: GPU-native reduction order (logits within 1e-2 of the CPU path); "
-                         "reference: bit-identical to the CPU reference")
-    ap.add_argument("--profile-step", action="store_true",
-                    help="prefill, then run one decode token inside the NVTX range 'decode_step' and exit")
+    ap.add_argument("--no-batch1", action="store_true", help="skip the batch-1 items")
+    ap.add_argument("--profile-step", choices=["batch64", "batch1"],
+                    help="reach the post-prompt state, run ONE decode step inside the NVTX range 'decode_step', exit")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -191,159 +385,72 @@ def main():
     td = tempfile.mkdtemp(prefix="hsbench")
     path = os.path.join(td, "qwen05.gguf")
     make_model(path)
-    numeric = hs.NUMERIC_FAST if args.numeric == "fast" else hs.NUMERIC_REFERENCE
-    m = hs.Model.load(path, max_ctx=MAX_CTX, device=local, numeric=numeric)
-    kv, s = m.kv(), m.scratch()
-    cfg = hs.SamplerCfg.default(temperature=TEMP, seed=SEED)
-    prompt = prompt_tokens()
-    # Prefill (untimed): the post-prefill state is every step's starting point.
-    toks, st, rng = hs.run_seq(m, kv, s, prompt, PROMPT_LEN, GEN, cfg, hs.Rng.seed(SEED), stop_at_filled=PROMPT_LEN)
-    snap_toks, snap_rng = np.array(toks, dtype=np.uint32), hs.Rng()
-    snap_rng.s[:] = list(rng.s)
-    snap_rng.draws = rng.draws
-    snap_state = (st.prompt_len, st.filled, st.max_tokens)
-    stream = torch.cuda.ExternalStream(s.stream)
-    lib = hs.lib()
-    import ctypes as C
-
-    def begin():
-        r = hs.Rng()
-        r.s[:] = list(snap_rng.s)
-        r.draws = snap_rng.draws
-        sst = hs.SeqState(*snap_state, 0, 0)
-        hs._check(lib.hs_seq_begin(s._h, kv._h, hs._ptr(snap_toks), len(snap_toks), MAX_CTX + 1, C.byref(sst),
-                                   C.byref(cfg), C.byref(r), 0))
-
-    def end_check():
-        out = np.zeros(MAX_CTX + 1, dtype=np.uint32)
-        n = C.c_uint64()
-        sst, r = hs.SeqState(), hs.Rng()
-        hs._check(lib.hs_seq_end(s._h, hs._ptr(out), C.byref(n), out.size, C.byref(sst), C.byref(r)))
-        return out[: n.value], sst
-
-    n_steps = PROMPT_LEN + GEN - snap_state[1]  # forwards in the decode phase
-    if args.profile_step:
-        for _ in range(3):
-            begin()
-            hs._check(lib.hs_seq_step(s._h, 1))
-            end_check()
-        begin()
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_push("decode_step")
-        hs._check(lib.hs_seq_step(s._h, 1))
-        torch.cuda.synchronize()
-        torch.cuda.nvtx.range_pop()
-        end_check()
-        print(json.dumps({"profile_step": "done", "launches": s.launches_per_step()}))
-        return
-    for _ in range(args.warmup):
-        begin()
-        hs._check(lib.hs_seq_step(s._h, n_steps))
-        ref_toks, ref_st = end_check()
-    assert len(ref_toks) == PROMPT_LEN + GEN and ref_st.done_reason == 2
-
-    # ---- device-resident timing
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ms = []
-    with ClockSampler(local) as clk:
-        for i in range(args.steps):
-            begin()
-            evs[i][0].record(stream)
-            hs._check(lib.hs_seq_step(s._h, n_steps))
-            evs[i][1].record(stream)
-        torch.cuda.synchronize()
-    ms = [a.elapsed_time(b) for a, b in evs]
-    final_toks, _ = end_check()
-    assert list(final_toks) == list(ref_toks), "decode is not deterministic across steps"
-    total_ms = float(sum(ms))
-    if world > 1:
-        t = torch.tensor([total_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-        dist.barrier()
-    ms_per_step = total_ms / args.steps
-    tokens_per_step = GEN
-    value = world * tokens_per_step * args.steps / (total_ms / 1000.0)
-
-    # ---- end to end through the C ABI with host buffers
-    e2e_ms = []
-    for i in range(args.steps):
-        r = hs.Rng()
-        r.s[:] = list(snap_rng.s)
-        r.draws = snap_rng.draws
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        out_toks, out_st, _ = hs.run_seq(m, kv, s, snap_toks, snap_state[0], snap_state[2], cfg, r,
-                                         filled=snap_state[1])
-        b.record(stream)
-        b.synchronize()
-        e2e_ms.append(a.elapsed_time(b))
-        assert list(out_toks) == list(ref_toks)
-    e2e_total = float(sum(e2e_ms))
-    if world > 1:
-        t = torch.tensor([e2e_total], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_total = float(t.item())
-    e2e_value = world * tokens_per_step * args.steps / (e2e_total / 1000.0)
-
-    if rank == 0:
-        peaks = {}
-        try:
-            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-        except (OSError, ValueError):
-            pass
-        peak = peaks.get("hbm_gbs")
-        peak_src = "measured"
-        if not peak:
-            peak, peak_src = 6650.0, "fallback"
-        bpt = bytes_per_token_avg()
-        achieved = bpt * (tokens_per_step / (ms_per_step / 1000.0)) / 1e9
-        traffic = None
-        tp = os.path.join(ROOT, "profiles", "decode_step_traffic.txt")
-        if os.path.exists(tp):
-            try:
-                for ln in open(tp):
-                    if ln.startswith("dram_bytes_per_token"):
-                        traffic = float(ln.split()[1])
-            except (OSError, ValueError, IndexError):
-                traffic = None
-        cpu = None
-        if not args.no_cpu_baseline:
-            threads = os.cpu_count() or 1
-            cv, _ = cpu_baseline(path, 24, threads)
-            cpu = {"value": cv, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": "24 decode tokens of the same sequence after an untimed 36-token prefill"}
-        launches = s.launches_per_step() * n_steps * args.steps
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32 (f16 weights)", "data": "synthetic",
-            "config": dict(workload_config(), parallelism=f"replicas x{world}" if world > 1 else "1 GPU",
-                           numeric=args.numeric),
-            "roofline": {"bound": "hbm", "kernel": "decode step (k_gemv x121, k_attention x24, sampler x2)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": peak_src, "traffic": traffic,
-                         "bytes_per_token": bpt, "frac_of_8TBps_nominal": achieved / 8000.0},
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": len(snap_toks) * 4 + CTL_BYTES,
-                    "d2h_bytes_per_step": (PROMPT_LEN + GEN) * 4 + 2 * CTL_BYTES},
-            "gpu_launches": launches,
-            "clocks": clk.summary(),
-        }
-        print(json.dumps(line), flush=True)
-    for o in (s, kv):
-        o.close()
-    m.close()
     try:
-        os.remove(path)
-        os.rmdir(td)
-    except OSError:
-        pass
-    if world > 1:
-        dist.destroy_process_group()
+        if args.profile_step == "batch1":
+            bench_batch1(hs, torch, dist, path, local, world, args)
+            return
+        b64 = bench_batch64(hs, torch, dist, path, local, world, args)
+        if args.profile_step:
+            return
+        b1 = None if args.no_batch1 else bench_batch1(hs, torch, dist, path, local, world, args)
+        if rank == 0:
+            peaks = {}
+            try:
+                peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+            except (OSError, ValueError):
+                pass
+            peak, peak_src = peaks.get("hbm_gbs"), "measured"
+            if not peak:
+                peak, peak_src = 6650.0, "fallback"
+            step_bytes = b64_bytes_per_step()
+            step_s = b64["ms_per_step"] / 1000.0 / b64["n_steps"]  # one batched decode step (one graph)
+            achieved = step_bytes / step_s / 1e9
+            traffic = None
+            tp = os.path.join(ROOT, "profiles", "batch64_step_traffic.txt")
+            if os.path.exists(tp):
+                for ln in open(tp):
+                    if ln.startswith("dram_bytes_per_step"):
+                        traffic = float(ln.split()[1])
+            cpu = None
+            if not args.no_cpu_baseline:
+                threads = os.cpu_count() or 1
+                cv = cpu_sample(path, b64_prompts()[0], B64_CTX, 12, threads)
+                cpu = {"value": cv, "unit": UNIT, "cores": threads, "kind": "port", "sample": CPU_SAMPLE}
+            line = {
+                "metric": METRIC, "value": b64["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": b64["ms_per_step"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32 activations as f16 hi/lo pairs on tcgen05, f32 accumulate (f16 weights)",
+                "data": "synthetic",
+                "config": dict(workload_config(), parallelism=f"independent sequences x{world} GPUs" if world > 1
+                               else "1 GPU", numeric="tc", decode_steps_per_step=b64["n_steps"]),
+                "roofline": {"bound": "hbm",
+                             "kernel": "one batched decode step (graph of %d kernels)" % b64["launches_per_decode_step"],
+                             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                             "peak_source": peak_src, "traffic": traffic, "bytes_per_decode_step": step_bytes,
+                             "frac_of_8TBps_nominal": achieved / 8000.0},
+                "cpu_baseline": cpu,
+                "e2e": {"value": b64["e2e_value"], "unit": UNIT, "h2d_bytes_per_step": b64["h2d"],
+                        "d2h_bytes_per_step": b64["d2h"]},
+                "gpu_launches": b64["gpu_launches"] + (b1["gpu_launches"] if b1 else 0),
+                "clocks": b64["clocks"],
+            }
+            if b1:
+                b1_ach = b1_bytes_per_token() * b1["value"] / world / 1e9
+                line["batch1"] = {"workload": "1 sequence, prompt 36, gen 120, temp 0.8, seed 99, numeric fast",
+                                  "value": b1["value"], "unit": UNIT, "ms_per_step": b1["ms_per_step"],
+                                  "e2e": b1["e2e_value"],
+                                  "roofline": {"achieved": b1_ach, "peak": peak, "unit": "GB/s",
+                                               "frac": b1_ach / peak, "bytes_per_token": b1_bytes_per_token()}}
+            print(json.dumps(line), flush=True)
+    finally:
+        try:
+            os.remove(path)
+            os.rmdir(td)
+        except OSError:
+            pass
+        if world > 1:
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":
