@@ -26,7 +26,6 @@ namespace {
 
 __device__ __forceinline__ uint32_t ldv(const uint32_t* p) { return *(const volatile uint32_t*)p; }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void split_f16(float x, uint16_t* hi, uint16_t* lo) {
@@ -36,9 +35,30 @@ __device__ __forceinline__ void split_f16(float x, uint16_t* hi, uint16_t* lo) {
 }
 
 constexpr uint32_t kNormThreads = 256;
-constexpr uint32_t kNormMaxPer = 8;  // d <= 2048
+constexpr uint32_t kNormMaxChunks = 2;  // float4 chunks per thread: d <= 2048
+constexpr uint32_t kMaxParts = 32;      // split-K partials a consumer adds
+
+__device__ __forceinline__ float4 f4add(float4 a, float4 b) {
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+// Sum of `n` split partials of one float4 chunk, in split order; the loads
+// are issued eight at a time so they overlap.
+__device__ __forceinline__ float4 sum_parts(const float* base, uint64_t stride, uint32_t n) {
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (uint32_t s0 = 0; s0 < n; s0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (uint32_t j = 0; j < 8; j++)
+            if (s0 + j < n) v[j] = __ldcg(reinterpret_cast<const float4*>(base + (s0 + j) * stride));
+#pragma unroll
+        for (uint32_t j = 0; j < 8; j++)
+            if (s0 + j < n) acc = f4add(acc, v[j]);
+    }
+    return acc;
+}
 
 // ---------------------------------------------------------------- RMSNorm
+// Thread t owns the float4 chunks t and t + 256 of the row.
 __global__ void __launch_bounds__(kNormThreads) k_tc_norm(const TcNormArgs a) {
     __shared__ float red[kNormThreads / 32];
     const uint32_t slot = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -54,28 +74,28 @@ __global__ void __launch_bounds__(kNormThreads) k_tc_norm(const TcNormArgs a) {
         if (tid == 0) atomicOr(&ctl->err, ERR_TOKEN);
         return;
     }
-    const uint32_t d = a.d;
-    float v[kNormMaxPer];
+    const uint32_t d4 = a.d / 4;
+    float4 v[kNormMaxChunks];
     float ss = 0.0f;
 #pragma unroll
-    for (uint32_t j = 0; j < kNormMaxPer; j++) {
-        const uint32_t i = tid + j * kNormThreads;
-        v[j] = 0.0f;
-        if (i >= d) continue;
-        float x;
+    for (uint32_t j = 0; j < kNormMaxChunks; j++) {
+        const uint32_t c = tid + j * kNormThreads;
+        v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (c >= d4) continue;
+        float4 x;
         if (a.embd) {
-            x = h2f(a.embd[(size_t)token * d + i]);
+            const uint2 e = *reinterpret_cast<const uint2*>(a.embd + (size_t)token * a.d + 4 * c);
+            x = make_float4(h2f(e.x & 0xffff), h2f(e.x >> 16), h2f(e.y & 0xffff), h2f(e.y >> 16));
         } else {
-            x = a.x[(size_t)slot * d + i];
-            if (a.n_part) {
-                float p = 0.0f;
-                for (uint32_t s = 0; s < a.n_part; s++) p = __fadd_rn(p, __ldcg(a.part + s * a.part_stride + (size_t)slot * d + i));
-                x = __fadd_rn(x, p);
-            }
+            x = *reinterpret_cast<const float4*>(a.x + (size_t)slot * a.d + 4 * c);
+            if (a.n_part) x = f4add(x, sum_parts(a.part + (size_t)slot * a.d + 4 * c, a.part_stride, a.n_part));
         }
-        if (a.embd || a.n_part) a.x[(size_t)slot * d + i] = x;
+        if (a.embd || a.n_part) *reinterpret_cast<float4*>(a.x + (size_t)slot * a.d + 4 * c) = x;
         v[j] = x;
-        ss = __fmaf_rn(x, x, ss);
+        ss = __fmaf_rn(x.x, x.x, ss);
+        ss = __fmaf_rn(x.y, x.y, ss);
+        ss = __fmaf_rn(x.z, x.z, ss);
+        ss = __fmaf_rn(x.w, x.w, ss);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
@@ -84,15 +104,21 @@ __global__ void __launch_bounds__(kNormThreads) k_tc_norm(const TcNormArgs a) {
     float tot = 0.0f;
 #pragma unroll
     for (uint32_t w = 0; w < kNormThreads / 32; w++) tot = __fadd_rn(tot, red[w]);
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)d), a.eps)));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)a.d), a.eps)));
 #pragma unroll
-    for (uint32_t j = 0; j < kNormMaxPer; j++) {
-        const uint32_t i = tid + j * kNormThreads;
-        if (i >= d) continue;
-        uint16_t hi, lo;
-        split_f16(__fmul_rn(__fmul_rn(v[j], scale), a.g[i]), &hi, &lo);
-        a.out_hi[(size_t)slot * d + i] = hi;
-        a.out_lo[(size_t)slot * d + i] = lo;
+    for (uint32_t j = 0; j < kNormMaxChunks; j++) {
+        const uint32_t c = tid + j * kNormThreads;
+        if (c >= d4) continue;
+        const float4 g = *reinterpret_cast<const float4*>(a.g + 4 * c);
+        const float y[4] = {__fmul_rn(__fmul_rn(v[j].x, scale), g.x), __fmul_rn(__fmul_rn(v[j].y, scale), g.y),
+                            __fmul_rn(__fmul_rn(v[j].z, scale), g.z), __fmul_rn(__fmul_rn(v[j].w, scale), g.w)};
+        uint16_t hi[4], lo[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) split_f16(y[q], &hi[q], &lo[q]);
+        *reinterpret_cast<uint2*>(a.out_hi + (size_t)slot * a.d + 4 * c) =
+            make_uint2(hi[0] | (uint32_t)hi[1] << 16, hi[2] | (uint32_t)hi[3] << 16);
+        *reinterpret_cast<uint2*>(a.out_lo + (size_t)slot * a.d + 4 * c) =
+            make_uint2(lo[0] | (uint32_t)lo[1] << 16, lo[2] | (uint32_t)lo[3] << 16);
     }
     tr.exit();
 }
@@ -100,6 +126,8 @@ __global__ void __launch_bounds__(kNormThreads) k_tc_norm(const TcNormArgs a) {
 // ---------------------------------------------------------------- attention
 constexpr uint32_t kAttnThreads = 256;
 constexpr uint32_t kChunk = 64;  // cached positions per K / V chunk
+constexpr uint32_t kNb = 4;      // chunk buffers in flight
+__device__ __forceinline__ void cp_wait_nb() { asm volatile("cp.async.wait_group %0;" ::"n"(kNb - 1) : "memory"); }
 
 template <int HD>
 __global__ void __launch_bounds__(kAttnThreads) k_tc_attention(const TcAttnArgs a) {
@@ -113,8 +141,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_tc_attention(const TcAttnArgs 
     float* qs = sm;                                  // [G][HD]
     float* kn = qs + 8 * HD;                         // [HD]
     float* vn = kn + HD;                             // [HD]
-    float* buf = vn + HD;                            // [2][kChunk][RS]
-    float* sc = buf + 2 * kChunk * RS;               // [G][max_ctx]
+    float* buf = vn + HD;                            // [kNb][kChunk][RS]
+    float* sc = buf + kNb * kChunk * RS;             // [G][max_ctx]
     float* inv = sc + (size_t)G * a.max_ctx;         // [8]
     const KTrace tr(a.trace, a.trace_slot);
     tr.enter();
@@ -137,15 +165,13 @@ __global__ void __launch_bounds__(kAttnThreads) k_tc_attention(const TcAttnArgs 
     }
     // q (G heads), k, v: split-K partials in split order, then the bias.
     const uint32_t qrow0 = kvh * G * HD, krow0 = a.nh * HD + kvh * HD, vrow0 = (a.nh + a.nkv) * HD + kvh * HD;
-    for (uint32_t idx = tid; idx < (G + 2) * HD; idx += kAttnThreads) {
+    for (uint32_t c = tid; c < (G + 2) * HD / 4; c += kAttnThreads) {
+        const uint32_t idx = 4 * c;
         const uint32_t row = idx < G * HD ? qrow0 + idx : (idx < (G + 1) * HD ? krow0 + idx - G * HD : vrow0 + idx - (G + 1) * HD);
-        float p = 0.0f;
-        for (uint32_t s = 0; s < a.n_part; s++)
-            p = __fadd_rn(p, __ldcg(a.qkv_part + s * a.part_stride + (size_t)slot * a.qkv_rows + row));
-        p = __fadd_rn(p, a.bias[row]);
-        if (idx < G * HD) qs[idx] = p;
-        else if (idx < (G + 1) * HD) kn[idx - G * HD] = p;
-        else vn[idx - (G + 1) * HD] = p;
+        float4 p = sum_parts(a.qkv_part + (size_t)slot * a.qkv_rows + row, a.part_stride, a.n_part);
+        p = f4add(p, *reinterpret_cast<const float4*>(a.bias + row));
+        float* dst = idx < G * HD ? qs + idx : (idx < (G + 1) * HD ? kn + idx - G * HD : vn + idx - (G + 1) * HD);
+        *reinterpret_cast<float4*>(dst) = p;
     }
     __syncthreads();
     // RoPE (NeoX pairs i, i + HD/2) on the query heads and the key.
@@ -172,97 +198,94 @@ __global__ void __launch_bounds__(kAttnThreads) k_tc_attention(const TcAttnArgs 
             atomicOr(reinterpret_cast<unsigned long long*>(&dirty[pg >> 6]), 1ull << (pg & 63));
     }
 
-    const uint32_t n = pos + 1, nchunks = (n + kChunk - 1) / kChunk;
-    // Chunk c of K (is_v = 0) or V (1) into buf[c & 1]; the row at `pos`
-    // comes from shared memory (this CTA just wrote it).
-    auto load_chunk = [&](uint32_t c, uint32_t is_v) {
-        float* dst = buf + (c & 1) * kChunk * RS;
-        const uint32_t c0 = c * kChunk, cnt = n - c0 < kChunk ? n - c0 : kChunk;
-        for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += kAttnThreads) {
-            const uint32_t r = idx / (HD / 4), c4 = idx % (HD / 4);
-            if (c0 + r == pos) {
-                const float* src = is_v ? vn : kn;
-                *reinterpret_cast<float4*>(dst + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(src + 4 * c4);
-            } else {
-                cp_async16(dst + r * RS + 4 * c4, kv + row_off(c0 + r, is_v) + 4 * c4);
+    const uint32_t n = pos + 1, nchunks = (n + kChunk - 1) / kChunk, items = 2 * nchunks;
+    // One pipeline over all K chunks then all V chunks, kNb buffers deep: item
+    // i lands in buf[i % kNb]; the row at `pos` comes from shared memory (this
+    // CTA just wrote it). Every iteration commits one cp.async group (empty
+    // past the end), so "item i is complete" is wait_group(kNb - 1).
+    auto issue = [&](uint32_t it) {
+        if (it < items) {
+            const uint32_t is_v = it >= nchunks, c = is_v ? it - nchunks : it;
+            float* dst = buf + (it % kNb) * kChunk * RS;
+            const uint32_t c0 = c * kChunk, cnt = n - c0 < kChunk ? n - c0 : kChunk;
+            for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += kAttnThreads) {
+                const uint32_t r = idx / (HD / 4), c4 = idx % (HD / 4);
+                if (c0 + r == pos) {
+                    const float* src = is_v ? vn : kn;
+                    *reinterpret_cast<float4*>(dst + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(src + 4 * c4);
+                } else {
+                    cp_async16(dst + r * RS + 4 * c4, kv + row_off(c0 + r, is_v) + 4 * c4);
+                }
             }
         }
         cp_commit();
     };
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-    // Scores: thread t takes position t % 64 of the chunk and heads t/64, t/64 + 4.
-    load_chunk(0, 0);
-    for (uint32_t c = 0; c < nchunks; c++) {
-        if (c + 1 < nchunks) {
-            load_chunk(c + 1, 0);
-            cp_wait_1();
-        } else {
-            cp_wait_0();
-        }
-        __syncthreads();
-        const uint32_t c0 = c * kChunk, r = tid % kChunk, p = c0 + r;
-        if (p < n) {
-            const float4* k4 = reinterpret_cast<const float4*>(buf + (c & 1) * kChunk * RS + r * RS);
-            for (uint32_t h = tid / kChunk; h < G; h += kAttnThreads / kChunk) {
-                const float4* q4 = reinterpret_cast<const float4*>(qs + h * HD);
-                float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-#pragma unroll
-                for (uint32_t d4 = 0; d4 < HD / 4; d4++) {
-                    const float4 kk = k4[d4], qq = q4[d4];
-                    s0 = __fmaf_rn(qq.x, kk.x, s0);
-                    s1 = __fmaf_rn(qq.y, kk.y, s1);
-                    s2 = __fmaf_rn(qq.z, kk.z, s2);
-                    s3 = __fmaf_rn(qq.w, kk.w, s3);
-                }
-                sc[(size_t)h * a.max_ctx + p] = __fmul_rn(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), scale);
-            }
-        }
-        __syncthreads();
-    }
-    // Softmax: warp h owns head h (lane-strided partials, fixed xor tree).
-    if (warp < G) {
-        float* s = sc + (size_t)warp * a.max_ctx;
-        float mx = -FLT_MAX;
-        for (uint32_t p = lane; p < n; p += 32) mx = fmaxf(mx, s[p]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float sum = 0.0f;
-        for (uint32_t p = lane; p < n; p += 32) {
-            const float e = __expf(__fsub_rn(s[p], mx));
-            s[p] = e;
-            sum = __fadd_rn(sum, e);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-        if (lane == 0) inv[warp] = __fdiv_rn(1.0f, sum);
-    }
-    // P.V: thread t owns dimension t % HD of heads t/HD, t/HD + HSETS, ...
     float acc[HPT];
 #pragma unroll
     for (uint32_t j = 0; j < HPT; j++) acc[j] = 0.0f;
     const uint32_t dd = tid % HD, hs0 = tid / HD;
-    load_chunk(0, 1);
-    for (uint32_t c = 0; c < nchunks; c++) {
-        if (c + 1 < nchunks) {
-            load_chunk(c + 1, 1);
-            cp_wait_1();
-        } else {
-            cp_wait_0();
-        }
+    for (uint32_t it = 0; it + 1 < kNb; it++) issue(it);
+    for (uint32_t it = 0; it < items; it++) {
+        issue(it + kNb - 1);
+        cp_wait_nb();
         __syncthreads();
-        const uint32_t c0 = c * kChunk, cnt = n - c0 < kChunk ? n - c0 : kChunk;
-        const float* vb = buf + (c & 1) * kChunk * RS;
+        const float* cb = buf + (it % kNb) * kChunk * RS;
+        if (it < nchunks) {
+            // Scores: thread t takes position t % 64 of the chunk and heads t/64, t/64 + 4.
+            const uint32_t c0 = it * kChunk, r = tid % kChunk, p = c0 + r;
+            if (p < n) {
+                const float4* k4 = reinterpret_cast<const float4*>(cb + r * RS);
+                for (uint32_t h = tid / kChunk; h < G; h += kAttnThreads / kChunk) {
+                    const float4* q4 = reinterpret_cast<const float4*>(qs + h * HD);
+                    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
 #pragma unroll
-        for (uint32_t j = 0; j < HPT; j++) {
-            const uint32_t h = hs0 + j * HSETS;
-            if (h >= G) break;
-            const float* ph = sc + (size_t)h * a.max_ctx + c0;
-            float s = acc[j];
-            for (uint32_t r = 0; r < cnt; r++) s = __fmaf_rn(ph[r], vb[r * RS + dd], s);
-            acc[j] = s;
+                    for (uint32_t d4 = 0; d4 < HD / 4; d4++) {
+                        const float4 kk = k4[d4], qq = q4[d4];
+                        s0 = __fmaf_rn(qq.x, kk.x, s0);
+                        s1 = __fmaf_rn(qq.y, kk.y, s1);
+                        s2 = __fmaf_rn(qq.z, kk.z, s2);
+                        s3 = __fmaf_rn(qq.w, kk.w, s3);
+                    }
+                    sc[(size_t)h * a.max_ctx + p] = __fmul_rn(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), scale);
+                }
+            }
+        } else {
+            if (it == nchunks) {
+                // Softmax: warp h owns head h (lane-strided partials, fixed xor tree).
+                if (warp < G) {
+                    float* sh = sc + (size_t)warp * a.max_ctx;
+                    float mx = -FLT_MAX;
+                    for (uint32_t p = lane; p < n; p += 32) mx = fmaxf(mx, sh[p]);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    float sum = 0.0f;
+                    for (uint32_t p = lane; p < n; p += 32) {
+                        const float e = __expf(__fsub_rn(sh[p], mx));
+                        sh[p] = e;
+                        sum = __fadd_rn(sum, e);
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+                    if (lane == 0) inv[warp] = __fdiv_rn(1.0f, sum);
+                }
+                __syncthreads();
+            }
+            // P.V: thread t owns dimension t % HD of heads t/HD, t/HD + HSETS, ...
+            const uint32_t c0 = (it - nchunks) * kChunk, cnt = n - c0 < kChunk ? n - c0 : kChunk;
+#pragma unroll
+            for (uint32_t j = 0; j < HPT; j++) {
+                const uint32_t h = hs0 + j * HSETS;
+                if (h >= G) break;
+                const float* ph = sc + (size_t)h * a.max_ctx + c0;
+                float sacc = acc[j];
+                for (uint32_t r = 0; r < cnt; r++) sacc = __fmaf_rn(ph[r], cb[r * RS + dd], sacc);
+                acc[j] = sacc;
+            }
         }
         __syncthreads();
     }
+    cp_wait_0();
 #pragma unroll
     for (uint32_t j = 0; j < HPT; j++) {
         const uint32_t h = hs0 + j * HSETS;
@@ -294,7 +317,7 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaS
 
 size_t tc_attention_smem(uint32_t head_dim, uint32_t groups, uint32_t max_ctx) {
     const size_t rs = head_dim + 4;
-    return (8 * head_dim + 2 * head_dim + 2 * kChunk * rs + (size_t)groups * max_ctx + 8) * sizeof(float);
+    return (8 * head_dim + 2 * head_dim + kNb * kChunk * rs + (size_t)groups * max_ctx + 8) * sizeof(float);
 }
 
 cudaError_t tc_ops_set_smem_limits(int optin) {
@@ -304,7 +327,7 @@ cudaError_t tc_ops_set_smem_limits(int optin) {
 }
 
 cudaError_t launch_tc_norm(const TcNormArgs& a, uint32_t slots, cudaStream_t st) {
-    if (a.d > kNormThreads * kNormMaxPer) return cudaErrorInvalidValue;
+    if (a.d % 4 || a.d > kNormThreads * kNormMaxChunks * 4 || a.n_part > kMaxParts) return cudaErrorInvalidValue;
     TcNormArgs c = a;
     void* args[] = {&c};
     return launch_pdl(reinterpret_cast<const void*>(k_tc_norm), dim3(slots), dim3(kNormThreads), 0, st, args);
