@@ -667,6 +667,164 @@ __global__ void __launch_bounds__(256) k_sample_cand(const SampleArgs a0) {
     tr.exit();
 }
 
+// Candidate kernel for wide slices (a multiple of 1024 logits per CTA, top
+// keys kmax <= 64): the same output as k_sample_cand (the CTA's kmax best
+// keys in key order) from an exact radix select instead of sorting. Each
+// thread holds slice/256 keys; 8-bit digits of the 64-bit key, most
+// significant first, narrow the prefix of the kmax-th smallest key until the
+// boundary bin is taken whole; the selected keys (exactly kmax, keys are
+// unique) are then ranked against each other.
+__global__ void __launch_bounds__(256) k_sample_cand_wide(const SampleArgs a0) {
+    const SampleArgs a = slot_args(a0);
+    constexpr uint32_t PER = kMaxSlice / 256;
+    __shared__ uint32_t win_cnt[kMaxSlice];
+    __shared__ uint32_t hist[256];
+    __shared__ uint64_t sel_keys[kMaxTopK];
+    __shared__ uint32_t n_sel, sh_digit, sh_need;
+    __shared__ float bv_s[8];
+    __shared__ uint32_t bi_s[8];
+    __shared__ DevCtl cs;
+    const uint32_t tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const uint32_t slice = a.slice, per = slice / 256;
+    const KTrace tr(a.trace, a.trace_slot);
+    tr.enter();
+    load_ctl(&cs, a.ctl);
+    __syncthreads();
+    const DevCtl* c = &cs;
+    const float pen = c->repeat_penalty;
+    const uint64_t nt = c->n_tokens;
+    const uint64_t nw = (pen != 1.0f && c->repeat_last_n > 0) ? (c->repeat_last_n < nt ? c->repeat_last_n : nt) : 0;
+    const uint32_t cta_base = blockIdx.x * slice;
+    const bool need = seq_needs_sample(c);
+    if (need && nw) {
+        for (uint32_t i = tid; i < slice; i += blockDim.x) win_cnt[i] = 0;
+        __syncthreads();
+        for (uint64_t i = nt - nw + tid; i < nt; i += blockDim.x) {
+            const uint32_t t = __ldcg(a.tokens + i);
+            if (t >= cta_base && t < cta_base + slice) atomicAdd(&win_cnt[t - cta_base], 1u);
+        }
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    tr.waited();
+    if (!need) return;
+    __syncthreads();
+    // Element j of thread t is id cta_base + j*256 + t (coalesced loads).
+    float v[PER];
+#pragma unroll
+    for (uint32_t j = 0; j < PER; j++) {
+        const uint32_t e = cta_base + j * 256 + tid;
+        v[j] = (j < per && e < a.vocab) ? __ldcg(a.logits + e) : 0.0f;
+        if (nw && j < per && e < a.vocab) {
+            // sampler.rs:105-110, each occurrence in the window once
+            uint32_t times = win_cnt[e - cta_base];
+            while (times--) v[j] = v[j] > 0.0f ? __fdiv_rn(v[j], pen) : __fmul_rn(v[j], pen);
+        }
+    }
+    if (c->temperature <= 0.0f) {
+        float bv = 0.0f;
+        uint32_t bi = 0xffffffffu;
+#pragma unroll
+        for (uint32_t j = 0; j < PER; j++) {
+            const uint32_t e = cta_base + j * 256 + tid;
+            if (j < per && e < a.vocab && !(v[j] != v[j]) && v[j] > __int_as_float(0xff800000) &&
+                arg_better(v[j], e, bv, bi)) {
+                bv = v[j];
+                bi = e;
+            }
+        }
+        warp_argbest(&bv, &bi);
+        if (lane == 0) {
+            bv_s[w] = bv;
+            bi_s[w] = bi;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float fv = bv_s[0];
+            uint32_t fi = bi_s[0];
+            for (int k = 1; k < 8; k++)
+                if (arg_better(bv_s[k], bi_s[k], fv, fi)) {
+                    fv = bv_s[k];
+                    fi = bi_s[k];
+                }
+            a.argbuf[blockIdx.x] = ((uint64_t)__float_as_uint(fv) << 32) | fi;
+        }
+        return;
+    }
+    // Keys ascend best-first; ids past the vocabulary (or past the slice) get
+    // keys above every real key, as in k_sample_cand.
+    uint64_t key[PER];
+#pragma unroll
+    for (uint32_t j = 0; j < PER; j++) {
+        const uint32_t e = cta_base + j * 256 + tid;
+        key[j] = (j < per && e < a.vocab) ? cand_key(v[j], e) : ~0ull - e;
+    }
+    const uint32_t K = a.kmax;
+    uint64_t prefix = 0, mask = 0;  // bits of the K-th key fixed so far
+    uint32_t needk = K;              // keys still to take at or below the prefix
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        hist[tid] = 0;
+        __syncthreads();
+#pragma unroll
+        for (uint32_t j = 0; j < PER; j++)
+            if (j < per && (key[j] & mask) == prefix) atomicAdd(&hist[(key[j] >> shift) & 255], 1u);
+        __syncthreads();
+        if (w == 0) {
+            // Inclusive scan over the 256 bins, 8 per lane, lanes in order.
+            uint32_t h8[8], s = 0;
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                h8[q] = hist[lane * 8 + q];
+                s += h8[q];
+            }
+            uint32_t incl = s;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= (uint32_t)o) incl += y;
+            }
+            uint32_t run = incl - s;
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+                if (run < needk && run + h8[q] >= needk) {
+                    sh_digit = lane * 8 + q;
+                    sh_need = needk - run;  // keys to take from the boundary bin
+                }
+                run += h8[q];
+            }
+        }
+        __syncthreads();
+        const uint32_t d = sh_digit;
+        prefix |= (uint64_t)d << shift;
+        mask |= 255ull << shift;
+        const bool whole = sh_need == hist[d];
+        needk = sh_need;
+        __syncthreads();
+        if (whole) break;
+    }
+    // Selected: keys below the prefix's bin, plus the whole boundary bin.
+    if (tid == 0) n_sel = 0;
+    __syncthreads();
+#pragma unroll
+    for (uint32_t j = 0; j < PER; j++) {
+        if (j >= per) continue;
+        const uint64_t kk = key[j];
+        if ((kk & mask) < prefix || (kk & mask) == prefix) {
+            const uint32_t at = atomicAdd(&n_sel, 1u);
+            if (at < kMaxTopK) sel_keys[at] = kk;
+        }
+    }
+    __syncthreads();
+    const uint32_t ns = n_sel < K ? n_sel : K;
+    for (uint32_t i = tid; i < ns; i += blockDim.x) {
+        const uint64_t kk = sel_keys[i];
+        uint32_t rank = 0;
+        for (uint32_t q = 0; q < ns; q++) rank += sel_keys[q] < kk ? 1u : 0u;
+        a.cand[(size_t)blockIdx.x * K + rank] = kk;
+    }
+    tr.exit();
+}
+
 constexpr uint32_t kFinalThreads = 256;
 
 __global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs a0) {
@@ -960,7 +1118,10 @@ size_t sample_final_smem(uint32_t n_cta, uint32_t kmax) {
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st) {
     const uint32_t slots = a.slots ? a.slots : 1;
-    cudaError_t e = launch_pdl(k_sample_cand, dim3(a.n_cta, slots), dim3(256), 0, st, a);
+    const bool wide = a.slice > kSampleSlice;
+    if (wide && (a.slice % 256 || a.slice > kMaxSlice || a.kmax > kMaxTopK)) return cudaErrorInvalidValue;
+    cudaError_t e = wide ? launch_pdl(k_sample_cand_wide, dim3(a.n_cta, slots), dim3(256), 0, st, a)
+                         : launch_pdl(k_sample_cand, dim3(a.n_cta, slots), dim3(256), 0, st, a);
     if (e != cudaSuccess) return e;
     return launch_pdl(k_sample_final, dim3(1, slots), dim3(kFinalThreads), sample_final_smem(a.n_cta, a.kmax), st, a);
 }

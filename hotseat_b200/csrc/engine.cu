@@ -1374,7 +1374,7 @@ struct hs_batch {
     uint32_t** track_tab = nullptr;
     void** tab_h = nullptr;        // pinned staging for the three tables
     uint64_t *cand = nullptr, *argbuf = nullptr;
-    uint32_t n_cta = 0, kmax_alloc = 0;
+    uint32_t n_cta = 0, kmax_alloc = 0, slice = 0;
     uint32_t* err = nullptr;       // GEMM error word (device)
     uint32_t err_h = 0;
     uint32_t layout = 0, page_shift = 0;
@@ -1511,6 +1511,7 @@ SampleArgs batch_sample_args(hs_batch* b, uint32_t n, uint32_t kmax) {
     a.logits_stride = b->m->cfg.vocab;
     a.cand_stride = (uint64_t)b->n_cta * kmax;
     a.tok_tab = b->tok_tab;
+    a.slice = b->slice;
     return a;
 }
 
@@ -1610,7 +1611,10 @@ int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out) {
         return e == cudaSuccess ? (int)HS_OK : fail(HS_E_CUDA, cudaGetErrorString(e));
     };
     b->tok_cap = (uint64_t)c.max_ctx + 1;
-    b->n_cta = (c.vocab + kSampleSlice - 1) / kSampleSlice;
+    // Large vocabularies take 4096 logits per candidate CTA (fewer, longer
+    // CTAs for many sequences at once); the selection is exact either way.
+    b->slice = c.vocab > kMaxSlice ? kMaxSlice : kSampleSlice;
+    b->n_cta = (c.vocab + b->slice - 1) / b->slice;
     if (b->n_cta > 256) return fail(HS_E_UNSUPPORTED, "vocab too large for the device sampler");
     b->kmax_alloc = b->n_cta > 1 ? kMaxTopK : kSampleSlice;
     int rc;

@@ -73,6 +73,9 @@ struct SampleArgs {
     uint32_t slots;
     uint64_t logits_stride, cand_stride;
     uint32_t* const* tok_tab;
+    // Logits per candidate CTA: 0 = kSampleSlice; else a multiple of it up to
+    // kMaxSlice, allowed only when kmax <= 64.
+    uint32_t slice;
 };
 
 int launch_dequant(uint32_t ty, const void* src, uint64_t n, void* dst, cudaStream_t st, int n_sm);
@@ -167,6 +170,7 @@ cudaError_t launch_tc_norm(const TcNormArgs& a, uint32_t slots, cudaStream_t st)
 cudaError_t launch_tc_attention(uint32_t head_dim, const TcAttnArgs& a, uint32_t slots, size_t smem, cudaStream_t st);
 
 constexpr uint32_t kSampleSlice = 1024;  // logits per CTA of the candidate kernel
+constexpr uint32_t kMaxSlice = 4096;     // largest slice a candidate CTA takes
 constexpr uint32_t kMaxTopK = 64;        // top_k supported by the device sampler
 
 }  // namespace hs
