@@ -382,6 +382,11 @@ int check_kv(const hs_model* m, const hs_kv* kv) {
     return HS_OK;
 }
 
+uint32_t env_u32(const char* name, uint32_t dflt) {
+    const char* v = std::getenv(name);
+    return v && *v ? (uint32_t)std::strtoul(v, nullptr, 10) : dflt;
+}
+
 // Tensor-core GEMM plan: weight-row tile, K splits and pipeline depth so
 // that about one work unit lands on each SM.
 //   TC_SILU : gate+up rows of one tile per CTA, no split (the SiLU needs
@@ -413,11 +418,21 @@ int plan_tc(TcGemmPlan* p, int epi, uint32_t rows, uint32_t K, const uint16_t* w
             }
         }
     } else {
-        uint32_t nt = K >= 2048 ? 128 : 64;
-        while (nt > 16 && nt / 2 >= rows) nt /= 2;
-        p->n_tile = nt;
-        const uint32_t tiles = (rows + nt - 1) / nt;
-        p->splits = std::max<uint32_t>(1, std::min<uint32_t>(kt_n, sm / std::max<uint32_t>(tiles, 1)));
+        // The most CTAs in one wave with at most HS_TC_MAX_SPLITS (32) partials for the
+        // consumer to add, then the wider tile (fewer activation re-reads).
+        const uint32_t max_splits = env_u32("HS_TC_MAX_SPLITS", 32);
+        uint32_t best = 0;
+        for (uint32_t nt : {128u, 64u, 32u, 16u}) {
+            const uint32_t tiles = (rows + nt - 1) / nt;
+            if (tiles > sm) continue;
+            const uint32_t S = std::max<uint32_t>(1, std::min<uint32_t>({kt_n, max_splits, sm / tiles}));
+            if (tiles * S > best) {
+                best = tiles * S;
+                p->n_tile = nt;
+                p->splits = S;
+            }
+        }
+        if (!best) return fail(HS_E_UNSUPPORTED, "no split-K plan fits");
     }
     p->n_tiles = (rows + p->n_tile - 1) / p->n_tile;
     const uint32_t units = p->n_tiles * p->splits;
