@@ -48,11 +48,11 @@ WEIGHT_BYTES = L * 2 * ((NH + 2 * NKV) * HD * D + D * NH * HD + 3 * FF * D) + V 
 SMALL_BYTES = L * 4 * (2 * D + (NH + 2 * NKV) * HD) + D * 4
 
 
-def workload_config():
-    return {"workload": "qwen2.5-0.5b-shape batched decode: 64 sequences, prompt 128, gen 256, temp 0.8, "
+def workload_config(world=1):
+    return {"workload": "qwen2.5-0.5b-shape batched decode: 64 sequences per GPU, prompt 128, gen 256, temp 0.8, "
                         "seed 99+i, f32 KV",
             "model_shape": "24L d896 14/2h hd64 ff4864 vocab151936 Q6_K-embd Q4_K-weights",
-            "global_batch": B64_SEQS, "max_ctx": B64_CTX,
+            "global_batch": B64_SEQS * world, "max_ctx": B64_CTX,
             "l2": "weights 0.99 GB stream per decode step > 126 MB L2 (no flush needed)"}
 
 
@@ -422,7 +422,7 @@ def main():
                 "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32 activations as f16 hi/lo pairs on tcgen05, f32 accumulate (f16 weights)",
                 "data": "synthetic",
-                "config": dict(workload_config(), parallelism=f"independent sequences x{world} GPUs" if world > 1
+                "config": dict(workload_config(world), parallelism=f"independent sequences x{world} GPUs" if world > 1
                                else "1 GPU", numeric="tc", decode_steps_per_step=b64["n_steps"]),
                 "roofline": {"bound": "hbm",
                              "kernel": "one batched decode step (graph of %d kernels)" % b64["launches_per_decode_step"],
