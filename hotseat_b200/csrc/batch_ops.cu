@@ -142,8 +142,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_tc_attention(const TcAttnArgs 
     float* kn = qs + 8 * HD;                         // [HD]
     float* vn = kn + HD;                             // [HD]
     float* buf = vn + HD;                            // [kNb][kChunk][RS]
-    float* sc = buf + kNb * kChunk * RS;             // [G][max_ctx]
-    float* inv = sc + (size_t)G * a.max_ctx;         // [8]
+    // [G][max_ctx] scores: shared memory, or this CTA's block of a global
+    // buffer when they do not fit.
+    float* sc = a.sc_global ? a.sc_global + ((size_t)blockIdx.y * a.nkv + blockIdx.x) * G * a.max_ctx
+                            : buf + kNb * kChunk * RS;
+    float* inv = buf + kNb * kChunk * RS + (a.sc_global ? 0 : (size_t)G * a.max_ctx);  // [8]
     const KTrace tr(a.trace, a.trace_slot);
     tr.enter();
     DevCtl* ctl = a.ctl + slot;

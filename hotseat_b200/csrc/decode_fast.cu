@@ -292,7 +292,9 @@ __global__ void __launch_bounds__(256) k_attention_fast(const AttnArgs a) {
     float* kb = part + 8 * HD;   // [PRE][RS]
     float* vb = kb + PRE * RS;   // [PRE][RS]
     float* cb = vb + PRE * RS;   // [CH][RS]
-    float* sc = cb + CH * RS;    // [max_ctx]
+    // [max_ctx] scores: shared memory, or this head's row of a global buffer
+    // when max_ctx scores do not fit next to the K/V staging.
+    float* sc = a.sc_global ? a.sc_global + (size_t)blockIdx.x * a.max_ctx : cb + CH * RS;
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const KTrace tr(a.trace, a.trace_slot);
     tr.enter();

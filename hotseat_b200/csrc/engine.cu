@@ -215,6 +215,7 @@ struct hs_model {
     std::vector<LayerDev> layers;
     GemvPlan head;
     size_t attn_smem = 0;
+    bool attn_global = false;     // attention scores in a global buffer (long max_ctx)
     uint32_t numeric = HS_NUMERIC_REFERENCE;
     TcGemmPlan thead;             // tensor-core LM head
     uint64_t tc_part_per_slot = 0;  // max over split-K GEMMs of splits * rows
@@ -262,6 +263,7 @@ struct hs_scratch {
     const hs_kv* graph_kv = nullptr;
     uint32_t graph_kmax = 0;
     uint32_t launches_fwd = 0;
+    float* sc_global = nullptr;     // attention scores [nh][max_ctx] for long contexts
     uint64_t* trace = nullptr;      // device, 4 u64 per launch slot (trace mode only)
     uint64_t* trace_init = nullptr; // pinned host template: start=~0, rest 0
     uint32_t trace_slots = 0;
@@ -275,7 +277,7 @@ struct hs_scratch {
         cudaFree(trace);
         cudaFreeHost(trace_init);
         for (void* p : {(void*)x, (void*)qkv, (void*)att, (void*)hb, (void*)logits, (void*)tokens, (void*)cand,
-                        (void*)argbuf})
+                        (void*)argbuf, (void*)sc_global})
             cudaFree(p);
     }
 };
@@ -495,6 +497,7 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         at.page_shift = kv->page_shift;
         at.trace = s->trace;
         at.trace_slot = slot++;
+        at.sc_global = s->sc_global;
         if (m->numeric == HS_NUMERIC_FAST)
             HS_CUDA_TRY(launch_attention_fast(c.head_dim, c.n_heads, m->attn_smem, at, st));
         else
@@ -722,9 +725,16 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
     }
     if (tc && n_heads / n_kv > 8) return fail(HS_E_UNSUPPORTED, "tensor-core path supports up to 8 query heads per KV head");
     if (tc && d_model > 2048) return fail(HS_E_UNSUPPORTED, "tensor-core path supports d_model up to 2048");
-    m->attn_smem = tc ? tc_attention_smem(hd, n_heads / n_kv, max_ctx)
-                      : fast ? attention_fast_smem(hd, max_ctx) : attention_smem(hd, max_ctx);
-    if (m->attn_smem > m->smem_cap) return fail(HS_E_UNSUPPORTED, "max_ctx too large for the attention kernel");
+    auto attn_smem_for = [&](uint32_t ctx) {
+        return tc ? tc_attention_smem(hd, n_heads / n_kv, ctx) : fast ? attention_fast_smem(hd, ctx) : attention_smem(hd, ctx);
+    };
+    m->attn_smem = attn_smem_for(max_ctx);
+    if (m->attn_smem > m->smem_cap) {
+        // Long contexts: the scores move to a global buffer (L2-resident per head).
+        m->attn_global = true;
+        m->attn_smem = attn_smem_for(0);
+    }
+    if (m->attn_smem > m->smem_cap) return fail(HS_E_UNSUPPORTED, "attention staging does not fit in shared memory");
 
     // Staging buffer for the largest quantised tensor.
     uint64_t max_raw = 0;
@@ -1040,6 +1050,7 @@ int hs_scratch_new(const hs_model* m, hs_scratch** out) {
     HS_CUDA_TRY(cudaMemset(s->ctl, 0, sizeof(DevCtl)));
     HS_CUDA_TRY(cudaMallocHost(&s->ctl_h, sizeof(DevCtl)));
     std::memset(s->ctl_h, 0, sizeof(DevCtl));
+    if (m->attn_global) HS_CUDA_TRY(cudaMalloc(&s->sc_global, (size_t)c.n_heads * c.max_ctx * 4));
     HS_CUDA_TRY(cudaMalloc(&s->x, c.d_model * 4));
     HS_CUDA_TRY(cudaMalloc(&s->qkv, (size_t)(c.n_heads + 2 * c.n_kv_heads) * c.head_dim * 4));
     HS_CUDA_TRY(cudaMalloc(&s->att, (size_t)c.n_heads * c.head_dim * 4));
@@ -1392,6 +1403,7 @@ struct hs_batch {
     uint32_t n_cta = 0, kmax_alloc = 0, slice = 0;
     uint32_t* err = nullptr;       // GEMM error word (device)
     uint32_t err_h = 0;
+    float* sc_global = nullptr;    // attention scores for long contexts [cap_slots][nh][max_ctx]
     uint32_t layout = 0, page_shift = 0;
     // Graphs by (slots, sampler width, KV layout, page shift); forward-only
     // graphs use sampler width 0. Value: the graph and its kernel count.
@@ -1406,7 +1418,8 @@ struct hs_batch {
         cudaFreeHost(tab_h);
         for (void* p : {(void*)x, (void*)part, (void*)logits, (void*)xn_hi, (void*)xn_lo, (void*)att_hi, (void*)att_lo,
                         (void*)hb_hi, (void*)hb_lo, (void*)ctl, (void*)tokens, (void*)tok_tab, (void*)kv_tab,
-                        (void*)dirty_tab, (void*)track_tab, (void*)cand, (void*)argbuf, (void*)err})
+                        (void*)dirty_tab, (void*)track_tab, (void*)cand, (void*)argbuf, (void*)err,
+                        (void*)sc_global})
             cudaFree(p);
     }
 };
@@ -1498,6 +1511,7 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches) {
         at.max_ctx = c.max_ctx;
         at.layout = b->layout;
         at.page_shift = b->page_shift;
+        at.sc_global = b->sc_global;
         cudaError_t e = launch_tc_attention(hd, at, n, m->attn_smem, b->st);
         if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
         (*launches)++;
@@ -1643,7 +1657,8 @@ int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out) {
         (rc = alloc(&b->ctl, C)) || (rc = alloc(&b->tokens, (uint64_t)C * b->tok_cap)) ||
         (rc = alloc(&b->tok_tab, C)) || (rc = alloc(&b->kv_tab, C)) || (rc = alloc(&b->dirty_tab, C)) ||
         (rc = alloc(&b->track_tab, C)) || (rc = alloc(&b->cand, (uint64_t)C * b->n_cta * b->kmax_alloc)) ||
-        (rc = alloc(&b->argbuf, (uint64_t)C * b->n_cta)) || (rc = alloc(&b->err, 1)))
+        (rc = alloc(&b->argbuf, (uint64_t)C * b->n_cta)) || (rc = alloc(&b->err, 1)) ||
+        (m->attn_global && (rc = alloc(&b->sc_global, (uint64_t)C * c.n_heads * c.max_ctx))))
         return rc;
     HS_CUDA_TRY(cudaMallocHost(&b->ctl_h, (size_t)C * sizeof(DevCtl)));
     std::memset(b->ctl_h, 0, (size_t)C * sizeof(DevCtl));

@@ -55,6 +55,7 @@ struct AttnArgs {
     uint32_t layer, nh, nkv, max_ctx, layout, page_shift;
     uint64_t* trace;
     uint32_t trace_slot;
+    float* sc_global;        // non-null: attention scores [nh][max_ctx] here instead of shared memory
 };
 
 struct SampleArgs {
@@ -162,6 +163,7 @@ struct TcAttnArgs {
     uint32_t layer, nh, nkv, max_ctx, layout, page_shift;
     uint64_t* trace;
     uint32_t trace_slot;
+    float* sc_global;        // non-null: scores [slots][nkv][groups][max_ctx] here instead of shared memory
 };
 
 size_t tc_attention_smem(uint32_t head_dim, uint32_t groups, uint32_t max_ctx);
