@@ -147,6 +147,7 @@ _SIGS = {
     "hs_batch_seq_end": (C.c_int, [_P, _P, _U64P, C.c_uint64, C.POINTER(SeqState), C.POINTER(Rng)]),
     "hs_batch_stream": (_P, [_P]),
     "hs_batch_launches_per_step": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
+    "hs_batch_trace": (C.c_int, [_P, _P, C.c_uint64, _U64P]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _f = getattr(_lib, _name)
@@ -432,6 +433,15 @@ class Batch:
         n = C.c_uint32()
         _check(_lib.hs_batch_launches_per_step(self._h, C.byref(n)))
         return n.value
+
+    def trace(self):
+        """Launch timeline of the last forward/step (needs HS_TRACE=1 at creation):
+        array [slots, 8]: entry, past-wait, exit, last entry, checkpoints 1-4 (ns)."""
+        used = C.c_uint64()
+        _check(_lib.hs_batch_trace(self._h, None, 0, C.byref(used)))
+        out = np.zeros((used.value, 8), dtype=np.uint64)
+        _check(_lib.hs_batch_trace(self._h, _ptr(out), used.value, C.byref(used)))
+        return out
 
     def _state(self, seqs, stop_at_filled):
         """seqs: list of dicts with tokens, prompt_len, max_tokens, cfg, rng, filled, done, done_reason."""

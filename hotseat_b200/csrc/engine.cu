@@ -216,6 +216,8 @@ struct hs_model {
     GemvPlan head;
     size_t attn_smem = 0;
     bool attn_global = false;     // attention scores in a global buffer (long max_ctx)
+    bool attn_split = false;      // split-KV attention (GPU-native paths)
+    uint32_t max_splits = 0;
     uint32_t numeric = HS_NUMERIC_REFERENCE;
     TcGemmPlan thead;             // tensor-core LM head
     uint64_t tc_part_per_slot = 0;  // max over split-K GEMMs of splits * rows
@@ -264,6 +266,9 @@ struct hs_scratch {
     uint32_t graph_kmax = 0;
     uint32_t launches_fwd = 0;
     float* sc_global = nullptr;     // attention scores [nh][max_ctx] for long contexts
+    float* att_part = nullptr;      // split-KV attention partials and counters
+    uint32_t* att_cnt = nullptr;
+    void** kv_tab = nullptr;        // one-entry KV / dirty / tracking tables for split attention
     uint64_t* trace = nullptr;      // device, 4 u64 per launch slot (trace mode only)
     uint64_t* trace_init = nullptr; // pinned host template: start=~0, rest 0
     uint32_t trace_slots = 0;
@@ -277,7 +282,7 @@ struct hs_scratch {
         cudaFree(trace);
         cudaFreeHost(trace_init);
         for (void* p : {(void*)x, (void*)qkv, (void*)att, (void*)hb, (void*)logits, (void*)tokens, (void*)cand,
-                        (void*)argbuf, (void*)sc_global})
+                        (void*)argbuf, (void*)sc_global, (void*)att_part, (void*)att_cnt, (void*)kv_tab})
             cudaFree(p);
     }
 };
@@ -498,7 +503,30 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         at.trace = s->trace;
         at.trace_slot = slot++;
         at.sc_global = s->sc_global;
-        if (m->numeric == HS_NUMERIC_FAST)
+        if (m->attn_split) {
+            SplitAttnArgs sa{};
+            sa.qkv = s->qkv;
+            sa.n_part = 1;
+            sa.kv = reinterpret_cast<float* const*>(s->kv_tab);
+            sa.dirty = reinterpret_cast<uint64_t* const*>(s->kv_tab + 1);
+            sa.tracking = reinterpret_cast<const uint32_t* const*>(s->kv_tab + 2);
+            sa.rope_cos = m->rope_cos;
+            sa.rope_sin = m->rope_sin;
+            sa.out_f32 = s->att;
+            sa.partials = s->att_part;
+            sa.counters = s->att_cnt;
+            sa.ctl = s->ctl;
+            sa.layer = l;
+            sa.nh = c.n_heads;
+            sa.nkv = c.n_kv_heads;
+            sa.max_ctx = c.max_ctx;
+            sa.layout = kv->spec.layout;
+            sa.page_shift = kv->page_shift;
+            sa.max_splits = m->max_splits;
+            sa.trace = s->trace;
+            sa.trace_slot = at.trace_slot;
+            HS_CUDA_TRY(launch_attn_split(c.head_dim, sa, 1, st));
+        } else if (m->numeric == HS_NUMERIC_FAST)
             HS_CUDA_TRY(launch_attention_fast(c.head_dim, c.n_heads, m->attn_smem, at, st));
         else
             HS_CUDA_TRY(launch_attention(c.head_dim, c.n_heads, m->attn_smem, at, st));
@@ -605,6 +633,10 @@ int ensure_graphs(hs_scratch* s, const hs_kv* kv, uint32_t kmax) {
     if (s->g_step) cudaGraphExecDestroy(s->g_step);
     s->g_fwd = s->g_step = nullptr;
     s->kmax = kmax;
+    if (s->kv_tab) {
+        void* t[3] = {kv->base, kv->dirty, kv->tracking};
+        HS_CUDA_TRY(cudaMemcpy(s->kv_tab, t, sizeof(t), cudaMemcpyHostToDevice));
+    }
     int rc = capture(s, kv, false, &s->g_fwd);
     if (rc == HS_OK) rc = capture(s, kv, true, &s->g_step);
     if (rc) return rc;
@@ -699,7 +731,6 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
     HS_CUDA_TRY(gemv_set_smem_limits(optin));
     HS_CUDA_TRY(fast_set_smem_limits(optin));
     HS_CUDA_TRY(tc_set_smem_limits(optin));
-    HS_CUDA_TRY(tc_ops_set_smem_limits(optin));
     m->numeric = numeric;
     const bool fast = numeric == HS_NUMERIC_FAST, tc = numeric == HS_NUMERIC_TC;
     hs_config& c = m->cfg;
@@ -725,11 +756,17 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
     }
     if (tc && n_heads / n_kv > 8) return fail(HS_E_UNSUPPORTED, "tensor-core path supports up to 8 query heads per KV head");
     if (tc && d_model > 2048) return fail(HS_E_UNSUPPORTED, "tensor-core path supports d_model up to 2048");
-    auto attn_smem_for = [&](uint32_t ctx) {
-        return tc ? tc_attention_smem(hd, n_heads / n_kv, ctx) : fast ? attention_fast_smem(hd, ctx) : attention_smem(hd, ctx);
-    };
-    m->attn_smem = attn_smem_for(max_ctx);
-    if (m->attn_smem > m->smem_cap) {
+    // Attention: the tensor-core path always splits the cached positions
+    // over CTAs; the fast path keeps one CTA per query head (quicker at
+    // short contexts) unless max_ctx scores do not fit in shared memory.
+    m->attn_split = tc || (fast && attention_fast_smem(hd, max_ctx) > m->smem_cap);
+    if (m->attn_split) {
+        m->max_splits = attn_max_splits(max_ctx);
+        HS_CUDA_TRY(attn_split_set_smem_limits(optin));
+    }
+    auto attn_smem_for = [&](uint32_t ctx) { return fast ? attention_fast_smem(hd, ctx) : attention_smem(hd, ctx); };
+    m->attn_smem = m->attn_split ? attn_split_smem(hd) : attn_smem_for(max_ctx);
+    if (!m->attn_split && m->attn_smem > m->smem_cap) {
         // Long contexts: the scores move to a global buffer (L2-resident per head).
         m->attn_global = true;
         m->attn_smem = attn_smem_for(0);
@@ -1051,6 +1088,13 @@ int hs_scratch_new(const hs_model* m, hs_scratch** out) {
     HS_CUDA_TRY(cudaMallocHost(&s->ctl_h, sizeof(DevCtl)));
     std::memset(s->ctl_h, 0, sizeof(DevCtl));
     if (m->attn_global) HS_CUDA_TRY(cudaMalloc(&s->sc_global, (size_t)c.n_heads * c.max_ctx * 4));
+    if (m->attn_split) {
+        const uint32_t G = c.n_heads / c.n_kv_heads;
+        HS_CUDA_TRY(cudaMalloc(&s->att_part, (size_t)c.n_kv_heads * m->max_splits * (G * c.head_dim + 2 * G) * 4));
+        HS_CUDA_TRY(cudaMalloc(&s->att_cnt, c.n_kv_heads * 4));
+        HS_CUDA_TRY(cudaMemset(s->att_cnt, 0, c.n_kv_heads * 4));
+        HS_CUDA_TRY(cudaMalloc(&s->kv_tab, 3 * sizeof(void*)));
+    }
     HS_CUDA_TRY(cudaMalloc(&s->x, c.d_model * 4));
     HS_CUDA_TRY(cudaMalloc(&s->qkv, (size_t)(c.n_heads + 2 * c.n_kv_heads) * c.head_dim * 4));
     HS_CUDA_TRY(cudaMalloc(&s->att, (size_t)c.n_heads * c.head_dim * 4));
@@ -1404,6 +1448,11 @@ struct hs_batch {
     uint32_t* err = nullptr;       // GEMM error word (device)
     uint32_t err_h = 0;
     float* sc_global = nullptr;    // attention scores for long contexts [cap_slots][nh][max_ctx]
+    float* att_part = nullptr;     // split-KV attention partials [cap_slots][nkv][max_splits][record]
+    uint32_t* att_cnt = nullptr;   // [cap_slots][nkv]
+    uint64_t* trace = nullptr;     // launch timeline (HS_TRACE=1 at creation): 8 u64 per launch
+    uint64_t* trace_init = nullptr;
+    uint32_t trace_slots = 0;
     uint32_t layout = 0, page_shift = 0;
     // Graphs by (slots, sampler width, KV layout, page shift); forward-only
     // graphs use sampler width 0. Value: the graph and its kernel count.
@@ -1416,10 +1465,12 @@ struct hs_batch {
         if (st) cudaStreamDestroy(st);
         cudaFreeHost(ctl_h);
         cudaFreeHost(tab_h);
+        cudaFreeHost(trace_init);
+        cudaFree(trace);
         for (void* p : {(void*)x, (void*)part, (void*)logits, (void*)xn_hi, (void*)xn_lo, (void*)att_hi, (void*)att_lo,
                         (void*)hb_hi, (void*)hb_lo, (void*)ctl, (void*)tokens, (void*)tok_tab, (void*)kv_tab,
                         (void*)dirty_tab, (void*)track_tab, (void*)cand, (void*)argbuf, (void*)err,
-                        (void*)sc_global})
+                        (void*)sc_global, (void*)att_part, (void*)att_cnt})
             cudaFree(p);
     }
 };
@@ -1455,6 +1506,8 @@ int batch_gemm(hs_batch* b, const TcGemmPlan& p, const uint16_t* a_hi, const uin
     a.out_hi = out_hi;
     a.out_lo = out_lo;
     a.err = b->err;
+    a.trace = b->trace;
+    a.trace_slot = *launches;
     cudaError_t e = launch_tc_gemm(q, mh, ml, a, b->st);
     if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("tensor-core GEMM launch: ") + cudaGetErrorString(e));
     (*launches)++;
@@ -1482,6 +1535,8 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches) {
         a.d = d;
         a.vocab = c.vocab;
         a.eps = c.eps;
+        a.trace = b->trace;
+        a.trace_slot = *launches;
         cudaError_t e = launch_tc_norm(a, n, b->st);
         if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("norm launch: ") + cudaGetErrorString(e));
         (*launches)++;
@@ -1491,28 +1546,38 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches) {
         const LayerDev& L = m->layers[l];
         if ((rc = norm(L.attn_norm, prev_down, l == 0))) return rc;
         if ((rc = batch_gemm(b, L.tq, b->xn_hi, b->xn_lo, n, b->part, nullptr, nullptr, qrows, launches))) return rc;
-        TcAttnArgs at{};
-        at.qkv_part = b->part;
-        at.n_part = L.tq.splits;
-        at.part_stride = (uint64_t)b->cap_slots * L.tq.rows;
-        at.bias = L.bqkv;
-        at.qkv_rows = qrows;
-        at.kv = b->kv_tab;
-        at.dirty = b->dirty_tab;
-        at.tracking = b->track_tab;
-        at.rope_cos = m->rope_cos;
-        at.rope_sin = m->rope_sin;
-        at.att_hi = b->att_hi;
-        at.att_lo = b->att_lo;
-        at.ctl = b->ctl;
-        at.layer = l;
-        at.nh = c.n_heads;
-        at.nkv = c.n_kv_heads;
-        at.max_ctx = c.max_ctx;
-        at.layout = b->layout;
-        at.page_shift = b->page_shift;
-        at.sc_global = b->sc_global;
-        cudaError_t e = launch_tc_attention(hd, at, n, m->attn_smem, b->st);
+        cudaError_t e;
+        if (m->attn_split) {
+            SplitAttnArgs sa{};
+            sa.qkv = b->part;
+            sa.n_part = L.tq.splits;
+            sa.part_stride = (uint64_t)b->cap_slots * L.tq.rows;
+            sa.bias = L.bqkv;
+            sa.qkv_rows = qrows;
+            sa.kv = b->kv_tab;
+            sa.dirty = b->dirty_tab;
+            sa.tracking = b->track_tab;
+            sa.rope_cos = m->rope_cos;
+            sa.rope_sin = m->rope_sin;
+            sa.out_hi = b->att_hi;
+            sa.out_lo = b->att_lo;
+            sa.out_stride = c.n_heads * hd;
+            sa.partials = b->att_part;
+            sa.counters = b->att_cnt;
+            sa.ctl = b->ctl;
+            sa.layer = l;
+            sa.nh = c.n_heads;
+            sa.nkv = c.n_kv_heads;
+            sa.max_ctx = c.max_ctx;
+            sa.layout = b->layout;
+            sa.page_shift = b->page_shift;
+            sa.max_splits = m->max_splits;
+            sa.trace = b->trace;
+            sa.trace_slot = *launches;
+            e = launch_attn_split(hd, sa, n, b->st);
+        } else {
+            return fail(HS_E_STATE, "internal: tensor-core model without split attention");
+        }
         if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
         (*launches)++;
         if ((rc = batch_gemm(b, L.to, b->att_hi, b->att_lo, n, b->part, nullptr, nullptr, d, launches))) return rc;
@@ -1557,7 +1622,10 @@ int batch_graph(hs_batch* b, uint32_t n, uint32_t kmax, cudaGraphExec_t* out, ui
     HS_CUDA_TRY(cudaStreamBeginCapture(b->st, cudaStreamCaptureModeThreadLocal));
     int rc = batch_enqueue_forward(b, n, launches);
     if (rc == HS_OK && kmax) {
-        cudaError_t e = launch_sample(batch_sample_args(b, n, kmax), b->st);
+        SampleArgs sa = batch_sample_args(b, n, kmax);
+        sa.trace = b->trace;
+        sa.trace_slot = *launches;  // and the next slot for the second kernel
+        cudaError_t e = launch_sample(sa, b->st);
         if (e != cudaSuccess) rc = fail(HS_E_CUDA, std::string("sampler launch: ") + cudaGetErrorString(e));
         *launches += 2;
     }
@@ -1658,11 +1726,25 @@ int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out) {
         (rc = alloc(&b->tok_tab, C)) || (rc = alloc(&b->kv_tab, C)) || (rc = alloc(&b->dirty_tab, C)) ||
         (rc = alloc(&b->track_tab, C)) || (rc = alloc(&b->cand, (uint64_t)C * b->n_cta * b->kmax_alloc)) ||
         (rc = alloc(&b->argbuf, (uint64_t)C * b->n_cta)) || (rc = alloc(&b->err, 1)) ||
-        (m->attn_global && (rc = alloc(&b->sc_global, (uint64_t)C * c.n_heads * c.max_ctx))))
+        (m->attn_global && (rc = alloc(&b->sc_global, (uint64_t)C * c.n_heads * c.max_ctx))) ||
+        (m->attn_split &&
+         ((rc = alloc(&b->att_part, (uint64_t)C * c.n_kv_heads * m->max_splits *
+                                        (c.n_heads / c.n_kv_heads * (c.head_dim + 2)))) ||
+          (rc = alloc(&b->att_cnt, (uint64_t)C * c.n_kv_heads)))))
         return rc;
     HS_CUDA_TRY(cudaMallocHost(&b->ctl_h, (size_t)C * sizeof(DevCtl)));
     std::memset(b->ctl_h, 0, (size_t)C * sizeof(DevCtl));
     HS_CUDA_TRY(cudaMallocHost(&b->tab_h, (size_t)3 * C * sizeof(void*)));
+    const char* tenv = getenv("HS_TRACE");
+    if (tenv && tenv[0] == '1') {
+        b->trace_slots = c.n_layers * 7 + 4;
+        HS_CUDA_TRY(cudaMalloc(&b->trace, (size_t)b->trace_slots * 64));
+        HS_CUDA_TRY(cudaMallocHost(&b->trace_init, (size_t)b->trace_slots * 64));
+        for (uint32_t i = 0; i < b->trace_slots; i++) {
+            b->trace_init[8 * i] = ~0ull;
+            for (int j = 1; j < 8; j++) b->trace_init[8 * i + j] = 0;
+        }
+    }
     std::vector<uint32_t*> rows(C);
     for (uint32_t i = 0; i < C; i++) rows[i] = b->tokens + (uint64_t)i * b->tok_cap;
     HS_CUDA_TRY(cudaMemcpy(b->tok_tab, rows.data(), C * sizeof(uint32_t*), cudaMemcpyHostToDevice));
@@ -1706,6 +1788,8 @@ int hs_forward_batch(const hs_model* m, hs_kv* const* kvs, const uint32_t* token
     cudaGraphExec_t g = nullptr;
     uint32_t launches = 0;
     if ((rc = batch_graph(b, n, 0, &g, &launches))) return rc;
+    if (b->trace)
+        HS_CUDA_TRY(cudaMemcpyAsync(b->trace, b->trace_init, (size_t)b->trace_slots * 64, cudaMemcpyHostToDevice, b->st));
     HS_CUDA_TRY(cudaGraphLaunch(g, b->st));
     return batch_sync(b, n);
 }
@@ -1778,7 +1862,23 @@ int hs_batch_seq_begin(hs_batch* b, hs_kv* const* kvs, uint32_t n, uint32_t* con
 int hs_batch_seq_step(hs_batch* b, uint32_t n_steps) {
     if (!b || !b->g_step) return fail(HS_E_ARG, "hs_batch_seq_begin has not been called");
     HS_CUDA_TRY(cudaSetDevice(b->m->device));
-    for (uint32_t i = 0; i < n_steps; i++) HS_CUDA_TRY(cudaGraphLaunch(b->g_step, b->st));
+    for (uint32_t i = 0; i < n_steps; i++) {
+        if (b->trace)
+            HS_CUDA_TRY(cudaMemcpyAsync(b->trace, b->trace_init, (size_t)b->trace_slots * 64, cudaMemcpyHostToDevice,
+                                        b->st));
+        HS_CUDA_TRY(cudaGraphLaunch(b->g_step, b->st));
+    }
+    return HS_OK;
+}
+
+int hs_batch_trace(hs_batch* b, uint64_t* out, uint64_t n_slots, uint64_t* used) {
+    if (!b || !used) return fail(HS_E_ARG, "null argument");
+    *used = b->trace_slots;
+    if (!b->trace) return fail(HS_E_STATE, "tracing is off (set HS_TRACE=1 before creating the batch)");
+    if (!out) return HS_OK;
+    HS_CUDA_TRY(cudaSetDevice(b->m->device));
+    HS_CUDA_TRY(cudaStreamSynchronize(b->st));
+    HS_CUDA_TRY(cudaMemcpy(out, b->trace, std::min<uint64_t>(n_slots, b->trace_slots) * 64, cudaMemcpyDeviceToHost));
     return HS_OK;
 }
 

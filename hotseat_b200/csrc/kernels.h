@@ -146,30 +146,41 @@ struct TcNormArgs {
     uint32_t trace_slot;
 };
 
-struct TcAttnArgs {
-    const float* qkv_part;   // split-K partials [n_part][slots][qkv_rows] of the QKV product
+// Split-KV decode attention (attn_split.cu), GPU-native paths.
+struct SplitAttnArgs {
+    const float* qkv;        // QKV product: sum of n_part partials (part_stride apart), then + bias
     uint32_t n_part;
     uint64_t part_stride;
-    const float* bias;       // [qkv_rows]
-    uint32_t qkv_rows;
-    float* const* kv;        // per-slot KV regions
-    uint64_t* const* dirty;  // per-slot page bitmaps
+    const float* bias;       // [qkv_rows] or null (already added)
+    uint32_t qkv_rows;       // elements between sequences' QKV rows
+    float* const* kv;        // per-sequence KV regions, dirty bitmaps, tracking flags
+    uint64_t* const* dirty;
     const uint32_t* const* tracking;
-    const float* rope_cos;   // [max_ctx][hd/2]
+    const float* rope_cos;
     const float* rope_sin;
-    uint16_t* att_hi;        // [slots][nh*hd] f16 pair of the attention output
-    uint16_t* att_lo;
-    DevCtl* ctl;
-    uint32_t layer, nh, nkv, max_ctx, layout, page_shift;
+    float* out_f32;          // non-null: f32 output; else the f16 hi/lo pair
+    uint16_t* out_hi;
+    uint16_t* out_lo;
+    uint32_t out_stride;     // elements between sequences' outputs
+    float* partials;         // [sequences][nkv][max_splits][groups*hd + 2*groups]
+    uint32_t* counters;      // [sequences][nkv], zero between launches
+    DevCtl* ctl;             // per-sequence control blocks
+    uint32_t layer, nh, nkv, max_ctx, layout, page_shift, max_splits;
     uint64_t* trace;
     uint32_t trace_slot;
-    float* sc_global;        // non-null: scores [slots][nkv][groups][max_ctx] here instead of shared memory
 };
+// Positions per split for n cached positions: a multiple of 64, so that at
+// most max_splits splits cover n.
+__host__ __device__ inline uint32_t attn_split_len(uint32_t n, uint32_t max_splits) {
+    const uint32_t chunks = (n + 63) / 64;
+    return (chunks + max_splits - 1) / max_splits * 64;
+}
+size_t attn_split_smem(uint32_t head_dim);
+uint32_t attn_max_splits(uint32_t max_ctx);
+cudaError_t attn_split_set_smem_limits(int optin);
+cudaError_t launch_attn_split(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, cudaStream_t st);
 
-size_t tc_attention_smem(uint32_t head_dim, uint32_t groups, uint32_t max_ctx);
-cudaError_t tc_ops_set_smem_limits(int optin);
 cudaError_t launch_tc_norm(const TcNormArgs& a, uint32_t slots, cudaStream_t st);
-cudaError_t launch_tc_attention(uint32_t head_dim, const TcAttnArgs& a, uint32_t slots, size_t smem, cudaStream_t st);
 
 constexpr uint32_t kSampleSlice = 1024;  // logits per CTA of the candidate kernel
 constexpr uint32_t kMaxSlice = 4096;     // largest slice a candidate CTA takes

@@ -1,0 +1,200 @@
+"""Kernel microbenchmarks of the token loop's building blocks (B200).
+
+    python -m hotseat_b200.microbench dequant     # Q4_K/Q6_K -> f16 load-time dequantisation
+    python -m hotseat_b200.microbench attention   # GQA decode attention at 1k-32k context
+
+dequant: the tensors of the seeded Qwen2.5-0.5B-shape GGUF (ffn_gate 4864x896
+and ffn_down 896x4864 in Q4_K, token_embd 151936x896 in Q6_K) plus the same
+embedding written in Q4_K, dequantised by hs_dequant_f16 from device memory;
+L2 is flushed (256 MB written) between timed launches. Bytes = quantised
+blocks read + 2 bytes per element written.
+
+attention: one forward of the 0.5B-shape model at position P (KV regions as
+allocated, so every cached row is read), batch 1 on the GPU-native path and
+batch 64 on the tensor-core path, with the launch timeline (HS_TRACE=1). The
+attention time of a layer is its kernel's exit minus the QKV kernel's exit
+(the work it adds after its input is ready), averaged over the 24 layers.
+Bytes = (P+1) x 1024 B of K and V read + 1024 B written per sequence and
+layer (14 query / 2 KV heads, head_dim 64, f32).
+
+Each line printed is one JSON object; peaks are the measured copy bandwidth
+in MEASURED_PEAKS.json when present.
+"""
+import json
+import os
+import struct
+import sys
+import tempfile
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _peak():
+    try:
+        return float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return 6650.0, "fallback"
+
+
+def gguf_tensors(path):
+    """name -> (ggml type, element count, absolute byte offset) of a GGUF v3 file."""
+    with open(path, "rb") as f:
+        data = f.read(1 << 26)
+    off = 0
+
+    def take(fmt):
+        nonlocal off
+        v = struct.unpack_from("<" + fmt, data, off)
+        off += struct.calcsize("<" + fmt)
+        return v[0] if len(v) == 1 else v
+
+    def string():
+        nonlocal off
+        n = take("Q")
+        s = data[off: off + n].decode()
+        off += n
+        return s
+
+    sizes = {0: 1, 1: 1, 2: 2, 3: 2, 4: 4, 5: 4, 6: 4, 7: 1, 10: 8, 11: 8, 12: 8}
+
+    def skip_value(t):
+        nonlocal off
+        if t == 8:
+            string()
+        elif t == 9:
+            et, n = take("I"), take("Q")
+            for _ in range(n):
+                skip_value(et)
+        else:
+            off += sizes[t]
+
+    assert data[:4] == b"GGUF"
+    off = 4
+    take("I")
+    n_t, n_kv = take("Q"), take("Q")
+    align = 32
+    for _ in range(n_kv):
+        key = string()
+        t = take("I")
+        if key == "general.alignment" and t == 4:
+            align = take("I")
+        else:
+            skip_value(t)
+    infos = []
+    for _ in range(n_t):
+        name = string()
+        nd = take("I")
+        n = 1
+        for _ in range(nd):
+            n *= take("Q")
+        infos.append((name, take("I"), n, take("Q")))
+    base = (off + align - 1) // align * align
+    return {name: (t, n, base + o) for name, t, n, o in infos}
+
+
+def block_bytes(t):
+    return {12: 144, 14: 210, 13: 176, 8: 34, 6: 22}[t]
+
+
+def bench_dequant(reps=10):
+    import torch
+    import hotseat_b200 as hs
+    peak, src = _peak()
+    td = tempfile.mkdtemp(prefix="hsmicro")
+    a = os.path.join(td, "q6.gguf")
+    b = os.path.join(td, "q4.gguf")
+    hs.write_synthetic_gguf(a, seed=1234, **hs.QWEN05)
+    hs.write_synthetic_gguf(b, seed=1234, embd_type=12, **dict(hs.QWEN05, n_layers=1))
+    cases = [(a, "blk.0.ffn_gate.weight", "4864x896"), (a, "blk.0.ffn_down.weight", "896x4864"),
+             (b, "token_embd.weight", "151936x896"), (a, "token_embd.weight", "151936x896")]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    for path, name, shape in cases:
+        t, n, at = gguf_tensors(path)[name]
+        nbytes = n // 256 * block_bytes(t)
+        with open(path, "rb") as f:
+            f.seek(at)
+            raw = np.frombuffer(f.read(nbytes), dtype=np.uint8)
+        src_d = torch.from_numpy(raw.copy()).cuda()
+        dst = torch.empty(n, dtype=torch.float16, device="cuda")
+        ms = []
+        for i in range(3 + reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            hs.dequant_f16(t, src_d.data_ptr(), n, dst.data_ptr(), stream.cuda_stream)
+            e1.record(stream)
+            e1.synchronize()
+            if i >= 3:
+                ms.append(e0.elapsed_time(e1))
+        us = 1000.0 * float(np.median(ms))
+        moved = nbytes + 2 * n
+        gbs = moved / us / 1e3
+        print(json.dumps({"bench": "dequant", "type": {12: "Q4_K", 14: "Q6_K"}[t], "shape": shape,
+                          "bytes": moved, "us": us, "GB/s": gbs, "frac": gbs / peak, "peak": peak,
+                          "peak_source": src, "l2": "flushed between launches"}), flush=True)
+    for p in (a, b):
+        os.remove(p)
+    os.rmdir(td)
+
+
+def _att_times(trace, per_layer, att_slot, layers):
+    t = trace.astype(np.int64)
+    out = []
+    for l in range(layers):
+        s = l * per_layer + att_slot
+        out.append((t[s, 2] - t[s - 1, 2]) / 1000.0)
+    return float(np.mean(out))
+
+
+def bench_attention(ctxs=(1024, 4096, 16384, 32767)):
+    os.environ["HS_TRACE"] = "1"
+    import hotseat_b200 as hs
+    peak, src = _peak()
+    td = tempfile.mkdtemp(prefix="hsmicro")
+    path = os.path.join(td, "q05.gguf")
+    hs.write_synthetic_gguf(path, seed=1234, **hs.QWEN05)
+    max_ctx = max(ctxs) + 8
+    layers, row = 24, 2 * 2 * 64 * 4
+    for batch, numeric in ((1, hs.NUMERIC_FAST), (64, hs.NUMERIC_TC)):
+        m = hs.Model.load(path, max_ctx=max_ctx, numeric=numeric)
+        kvs = [m.kv() for _ in range(batch)]
+        if batch == 1:
+            s = m.scratch()
+        else:
+            bt = hs.Batch(m, batch)
+        for p in ctxs:
+            res = []
+            for _ in range(3):
+                if batch == 1:
+                    m.forward(kvs[0], 17, p, s)
+                    res.append(_att_times(s.trace(), 5, 1, layers))
+                else:
+                    bt.forward(kvs, list(range(17, 17 + batch)), [p] * batch)
+                    res.append(_att_times(bt.trace(), 7, 2, layers))
+            us = float(np.median(res[1:]))
+            moved = batch * ((p + 1) * row + row)
+            gbs = moved / us / 1e3
+            print(json.dumps({"bench": "attention", "batch": batch, "context": p + 1,
+                              "numeric": "fast" if batch == 1 else "tc", "bytes_per_layer": moved,
+                              "us_per_layer": us, "GB/s": gbs, "frac": gbs / peak, "peak": peak,
+                              "peak_source": src}), flush=True)
+        for k in kvs:
+            k.close()
+        if batch == 1:
+            s.close()
+        else:
+            bt.close()
+        m.close()
+    os.remove(path)
+    os.rmdir(td)
+
+
+if __name__ == "__main__":
+    which = sys.argv[1] if len(sys.argv) > 1 else "all"
+    if which in ("dequant", "all"):
+        bench_dequant()
+    if which in ("attention", "all"):
+        bench_attention()
