@@ -139,6 +139,7 @@ _SIGS = {
     "hs_batch_free": (None, [_P]),
     "hs_forward_batch": (C.c_int, [_P, _P, _P, _P, C.c_uint32, _P]),
     "hs_batch_logits": (C.c_int, [_P, C.c_uint32, _P, C.c_uint64]),
+    "hs_prefill": (C.c_int, [_P, _P, _P, C.c_uint32, C.c_uint32, _P]),
     "hs_batch_seq_run": (C.c_int, [_P, _P, _P, C.c_uint32, _P, _U64P, C.c_uint64, C.POINTER(SeqState),
                                    C.POINTER(SamplerCfg), C.POINTER(Rng), C.c_uint64]),
     "hs_batch_seq_begin": (C.c_int, [_P, _P, C.c_uint32, _P, _U64P, C.c_uint64, C.POINTER(SeqState),
@@ -419,6 +420,11 @@ class Batch:
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
         p = np.ascontiguousarray(pos, dtype=np.uint32)
         _check(_lib.hs_forward_batch(self.model._h, self._kv_table(kvs), _ptr(t), _ptr(p), len(kvs), self._h))
+
+    def prefill(self, kv, tokens, pos0=0):
+        """Forward a prompt's tokens (one sequence) as GEMM rows; fills its KV."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        _check(_lib.hs_prefill(self.model._h, kv._h, _ptr(t), t.size, pos0, self._h))
 
     def logits(self, slot):
         out = np.zeros(self.model.cfg.vocab, dtype=np.float32)

@@ -74,7 +74,11 @@ __global__ void __launch_bounds__(kThreads) k_attn_split(const SplitAttnArgs a) 
         return;
     }
     const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits), S = (n + L - 1) / L;
-    if (s >= S) return;
+    // Prefill runs append (every token's k, v) and attend (reading all rows
+    // from memory) as two launches, so tokens of one sequence in one batch
+    // see each other's rows.
+    const bool append = a.mode != ATTN_ATTEND_ONLY, attend = a.mode != ATTN_APPEND_ONLY;
+    if (s >= (attend ? S : 1u)) return;
     const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n;
     float* kv = a.kv[slot];
     const uint64_t plane = (uint64_t)a.max_ctx * a.nkv * HD;
@@ -118,7 +122,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_split(const SplitAttnArgs a) 
         hs_l[tid] = 0.0f;
     }
     __syncthreads();
-    if (s == 0) {
+    if (s == 0 && append) {
         if (tid < HD) {
             kv[row_off(pos, 0) + tid] = kn[tid];
             kv[row_off(pos, 1) + tid] = vn[tid];
@@ -133,6 +137,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_split(const SplitAttnArgs a) 
         }
     }
 
+    if (!attend) return;
     const uint32_t nch = (p1 - p0 + kCh - 1) / kCh;
     auto issue = [&](uint32_t c) {
         if (c < nch) {
@@ -141,7 +146,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_split(const SplitAttnArgs a) 
             float* vd = vb + (c & 1) * kCh * RS;
             for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += kThreads) {
                 const uint32_t r = idx / (HD / 4), c4 = idx % (HD / 4);
-                if (c0 + r == pos) {
+                if (c0 + r == pos && append) {
                     *reinterpret_cast<float4*>(kd + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(kn + 4 * c4);
                     *reinterpret_cast<float4*>(vd + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(vn + 4 * c4);
                 } else {
@@ -311,7 +316,7 @@ cudaError_t launch_attn_split(uint32_t head_dim, const SplitAttnArgs& a, uint32_
     if (a.nkv == 0 || a.nh % a.nkv || a.nh / a.nkv > 8 || a.max_splits == 0 || (!a.out_f32 && !a.out_hi))
         return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(a.max_splits, a.nkv, slots);
+    cfg.gridDim = dim3(a.mode == ATTN_APPEND_ONLY ? 1 : a.max_splits, a.nkv, slots);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = attn_split_smem(head_dim);
     cfg.stream = st;

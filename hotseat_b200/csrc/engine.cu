@@ -1515,7 +1515,7 @@ int batch_gemm(hs_batch* b, const TcGemmPlan& p, const uint16_t* a_hi, const uin
 }
 
 // One batched forward for slots [0, n): 7 launches per layer + final norm + LM head.
-int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches) {
+int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool prefill) {
     const hs_model* m = b->m;
     const hs_config& c = m->cfg;
     const uint32_t d = c.d_model, hd = c.head_dim, qrows = (c.n_heads + 2 * c.n_kv_heads) * hd;
@@ -1574,6 +1574,15 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches) {
             sa.max_splits = m->max_splits;
             sa.trace = b->trace;
             sa.trace_slot = *launches;
+            if (prefill) {
+                // tokens of one sequence: every k, v appended before any attends
+                sa.mode = ATTN_APPEND_ONLY;
+                e = launch_attn_split(hd, sa, n, b->st);
+                if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
+                (*launches)++;
+                sa.mode = ATTN_ATTEND_ONLY;
+                sa.trace_slot = *launches;
+            }
             e = launch_attn_split(hd, sa, n, b->st);
         } else {
             return fail(HS_E_STATE, "internal: tensor-core model without split attention");
@@ -1586,6 +1595,7 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches) {
         if ((rc = batch_gemm(b, L.tdown, b->hb_hi, b->hb_lo, n, b->part, nullptr, nullptr, d, launches))) return rc;
         prev_down = &L.tdown;
     }
+    if (prefill) return HS_OK;  // prompt positions: no logits (x past the last layer is not read)
     if ((rc = norm(m->out_norm, prev_down, false))) return rc;
     return batch_gemm(b, m->thead, b->xn_hi, b->xn_lo, n, b->logits, nullptr, nullptr, c.vocab, launches);
 }
@@ -1609,8 +1619,10 @@ SampleArgs batch_sample_args(hs_batch* b, uint32_t n, uint32_t kmax) {
     return a;
 }
 
-int batch_graph(hs_batch* b, uint32_t n, uint32_t kmax, cudaGraphExec_t* out, uint32_t* launches) {
-    const uint64_t key = (uint64_t)n | (uint64_t)kmax << 16 | (uint64_t)b->layout << 32 | (uint64_t)b->page_shift << 40;
+int batch_graph(hs_batch* b, uint32_t n, uint32_t kmax, cudaGraphExec_t* out, uint32_t* launches,
+                bool prefill = false) {
+    const uint64_t key = (uint64_t)n | (uint64_t)kmax << 16 | (uint64_t)b->layout << 32 | (uint64_t)b->page_shift << 40 |
+                         (uint64_t)prefill << 48;
     auto it = b->graphs.find(key);
     if (it != b->graphs.end()) {
         *out = it->second.first;
@@ -1620,7 +1632,7 @@ int batch_graph(hs_batch* b, uint32_t n, uint32_t kmax, cudaGraphExec_t* out, ui
     *launches = 0;
     cudaGraph_t g = nullptr;
     HS_CUDA_TRY(cudaStreamBeginCapture(b->st, cudaStreamCaptureModeThreadLocal));
-    int rc = batch_enqueue_forward(b, n, launches);
+    int rc = batch_enqueue_forward(b, n, launches, prefill);
     if (rc == HS_OK && kmax) {
         SampleArgs sa = batch_sample_args(b, n, kmax);
         sa.trace = b->trace;
@@ -1645,7 +1657,7 @@ int batch_graph(hs_batch* b, uint32_t n, uint32_t kmax, cudaGraphExec_t* out, ui
 }
 
 // Per-slot KV tables (all regions must share layout and page size).
-int batch_kv_tables(hs_batch* b, hs_kv* const* kvs, uint32_t n) {
+int batch_kv_tables(hs_batch* b, hs_kv* const* kvs, uint32_t n, bool same_sequence = false) {
     const hs_model* m = b->m;
     for (uint32_t i = 0; i < n; i++) {
         if (!kvs[i]) return fail(HS_E_ARG, "null KV region");
@@ -1653,7 +1665,7 @@ int batch_kv_tables(hs_batch* b, hs_kv* const* kvs, uint32_t n) {
         if (rc) return rc;
         if (kvs[i]->spec.layout != kvs[0]->spec.layout || kvs[i]->page_shift != kvs[0]->page_shift)
             return fail(HS_E_ARG, "KV regions of one batch must share layout and page size");
-        for (uint32_t j = 0; j < i; j++)
+        for (uint32_t j = 0; j < i && !same_sequence; j++)
             if (kvs[j] == kvs[i]) return fail(HS_E_ARG, "a KV region appears twice in one batch");
     }
     b->layout = kvs[0]->spec.layout;
@@ -1691,7 +1703,7 @@ extern "C" {
 int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out) {
     if (!m || !out) return fail(HS_E_ARG, "null argument");
     if (m->numeric != HS_NUMERIC_TC) return fail(HS_E_UNSUPPORTED, "hs_batch needs a model loaded with HS_NUMERIC_TC");
-    if (max_seqs == 0 || max_seqs > 128) return fail(HS_E_ARG, "max_seqs must be 1..128");
+    if (max_seqs == 0 || max_seqs > 1024) return fail(HS_E_ARG, "max_seqs must be 1..1024");
     HS_CUDA_TRY(cudaSetDevice(m->device));
     auto b = std::make_unique<hs_batch>();
     b->m = m;
@@ -1792,6 +1804,42 @@ int hs_forward_batch(const hs_model* m, hs_kv* const* kvs, const uint32_t* token
         HS_CUDA_TRY(cudaMemcpyAsync(b->trace, b->trace_init, (size_t)b->trace_slots * 64, cudaMemcpyHostToDevice, b->st));
     HS_CUDA_TRY(cudaGraphLaunch(g, b->st));
     return batch_sync(b, n);
+}
+
+int hs_prefill(const hs_model* m, hs_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0, hs_batch* b) {
+    if (!m || !b || b->m != m || !kv || (!tokens && n)) return fail(HS_E_ARG, "null or mismatched argument");
+    int rc = check_kv(m, kv);
+    if (rc) return rc;
+    if ((uint64_t)pos0 + n > m->cfg.max_ctx) return fail(HS_E_ARG, "prompt runs past max_ctx");
+    for (uint32_t i = 0; i < n; i++)
+        if (tokens[i] >= m->cfg.vocab) return fail(HS_E_ARG, "token " + std::to_string(tokens[i]) + " out of range");
+    HS_CUDA_TRY(cudaSetDevice(m->device));
+    const uint32_t C = b->cap_slots;
+    std::vector<hs_kv*> same(std::min(C, std::max(n, 1u)), kv);
+    for (uint32_t off = 0; off < n; off += C) {
+        const uint32_t cnt = std::min(C, n - off);
+        if ((rc = batch_kv_tables(b, same.data(), cnt, true))) return rc;
+        for (uint32_t i = 0; i < cnt; i++) {
+            DevCtl& h = b->ctl_h[i];
+            std::memset(&h, 0, sizeof(DevCtl));
+            h.token = tokens[off + i];
+            h.pos = pos0 + off + i;
+            h.active = 1;
+            h.mode = 1;
+            h.vocab = m->cfg.vocab;
+            h.max_ctx = m->cfg.max_ctx;
+        }
+        HS_CUDA_TRY(cudaMemcpyAsync(b->ctl, b->ctl_h, (size_t)cnt * sizeof(DevCtl), cudaMemcpyHostToDevice, b->st));
+        cudaGraphExec_t g = nullptr;
+        uint32_t launches = 0;
+        if ((rc = batch_graph(b, cnt, 0, &g, &launches, true))) return rc;
+        if (b->trace)
+            HS_CUDA_TRY(cudaMemcpyAsync(b->trace, b->trace_init, (size_t)b->trace_slots * 64, cudaMemcpyHostToDevice,
+                                        b->st));
+        HS_CUDA_TRY(cudaGraphLaunch(g, b->st));
+        if ((rc = batch_sync(b, cnt))) return rc;
+    }
+    return HS_OK;
 }
 
 int hs_batch_logits(hs_batch* b, uint32_t slot, float* host, uint64_t n) {

@@ -166,9 +166,11 @@ struct SplitAttnArgs {
     uint32_t* counters;      // [sequences][nkv], zero between launches
     DevCtl* ctl;             // per-sequence control blocks
     uint32_t layer, nh, nkv, max_ctx, layout, page_shift, max_splits;
+    uint32_t mode;           // ATTN_* below
     uint64_t* trace;
     uint32_t trace_slot;
 };
+enum AttnMode : uint32_t { ATTN_FULL = 0, ATTN_APPEND_ONLY = 1, ATTN_ATTEND_ONLY = 2 };
 // Positions per split for n cached positions: a multiple of 64, so that at
 // most max_splits splits cover n.
 __host__ __device__ inline uint32_t attn_split_len(uint32_t n, uint32_t max_splits) {

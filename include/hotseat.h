@@ -203,12 +203,19 @@ int hs_seq_end(hs_scratch* s, uint32_t* tokens, uint64_t* n_tokens, uint64_t cap
  * region, history, SeqState, sampler config and RNG. No counterpart type in
  * the reference. */
 typedef struct hs_batch hs_batch;
-int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out);
+int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out); /* max_seqs 1..1024 */
 void hs_batch_free(hs_batch* b);
 /* One Model::forward for each of n sequences: tokens[i] at pos[i], appending
  * to kvs[i] (all regions of one layout and page size). Blocks until done. */
 int hs_forward_batch(const hs_model* m, hs_kv* const* kvs, const uint32_t* tokens, const uint32_t* pos, uint32_t n,
                      hs_batch* b);
+/* Prompt prefill: Model::forward for tokens[0..n) of ONE sequence at
+ * positions pos0.., appended to `kv`, with the tokens as the rows of each
+ * GEMM (up to the batch capacity per pass) instead of one token per step.
+ * No logits; the KV rows are bit-identical to n single-token steps. Follow
+ * with hs_batch_seq_run from filled = pos0 + n: the sequence's next
+ * (last prompt) token then produces the logits of the first sample. */
+int hs_prefill(const hs_model* m, hs_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0, hs_batch* b);
 /* Logits of sequence `slot` from the last hs_forward_batch. */
 int hs_batch_logits(hs_batch* b, uint32_t slot, float* host, uint64_t n);
 /* hs_seq_run for n sequences at once: sequence i uses kvs[i], its history
@@ -228,6 +235,9 @@ int hs_batch_seq_end(hs_batch* b, uint32_t* const* tokens, uint64_t* n_tokens, u
 /* The batch's CUDA stream (cudaStream_t), and kernels launched per step. */
 void* hs_batch_stream(hs_batch* b);
 int hs_batch_launches_per_step(hs_batch* b, uint32_t* out);
+/* Launch timeline of the last batched forward or step (HS_TRACE=1 in the
+ * environment when the batch is created), in the layout of hs_scratch_trace. */
+int hs_batch_trace(hs_batch* b, uint64_t* out, uint64_t n_slots, uint64_t* used);
 
 /* The scratch's CUDA stream (cudaStream_t), for event timing. */
 void* hs_scratch_stream(hs_scratch* s);
