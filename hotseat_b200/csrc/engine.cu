@@ -203,7 +203,8 @@ struct LayerDev {
     float *attn_norm = nullptr, *ffn_norm = nullptr, *bqkv = nullptr;
     uint16_t *wqkv = nullptr, *wo = nullptr, *wgate = nullptr, *wup = nullptr, *wdown = nullptr;
     GemvPlan qkv, o, gu, down;
-    TcGemmPlan tq, to, tgu, tdown;  // tensor-core path
+    TcGemmPlan tq, to, tgu, tdown;  // tensor-core path (decode: split-K over a few M tiles)
+    TcGemmPlan pq, po, pgu, pdown;  // tensor-core prefill (many M tiles, no split)
 };
 
 struct hs_model {
@@ -402,7 +403,7 @@ uint32_t env_u32(const char* name, uint32_t dflt) {
 //   TC_PART : 64/128-row tiles, K split so tiles x splits ~ SM count; the
 //             consumer adds the split partials in split order.
 int plan_tc(TcGemmPlan* p, int epi, uint32_t rows, uint32_t K, const uint16_t* w0, const uint16_t* w1, int n_sm,
-            size_t smem_cap) {
+            size_t smem_cap, bool prefill = false) {
     if (K % 64) return fail(HS_E_UNSUPPORTED, "GEMM reduction length must be a multiple of 64");
     const bool silu = epi == TC_SILU;
     const uint32_t kt_n = K / 64, sm = (uint32_t)n_sm;
@@ -410,7 +411,13 @@ int plan_tc(TcGemmPlan* p, int epi, uint32_t rows, uint32_t K, const uint16_t* w
     p->K = K;
     p->rows = rows;
     p->splits = 1;
-    if (silu) {
+    if (prefill) {
+        // Prompt passes bring many 64-token M tiles: wide weight tiles, one
+        // K split, parallelism from the M dimension.
+        uint32_t nt = silu ? 64 : 128;
+        while (nt > 16 && nt / 2 >= rows) nt /= 2;
+        p->n_tile = nt;
+    } else if (silu) {
         uint32_t nt = 8;
         while (nt < 128 && (rows + nt - 1) / nt > sm) nt += 8;
         p->n_tile = nt;
@@ -424,7 +431,7 @@ int plan_tc(TcGemmPlan* p, int epi, uint32_t rows, uint32_t K, const uint16_t* w
                 p->n_tile = nt;
             }
         }
-    } else {
+    } else if (!prefill) {
         // The most CTAs in one wave with at most HS_TC_MAX_SPLITS (32) partials for the
         // consumer to add, then the wider tile (fewer activation re-reads).
         const uint32_t max_splits = env_u32("HS_TC_MAX_SPLITS", 32);
@@ -834,7 +841,12 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
                 (rc = plan_tc(&L.tgu, TC_SILU, d_ff, d_model, L.wgate, L.wup, m->n_sm, m->smem_cap)) ||
                 (rc = plan_tc(&L.tdown, TC_PART, d_model, d_ff, L.wdown, nullptr, m->n_sm, m->smem_cap)))
                 return rc;
-            for (const TcGemmPlan* q : {&L.tq, &L.to, &L.tdown})
+            if ((rc = plan_tc(&L.pq, TC_PART, (uint32_t)qrows, d_model, L.wqkv, nullptr, m->n_sm, m->smem_cap, true)) ||
+                (rc = plan_tc(&L.po, TC_PART, d_model, n_heads * hd, L.wo, nullptr, m->n_sm, m->smem_cap, true)) ||
+                (rc = plan_tc(&L.pgu, TC_SILU, d_ff, d_model, L.wgate, L.wup, m->n_sm, m->smem_cap, true)) ||
+                (rc = plan_tc(&L.pdown, TC_PART, d_model, d_ff, L.wdown, nullptr, m->n_sm, m->smem_cap, true)))
+                return rc;
+            for (const TcGemmPlan* q : {&L.tq, &L.to, &L.tdown, &L.pq, &L.po, &L.pdown})
                 m->tc_part_per_slot = std::max<uint64_t>(m->tc_part_per_slot, (uint64_t)q->splits * q->rows);
             continue;
         }
@@ -1544,14 +1556,18 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool pref
     };
     for (uint32_t l = 0; l < c.n_layers; l++) {
         const LayerDev& L = m->layers[l];
+        const TcGemmPlan& Pq = prefill ? L.pq : L.tq;
+        const TcGemmPlan& Po = prefill ? L.po : L.to;
+        const TcGemmPlan& Pgu = prefill ? L.pgu : L.tgu;
+        const TcGemmPlan& Pdown = prefill ? L.pdown : L.tdown;
         if ((rc = norm(L.attn_norm, prev_down, l == 0))) return rc;
-        if ((rc = batch_gemm(b, L.tq, b->xn_hi, b->xn_lo, n, b->part, nullptr, nullptr, qrows, launches))) return rc;
+        if ((rc = batch_gemm(b, Pq, b->xn_hi, b->xn_lo, n, b->part, nullptr, nullptr, qrows, launches))) return rc;
         cudaError_t e;
         if (m->attn_split) {
             SplitAttnArgs sa{};
             sa.qkv = b->part;
-            sa.n_part = L.tq.splits;
-            sa.part_stride = (uint64_t)b->cap_slots * L.tq.rows;
+            sa.n_part = Pq.splits;
+            sa.part_stride = (uint64_t)b->cap_slots * Pq.rows;
             sa.bias = L.bqkv;
             sa.qkv_rows = qrows;
             sa.kv = b->kv_tab;
@@ -1589,11 +1605,11 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool pref
         }
         if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
         (*launches)++;
-        if ((rc = batch_gemm(b, L.to, b->att_hi, b->att_lo, n, b->part, nullptr, nullptr, d, launches))) return rc;
-        if ((rc = norm(L.ffn_norm, &L.to, false))) return rc;
-        if ((rc = batch_gemm(b, L.tgu, b->xn_hi, b->xn_lo, n, nullptr, b->hb_hi, b->hb_lo, c.d_ff, launches))) return rc;
-        if ((rc = batch_gemm(b, L.tdown, b->hb_hi, b->hb_lo, n, b->part, nullptr, nullptr, d, launches))) return rc;
-        prev_down = &L.tdown;
+        if ((rc = batch_gemm(b, Po, b->att_hi, b->att_lo, n, b->part, nullptr, nullptr, d, launches))) return rc;
+        if ((rc = norm(L.ffn_norm, &Po, false))) return rc;
+        if ((rc = batch_gemm(b, Pgu, b->xn_hi, b->xn_lo, n, nullptr, b->hb_hi, b->hb_lo, c.d_ff, launches))) return rc;
+        if ((rc = batch_gemm(b, Pdown, b->hb_hi, b->hb_lo, n, b->part, nullptr, nullptr, d, launches))) return rc;
+        prev_down = &Pdown;
     }
     if (prefill) return HS_OK;  // prompt positions: no logits (x past the last layer is not read)
     if ((rc = norm(m->out_norm, prev_down, false))) return rc;

@@ -2,6 +2,7 @@
 
     python -m hotseat_b200.microbench dequant     # Q4_K/Q6_K -> f16 load-time dequantisation
     python -m hotseat_b200.microbench attention   # GQA decode attention at 1k-32k context
+    python -m hotseat_b200.microbench prefill     # 1.5B shape: 16 x 2048-token prefill, 512 greedy steps
 
 dequant: the tensors of the seeded Qwen2.5-0.5B-shape GGUF (ffn_gate 4864x896
 and ffn_down 896x4864 in Q4_K, token_embd 151936x896 in Q6_K) plus the same
@@ -16,6 +17,13 @@ attention time of a layer is its kernel's exit minus the QKV kernel's exit
 (the work it adds after its input is ready), averaged over the 24 layers.
 Bytes = (P+1) x 1024 B of K and V read + 1024 B written per sequence and
 layer (14 query / 2 KV heads, head_dim 64, f32).
+
+prefill: the seeded Qwen2.5-1.5B-shape GGUF (28 layers, d 1536, 12/2 heads,
+head_dim 128, ff 8960, vocab 151936), 16 sequences with 2048-token
+uniform-random prompts, each prefilled by hs_prefill (2047 tokens as GEMM rows,
+up to 512 per pass), then the 16 decoded together for 512 greedy tokens
+(temperature 0, penalty 1.1). FLOPs = 2 x (non-embedding weights) per token
+for the GEMMs (the tensor cores execute twice that: f16 hi and lo halves).
 
 Each line printed is one JSON object; peaks are the measured copy bandwidth
 in MEASURED_PEAKS.json when present.
@@ -192,9 +200,80 @@ def bench_attention(ctxs=(1024, 4096, 16384, 32767)):
     os.rmdir(td)
 
 
+def bench_prefill(n_seqs=16, prompt=2048, gen=512):
+    import torch
+    import hotseat_b200 as hs
+    peak_bw, _ = _peak()
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        tflops, tsrc = float(peaks["bf16_tflops"]), "measured"
+    except (OSError, ValueError, KeyError):
+        tflops, tsrc = 1590.0, "fallback"
+    td = tempfile.mkdtemp(prefix="hsmicro")
+    path = os.path.join(td, "q15.gguf")
+    hs.write_synthetic_gguf(path, seed=1234, **hs.QWEN15)
+    c = hs.QWEN15
+    hd = c["d_model"] // c["n_heads"]
+    qrows = (c["n_heads"] + 2 * c["n_kv_heads"]) * hd
+    layer_w = c["d_model"] * qrows + c["d_model"] * c["d_model"] + 3 * c["d_model"] * c["d_ff"]
+    m = hs.Model.load(path, max_ctx=prompt + gen + 8, numeric=hs.NUMERIC_TC)
+    kvs = [m.kv() for _ in range(n_seqs)]
+    prompts = [[int(t) for t in np.random.default_rng(2048 + i).integers(0, c["vocab"], size=prompt)]
+               for i in range(n_seqs)]
+    pb = hs.Batch(m, 512)
+    stream = torch.cuda.ExternalStream(pb.stream)
+    pb.prefill(kvs[0], prompts[0][:512])  # warm-up (graphs)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for kv, p in zip(kvs, prompts):
+        pb.prefill(kv, p[:-1])
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    toks = n_seqs * (prompt - 1)
+    flops = 2.0 * c["n_layers"] * layer_w * toks
+    tf = flops / (ms / 1000.0) / 1e12
+    print(json.dumps({"bench": "prefill", "model": "qwen2.5-1.5b-shape", "sequences": n_seqs, "prompt": prompt,
+                      "ms": ms, "tok/s": toks / (ms / 1000.0), "gemm_TFLOP/s": tf, "peak_TFLOP/s": tflops,
+                      "frac": tf / tflops, "peak_source": tsrc,
+                      "note": "algorithmic 2*weights*tokens; the tensor cores run twice that (hi/lo halves)"}),
+          flush=True)
+    cfg = hs.SamplerCfg.default(temperature=0.0)
+    db = hs.Batch(m, n_seqs)
+    seqs = [dict(tokens=p, prompt_len=prompt, max_tokens=gen, cfg=cfg, rng=hs.Rng.seed(i), filled=prompt - 1)
+            for i, p in enumerate(prompts)]
+    dstream = torch.cuda.ExternalStream(db.stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(dstream)
+    out = db.run_seqs(kvs, seqs)
+    e1.record(dstream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    gen_toks = sum(len(t) - prompt for t, _, _ in out)
+    step_bytes = c["n_layers"] * layer_w * 2 + c["vocab"] * c["d_model"] * 2
+    steps = max(len(t) - prompt for t, _, _ in out) + 1
+    kv_row = c["n_layers"] * 2 * c["n_kv_heads"] * hd * 4
+    kv_bytes = n_seqs * kv_row * np.mean([p + 1 for p in range(prompt - 1, prompt + gen - 1)])
+    gbs = (step_bytes + kv_bytes) * steps / (ms / 1000.0) / 1e9
+    print(json.dumps({"bench": "decode", "model": "qwen2.5-1.5b-shape", "batch": n_seqs, "context_from": prompt,
+                      "generated": gen_toks, "ms": ms, "tok/s": gen_toks / (ms / 1000.0), "GB/s": gbs,
+                      "frac": gbs / peak_bw, "note": "hs_batch_seq_run end to end, greedy, penalty 1.1"}),
+          flush=True)
+    for k in kvs:
+        k.close()
+    pb.close()
+    db.close()
+    m.close()
+    os.remove(path)
+    os.rmdir(td)
+
+
 if __name__ == "__main__":
     which = sys.argv[1] if len(sys.argv) > 1 else "all"
     if which in ("dequant", "all"):
         bench_dequant()
     if which in ("attention", "all"):
         bench_attention()
+    if which in ("prefill", "all"):
+        bench_prefill()
