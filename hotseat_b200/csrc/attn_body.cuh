@@ -1,0 +1,356 @@
+// One (split, KV head, sequence) item of the split-KV GQA decode attention
+// (model.rs:259-305 with an online softmax over chunks of 64 cached
+// positions), shared by the split-attention kernel (attn_split.cu) and the
+// persistent token kernel (token_fast.cu).
+//
+// A sequence at `pos` has n = pos+1 positions; split_len(n) positions per
+// split (a multiple of 64, at most max_splits splits) and S = ceil(n /
+// split_len) splits. The item rebuilds q (the group's query heads) and the new
+// k, v from the QKV product (split-K partials added in split order, then the
+// bias), applies RoPE (model.rs:365-373); split 0 appends k, v at `pos` to the
+// sequence's KV region and marks the dirty pages (model.rs:268-275); the split
+// holding `pos` uses its own copy of that row.
+//
+// Per chunk: scores for the group's heads, chunk maximum, rescale of the
+// running sum and output, P.V. A single split writes the normalised output;
+// otherwise each split writes (max, sum, unnormalised output) and the item
+// that arrives last at the (sequence, KV head) counter combines the splits in
+// split order and resets the counter. Every choice depends on n and max_ctx
+// only, never on the batch or the grid, so a sequence's bits are the same in
+// any batch and in either kernel. NBUF (1 or 2) is the number of K/V chunk
+// buffers: it changes how loads overlap compute, not the arithmetic.
+//
+// Runs on threads 0..255 of the CTA and synchronises them with named barrier
+// 1, so a CTA may keep other warps (a producer) outside it.
+#pragma once
+
+#include <cfloat>
+
+#include "kernels.h"
+
+namespace hs {
+namespace attn {
+
+constexpr uint32_t kThreads = 256;
+constexpr uint32_t kCh = 64;  // positions per chunk
+
+__device__ __forceinline__ uint32_t ldv(const uint32_t* p) { return *(const volatile uint32_t*)p; }
+__device__ __forceinline__ void sync256() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void split_f16(float x, uint16_t* hi, uint16_t* lo) {
+    const __half h = __float2half_rn(x);
+    *hi = __half_as_ushort(h);
+    *lo = __half_as_ushort(__float2half_rn(__fsub_rn(x, __half2float(h))));
+}
+__device__ __forceinline__ float4 f4add(float4 a, float4 b) {
+    return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+
+// Shared memory of one item (floats): q [8][HD], k, v [HD], K/V chunks
+// [2][NBUF][kCh][HD+4], probabilities [8][kCh], per-head max/rescale/sum
+// [3][8], a flag word (4 floats), the RoPE row of `pos` [HD/2 cos, HD/2 sin].
+__host__ __device__ constexpr size_t item_smem(uint32_t hd, uint32_t nbuf) {
+    return (8 * hd + 2 * hd + 2 * nbuf * kCh * (hd + 4) + 8 * kCh + 3 * 8 + 4 + hd) * sizeof(float);
+}
+__host__ __device__ constexpr uint32_t item_rope_off(uint32_t hd, uint32_t nbuf) {
+    return 8 * hd + 2 * hd + 2 * nbuf * kCh * (hd + 4) + 8 * kCh + 3 * 8 + 4;
+}
+
+// Split-order combine of the S published splits of one (sequence, KV head)
+// for output element idx (head idx / HD of the group, dimension idx % HD):
+// the maximum of the split maxima, then the rescaled sums and outputs in
+// split order. GLOBAL: the partials are read through L2 (written by other
+// CTAs); else from a shared-memory copy.
+template <bool GLOBAL>
+__device__ __forceinline__ float combine(const float* part, uint32_t S, uint32_t G, uint32_t hd, uint32_t idx) {
+    const uint32_t rec = G * hd + 2 * G, h = idx / hd;
+    auto ld = [&](size_t i) { return GLOBAL ? __ldcg(part + i) : part[i]; };
+    float M = -FLT_MAX;
+    for (uint32_t q = 0; q < S; q++) M = fmaxf(M, ld((size_t)q * rec + G * hd + h));
+    float num = 0.0f, den = 0.0f;
+    for (uint32_t q = 0; q < S; q++) {
+        const float w = __expf(__fsub_rn(ld((size_t)q * rec + G * hd + h), M));
+        num = __fadd_rn(num, __fmul_rn(w, ld((size_t)q * rec + idx)));
+        den = __fadd_rn(den, __fmul_rn(w, ld((size_t)q * rec + G * hd + G + h)));
+    }
+    return __fdiv_rn(num, den);
+}
+
+__device__ __forceinline__ uint64_t kv_row_off(const SplitAttnArgs& a, uint32_t layer, uint32_t kvh, uint32_t hd,
+                                               uint32_t p, uint32_t is_v) {
+    const uint64_t plane = (uint64_t)a.max_ctx * a.nkv * hd;
+    const uint64_t within = a.layout == 0 ? ((uint64_t)p * a.nkv + kvh) * hd : ((uint64_t)kvh * a.max_ctx + p) * hd;
+    return (uint64_t)layer * 2 * plane + (is_v ? plane : 0) + within;
+}
+
+// Issues (and commits) the asynchronous loads of the cached rows of an
+// item's first chunk, all but `pos`, into its K/V buffers: those rows do not
+// depend on this token, so a caller may start them before the QKV product
+// exists and then run item(..., prefetched = true).
+template <int HD, int NBUF>
+__device__ void prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t slot,
+                         uint32_t pos, float* sm) {
+    constexpr uint32_t RS = HD + 4;
+    float* kb = sm + 10 * HD;
+    float* vb = kb + NBUF * kCh * RS;
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits);
+    const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n, cnt = p1 - p0 < kCh ? p1 - p0 : kCh;
+    const float* kv = a.kv[slot];
+    float* rope = sm + item_rope_off(HD, NBUF);
+    if (threadIdx.x < HD / 4) {  // HD/8 16-byte pieces of each of the cos and sin halves
+        const uint32_t i = threadIdx.x % (HD / 8), half = threadIdx.x / (HD / 8);
+        const float* src = (half ? a.rope_sin : a.rope_cos) + (size_t)pos * (HD / 2) + 4 * i;
+        cp_async16(rope + half * (HD / 2) + 4 * i, src);
+    }
+    for (uint32_t idx = threadIdx.x; idx < cnt * (HD / 4); idx += kThreads) {
+        const uint32_t r = idx / (HD / 4), c4 = idx % (HD / 4);
+        if (p0 + r == pos) continue;
+        cp_async16(kb + r * RS + 4 * c4, kv + kv_row_off(a, layer, kvh, HD, p0 + r, 0) + 4 * c4);
+        cp_async16(vb + r * RS + 4 * c4, kv + kv_row_off(a, layer, kvh, HD, p0 + r, 1) + 4 * c4);
+    }
+    cp_commit();
+}
+
+// Preconditions (checked by the caller): the sequence is active, pos <
+// max_ctx, s < S (attend) or s == 0 (append only); `prefetched` only in
+// ATTN_FULL mode after prefetch() of the same item (which also loaded the
+// RoPE row). `layer` selects the KV planes (a.layer is not read). With
+// `reader_combines`, several splits only publish their partials: the reader
+// of the output combines them (combine()) after a grid-wide barrier.
+template <int HD, int NBUF>
+__device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t slot, uint32_t pos,
+                     float* sm, bool prefetched = false, bool reader_combines = false) {
+    static_assert(NBUF == 1 || NBUF == 2, "one or two chunk buffers");
+    constexpr uint32_t RS = HD + 4, HALF = HD / 2;
+    constexpr uint32_t HSETS = kThreads / HD, HPT = (8 + HSETS - 1) / HSETS;
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t G = a.nh / a.nkv;
+    float* qs = sm;                        // [8][HD]
+    float* kn = qs + 8 * HD;               // [HD]
+    float* vn = kn + HD;                   // [HD]
+    float* kb = vn + HD;                   // [NBUF][kCh][RS]
+    float* vb = kb + NBUF * kCh * RS;      // [NBUF][kCh][RS]
+    float* sp = vb + NBUF * kCh * RS;      // [8][kCh] scores, then probabilities
+    float* hs_m = sp + 8 * kCh;            // [8] running maximum per head
+    float* hs_f = hs_m + 8;                // [8] rescale of the running sums this chunk
+    float* hs_l = hs_f + 8;                // [8] running sums
+    uint32_t* flag = reinterpret_cast<uint32_t*>(hs_l + 8);
+    const float* rope = sm + item_rope_off(HD, NBUF);
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits), S = (n + L - 1) / L;
+    // Prefill runs append (every token's k, v) and attend (reading all rows
+    // from memory) as two launches, so tokens of one sequence in one batch
+    // see each other's rows.
+    const bool append = a.mode != ATTN_ATTEND_ONLY, attend = a.mode != ATTN_APPEND_ONLY;
+    const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n;
+    float* kv = a.kv[slot];
+    auto row_off = [&](uint32_t p, uint32_t is_v) -> uint64_t { return kv_row_off(a, layer, kvh, HD, p, is_v); };
+    // split 0 appends the new row; read the tracking flag now, mark later
+    const bool track = s == 0 && append && tid < 2 && ldv(a.tracking[slot]) != 0;
+
+    // q, k, v of this group; split-K partials in split order, then the bias.
+    const uint32_t qrow0 = kvh * G * HD, krow0 = a.nh * HD + kvh * HD, vrow0 = (a.nh + a.nkv) * HD + kvh * HD;
+    for (uint32_t c = tid; c < (G + 2) * HD / 4; c += kThreads) {
+        const uint32_t idx = 4 * c;
+        const uint32_t row = idx < G * HD ? qrow0 + idx : (idx < (G + 1) * HD ? krow0 + idx - G * HD : vrow0 + idx - (G + 1) * HD);
+        const float* src = a.qkv + (size_t)slot * a.qkv_rows + row;
+        float4 p = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (uint32_t q0 = 0; q0 < a.n_part; q0 += 8) {
+            float4 v[8];
+#pragma unroll
+            for (uint32_t j = 0; j < 8; j++)
+                if (q0 + j < a.n_part) v[j] = __ldcg(reinterpret_cast<const float4*>(src + (q0 + j) * a.part_stride));
+#pragma unroll
+            for (uint32_t j = 0; j < 8; j++)
+                if (q0 + j < a.n_part) p = f4add(p, v[j]);
+        }
+        if (a.bias) p = f4add(p, *reinterpret_cast<const float4*>(a.bias + row));
+        float* dst = idx < G * HD ? qs + idx : (idx < (G + 1) * HD ? kn + idx - G * HD : vn + idx - (G + 1) * HD);
+        *reinterpret_cast<float4*>(dst) = p;
+    }
+    if (prefetched) cp_wait0();  // the RoPE row (and the first chunk)
+    sync256();
+    for (uint32_t idx = tid; idx < (G + 1) * HALF; idx += kThreads) {
+        const uint32_t h = idx / HALF, i = idx % HALF;
+        float* r = h < G ? qs + h * HD : kn;
+        const float c = prefetched ? rope[i] : a.rope_cos[(size_t)pos * HALF + i];
+        const float sn = prefetched ? rope[HALF + i] : a.rope_sin[(size_t)pos * HALF + i];
+        const float x0 = r[i], x1 = r[i + HALF];
+        r[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+        r[i + HALF] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+    }
+    if (tid < 8) {
+        hs_m[tid] = -FLT_MAX;
+        hs_l[tid] = 0.0f;
+    }
+    sync256();
+    if (s == 0 && append && tid < HD) {
+        kv[row_off(pos, 0) + tid] = kn[tid];
+        kv[row_off(pos, 1) + tid] = vn[tid];
+    }
+    // Dirty-page bits of the appended row, set after the row is visible (a
+    // harvest may run concurrently); called after a block barrier that
+    // follows the row's stores.
+    auto mark_dirty = [&]() {
+        if (track) {
+            __threadfence();
+            const uint64_t off = row_off(pos, tid) * 4, last = off + HD * 4 - 1;
+            uint64_t* dirty = a.dirty[slot];
+            for (uint64_t pg = off >> a.page_shift; pg <= (last >> a.page_shift); pg++)
+                atomicOr(reinterpret_cast<unsigned long long*>(&dirty[pg >> 6]), 1ull << (pg & 63));
+        }
+    };
+    if (!attend) {
+        sync256();
+        mark_dirty();
+        return;
+    }
+
+    const uint32_t nch = (p1 - p0 + kCh - 1) / kCh;
+    auto issue = [&](uint32_t c) {
+        if (c < nch) {
+            const uint32_t c0 = p0 + c * kCh, cnt = p1 - c0 < kCh ? p1 - c0 : kCh;
+            float* kd = kb + (c % NBUF) * kCh * RS;
+            float* vd = vb + (c % NBUF) * kCh * RS;
+            for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += kThreads) {
+                const uint32_t r = idx / (HD / 4), c4 = idx % (HD / 4);
+                if (c0 + r == pos && append) {
+                    *reinterpret_cast<float4*>(kd + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(kn + 4 * c4);
+                    *reinterpret_cast<float4*>(vd + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(vn + 4 * c4);
+                } else if (!(prefetched && c == 0)) {
+                    cp_async16(kd + r * RS + 4 * c4, kv + row_off(c0 + r, 0) + 4 * c4);
+                    cp_async16(vd + r * RS + 4 * c4, kv + row_off(c0 + r, 1) + 4 * c4);
+                }
+            }
+        }
+        cp_commit();
+    };
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+    float o[HPT];
+#pragma unroll
+    for (uint32_t j = 0; j < HPT; j++) o[j] = 0.0f;
+    const uint32_t dd = tid % HD, hs0 = tid / HD;
+    if (NBUF == 2) issue(0);
+    for (uint32_t c = 0; c < nch; c++) {
+        if (NBUF == 2) {
+            issue(c + 1);
+            cp_wait1();
+        } else {
+            issue(c);
+            cp_wait0();
+        }
+        sync256();
+        const uint32_t c0 = p0 + c * kCh, cnt = p1 - c0 < kCh ? p1 - c0 : kCh;
+        const float* kc = kb + (c % NBUF) * kCh * RS;
+        const float* vc = vb + (c % NBUF) * kCh * RS;
+        // scores: thread t takes position t % 64 and heads t/64, t/64 + 4
+        {
+            const uint32_t r = tid % kCh;
+            for (uint32_t h = tid / kCh; h < G; h += kThreads / kCh) {
+                float v = -FLT_MAX;
+                if (r < cnt) {
+                    const float4* k4 = reinterpret_cast<const float4*>(kc + r * RS);
+                    const float4* q4 = reinterpret_cast<const float4*>(qs + h * HD);
+                    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+#pragma unroll
+                    for (uint32_t d4 = 0; d4 < HD / 4; d4++) {
+                        const float4 kk = k4[d4], qq = q4[d4];
+                        s0 = __fmaf_rn(qq.x, kk.x, s0);
+                        s1 = __fmaf_rn(qq.y, kk.y, s1);
+                        s2 = __fmaf_rn(qq.z, kk.z, s2);
+                        s3 = __fmaf_rn(qq.w, kk.w, s3);
+                    }
+                    v = __fmul_rn(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), scale);
+                }
+                sp[h * kCh + r] = v;
+            }
+        }
+        sync256();
+        // online softmax: warp h owns head h
+        if (warp < G) {
+            float* sh = sp + warp * kCh;
+            const float a0 = sh[lane], a1 = sh[lane + 32];
+            float mx = fmaxf(a0, a1);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float m_old = hs_m[warp], m_new = fmaxf(m_old, mx);
+            const float e0 = lane < cnt ? __expf(__fsub_rn(a0, m_new)) : 0.0f;
+            const float e1 = lane + 32 < cnt ? __expf(__fsub_rn(a1, m_new)) : 0.0f;
+            sh[lane] = e0;
+            sh[lane + 32] = e1;
+            float sum = __fadd_rn(e0, e1);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
+            if (lane == 0) {
+                const float f = m_old == -FLT_MAX ? 0.0f : __expf(__fsub_rn(m_old, m_new));
+                hs_f[warp] = f;
+                hs_m[warp] = m_new;
+                hs_l[warp] = __fadd_rn(__fmul_rn(hs_l[warp], f), sum);
+            }
+        }
+        sync256();
+        // P.V: thread t owns dimension t % HD of heads t/HD, t/HD + HSETS, ...
+#pragma unroll
+        for (uint32_t j = 0; j < HPT; j++) {
+            const uint32_t h = hs0 + j * HSETS;
+            if (h >= G) break;
+            const float* ph = sp + h * kCh;
+            float acc = 0.0f;
+            for (uint32_t r = 0; r < cnt; r++) acc = __fmaf_rn(ph[r], vc[r * RS + dd], acc);
+            o[j] = __fadd_rn(__fmul_rn(o[j], hs_f[h]), acc);
+        }
+        sync256();
+    }
+    cp_wait0();
+    mark_dirty();
+
+    auto store = [&](size_t at, float v) {
+        if (a.out_f32) {
+            a.out_f32[at] = v;
+        } else {
+            uint16_t hi, lo;
+            split_f16(v, &hi, &lo);
+            a.out_hi[at] = hi;
+            a.out_lo[at] = lo;
+        }
+    };
+    if (S == 1) {
+#pragma unroll
+        for (uint32_t j = 0; j < HPT; j++) {
+            const uint32_t h = hs0 + j * HSETS;
+            if (h < G) store((size_t)slot * a.out_stride + (size_t)(kvh * G + h) * HD + dd, __fdiv_rn(o[j], hs_l[h]));
+        }
+        return;
+    }
+    // Several splits: publish (unnormalised output, max, sum); the last item
+    // to arrive combines all splits in split order.
+    const uint32_t rec = G * HD + 2 * G;
+    float* part = a.partials + ((size_t)(slot * a.nkv + kvh) * a.max_splits) * rec;
+#pragma unroll
+    for (uint32_t j = 0; j < HPT; j++) {
+        const uint32_t h = hs0 + j * HSETS;
+        if (h < G) part[(size_t)s * rec + h * HD + dd] = o[j];
+    }
+    if (tid < G) {
+        part[(size_t)s * rec + G * HD + tid] = hs_m[tid];
+        part[(size_t)s * rec + G * HD + G + tid] = hs_l[tid];
+    }
+    if (reader_combines) return;
+    __threadfence();
+    sync256();
+    uint32_t* counter = a.counters + slot * a.nkv + kvh;
+    if (tid == 0) *flag = atomicAdd(counter, 1u) == S - 1 ? 1u : 0u;
+    sync256();
+    const bool last = *flag != 0;
+    sync256();  // the flag word is rewritten by the next item
+    if (!last) return;
+    __threadfence();
+    for (uint32_t idx = tid; idx < G * HD; idx += kThreads)
+        store((size_t)slot * a.out_stride + (size_t)kvh * G * HD + idx, combine<true>(part, S, G, HD, idx));
+    if (tid == 0) *counter = 0;
+}
+
+}  // namespace attn
+}  // namespace hs

@@ -1,9 +1,9 @@
 // Batch-1 token-loop kernels in the GPU-native numeric order ("fast" mode).
 //
 // Same model and the same fused prologues/epilogues as decode.cu (RMSNorm on
-// the way in; bias, residual add or SiLU gate on the way out; RoPE, KV append
-// and dirty-page marking in attention), but every reduction uses a fixed
-// parallel shape instead of the reference's eight serial lanes:
+// the way in; bias, residual add or SiLU gate on the way out), but every
+// reduction uses a fixed parallel shape instead of the reference's eight
+// serial lanes:
 //
 //   GEMV row r:  a group of T threads (T = 32..256, from the row length only);
 //                thread t owns the 16-byte weight chunks t, t+T, t+2T, ... and
@@ -12,16 +12,15 @@
 //                order; the group then reduces by a fixed xor tree and a fixed
 //                warp order.
 //   RMSNorm:     sum of squares over 32 lanes, xor tree.
-//   attention:   per-position dot products, block max/sum in a fixed tree,
-//                P.V split by warps over positions and combined in warp order.
+//   attention:   split-KV with an online softmax (attn_split.cu).
+//
+// token_fast.cu runs the same arithmetic as one persistent kernel per token.
 //
 // Each choice depends only on the tensor shapes, never on the SM count or on
 // the batch, so the result for a sequence is bit-identical on every B200 and
 // across a migration between GPUs. It is not bit-identical to the CPU
 // reference (the serial lane order is what makes that path slow on a GPU);
 // the token loop holds it to logits within 1e-2 of the CPU path.
-#include <cfloat>
-
 #include "common.h"
 #include "kernels.h"
 
@@ -271,183 +270,6 @@ __global__ void __launch_bounds__(256) k_gemv_fast(const __grid_constant__ CUten
     tr.exit();
 }
 
-// ------------------------------------------------------------ attention
-template <int HD>
-struct FastAttnShape {
-    static constexpr int RS = HD + 4;       // padded row stride (floats)
-    static constexpr int PRE = 12288 / HD;  // rows of K and V prefetched before the wait
-    static constexpr int CH = 4096 / HD;    // rows per streamed chunk beyond PRE
-};
-
-template <int HD>
-__global__ void __launch_bounds__(256) k_attention_fast(const AttnArgs a) {
-    extern __shared__ __align__(16) float sm[];
-    using S = FastAttnShape<HD>;
-    constexpr int RS = S::RS, PRE = S::PRE, CH = S::CH, HALF = HD / 2, DPL = HD / 32;  // dims per lane
-    float* q = sm;
-    float* kc = q + HD;
-    float* vc = kc + HD;
-    float* red = vc + HD;        // [64]
-    float* part = red + 64;      // [8][HD]
-    float* kb = part + 8 * HD;   // [PRE][RS]
-    float* vb = kb + PRE * RS;   // [PRE][RS]
-    float* cb = vb + PRE * RS;   // [CH][RS]
-    // [max_ctx] scores: shared memory, or this head's row of a global buffer
-    // when max_ctx scores do not fit next to the K/V staging.
-    float* sc = a.sc_global ? a.sc_global + (size_t)blockIdx.x * a.max_ctx : cb + CH * RS;
-    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const KTrace tr(a.trace, a.trace_slot);
-    tr.enter();
-    DevCtl* ctl = a.ctl;
-    const uint32_t h = blockIdx.x, groups = a.nh / a.nkv, kvh = h / groups;
-    const uint64_t plane = (uint64_t)a.max_ctx * a.nkv * HD;
-    const uint64_t lbase = (uint64_t)a.layer * 2 * plane;
-    auto row_off = [&](uint32_t p, uint32_t is_v) -> uint64_t {
-        uint64_t within = a.layout == 0 ? ((uint64_t)p * a.nkv + kvh) * HD : ((uint64_t)kvh * a.max_ctx + p) * HD;
-        return lbase + (is_v ? plane : 0) + within;
-    };
-    const bool run = ld_volatile(&ctl->active) != 0;
-    const uint32_t pos = ld_volatile(&ctl->pos);
-    const bool pos_ok = pos < a.max_ctx;
-    const uint32_t npre = run && pos_ok ? min(pos, (uint32_t)PRE) : 0;
-    for (uint32_t idx = tid; idx < npre * (HD / 4); idx += blockDim.x) {
-        const uint32_t p = idx / (HD / 4), c4 = idx % (HD / 4);
-        cp_async16(kb + p * RS + 4 * c4, a.kv + row_off(p, 0) + 4 * c4);
-        cp_async16(vb + p * RS + 4 * c4, a.kv + row_off(p, 1) + 4 * c4);
-    }
-    pdl_launch_dependents();
-    pdl_wait();
-    tr.waited();
-    if (!run || !pos_ok) {
-        cp_async_wait_all();
-        if (run && tid == 0 && blockIdx.x == 0) atomicOr(&ctl->err, ERR_POS);
-        return;
-    }
-    if (tid < HD) {
-        q[tid] = __ldcg(a.qkv + h * HD + tid);
-        kc[tid] = __ldcg(a.qkv + a.nh * HD + kvh * HD + tid);
-        vc[tid] = __ldcg(a.qkv + (a.nh + a.nkv) * HD + kvh * HD + tid);
-    }
-    __syncthreads();
-    if (tid < HALF) {
-        const float c = a.rope_cos[(size_t)pos * HALF + tid], s = a.rope_sin[(size_t)pos * HALF + tid];
-        float x0 = q[tid], x1 = q[tid + HALF];
-        q[tid] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        q[tid + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-        x0 = kc[tid];
-        x1 = kc[tid + HALF];
-        kc[tid] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        kc[tid + HALF] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-    }
-    __syncthreads();
-    if (h % groups == 0) {
-        if (tid < HD) {
-            a.kv[row_off(pos, 0) + tid] = kc[tid];
-            a.kv[row_off(pos, 1) + tid] = vc[tid];
-        }
-        __syncthreads();
-        if (tid < 2 && ld_volatile(a.tracking)) {
-            __threadfence();
-            const uint64_t off = row_off(pos, tid) * 4, last = off + HD * 4 - 1;
-            for (uint64_t pg = off >> a.page_shift; pg <= (last >> a.page_shift); pg++)
-                atomicOr(reinterpret_cast<unsigned long long*>(&a.dirty[pg >> 6]), 1ull << (pg & 63));
-        }
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    tr.mark(1);
-
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-    const uint32_t n = pos + 1;
-    // 16-byte row reads: the 68/132-float row stride puts 8 consecutive rows
-    // in 8 different bank groups.
-    auto score = [&](const float* kr) -> float {
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        const float4* k4 = reinterpret_cast<const float4*>(kr);
-        const float4* q4 = reinterpret_cast<const float4*>(q);
-#pragma unroll
-        for (int d = 0; d < HD / 4; d += 2) {
-            const float4 ka = k4[d], kb2 = k4[d + 1], qa = q4[d], qb = q4[d + 1];
-            acc[0] = __fmaf_rn(qa.x, ka.x, acc[0]);
-            acc[1] = __fmaf_rn(qa.y, ka.y, acc[1]);
-            acc[2] = __fmaf_rn(qa.z, ka.z, acc[2]);
-            acc[3] = __fmaf_rn(qa.w, ka.w, acc[3]);
-            acc[4] = __fmaf_rn(qb.x, kb2.x, acc[4]);
-            acc[5] = __fmaf_rn(qb.y, kb2.y, acc[5]);
-            acc[6] = __fmaf_rn(qb.z, kb2.z, acc[6]);
-            acc[7] = __fmaf_rn(qb.w, kb2.w, acc[7]);
-        }
-        return (((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]))) * scale;
-    };
-    for (uint32_t p = tid; p < npre; p += blockDim.x) sc[p] = score(kb + p * RS);
-    if (tid == 0) sc[pos] = score(kc);
-    for (uint32_t c0 = npre; c0 < pos; c0 += CH) {
-        const uint32_t cnt = min((uint32_t)CH, pos - c0);
-        __syncthreads();
-        for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += blockDim.x) {
-            const uint32_t rr = idx / (HD / 4), c4 = idx % (HD / 4);
-            *reinterpret_cast<float4*>(cb + rr * RS + 4 * c4) =
-                __ldcg(reinterpret_cast<const float4*>(a.kv + row_off(c0 + rr, 0) + 4 * c4));
-        }
-        __syncthreads();
-        if (tid < cnt) sc[c0 + tid] = score(cb + tid * RS);
-    }
-    __syncthreads();
-    // max, exp, sum: fixed trees
-    float mx = __int_as_float(0xff800000);
-    for (uint32_t p = tid; p < n; p += blockDim.x) mx = fmaxf(mx, sc[p]);
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    mx = red[0];
-    for (uint32_t w = 1; w < 8; w++) mx = fmaxf(mx, red[w]);
-    float sum = 0.0f;
-    for (uint32_t p = tid; p < n; p += blockDim.x) {
-        const float e = ref_exp(sc[p] - mx);
-        sc[p] = e;
-        sum += e;
-    }
-    sum = warp_sum(sum);
-    __syncthreads();
-    if (lane == 0) red[8 + warp] = sum;
-    __syncthreads();
-    float total = 0.0f;
-    for (uint32_t w = 0; w < 8; w++) total += red[8 + w];
-    const float inv = 1.0f / total;
-    tr.mark(2);
-    // P.V: warp w takes positions p = w, w+8, ...; lane owns DPL dims.
-    float o[DPL];
-#pragma unroll
-    for (int i = 0; i < DPL; i++) o[i] = 0.0f;
-    auto accum = [&](uint32_t p, const float* vr) {
-        const float pw = sc[p];
-#pragma unroll
-        for (int i = 0; i < DPL; i++) o[i] = __fmaf_rn(pw, vr[lane * DPL + i], o[i]);
-    };
-    for (uint32_t p = warp; p < npre; p += 8) accum(p, vb + p * RS);
-    for (uint32_t c0 = npre; c0 < pos; c0 += CH) {
-        const uint32_t cnt = min((uint32_t)CH, pos - c0);
-        __syncthreads();
-        for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += blockDim.x) {
-            const uint32_t rr = idx / (HD / 4), c4 = idx % (HD / 4);
-            *reinterpret_cast<float4*>(cb + rr * RS + 4 * c4) =
-                __ldcg(reinterpret_cast<const float4*>(a.kv + row_off(c0 + rr, 1) + 4 * c4));
-        }
-        __syncthreads();
-        for (uint32_t t = warp; t < cnt; t += 8) accum(c0 + t, cb + t * RS);
-    }
-    if (warp == pos % 8) accum(pos, vc);
-#pragma unroll
-    for (int i = 0; i < DPL; i++) part[warp * HD + lane * DPL + i] = o[i];
-    __syncthreads();
-    if (tid < HD) {
-        float v = 0.0f;
-        for (uint32_t w = 0; w < 8; w++) v += part[w * HD + tid];
-        a.att[h * HD + tid] = v * inv;
-    }
-    tr.exit();
-}
-
 template <int OUT, int CMAX>
 cudaError_t launch_fast_t(const GemvPlan& p, const GemvArgs& a, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
@@ -491,8 +313,6 @@ cudaError_t fast_set_smem_limits(int optin) {
     HS_SETF_ALL(OUT_STORE) HS_SETF_ALL(OUT_RESID) HS_SETF_ALL(OUT_SILU)
 #undef HS_SETF_ALL
 #undef HS_SETF
-    if (e == cudaSuccess) e = allow_smem_fast(k_attention_fast<64>, optin);
-    if (e == cudaSuccess) e = allow_smem_fast(k_attention_fast<128>, optin);
     return e;
 }
 
@@ -509,27 +329,6 @@ cudaError_t launch_gemv_fast(const GemvPlan& p, const GemvArgs& a, cudaStream_t 
         default: return cudaErrorInvalidValue;
     }
 #undef HS_CASE
-}
-
-size_t attention_fast_smem(uint32_t head_dim, uint32_t max_ctx) {
-    const size_t rs = head_dim + 4, pre = 12288 / head_dim, ch = 4096 / head_dim;
-    return (3 * head_dim + 64 + 8 * head_dim + (2 * pre + ch) * rs + max_ctx) * sizeof(float);
-}
-
-cudaError_t launch_attention_fast(uint32_t head_dim, uint32_t nh, size_t smem, const AttnArgs& a, cudaStream_t st) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(nh);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (head_dim == 64) return cudaLaunchKernelEx(&cfg, k_attention_fast<64>, a);
-    if (head_dim == 128) return cudaLaunchKernelEx(&cfg, k_attention_fast<128>, a);
-    return cudaErrorInvalidValue;
 }
 
 }  // namespace hs

@@ -221,6 +221,9 @@ struct hs_model {
     uint32_t max_splits = 0;
     uint32_t numeric = HS_NUMERIC_REFERENCE;
     TcGemmPlan thead;             // tensor-core LM head
+    bool tok = false;             // fast path: one persistent kernel per token (token_fast.cu)
+    TokenPlan tokp;
+    TokLayer* tok_layers = nullptr;  // device copy of the layers' weight pointers
     uint64_t tc_part_per_slot = 0;  // max over split-K GEMMs of splits * rows
     const uint16_t* head_w = nullptr;
     std::map<std::string, TensorRef> tensors;
@@ -261,7 +264,7 @@ struct hs_scratch {
     uint32_t* tokens = nullptr;
     uint64_t cap = 0;
     uint64_t *cand = nullptr, *argbuf = nullptr;
-    uint32_t n_cta = 0, kmax = 0;
+    uint32_t n_cta = 0, kmax = 0, slice = 0;  // sampler: candidate CTAs, keys kept per CTA, logits per CTA
     cudaGraphExec_t g_fwd = nullptr, g_step = nullptr;
     const hs_kv* graph_kv = nullptr;
     uint32_t graph_kmax = 0;
@@ -270,6 +273,7 @@ struct hs_scratch {
     float* att_part = nullptr;      // split-KV attention partials and counters
     uint32_t* att_cnt = nullptr;
     void** kv_tab = nullptr;        // one-entry KV / dirty / tracking tables for split attention
+    uint32_t* tok_bar = nullptr;    // grid barrier counter of the persistent token kernel
     uint64_t* trace = nullptr;      // device, 4 u64 per launch slot (trace mode only)
     uint64_t* trace_init = nullptr; // pinned host template: start=~0, rest 0
     uint32_t trace_slots = 0;
@@ -283,7 +287,8 @@ struct hs_scratch {
         cudaFree(trace);
         cudaFreeHost(trace_init);
         for (void* p : {(void*)x, (void*)qkv, (void*)att, (void*)hb, (void*)logits, (void*)tokens, (void*)cand,
-                        (void*)argbuf, (void*)sc_global, (void*)att_part, (void*)att_cnt, (void*)kv_tab})
+                        (void*)argbuf, (void*)sc_global, (void*)att_part, (void*)att_cnt, (void*)kv_tab,
+                        (void*)tok_bar})
             cudaFree(p);
     }
 };
@@ -454,6 +459,9 @@ int plan_tc(TcGemmPlan* p, int epi, uint32_t rows, uint32_t K, const uint16_t* w
     p->m_tiles = 1;
     const uint32_t per_cta = (units + p->grid - 1) / p->grid * ((kt_n + p->splits - 1) / p->splits);
     uint32_t nst = std::min<uint32_t>(16, per_cta);
+    // A smaller budget lets the next kernel's CTA share the SM and start its
+    // weight prefetch (programmatic dependent launch) while this one drains.
+    smem_cap = std::min<size_t>(smem_cap, (size_t)env_u32("HS_TC_SMEM_KB", 1024) * 1024);
     while (nst > 1 && tc_gemm_smem(p->n_tile, nst, silu) > smem_cap) nst--;
     p->nst = nst;
     p->smem = tc_gemm_smem(p->n_tile, nst, silu);
@@ -463,10 +471,77 @@ int plan_tc(TcGemmPlan* p, int epi, uint32_t rows, uint32_t K, const uint16_t* w
     return rc;
 }
 
-// Enqueue one forward pass (the 5 kernels per layer + final norm/LM head).
+// Split-KV attention over the scratch's one sequence (layer set by the caller).
+SplitAttnArgs scratch_attn_args(const hs_scratch* s, const hs_kv* kv) {
+    const hs_model* m = s->m;
+    const hs_config& c = m->cfg;
+    SplitAttnArgs sa{};
+    sa.qkv = s->qkv;
+    sa.n_part = 1;
+    sa.kv = reinterpret_cast<float* const*>(s->kv_tab);
+    sa.dirty = reinterpret_cast<uint64_t* const*>(s->kv_tab + 1);
+    sa.tracking = reinterpret_cast<const uint32_t* const*>(s->kv_tab + 2);
+    sa.rope_cos = m->rope_cos;
+    sa.rope_sin = m->rope_sin;
+    sa.out_f32 = s->att;
+    sa.partials = s->att_part;
+    sa.counters = s->att_cnt;
+    sa.ctl = s->ctl;
+    sa.nh = c.n_heads;
+    sa.nkv = c.n_kv_heads;
+    sa.max_ctx = c.max_ctx;
+    sa.layout = kv->spec.layout;
+    sa.page_shift = kv->page_shift;
+    sa.max_splits = m->max_splits;
+    sa.trace = s->trace;
+    return sa;
+}
+
+// The fast path's whole token as one persistent kernel (after zeroing its
+// grid barrier counter).
+int enqueue_token_kernel(hs_scratch* s, const hs_kv* kv) {
+    const hs_model* m = s->m;
+    const hs_config& c = m->cfg;
+    TokenArgs a{};
+    a.layers = m->tok_layers;
+    a.n_layers = c.n_layers;
+    a.d = c.d_model;
+    a.ff = c.d_ff;
+    a.nh = c.n_heads;
+    a.nkv = c.n_kv_heads;
+    a.hd = c.head_dim;
+    a.vocab = c.vocab;
+    a.eps = c.eps;
+    a.embd = m->embd;
+    a.out_norm = m->out_norm;
+    a.head_w = m->head_w;
+    a.x = s->x;
+    a.qkv = s->qkv;
+    a.att = s->att;
+    a.hb = s->hb;
+    a.logits = s->logits;
+    a.attn = scratch_attn_args(s, kv);
+    a.attn.trace = nullptr;
+    a.ctl = s->ctl;
+    a.bar = s->tok_bar;
+    a.slot_bytes = m->tokp.slot_bytes;
+    a.nslot = m->tokp.nslot;
+    a.trace = s->trace;
+    a.trace_slot = 0;
+    // trace slots 0-2: this kernel and the two sampler kernels; then the
+    // timeline, 12 words per barrier interval (5 per layer, then the head)
+    a.phase_ts = s->trace ? s->trace + 3 * 8 : nullptr;
+    HS_CUDA_TRY(cudaMemsetAsync(s->tok_bar, 0, sizeof(uint32_t), s->st));
+    HS_CUDA_TRY(launch_token_fast(m->tokp, a, s->st));
+    return HS_OK;
+}
+
+// Enqueue one forward pass (the 5 kernels per layer + final norm/LM head, or
+// the fast path's single persistent kernel).
 int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
     const hs_model* m = s->m;
     const hs_config& c = m->cfg;
+    if (m->tok) return enqueue_token_kernel(s, kv);
     cudaStream_t st = s->st;
     uint32_t slot = 0;
     for (uint32_t l = 0; l < c.n_layers; l++) {
@@ -511,31 +586,11 @@ int enqueue_forward(hs_scratch* s, const hs_kv* kv) {
         at.trace_slot = slot++;
         at.sc_global = s->sc_global;
         if (m->attn_split) {
-            SplitAttnArgs sa{};
-            sa.qkv = s->qkv;
-            sa.n_part = 1;
-            sa.kv = reinterpret_cast<float* const*>(s->kv_tab);
-            sa.dirty = reinterpret_cast<uint64_t* const*>(s->kv_tab + 1);
-            sa.tracking = reinterpret_cast<const uint32_t* const*>(s->kv_tab + 2);
-            sa.rope_cos = m->rope_cos;
-            sa.rope_sin = m->rope_sin;
-            sa.out_f32 = s->att;
-            sa.partials = s->att_part;
-            sa.counters = s->att_cnt;
-            sa.ctl = s->ctl;
+            SplitAttnArgs sa = scratch_attn_args(s, kv);
             sa.layer = l;
-            sa.nh = c.n_heads;
-            sa.nkv = c.n_kv_heads;
-            sa.max_ctx = c.max_ctx;
-            sa.layout = kv->spec.layout;
-            sa.page_shift = kv->page_shift;
-            sa.max_splits = m->max_splits;
-            sa.trace = s->trace;
             sa.trace_slot = at.trace_slot;
             HS_CUDA_TRY(launch_attn_split(c.head_dim, sa, 1, st));
-        } else if (m->numeric == HS_NUMERIC_FAST)
-            HS_CUDA_TRY(launch_attention_fast(c.head_dim, c.n_heads, m->attn_smem, at, st));
-        else
+        } else
             HS_CUDA_TRY(launch_attention(c.head_dim, c.n_heads, m->attn_smem, at, st));
         GemvArgs o{};
         o.ctl = s->ctl;
@@ -608,6 +663,7 @@ SampleArgs sample_args(hs_scratch* s) {
     a.vocab = s->m->cfg.vocab;
     a.n_cta = s->n_cta;
     a.kmax = s->kmax;
+    a.slice = s->slice;
     a.trace = s->trace;
     a.trace_slot = s->launches_fwd;  // and launches_fwd + 1 for the second kernel
     return a;
@@ -763,20 +819,28 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
     }
     if (tc && n_heads / n_kv > 8) return fail(HS_E_UNSUPPORTED, "tensor-core path supports up to 8 query heads per KV head");
     if (tc && d_model > 2048) return fail(HS_E_UNSUPPORTED, "tensor-core path supports d_model up to 2048");
-    // Attention: the tensor-core path always splits the cached positions
-    // over CTAs; the fast path keeps one CTA per query head (quicker at
-    // short contexts) unless max_ctx scores do not fit in shared memory.
-    m->attn_split = tc || (fast && attention_fast_smem(hd, max_ctx) > m->smem_cap);
+    // Attention: the GPU-native paths split the cached positions over CTAs
+    // (split-KV with an online softmax); the exact path keeps one CTA per
+    // query head in the reference's order.
+    m->attn_split = tc || fast;
     if (m->attn_split) {
         m->max_splits = attn_max_splits(max_ctx);
         HS_CUDA_TRY(attn_split_set_smem_limits(optin));
     }
-    auto attn_smem_for = [&](uint32_t ctx) { return fast ? attention_fast_smem(hd, ctx) : attention_smem(hd, ctx); };
-    m->attn_smem = m->attn_split ? attn_split_smem(hd) : attn_smem_for(max_ctx);
+    m->attn_smem = m->attn_split ? attn_split_smem(hd) : attention_smem(hd, max_ctx);
     if (!m->attn_split && m->attn_smem > m->smem_cap) {
         // Long contexts: the scores move to a global buffer (L2-resident per head).
         m->attn_global = true;
-        m->attn_smem = attn_smem_for(0);
+        m->attn_smem = attention_smem(hd, 0);
+    }
+    // Fast path: the whole token as one persistent kernel when the shapes
+    // fit (HS_TOKEN_KERNEL=0 keeps the per-kernel launches; same bits).
+    if (fast && env_u32("HS_TOKEN_KERNEL", 1) != 0 &&
+        token_fast_plan(&m->tokp, n_layers, d_model, d_ff, n_heads, n_kv, hd, (uint32_t)vocab, m->n_sm,
+                        std::min<size_t>(m->smem_cap, (size_t)env_u32("HS_TOKEN_SMEM_KB", 1024) * 1024),
+                        env_u32("HS_TOKEN_SLOT_KB", 0) * 1024)) {
+        HS_CUDA_TRY(token_fast_set_smem_limits(optin));
+        m->tok = token_fast_resident(m->tokp);
     }
     if (m->attn_smem > m->smem_cap) return fail(HS_E_UNSUPPORTED, "attention staging does not fit in shared memory");
 
@@ -858,6 +922,15 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
             return rc;
     }
     m->head_w = head_w;
+    if (m->tok) {
+        std::vector<TokLayer> tl(n_layers);
+        for (uint32_t l = 0; l < n_layers; l++) {
+            const LayerDev& L = m->layers[l];
+            tl[l] = TokLayer{L.attn_norm, L.ffn_norm, L.bqkv, L.wqkv, L.wo, L.wgate, L.wup, L.wdown};
+        }
+        if ((rc = dev_alloc(m.get(), &m->tok_layers, n_layers))) return rc;
+        HS_CUDA_TRY(cudaMemcpy(m->tok_layers, tl.data(), n_layers * sizeof(TokLayer), cudaMemcpyHostToDevice));
+    }
     if (tc) {
         if ((rc = plan_tc(&m->thead, TC_STORE, (uint32_t)vocab, d_model, head_w, nullptr, m->n_sm, m->smem_cap)))
             return rc;
@@ -1114,18 +1187,27 @@ int hs_scratch_new(const hs_model* m, hs_scratch** out) {
     HS_CUDA_TRY(cudaMalloc(&s->logits, (size_t)c.vocab * 4));
     s->cap = (uint64_t)c.max_ctx + 1;
     HS_CUDA_TRY(cudaMalloc(&s->tokens, s->cap * 4));
-    s->n_cta = (c.vocab + kSampleSlice - 1) / kSampleSlice;
+    // Large vocabularies: 4096-logit slices per candidate CTA (exact radix
+    // select of the best 64); the kept candidates are the same exact top-k.
+    s->slice = c.vocab > kMaxSlice ? kMaxSlice : kSampleSlice;
+    s->n_cta = (c.vocab + s->slice - 1) / s->slice;
     if (s->n_cta > 256) return fail(HS_E_UNSUPPORTED, "vocab too large for the device sampler");
     HS_CUDA_TRY(cudaMalloc(&s->cand, (size_t)s->n_cta * kSampleSlice * 8));
     HS_CUDA_TRY(cudaMalloc(&s->argbuf, (size_t)s->n_cta * 8));
-    s->launches_fwd = c.n_layers * 5 + 1;
+    if (m->tok) {
+        HS_CUDA_TRY(cudaMalloc(&s->tok_bar, sizeof(uint32_t)));
+        HS_CUDA_TRY(cudaMemset(s->tok_bar, 0, sizeof(uint32_t)));
+    }
+    s->launches_fwd = m->tok ? 1 : c.n_layers * 5 + 1;
     const char* tenv = getenv("HS_TRACE");
     if (tenv && tenv[0] == '1') {
-        s->trace_slots = s->launches_fwd + 2;
+        s->trace_slots = s->launches_fwd + 2 + (m->tok ? (12 * (5 * c.n_layers + 1) + 7) / 8 : 0);
         HS_CUDA_TRY(cudaMalloc(&s->trace, (size_t)s->trace_slots * 8 * 8));
         HS_CUDA_TRY(cudaMallocHost(&s->trace_init, (size_t)s->trace_slots * 8 * 8));
         for (uint32_t i = 0; i < s->trace_slots; i++) {
-            s->trace_init[8 * i] = ~0ull;
+            // launch slots start at ~0 (the entry is a minimum); the token
+            // kernel's timeline words after them start at 0
+            s->trace_init[8 * i] = i < s->launches_fwd + 2 ? ~0ull : 0;
             for (int j = 1; j < 8; j++) s->trace_init[8 * i + j] = 0;
         }
     }

@@ -93,8 +93,6 @@ cudaError_t gemv_set_smem_limits(int optin);
 uint32_t fast_cmax_for(uint32_t chunks_per_thread);
 cudaError_t fast_set_smem_limits(int optin);
 cudaError_t launch_gemv_fast(const GemvPlan& p, const GemvArgs& a, cudaStream_t st);
-size_t attention_fast_smem(uint32_t head_dim, uint32_t max_ctx);
-cudaError_t launch_attention_fast(uint32_t head_dim, uint32_t nh, size_t smem, const AttnArgs& a, cudaStream_t st);
 
 // Tensor-core path (batch_tc.cu).
 enum TcEpi : int { TC_STORE = 0, TC_PART = 1, TC_SILU = 2 };
@@ -183,6 +181,44 @@ cudaError_t attn_split_set_smem_limits(int optin);
 cudaError_t launch_attn_split(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, cudaStream_t st);
 
 cudaError_t launch_tc_norm(const TcNormArgs& a, uint32_t slots, cudaStream_t st);
+
+// One decode token of the fast path as one persistent kernel (token_fast.cu).
+struct TokLayer {
+    const float *attn_norm, *ffn_norm, *bqkv;
+    const uint16_t *wqkv, *wo, *wgate, *wup, *wdown;
+};
+struct TokenArgs {
+    const TokLayer* layers;  // device [n_layers]
+    uint32_t n_layers, d, ff, nh, nkv, hd, vocab;
+    float eps;
+    const uint16_t* embd;    // [vocab][d]
+    const float* out_norm;
+    const uint16_t* head_w;  // [vocab][d]
+    float *x, *qkv, *att, *hb, *logits;
+    SplitAttnArgs attn;      // attention items (qkv, att, KV tables, partials, counters)
+    DevCtl* ctl;
+    uint32_t* bar;           // grid barrier counter, zero at launch
+    uint32_t slot_bytes;     // weight ring: slot size (multiple of 1024) and count
+    uint32_t nslot;
+    uint64_t* trace;
+    uint32_t trace_slot;
+    uint64_t* phase_ts;      // trace mode: %globaltimer at CTA 0's exit of every grid barrier
+};
+struct TokenPlan {
+    uint32_t grid = 0, slot_bytes = 0, nslot = 0;
+    int shape = -1;          // compiled shape class
+    size_t smem = 0;
+};
+// Plans the launch for the given shapes within `smem_cap` (ring slots of
+// `slot_only` bytes when non-zero); false if they do not fit (the per-kernel
+// path is then used).
+bool token_fast_plan(TokenPlan* p, uint32_t n_layers, uint32_t d, uint32_t ff, uint32_t nh, uint32_t nkv,
+                     uint32_t hd, uint32_t vocab, int n_sm, size_t smem_cap, uint32_t slot_only);
+cudaError_t token_fast_set_smem_limits(int optin);
+// One CTA of the planned size fits on an SM (so the cooperative grid of one
+// CTA per SM is resident).
+bool token_fast_resident(const TokenPlan& p);
+cudaError_t launch_token_fast(const TokenPlan& p, const TokenArgs& a, cudaStream_t st);
 
 constexpr uint32_t kSampleSlice = 1024;  // logits per CTA of the candidate kernel
 constexpr uint32_t kMaxSlice = 4096;     // largest slice a candidate CTA takes

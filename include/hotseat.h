@@ -212,7 +212,9 @@ int hs_forward_batch(const hs_model* m, hs_kv* const* kvs, const uint32_t* token
 /* Prompt prefill: Model::forward for tokens[0..n) of ONE sequence at
  * positions pos0.., appended to `kv`, with the tokens as the rows of each
  * GEMM (up to the batch capacity per pass) instead of one token per step.
- * No logits; the KV rows are bit-identical to n single-token steps. Follow
+ * No logits. Its GEMMs use wide tiles without the decode steps' K splits,
+ * so the KV rows match single-token steps within the path's tolerance (and
+ * are bit-identical however the prompt is cut into calls). Follow
  * with hs_batch_seq_run from filled = pos0 + n: the sequence's next
  * (last prompt) token then produces the logits of the first sample. */
 int hs_prefill(const hs_model* m, hs_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0, hs_batch* b);
