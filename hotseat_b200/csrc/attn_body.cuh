@@ -66,7 +66,7 @@ __host__ __device__ constexpr uint32_t item_rope_off(uint32_t hd, uint32_t nbuf)
 // CTAs); else from a shared-memory copy.
 template <bool GLOBAL>
 __device__ __forceinline__ float combine(const float* part, uint32_t S, uint32_t G, uint32_t hd, uint32_t idx) {
-    const uint32_t rec = G * hd + 2 * G, h = idx / hd;
+    const uint32_t rec = attn_record(G, hd), h = idx / hd;
     auto ld = [&](size_t i) { return GLOBAL ? __ldcg(part + i) : part[i]; };
     float M = -FLT_MAX;
     for (uint32_t q = 0; q < S; q++) M = fmaxf(M, ld((size_t)q * rec + G * hd + h));
@@ -122,7 +122,12 @@ __device__ void prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uin
 // of the output combines them (combine()) after a grid-wide barrier.
 template <int HD, int NBUF>
 __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t slot, uint32_t pos,
-                     float* sm, bool prefetched = false, bool reader_combines = false) {
+                     float* sm, bool prefetched = false, bool reader_combines = false, uint64_t* probe = nullptr) {
+    // probe (timing): thread 0 stores clock64() at the item's checkpoints
+    auto at = [&](int k) {
+        if (probe && threadIdx.x == 0) probe[k] = clock64();
+    };
+    at(0);
     static_assert(NBUF == 1 || NBUF == 2, "one or two chunk buffers");
     constexpr uint32_t RS = HD + 4, HALF = HD / 2;
     constexpr uint32_t HSETS = kThreads / HD, HPT = (8 + HSETS - 1) / HSETS;
@@ -172,6 +177,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     }
     if (prefetched) cp_wait0();  // the RoPE row (and the first chunk)
     sync256();
+    at(1);
     for (uint32_t idx = tid; idx < (G + 1) * HALF; idx += kThreads) {
         const uint32_t h = idx / HALF, i = idx % HALF;
         float* r = h < G ? qs + h * HD : kn;
@@ -186,6 +192,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
         hs_l[tid] = 0.0f;
     }
     sync256();
+    at(2);
     if (s == 0 && append && tid < HD) {
         kv[row_off(pos, 0) + tid] = kn[tid];
         kv[row_off(pos, 1) + tid] = vn[tid];
@@ -242,32 +249,48 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
             cp_wait0();
         }
         sync256();
+        if (c == 0) at(3);
         const uint32_t c0 = p0 + c * kCh, cnt = p1 - c0 < kCh ? p1 - c0 : kCh;
         const float* kc = kb + (c % NBUF) * kCh * RS;
         const float* vc = vb + (c % NBUF) * kCh * RS;
         // scores: thread t takes position t % 64 and heads t/64, t/64 + 4
+        // (each K row read once for both heads)
         {
-            const uint32_t r = tid % kCh;
-            for (uint32_t h = tid / kCh; h < G; h += kThreads / kCh) {
-                float v = -FLT_MAX;
-                if (r < cnt) {
-                    const float4* k4 = reinterpret_cast<const float4*>(kc + r * RS);
-                    const float4* q4 = reinterpret_cast<const float4*>(qs + h * HD);
-                    float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+            constexpr uint32_t HSETS_S = kThreads / kCh, HPT_S = (8 + HSETS_S - 1) / HSETS_S;
+            const uint32_t r = tid % kCh, h0 = tid / kCh;
+            float sc[HPT_S][4];
 #pragma unroll
-                    for (uint32_t d4 = 0; d4 < HD / 4; d4++) {
-                        const float4 kk = k4[d4], qq = q4[d4];
-                        s0 = __fmaf_rn(qq.x, kk.x, s0);
-                        s1 = __fmaf_rn(qq.y, kk.y, s1);
-                        s2 = __fmaf_rn(qq.z, kk.z, s2);
-                        s3 = __fmaf_rn(qq.w, kk.w, s3);
+            for (uint32_t j = 0; j < HPT_S; j++) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+            if (r < cnt) {
+                const float4* k4 = reinterpret_cast<const float4*>(kc + r * RS);
+#pragma unroll
+                for (uint32_t d4 = 0; d4 < HD / 4; d4++) {
+                    const float4 kk = k4[d4];
+#pragma unroll
+                    for (uint32_t j = 0; j < HPT_S; j++) {
+                        const uint32_t h = h0 + j * HSETS_S;
+                        if (h < G) {
+                            const float4 qq = reinterpret_cast<const float4*>(qs + h * HD)[d4];
+                            sc[j][0] = __fmaf_rn(qq.x, kk.x, sc[j][0]);
+                            sc[j][1] = __fmaf_rn(qq.y, kk.y, sc[j][1]);
+                            sc[j][2] = __fmaf_rn(qq.z, kk.z, sc[j][2]);
+                            sc[j][3] = __fmaf_rn(qq.w, kk.w, sc[j][3]);
+                        }
                     }
-                    v = __fmul_rn(__fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3)), scale);
                 }
-                sp[h * kCh + r] = v;
+            }
+#pragma unroll
+            for (uint32_t j = 0; j < HPT_S; j++) {
+                const uint32_t h = h0 + j * HSETS_S;
+                if (h < G)
+                    sp[h * kCh + r] = r < cnt ? __fmul_rn(__fadd_rn(__fadd_rn(sc[j][0], sc[j][1]),
+                                                                    __fadd_rn(sc[j][2], sc[j][3])),
+                                                          scale)
+                                              : -FLT_MAX;
             }
         }
         sync256();
+        if (c == 0) at(4);
         // online softmax: warp h owns head h
         if (warp < G) {
             float* sh = sp + warp * kCh;
@@ -291,19 +314,33 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
             }
         }
         sync256();
-        // P.V: thread t owns dimension t % HD of heads t/HD, t/HD + HSETS, ...
+        if (c == 0) at(5);
+        // P.V: thread t owns dimension t % HD of heads t/HD, t/HD + HSETS,
+        // ...: one chain per head over the positions in order, each V
+        // element read once for all of them
+        {
+            float pv[HPT];
 #pragma unroll
-        for (uint32_t j = 0; j < HPT; j++) {
-            const uint32_t h = hs0 + j * HSETS;
-            if (h >= G) break;
-            const float* ph = sp + h * kCh;
-            float acc = 0.0f;
-            for (uint32_t r = 0; r < cnt; r++) acc = __fmaf_rn(ph[r], vc[r * RS + dd], acc);
-            o[j] = __fadd_rn(__fmul_rn(o[j], hs_f[h]), acc);
+            for (uint32_t j = 0; j < HPT; j++) pv[j] = 0.0f;
+#pragma unroll 4
+            for (uint32_t r = 0; r < cnt; r++) {
+                const float vv = vc[r * RS + dd];
+#pragma unroll
+                for (uint32_t j = 0; j < HPT; j++) {
+                    const uint32_t h = hs0 + j * HSETS;
+                    if (h < G) pv[j] = __fmaf_rn(sp[h * kCh + r], vv, pv[j]);
+                }
+            }
+#pragma unroll
+            for (uint32_t j = 0; j < HPT; j++) {
+                const uint32_t h = hs0 + j * HSETS;
+                if (h < G) o[j] = __fadd_rn(__fmul_rn(o[j], hs_f[h]), pv[j]);
+            }
         }
         sync256();
     }
     cp_wait0();
+    at(6);
     mark_dirty();
 
     auto store = [&](size_t at, float v) {
@@ -326,7 +363,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     }
     // Several splits: publish (unnormalised output, max, sum); the last item
     // to arrive combines all splits in split order.
-    const uint32_t rec = G * HD + 2 * G;
+    const uint32_t rec = attn_record(G, HD);
     float* part = a.partials + ((size_t)(slot * a.nkv + kvh) * a.max_splits) * rec;
 #pragma unroll
     for (uint32_t j = 0; j < HPT; j++) {
@@ -337,7 +374,10 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
         part[(size_t)s * rec + G * HD + tid] = hs_m[tid];
         part[(size_t)s * rec + G * HD + G + tid] = hs_l[tid];
     }
-    if (reader_combines) return;
+    if (reader_combines) {
+        at(7);
+        return;
+    }
     __threadfence();
     sync256();
     uint32_t* counter = a.counters + slot * a.nkv + kvh;

@@ -529,7 +529,7 @@ int enqueue_token_kernel(hs_scratch* s, const hs_kv* kv) {
     a.trace = s->trace;
     a.trace_slot = 0;
     // trace slots 0-2: this kernel and the two sampler kernels; then the
-    // timeline, 12 words per barrier interval (5 per layer, then the head)
+    // timeline, 20 words per barrier interval (5 per layer, then the head)
     a.phase_ts = s->trace ? s->trace + 3 * 8 : nullptr;
     HS_CUDA_TRY(cudaMemsetAsync(s->tok_bar, 0, sizeof(uint32_t), s->st));
     HS_CUDA_TRY(launch_token_fast(m->tokp, a, s->st));
@@ -1175,7 +1175,7 @@ int hs_scratch_new(const hs_model* m, hs_scratch** out) {
     if (m->attn_global) HS_CUDA_TRY(cudaMalloc(&s->sc_global, (size_t)c.n_heads * c.max_ctx * 4));
     if (m->attn_split) {
         const uint32_t G = c.n_heads / c.n_kv_heads;
-        HS_CUDA_TRY(cudaMalloc(&s->att_part, (size_t)c.n_kv_heads * m->max_splits * (G * c.head_dim + 2 * G) * 4));
+        HS_CUDA_TRY(cudaMalloc(&s->att_part, (size_t)c.n_kv_heads * m->max_splits * attn_record(G, c.head_dim) * 4));
         HS_CUDA_TRY(cudaMalloc(&s->att_cnt, c.n_kv_heads * 4));
         HS_CUDA_TRY(cudaMemset(s->att_cnt, 0, c.n_kv_heads * 4));
         HS_CUDA_TRY(cudaMalloc(&s->kv_tab, 3 * sizeof(void*)));
@@ -1201,7 +1201,7 @@ int hs_scratch_new(const hs_model* m, hs_scratch** out) {
     s->launches_fwd = m->tok ? 1 : c.n_layers * 5 + 1;
     const char* tenv = getenv("HS_TRACE");
     if (tenv && tenv[0] == '1') {
-        s->trace_slots = s->launches_fwd + 2 + (m->tok ? (12 * (5 * c.n_layers + 1) + 7) / 8 : 0);
+        s->trace_slots = s->launches_fwd + 2 + (m->tok ? (20 * (5 * c.n_layers + 1) + 7) / 8 : 0);
         HS_CUDA_TRY(cudaMalloc(&s->trace, (size_t)s->trace_slots * 8 * 8));
         HS_CUDA_TRY(cudaMallocHost(&s->trace_init, (size_t)s->trace_slots * 8 * 8));
         for (uint32_t i = 0; i < s->trace_slots; i++) {
@@ -1839,7 +1839,7 @@ int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out) {
         (m->attn_global && (rc = alloc(&b->sc_global, (uint64_t)C * c.n_heads * c.max_ctx))) ||
         (m->attn_split &&
          ((rc = alloc(&b->att_part, (uint64_t)C * c.n_kv_heads * m->max_splits *
-                                        (c.n_heads / c.n_kv_heads * (c.head_dim + 2)))) ||
+                                        attn_record(c.n_heads / c.n_kv_heads, c.head_dim))) ||
           (rc = alloc(&b->att_cnt, (uint64_t)C * c.n_kv_heads)))))
         return rc;
     HS_CUDA_TRY(cudaMallocHost(&b->ctl_h, (size_t)C * sizeof(DevCtl)));

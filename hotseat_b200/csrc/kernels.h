@@ -160,7 +160,7 @@ struct SplitAttnArgs {
     uint16_t* out_hi;
     uint16_t* out_lo;
     uint32_t out_stride;     // elements between sequences' outputs
-    float* partials;         // [sequences][nkv][max_splits][groups*hd + 2*groups]
+    float* partials;         // [sequences][nkv][max_splits][attn_record(groups, hd)]
     uint32_t* counters;      // [sequences][nkv], zero between launches
     DevCtl* ctl;             // per-sequence control blocks
     uint32_t layer, nh, nkv, max_ctx, layout, page_shift, max_splits;
@@ -174,6 +174,11 @@ enum AttnMode : uint32_t { ATTN_FULL = 0, ATTN_APPEND_ONLY = 1, ATTN_ATTEND_ONLY
 __host__ __device__ inline uint32_t attn_split_len(uint32_t n, uint32_t max_splits) {
     const uint32_t chunks = (n + 63) / 64;
     return (chunks + max_splits - 1) / max_splits * 64;
+}
+// Floats per published split of one (sequence, KV head): the group's
+// unnormalised outputs [G][hd], maxima [G], sums [G], padded to 16 bytes.
+__host__ __device__ inline uint32_t attn_record(uint32_t groups, uint32_t hd) {
+    return (groups * hd + 2 * groups + 3) / 4 * 4;
 }
 size_t attn_split_smem(uint32_t head_dim);
 uint32_t attn_max_splits(uint32_t max_ctx);

@@ -322,11 +322,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
     // 0's [input ready, rows done, barrier arrive, barrier exit (%globaltimer
     // ns), SM cycles waiting for weight tiles, tiles, SM cycles computing
     // rows, SM cycles in the epilogue], then over all CTAs [~earliest
-    // arrival, latest arrival], 2 words spare.
+    // arrival, latest arrival], 2 words spare, then (attention intervals)
+    // the clock64 checkpoints of CTA 0's first attention item.
     const bool tmark = a.phase_ts && b == 0 && tid == 0;
     uint64_t epi_cy = 0;
     auto mark = [&](uint32_t k, uint64_t v) {
-        if (tmark) a.phase_ts[12 * epoch + k] = v;
+        if (tmark) a.phase_ts[20 * epoch + k] = v;
     };
     // Grid barrier: thread 0 of every CTA arrives once per barrier and waits
     // (bounded) until all CTAs have; the named barrier releases the others.
@@ -340,8 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
             mark(2, tmark ? gtime() : 0);
             if (a.phase_ts) {  // arrival spread over CTAs: latest, and latest of the complements (earliest)
                 const unsigned long long t = gtime();
-                atomicMax(reinterpret_cast<unsigned long long*>(a.phase_ts + 12 * epoch + 9), t);
-                atomicMax(reinterpret_cast<unsigned long long*>(a.phase_ts + 12 * epoch + 8), ~t);
+                atomicMax(reinterpret_cast<unsigned long long*>(a.phase_ts + 20 * epoch + 9), t);
+                atomicMax(reinterpret_cast<unsigned long long*>(a.phase_ts + 20 * epoch + 8), ~t);
             }
             rs.wait_cy = rs.tiles = rs.comp_cy = epi_cy = 0;
             epoch++;
@@ -356,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
                     gdead = true;
                 }
             }
-            if (tmark) a.phase_ts[12 * (epoch - 1) + 3] = gtime();
+            if (tmark) a.phase_ts[20 * (epoch - 1) + 3] = gtime();
         }
         attn::sync256();
     };
@@ -399,22 +400,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
         }
         attn::sync256();
     };
-    // Copies n floats global -> shared through L2, 4 loads in flight per thread.
-    auto stage = [&](float* dst, const float* src, uint32_t n) {
-        for (uint32_t base = 0; base < n; base += 4 * kConsumers) {
-            float v[4];
-#pragma unroll
-            for (uint32_t k = 0; k < 4; k++) {
-                const uint32_t i = base + k * kConsumers + tid;
-                if (i < n) v[k] = __ldcg(src + i);
-            }
-#pragma unroll
-            for (uint32_t k = 0; k < 4; k++) {
-                const uint32_t i = base + k * kConsumers + tid;
-                if (i < n) dst[i] = v[k];
-            }
-        }
-    };
     // x = n floats (a multiple of 4) from global memory, as asynchronous
     // 16-byte copies through L2: all in flight at once.
     auto copy_x = [&](const float* src, uint32_t n) {
@@ -425,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
     };
     if (ok) {
         const uint32_t n = pos + 1, Ls = attn_split_len(n, a.attn.max_splits), S = (n + Ls - 1) / Ls;
-        const uint32_t G_ = a.nh / nkv, rec = G_ * a.hd + 2 * G_;
+        const uint32_t G_ = a.nh / nkv, rec = attn_record(G_, a.hd);
         const bool reader_combines = S > 1 && S <= kReaderCombine &&
                                      ((size_t)nkv * S * rec + a.nh * (S + 1)) * 4 <= attn::item_smem(HD, attn_buf(HD));
         const uint32_t qrows = (a.nh + 2 * nkv) * a.hd;
@@ -455,8 +440,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
                     // memory (the attention item's space), combine in split order
                     float* ps = att_sm;
                     const uint32_t per_kvh = S * rec, gh = G_ * a.hd;
-                    for (uint32_t kvh = 0; kvh < nkv; kvh++)
-                        stage(ps + kvh * per_kvh, a.attn.partials + (size_t)kvh * a.attn.max_splits * rec, per_kvh);
+                    for (uint32_t kvh = 0; kvh < nkv; kvh++) {  // 16-byte records: async copies
+                        const float* src = a.attn.partials + (size_t)kvh * a.attn.max_splits * rec;
+                        for (uint32_t i = tid; i < per_kvh / 4; i += kConsumers)
+                            cp_async16(ps + kvh * per_kvh + 4 * i, src + 4 * i);
+                    }
+                    attn::cp_commit();
+                    attn::cp_wait0();
+                    mark(10, tmark ? gtime() : 0);
                     // per query head: the split weights exp(m_q - M) and the
                     // rescaled sum, then every output element's weighted sum
                     // (the same operations as attn::combine, shared per head)
@@ -476,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
                         hw[tid * (S + 1) + S] = den;
                     }
                     attn::sync256();
+                    mark(11, tmark ? gtime() : 0);
                     for (uint32_t idx = tid; idx < a.nh * a.hd; idx += kConsumers) {
                         const uint32_t head = idx / a.hd, kvh = head / G_;
                         const float* pk = ps + kvh * per_kvh + idx - kvh * gh;
@@ -532,7 +524,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
                 // attention: item i = s * nkv + kvh for the S splits of this position
                 mark(0, tmark ? gtime() : 0);
                 for (uint32_t i = b; i < S * nkv; i += G) {
-                    attn::item<HD, attn_buf(HD)>(a.attn, l, i / nkv, i % nkv, 0, pos, att_sm, i == b, reader_combines);
+                    attn::item<HD, attn_buf(HD)>(a.attn, l, i / nkv, i % nkv, 0, pos, att_sm, i == b, reader_combines,
+                                                 tmark && i == b ? a.phase_ts + 20 * epoch + 12 : nullptr);
                     attn::sync256();
                 }
                 pre = tid < dr1 - dr0 ? __ldcg(a.x + dr0 + tid) : 0.0f;
@@ -604,8 +597,8 @@ bool token_fast_plan(TokenPlan* p, uint32_t n_layers, uint32_t d, uint32_t ff, u
     const uint32_t unit = (kConsumers / row_threads(d)) * d * 2;
     bool found = false;
     for (int pass = 0; pass < 2 && !found; pass++) {
-        for (uint32_t slot = 16384; slot <= 65536; slot += 1024) {
-            if (pass == 0 && slot % unit) continue;
+        for (uint32_t slot = pass == 0 ? unit : 16384; slot <= 65536; slot += pass == 0 ? unit : 1024) {
+            if (slot < 16384 || slot % 16) continue;
             // a slot holds at least one row of every matrix (one of each of the gate/up pair)
             if (slot < 4 * d || slot < 2 * ff || slot < 2 * nh * hd || (slot_only && slot != slot_only)) continue;
             for (uint32_t nslot = 4; nslot <= 12; nslot++) {
