@@ -3,6 +3,7 @@
     python -m hotseat_b200.microbench dequant     # Q4_K/Q6_K -> f16 load-time dequantisation
     python -m hotseat_b200.microbench attention   # GQA decode attention at 1k-32k context
     python -m hotseat_b200.microbench prefill     # 1.5B shape: 16 x 2048-token prefill, 512 greedy steps
+    python -m hotseat_b200.microbench token       # batch-1 persistent token kernel: phase timeline
 
 dequant: the tensors of the seeded Qwen2.5-0.5B-shape GGUF (ffn_gate 4864x896
 and ffn_down 896x4864 in Q4_K, token_embd 151936x896 in Q6_K) plus the same
@@ -11,8 +12,10 @@ L2 is flushed (256 MB written) between timed launches. Bytes = quantised
 blocks read + 2 bytes per element written.
 
 attention: one forward of the 0.5B-shape model at position P (KV regions as
-allocated, so every cached row is read), batch 1 on the GPU-native path and
-batch 64 on the tensor-core path, with the launch timeline (HS_TRACE=1). The
+allocated, so every cached row is read), batch 1 on the GPU-native path (its
+per-kernel form, HS_TOKEN_KERNEL=0, so that attention is a launch of its
+own) and batch 64 on the tensor-core path, with the launch timeline
+(HS_TRACE=1). The
 attention time of a layer is its kernel's exit minus the QKV kernel's exit
 (the work it adds after its input is ready), averaged over the 24 layers.
 Bytes = (P+1) x 1024 B of K and V read + 1024 B written per sequence and
@@ -24,6 +27,12 @@ uniform-random prompts, each prefilled by hs_prefill (2047 tokens as GEMM rows,
 up to 512 per pass), then the 16 decoded together for 512 greedy tokens
 (temperature 0, penalty 1.1). FLOPs = 2 x (non-embedding weights) per token
 for the GEMMs (the tensor cores execute twice that: f16 hi and lo halves).
+
+token: the C1 workload (36-token prompt, sampled at temperature 0.8, seed
+99) decoded to 60 and to 120 tokens by the persistent token kernel with the
+trace on; the kernel's timeline of its last step, from CTA 0 (per phase of
+layers 1-23, averaged: input ready, rows done, barrier) and over all CTAs
+(arrival spread, last arrival to release), plus the LM head.
 
 Each line printed is one JSON object; peaks are the measured copy bandwidth
 in MEASURED_PEAKS.json when present.
@@ -167,7 +176,9 @@ def bench_attention(ctxs=(1024, 4096, 16384, 32767)):
     max_ctx = max(ctxs) + 8
     layers, row = 24, 2 * 2 * 64 * 4
     for batch, numeric in ((1, hs.NUMERIC_FAST), (64, hs.NUMERIC_TC)):
+        os.environ["HS_TOKEN_KERNEL"] = "0"
         m = hs.Model.load(path, max_ctx=max_ctx, numeric=numeric)
+        del os.environ["HS_TOKEN_KERNEL"]
         kvs = [m.kv() for _ in range(batch)]
         if batch == 1:
             s = m.scratch()
@@ -269,6 +280,56 @@ def bench_prefill(n_seqs=16, prompt=2048, gen=512):
     os.rmdir(td)
 
 
+def bench_token():
+    os.environ["HS_TRACE"] = "1"
+    import hotseat_b200 as hs
+    td = tempfile.mkdtemp(prefix="hsmicro")
+    path = os.path.join(td, "q05.gguf")
+    hs.write_synthetic_gguf(path, seed=1234, **hs.QWEN05)
+    m = hs.Model.load(path, max_ctx=256, numeric=hs.NUMERIC_FAST)
+    s = m.scratch()
+    if s.launches_per_step() != 3:
+        raise RuntimeError("the persistent token kernel is not in use for this model")
+    rng = np.random.default_rng(36)
+    prompt = [int(t) for t in rng.integers(0, hs.QWEN05["vocab"], size=36)]
+    cfg = hs.SamplerCfg.default(temperature=0.8, seed=99)
+    L, ghz = 24, 1.965
+    for ntok in (60, 120):
+        kv = m.kv()
+        hs.run_seq(m, kv, s, prompt, 36, ntok, cfg, hs.Rng.seed(99))
+        kv.close()
+        t = s.trace()
+        k = t[0].astype(np.int64)
+        # timeline words after the 3 launch slots: 20 per barrier interval
+        flat = t[3:].reshape(-1)[: 20 * (5 * L + 1)].reshape(5 * L + 1, 20)
+        body = flat[: 5 * L].astype(np.int64).reshape(L, 5, 20)
+        prev_exit = np.concatenate([[k[0]], body.reshape(-1, 20)[:-1, 3]]).reshape(L, 5)
+        earliest = (~flat[: 5 * L, 8]).astype(np.int64).reshape(L, 5)
+        latest = flat[: 5 * L, 9].astype(np.int64).reshape(L, 5)
+        sl = slice(1, L)
+        phases = {}
+        for i, name in enumerate(["qkv", "attention", "o", "gate_up", "down"]):
+            phases[name] = {
+                "input_us": float(((body[sl, i, 0] - prev_exit[sl, i]) / 1e3).mean()),
+                "rows_us": float(((body[sl, i, 1] - body[sl, i, 0]) / 1e3).mean()),
+                "tiles": float(body[sl, i, 5].mean()),
+                "tile_wait_us": float((body[sl, i, 4] / ghz / 1e3).mean()),
+                "tile_compute_us": float((body[sl, i, 6] / ghz / 1e3).mean()),
+                "barrier_us": float(((body[sl, i, 3] - body[sl, i, 2]) / 1e3).mean()),
+                "arrival_spread_us": float(((latest[sl, i] - earliest[sl, i]) / 1e3).mean()),
+                "last_arrival_to_release_us": float(((body[sl, i, 3] - latest[sl, i]) / 1e3).mean()),
+            }
+        h = flat[5 * L].astype(np.int64)
+        print(json.dumps({"bench": "token_kernel", "prompt": 36, "max_tokens": ntok, "kernel_us": float((k[2] - k[0]) / 1e3),
+                          "per_layer": phases, "lm_head_us": float((h[1] - h[0]) / 1e3),
+                          "lm_head_tiles": int(h[5]),
+                          "sampler_us": [float((int(t[i][2]) - int(t[i][0])) / 1e3) for i in (1, 2)]}), flush=True)
+    s.close()
+    m.close()
+    os.remove(path)
+    os.rmdir(td)
+
+
 if __name__ == "__main__":
     which = sys.argv[1] if len(sys.argv) > 1 else "all"
     if which in ("dequant", "all"):
@@ -277,3 +338,5 @@ if __name__ == "__main__":
         bench_attention()
     if which in ("prefill", "all"):
         bench_prefill()
+    if which in ("token", "all"):
+        bench_token()
