@@ -17,8 +17,9 @@
 // that arrives last at the (sequence, KV head) counter combines the splits in
 // split order and resets the counter. Every choice depends on n and max_ctx
 // only, never on the batch or the grid, so a sequence's bits are the same in
-// any batch and in either kernel. NBUF (1 or 2) is the number of K/V chunk
-// buffers: it changes how loads overlap compute, not the arithmetic.
+// any batch and in either kernel. NBUF (1-4) is the number of K/V chunk
+// buffers (NBUF - 1 chunks load while one computes): it changes how loads
+// overlap compute, not the arithmetic.
 //
 // Runs on threads 0..255 of the CTA and synchronises them with named barrier
 // 1, so a CTA may keep other warps (a producer) outside it.
@@ -37,8 +38,11 @@ constexpr uint32_t kCh = 64;  // positions per chunk
 __device__ __forceinline__ uint32_t ldv(const uint32_t* p) { return *(const volatile uint32_t*)p; }
 __device__ __forceinline__ void sync256() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 __device__ __forceinline__ void split_f16(float x, uint16_t* hi, uint16_t* lo) {
     const __half h = __float2half_rn(x);
@@ -128,7 +132,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
         if (probe && threadIdx.x == 0) probe[k] = clock64();
     };
     at(0);
-    static_assert(NBUF == 1 || NBUF == 2, "one or two chunk buffers");
+    static_assert(NBUF >= 1 && NBUF <= 4, "one to four chunk buffers");
     constexpr uint32_t RS = HD + 4, HALF = HD / 2;
     constexpr uint32_t HSETS = kThreads / HD, HPT = (8 + HSETS - 1) / HSETS;
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -239,15 +243,13 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
 #pragma unroll
     for (uint32_t j = 0; j < HPT; j++) o[j] = 0.0f;
     const uint32_t dd = tid % HD, hs0 = tid / HD;
-    if (NBUF == 2) issue(0);
+    // chunks 0 .. NBUF-2 in flight before the loop; each iteration issues
+    // chunk c + NBUF - 1 (an empty group past the end) and waits for chunk c
+#pragma unroll
+    for (uint32_t c = 0; c + 1 < NBUF; c++) issue(c);
     for (uint32_t c = 0; c < nch; c++) {
-        if (NBUF == 2) {
-            issue(c + 1);
-            cp_wait1();
-        } else {
-            issue(c);
-            cp_wait0();
-        }
+        issue(c + NBUF - 1);
+        cp_wait<NBUF - 1>();
         sync256();
         if (c == 0) at(3);
         const uint32_t c0 = p0 + c * kCh, cnt = p1 - c0 < kCh ? p1 - c0 : kCh;
@@ -322,8 +324,24 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
             float pv[HPT];
 #pragma unroll
             for (uint32_t j = 0; j < HPT; j++) pv[j] = 0.0f;
-#pragma unroll 4
-            for (uint32_t r = 0; r < cnt; r++) {
+            // four positions at a time: their probabilities as one 16-byte read
+            uint32_t r = 0;
+            for (; r + 4 <= cnt; r += 4) {
+                const float v0 = vc[r * RS + dd], v1 = vc[(r + 1) * RS + dd], v2 = vc[(r + 2) * RS + dd],
+                            v3 = vc[(r + 3) * RS + dd];
+#pragma unroll
+                for (uint32_t j = 0; j < HPT; j++) {
+                    const uint32_t h = hs0 + j * HSETS;
+                    if (h < G) {
+                        const float4 p4 = *reinterpret_cast<const float4*>(sp + h * kCh + r);
+                        pv[j] = __fmaf_rn(p4.x, v0, pv[j]);
+                        pv[j] = __fmaf_rn(p4.y, v1, pv[j]);
+                        pv[j] = __fmaf_rn(p4.z, v2, pv[j]);
+                        pv[j] = __fmaf_rn(p4.w, v3, pv[j]);
+                    }
+                }
+            }
+            for (; r < cnt; r++) {
                 const float vv = vc[r * RS + dd];
 #pragma unroll
                 for (uint32_t j = 0; j < HPT; j++) {

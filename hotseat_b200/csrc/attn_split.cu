@@ -25,6 +25,10 @@
 namespace hs {
 namespace {
 
+// K/V chunk buffers: three chunks load while one computes (two at
+// head_dim 128, for shared memory).
+__host__ __device__ constexpr int nbuf(int hd) { return hd == 64 ? 4 : 3; }
+
 template <int HD>
 __global__ void __launch_bounds__(attn::kThreads) k_attn_split(const SplitAttnArgs a) {
     extern __shared__ __align__(16) float sm[];
@@ -43,13 +47,13 @@ __global__ void __launch_bounds__(attn::kThreads) k_attn_split(const SplitAttnAr
     }
     const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits), S = (n + L - 1) / L;
     if (s >= (a.mode != ATTN_APPEND_ONLY ? S : 1u)) return;
-    attn::item<HD, 2>(a, a.layer, s, kvh, slot, pos, sm);
+    attn::item<HD, nbuf(HD)>(a, a.layer, s, kvh, slot, pos, sm);
     tr.exit();
 }
 
 }  // namespace
 
-size_t attn_split_smem(uint32_t head_dim) { return attn::item_smem(head_dim, 2); }
+size_t attn_split_smem(uint32_t head_dim) { return attn::item_smem(head_dim, nbuf((int)head_dim)); }
 
 uint32_t attn_max_splits(uint32_t max_ctx) {
     const uint32_t chunks = (max_ctx + attn::kCh - 1) / attn::kCh;

@@ -824,7 +824,12 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
     // query head in the reference's order.
     m->attn_split = tc || fast;
     if (m->attn_split) {
-        m->max_splits = attn_max_splits(max_ctx);
+        // Batch 1 spreads a sequence's positions over many CTAs (64 per
+        // split); a batch already has a (sequence, KV head) item per SM or
+        // more, so the tensor-core path splits only past 1024 positions per
+        // split: no combine at short contexts. Both depend on max_ctx only,
+        // never on the batch.
+        m->max_splits = tc ? std::max<uint32_t>(1, (max_ctx + 1023) / 1024) : attn_max_splits(max_ctx);
         HS_CUDA_TRY(attn_split_set_smem_limits(optin));
     }
     m->attn_smem = m->attn_split ? attn_split_smem(hd) : attention_smem(hd, max_ctx);
