@@ -188,15 +188,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr uint32_t a_half = 64 * 128;           // one 64-column box of 64 slots
     const uint32_t nt = a.n_tile, N = NMAT * nt;
     const uint32_t w_bytes = nt * 128;              // one 64-column box of nt rows
-    const uint32_t stage_bytes = 2 * a_half + NMAT * w_bytes;
+    const bool wres = a.wres != 0;
+    // stages: activation boxes (+ weight boxes unless resident)
+    const uint32_t stage_bytes = 2 * a_half + (wres ? 0 : NMAT * w_bytes);
     const uint32_t nst = a.nst;
-    float* xchg = reinterpret_cast<float*>(smem + nst * stage_bytes);
+    const uint32_t kw = wres ? (a.K / 64 + a.splits - 1) / a.splits : 0;  // resident k-blocks
+    uint8_t* wreg = smem + nst * stage_bytes;       // resident weight boxes, NMAT per k-block
+    float* xchg = reinterpret_cast<float*>(wreg + kw * NMAT * w_bytes);
     uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + 64 * kXchgStride * NMAT + 2);
     uint64_t* full = bars;
     uint64_t* empty = bars + nst;
     uint64_t* tfull = bars + 2 * nst;
     uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* wfull = tempty + 2;                   // resident weights landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wfull + 1);
     volatile uint32_t* epi_flag = tmem_slot + 1;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const KTrace tr(a.trace, a.trace_slot);
@@ -226,6 +231,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], 128);
         }
+        mbar_init(wfull, 1);
         mbar_init_fence();
     }
     if (warp == 0) {
@@ -255,7 +261,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tma_load_2d(st, &tm_ahi, (int)(kt * 64), (int)m0, &full[s]);
                 tma_load_2d(st + a_half, &tm_alo, (int)(kt * 64), (int)m0, &full[s]);
             };
-            for (uint32_t u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            if (wres) {
+                // The CTA's one unit: all its weight boxes now, then the
+                // activation boxes through the ring after the wait.
+                const uint32_t u = blockIdx.x;
+                if (u < n_units) {
+                    const uint32_t tile = u / S;
+                    uint32_t k0, k1;
+                    k_range(u % S, &k0, &k1);
+                    mbar_expect_tx(wfull, (k1 - k0) * NMAT * w_bytes);
+                    for (uint32_t kt = k0; kt < k1; kt++) {
+                        uint8_t* dst = wreg + (kt - k0) * NMAT * w_bytes;
+                        tma_load_2d(dst, &tm_w0, (int)(kt * 64), (int)(tile * nt), wfull);
+                        if (NMAT == 2) tma_load_2d(dst + w_bytes, &tm_w1, (int)(kt * 64), (int)(tile * nt), wfull);
+                    }
+                    pdl_wait();
+                    if (a.trace && blockIdx.x == 0 && blockIdx.y == 0) a.trace[8 * a.trace_slot + 1] = gtime();
+                    for (uint32_t kt = k0; kt < k1; kt++, it++) {
+                        const uint32_t s = it % nst, r = it / nst;
+                        if (r > 0 && !mbar_wait_bounded(&empty[s], (r - 1) & 1, kLimit)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(&full[s], stage_bytes);
+                        a_load(s, kt);
+                    }
+                }
+                waited = true;
+            }
+            for (uint32_t u = blockIdx.x; u < n_units && ok && !wres; u += gridDim.x) {
                 const uint32_t tile = u / S;
                 uint32_t k0, k1;
                 k_range(u % S, &k0, &k1);
@@ -289,6 +323,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane == 0) {
             const uint32_t idesc = tc_idesc(128, N);
             uint32_t it = 0, t = 0;
+            if (wres && blockIdx.x < n_units && !mbar_wait_bounded(wfull, 0, kLimit)) ok = false;
             for (uint32_t u = blockIdx.x; u < n_units && ok; u += gridDim.x, t++) {
                 const uint32_t b = t % acc.nbuf, use = t / acc.nbuf;
                 if (use > 0 && !mbar_wait_bounded(&tempty[b], (use - 1) & 1, kLimit)) {
@@ -308,7 +343,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (it == 0) tr_mark(a.trace, a.trace_slot, 1);
                     tc_fence_after();
                     const uint8_t* st = smem + s * stage_bytes;
-                    const uint64_t da = sw128_desc(st), dw = sw128_desc(st + 2 * a_half);
+                    const uint64_t da = sw128_desc(st);
+                    const uint64_t dw = sw128_desc(wres ? wreg + (kt - k0) * NMAT * w_bytes : st + 2 * a_half);
 #pragma unroll
                     for (uint32_t kk = 0; kk < 4; kk++) {
                         // +32 bytes along K per 16-element step, inside the swizzle atom
@@ -437,7 +473,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 size_t tc_gemm_smem(uint32_t n_tile, uint32_t nst, bool silu) {
     const uint32_t nmat = silu ? 2 : 1;
     const size_t stage = 2 * 64 * 128 + nmat * (size_t)n_tile * 128;
-    return 1024 + nst * stage + (64 * kXchgStride * nmat + 2) * 4 + (2 * nst + 4) * 8 + 16;
+    return 1024 + nst * stage + (64 * kXchgStride * nmat + 2) * 4 + (2 * nst + 5) * 8 + 16;
+}
+
+size_t tc_gemm_smem_wres(uint32_t n_tile, uint32_t nst, bool silu, uint32_t kw) {
+    const uint32_t nmat = silu ? 2 : 1;
+    return 1024 + nst * (size_t)(2 * 64 * 128) + (size_t)kw * nmat * n_tile * 128 + (64 * kXchgStride * nmat + 2) * 4 +
+           (2 * nst + 5) * 8 + 16;
 }
 
 bool tc_tile_ok(uint32_t n_tile, bool silu) {
@@ -463,7 +505,8 @@ cudaError_t launch_tc_gemm(const TcGemmPlan& p, const CUtensorMap& ahi, const CU
     const bool silu = p.epi == TC_SILU;
     if (p.nst == 0 || p.nst > kMaxStages || !tc_tile_ok(p.n_tile, silu) || p.K % 64 || p.splits == 0 ||
         p.splits > p.K / 64 || (silu && p.splits != 1) || a.n_tile != p.n_tile || a.splits != p.splits ||
-        a.nst != p.nst || a.K != p.K)
+        a.nst != p.nst || a.K != p.K || a.wres != (p.wres ? 1u : 0u) ||
+        (p.wres && p.n_tiles * p.splits > p.grid))  // weights resident: one unit per CTA
         return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(p.grid, p.m_tiles);

@@ -465,6 +465,19 @@ int plan_tc(TcGemmPlan* p, int epi, uint32_t rows, uint32_t K, const uint16_t* w
     while (nst > 1 && tc_gemm_smem(p->n_tile, nst, silu) > smem_cap) nst--;
     p->nst = nst;
     p->smem = tc_gemm_smem(p->n_tile, nst, silu);
+    // One unit per CTA: keep all its weight boxes in shared memory, loaded
+    // before the dependency wait, and stream only the activations after it
+    // (HS_TC_WRES=0 keeps weights and activations in the same stages).
+    if (units <= p->grid && env_u32("HS_TC_WRES", 1) != 0) {
+        const uint32_t kw = (kt_n + p->splits - 1) / p->splits;
+        uint32_t na = std::min<uint32_t>(16, kw);
+        while (na > 1 && tc_gemm_smem_wres(p->n_tile, na, silu, kw) > smem_cap) na--;
+        if (tc_gemm_smem_wres(p->n_tile, na, silu, kw) <= smem_cap && (na >= 2 || kw == 1)) {
+            p->wres = true;
+            p->nst = na;
+            p->smem = tc_gemm_smem_wres(p->n_tile, na, silu, kw);
+        }
+    }
     if (p->smem > smem_cap || !tc_tile_ok(p->n_tile, silu)) return fail(HS_E_UNSUPPORTED, "tensor-core GEMM tile does not fit");
     int rc = make_weight_map(&p->tm0, w0, K, rows, p->n_tile);
     if (rc == HS_OK) rc = make_weight_map(&p->tm1, w1 ? w1 : w0, K, rows, p->n_tile);
@@ -1599,6 +1612,7 @@ int batch_gemm(hs_batch* b, const TcGemmPlan& p, const uint16_t* a_hi, const uin
     a.splits = p.splits;
     a.slots = n;
     a.nst = p.nst;
+    a.wres = p.wres ? 1u : 0u;
     a.ld = ld;
     a.part_stride = (uint64_t)b->cap_slots * p.rows;
     a.out = out;

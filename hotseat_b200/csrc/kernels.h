@@ -104,7 +104,9 @@ struct TcGemmArgs {
     uint32_t n_tiles;        // ceil(rows / n_tile)
     uint32_t splits;         // K splits per tile (TC_PART: partial sums per split)
     uint32_t slots;          // live activation rows (groups of 64 along gridDim.y)
-    uint32_t nst;            // shared-memory pipeline stages
+    uint32_t nst;            // shared-memory pipeline stages (activations only when wres)
+    uint32_t wres;           // 1: the CTA's one unit keeps all its weight boxes in shared memory,
+                             //    loaded before the dependency wait; only activations stream
     uint32_t ld;             // row stride (elements) of the outputs
     uint64_t part_stride;    // TC_PART: elements between splits
     float* out;              // TC_STORE: out = D; TC_PART: out[split] = partial D
@@ -118,11 +120,14 @@ struct TcGemmArgs {
 struct TcGemmPlan {
     int epi = TC_STORE;
     uint32_t K = 0, rows = 0, n_tile = 0, n_tiles = 0, splits = 1, nst = 0, grid = 0, m_tiles = 1;
+    bool wres = false;       // weights resident (see TcGemmArgs::wres)
     size_t smem = 0;
     CUtensorMap tm0{}, tm1{};  // weight boxes {64 columns, n_tile rows}
 };
 
 size_t tc_gemm_smem(uint32_t n_tile, uint32_t nst, bool silu);
+// Weights-resident layout: nst activation stages + kw k-blocks of weight boxes.
+size_t tc_gemm_smem_wres(uint32_t n_tile, uint32_t nst, bool silu, uint32_t kw);
 bool tc_tile_ok(uint32_t n_tile, bool silu);
 cudaError_t tc_set_smem_limits(int optin);
 cudaError_t launch_tc_gemm(const TcGemmPlan& p, const CUtensorMap& ahi, const CUtensorMap& alo, const TcGemmArgs& a,
