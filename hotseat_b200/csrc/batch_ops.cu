@@ -34,17 +34,19 @@ constexpr uint32_t kMaxParts = 32;      // split-K partials a consumer adds
 __device__ __forceinline__ float4 f4add(float4 a, float4 b) {
     return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
 }
-// Sum of `n` split partials of one float4 chunk, in split order; the loads
-// are issued eight at a time so they overlap.
+// Sum of `n` split partials of one float4 chunk, in split order; all the
+// loads (up to 24) are issued before the first add so they overlap in one
+// round trip.
 __device__ __forceinline__ float4 sum_parts(const float* base, uint64_t stride, uint32_t n) {
+    constexpr uint32_t B = 24;
     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (uint32_t s0 = 0; s0 < n; s0 += 8) {
-        float4 v[8];
+    for (uint32_t s0 = 0; s0 < n; s0 += B) {
+        float4 v[B];
 #pragma unroll
-        for (uint32_t j = 0; j < 8; j++)
+        for (uint32_t j = 0; j < B; j++)
             if (s0 + j < n) v[j] = __ldcg(reinterpret_cast<const float4*>(base + (s0 + j) * stride));
 #pragma unroll
-        for (uint32_t j = 0; j < 8; j++)
+        for (uint32_t j = 0; j < B; j++)
             if (s0 + j < n) acc = f4add(acc, v[j]);
     }
     return acc;
