@@ -53,14 +53,37 @@ __device__ __forceinline__ float4 f4add(float4 a, float4 b) {
     return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
 }
 
-// Shared memory of one item (floats): q [8][HD], k, v [HD], K/V chunks
-// [2][NBUF][kCh][HD+4], probabilities [8][kCh], per-head max/rescale/sum
-// [3][8], a flag word (4 floats), the RoPE row of `pos` [HD/2 cos, HD/2 sin].
-__host__ __device__ constexpr size_t item_smem(uint32_t hd, uint32_t nbuf) {
-    return (8 * hd + 2 * hd + 2 * nbuf * kCh * (hd + 4) + 8 * kCh + 3 * 8 + 4 + hd) * sizeof(float);
-}
+// Row strides (floats) of the K and V chunk buffers and of the score rows,
+// chosen so that the tensor-core operand reads of a warp hit 32 distinct
+// banks (K: 4 (row) + column; V: 8 (row) + column; scores: 4 (head) + position).
+__host__ __device__ constexpr uint32_t k_stride(uint32_t hd) { return hd + 4; }
+__host__ __device__ constexpr uint32_t v_stride(uint32_t hd) { return hd + 8; }
+constexpr uint32_t SPS = kCh + 4;
+
+// Shared memory of one item (floats): q [8][HD], k, v [HD], K chunks
+// [NBUF][kCh][HD+4], V chunks [NBUF][kCh][HD+8], scores [2][8][SPS] (the two
+// halves of the dimensions; probabilities in the first), per-head
+// max/rescale/sum [3][8], a flag word (4 floats), q as tf32 operand fragments
+// [2 halves][HD/16 k-steps][32 lanes][4] (hi, hi, lo, lo), the RoPE row of
+// `pos` [HD/2 cos, HD/2 sin].
 __host__ __device__ constexpr uint32_t item_rope_off(uint32_t hd, uint32_t nbuf) {
-    return 8 * hd + 2 * hd + 2 * nbuf * kCh * (hd + 4) + 8 * kCh + 3 * 8 + 4;
+    return 8 * hd + 2 * hd + nbuf * kCh * (k_stride(hd) + v_stride(hd)) + 2 * 8 * SPS + 3 * 8 + 4 + 16 * hd;
+}
+__host__ __device__ constexpr size_t item_smem(uint32_t hd, uint32_t nbuf) {
+    return (item_rope_off(hd, nbuf) + hd) * sizeof(float);
+}
+
+// x as a tf32 pair: hi = x rounded to tf32, lo = the rest rounded to tf32.
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(x));
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(__fsub_rn(x, __uint_as_float(hi))));
+}
+// c += a . b, one m16n8k8 tile (a row-major 16x8, b column-major 8x8).
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
 }
 
 // Split-order combine of the S published splits of one (sequence, KV head)
@@ -90,18 +113,21 @@ __device__ __forceinline__ uint64_t kv_row_off(const SplitAttnArgs& a, uint32_t 
     return (uint64_t)layer * 2 * plane + (is_v ? plane : 0) + within;
 }
 
-// Issues (and commits) the asynchronous loads of the cached rows of an
-// item's first chunk, all but `pos`, into its K/V buffers: those rows do not
-// depend on this token, so a caller may start them before the QKV product
-// exists and then run item(..., prefetched = true).
+// Issues the asynchronous loads of the RoPE row and of the cached rows of
+// an item's first `nch` chunks (at most NBUF), all but `pos`, into its
+// buffers, one commit group per chunk (the RoPE row with the first): those
+// rows do not depend on this token, so a caller may start them before the
+// QKV product exists and then run item(..., npre = the chunks issued).
+// Returns the chunks issued (fewer when the split has fewer).
 template <int HD, int NBUF>
-__device__ void prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t slot,
-                         uint32_t pos, float* sm) {
-    constexpr uint32_t RS = HD + 4;
+__device__ uint32_t prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t slot,
+                             uint32_t pos, float* sm, uint32_t nch = 1) {
+    constexpr uint32_t RSK = k_stride(HD), RSV = v_stride(HD);
     float* kb = sm + 10 * HD;
-    float* vb = kb + NBUF * kCh * RS;
+    float* vb = kb + NBUF * kCh * RSK;
     const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits);
-    const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n, cnt = p1 - p0 < kCh ? p1 - p0 : kCh;
+    const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n, have = (p1 - p0 + kCh - 1) / kCh;
+    if (nch > have) nch = have;
     const float* kv = a.kv[slot];
     float* rope = sm + item_rope_off(HD, NBUF);
     if (threadIdx.x < HD / 4) {  // HD/8 16-byte pieces of each of the cos and sin halves
@@ -109,44 +135,66 @@ __device__ void prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uin
         const float* src = (half ? a.rope_sin : a.rope_cos) + (size_t)pos * (HD / 2) + 4 * i;
         cp_async16(rope + half * (HD / 2) + 4 * i, src);
     }
-    for (uint32_t idx = threadIdx.x; idx < cnt * (HD / 4); idx += kThreads) {
-        const uint32_t r = idx / (HD / 4), c4 = idx % (HD / 4);
-        if (p0 + r == pos) continue;
-        cp_async16(kb + r * RS + 4 * c4, kv + kv_row_off(a, layer, kvh, HD, p0 + r, 0) + 4 * c4);
-        cp_async16(vb + r * RS + 4 * c4, kv + kv_row_off(a, layer, kvh, HD, p0 + r, 1) + 4 * c4);
+    for (uint32_t c = 0; c < nch; c++) {
+        const uint32_t c0 = p0 + c * kCh, cnt = p1 - c0 < kCh ? p1 - c0 : kCh;
+        for (uint32_t idx = threadIdx.x; idx < cnt * (HD / 4); idx += kThreads) {
+            const uint32_t r = idx / (HD / 4), c4 = idx % (HD / 4);
+            if (c0 + r == pos) continue;
+            cp_async16(kb + (c * kCh + r) * RSK + 4 * c4, kv + kv_row_off(a, layer, kvh, HD, c0 + r, 0) + 4 * c4);
+            cp_async16(vb + (c * kCh + r) * RSV + 4 * c4, kv + kv_row_off(a, layer, kvh, HD, c0 + r, 1) + 4 * c4);
+        }
+        cp_commit();
     }
-    cp_commit();
+    if (nch == 0) cp_commit();  // the RoPE row alone
+    return nch > 0 ? nch : 1;
 }
 
-// Preconditions (checked by the caller): the sequence is active, pos <
-// max_ctx, s < S (attend) or s == 0 (append only); `prefetched` only in
-// ATTN_FULL mode after prefetch() of the same item (which also loaded the
-// RoPE row). `layer` selects the KV planes (a.layer is not read). With
+// Waits until at most n (0..3) commit groups are pending.
+__device__ __forceinline__ void cp_wait_pending(uint32_t n) {
+    switch (n) {
+        case 0: cp_wait<0>(); break;
+        case 1: cp_wait<1>(); break;
+        case 2: cp_wait<2>(); break;
+        default: cp_wait<3>(); break;
+    }
+}
+
+// One item: split s of KV head kvh, query-head part hpart, for sequence
+// slot `slot` at `pos`. Preconditions (checked by the caller): the sequence
+// is active, pos < max_ctx, s < S (attend) or s == 0 (append only); `npre` >
+// 0 only in ATTN_FULL mode, as prefetch()'s return for the same item (whose
+// first group also loaded the RoPE row), with no commit group issued since.
+// `layer` selects the KV planes (a.layer is not read). TC: the chunk
+// products on the tensor cores, else on the CUDA cores. With
 // `reader_combines`, several splits only publish their partials: the reader
 // of the output combines them (combine()) after a grid-wide barrier.
-template <int HD, int NBUF>
-__device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t slot, uint32_t pos,
-                     float* sm, bool prefetched = false, bool reader_combines = false, uint64_t* probe = nullptr) {
+template <int HD, int NBUF, bool TC>
+__device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t hpart, uint32_t slot,
+                     uint32_t pos, float* sm, uint32_t npre = 0, bool reader_combines = false,
+                     uint64_t* probe = nullptr) {
     // probe (timing): thread 0 stores clock64() at the item's checkpoints
     auto at = [&](int k) {
         if (probe && threadIdx.x == 0) probe[k] = clock64();
     };
     at(0);
     static_assert(NBUF >= 1 && NBUF <= 4, "one to four chunk buffers");
-    constexpr uint32_t RS = HD + 4, HALF = HD / 2;
+    constexpr uint32_t RSK = k_stride(HD), RSV = v_stride(HD), HALF = HD / 2;
     constexpr uint32_t HSETS = kThreads / HD, HPT = (8 + HSETS - 1) / HSETS;
     const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t G = a.nh / a.nkv;
+    // this item's query heads: part hpart of the group's Gf heads
+    const uint32_t Gf = a.nh / a.nkv, hsplit = attn_head_split(a);
+    const uint32_t hlo = hpart * Gf / hsplit, G = (hpart + 1) * Gf / hsplit - hlo;
     float* qs = sm;                        // [8][HD]
     float* kn = qs + 8 * HD;               // [HD]
     float* vn = kn + HD;                   // [HD]
-    float* kb = vn + HD;                   // [NBUF][kCh][RS]
-    float* vb = kb + NBUF * kCh * RS;      // [NBUF][kCh][RS]
-    float* sp = vb + NBUF * kCh * RS;      // [8][kCh] scores, then probabilities
-    float* hs_m = sp + 8 * kCh;            // [8] running maximum per head
+    float* kb = vn + HD;                   // [NBUF][kCh][RSK]
+    float* vb = kb + NBUF * kCh * RSK;     // [NBUF][kCh][RSV]
+    float* sp = vb + NBUF * kCh * RSV;     // [2][8][SPS] scores, then probabilities
+    float* hs_m = sp + 2 * 8 * SPS;        // [8] running maximum per head
     float* hs_f = hs_m + 8;                // [8] rescale of the running sums this chunk
     float* hs_l = hs_f + 8;                // [8] running sums
     uint32_t* flag = reinterpret_cast<uint32_t*>(hs_l + 8);
+    uint4* qfrag = reinterpret_cast<uint4*>(hs_l + 12);  // [2][HD/16][32]
     const float* rope = sm + item_rope_off(HD, NBUF);
     const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits), S = (n + L - 1) / L;
     // Prefill runs append (every token's k, v) and attend (reading all rows
@@ -156,11 +204,13 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n;
     float* kv = a.kv[slot];
     auto row_off = [&](uint32_t p, uint32_t is_v) -> uint64_t { return kv_row_off(a, layer, kvh, HD, p, is_v); };
-    // split 0 appends the new row; read the tracking flag now, mark later
-    const bool track = s == 0 && append && tid < 2 && ldv(a.tracking[slot]) != 0;
+    // split 0's first head part appends the new row; read the tracking flag
+    // now, mark later
+    const bool appender = s == 0 && hpart == 0 && append;
+    const bool track = appender && tid < 2 && ldv(a.tracking[slot]) != 0;
 
     // q, k, v of this group; split-K partials in split order, then the bias.
-    const uint32_t qrow0 = kvh * G * HD, krow0 = a.nh * HD + kvh * HD, vrow0 = (a.nh + a.nkv) * HD + kvh * HD;
+    const uint32_t qrow0 = (kvh * Gf + hlo) * HD, krow0 = a.nh * HD + kvh * HD, vrow0 = (a.nh + a.nkv) * HD + kvh * HD;
     for (uint32_t c = tid; c < (G + 2) * HD / 4; c += kThreads) {
         const uint32_t idx = 4 * c;
         const uint32_t row = idx < G * HD ? qrow0 + idx : (idx < (G + 1) * HD ? krow0 + idx - G * HD : vrow0 + idx - (G + 1) * HD);
@@ -179,7 +229,8 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
         float* dst = idx < G * HD ? qs + idx : (idx < (G + 1) * HD ? kn + idx - G * HD : vn + idx - (G + 1) * HD);
         *reinterpret_cast<float4*>(dst) = p;
     }
-    if (prefetched) cp_wait0();  // the RoPE row (and the first chunk)
+    const bool prefetched = npre > 0;
+    if (prefetched) cp_wait_pending(npre - 1);  // the RoPE row and the first chunk
     sync256();
     at(1);
     for (uint32_t idx = tid; idx < (G + 1) * HALF; idx += kThreads) {
@@ -197,7 +248,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     }
     sync256();
     at(2);
-    if (s == 0 && append && tid < HD) {
+    if (appender && tid < HD) {
         kv[row_off(pos, 0) + tid] = kn[tid];
         kv[row_off(pos, 1) + tid] = vn[tid];
     }
@@ -223,26 +274,63 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     auto issue = [&](uint32_t c) {
         if (c < nch) {
             const uint32_t c0 = p0 + c * kCh, cnt = p1 - c0 < kCh ? p1 - c0 : kCh;
-            float* kd = kb + (c % NBUF) * kCh * RS;
-            float* vd = vb + (c % NBUF) * kCh * RS;
+            float* kd = kb + (c % NBUF) * kCh * RSK;
+            float* vd = vb + (c % NBUF) * kCh * RSV;
             for (uint32_t idx = tid; idx < cnt * (HD / 4); idx += kThreads) {
                 const uint32_t r = idx / (HD / 4), c4 = idx % (HD / 4);
                 if (c0 + r == pos && append) {
-                    *reinterpret_cast<float4*>(kd + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(kn + 4 * c4);
-                    *reinterpret_cast<float4*>(vd + r * RS + 4 * c4) = *reinterpret_cast<const float4*>(vn + 4 * c4);
-                } else if (!(prefetched && c == 0)) {
-                    cp_async16(kd + r * RS + 4 * c4, kv + row_off(c0 + r, 0) + 4 * c4);
-                    cp_async16(vd + r * RS + 4 * c4, kv + row_off(c0 + r, 1) + 4 * c4);
+                    *reinterpret_cast<float4*>(kd + r * RSK + 4 * c4) = *reinterpret_cast<const float4*>(kn + 4 * c4);
+                    *reinterpret_cast<float4*>(vd + r * RSV + 4 * c4) = *reinterpret_cast<const float4*>(vn + 4 * c4);
+                } else if (c >= npre) {
+                    cp_async16(kd + r * RSK + 4 * c4, kv + row_off(c0 + r, 0) + 4 * c4);
+                    cp_async16(vd + r * RSV + 4 * c4, kv + row_off(c0 + r, 1) + 4 * c4);
                 }
             }
+            // TC: V rows past the split's end are zero (the tiles span the
+            // whole chunk; their probabilities are 0, and 0 times a stale
+            // non-finite value would not be)
+            if constexpr (TC)
+                for (uint32_t idx = cnt * (HD / 4) + tid; idx < kCh * (HD / 4); idx += kThreads)
+                    *reinterpret_cast<float4*>(vd + (idx / (HD / 4)) * RSV + 4 * (idx % (HD / 4))) =
+                        make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
-        cp_commit();
+        if (c >= npre) cp_commit();  // a prefetched chunk's group is committed already
     };
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-    float o[HPT];
+    // TC: both products of a chunk on the tensor cores (mma.sync m16n8k8,
+    // tf32 operands split hi + lo so that lo*hi + hi*lo + hi*hi keeps about
+    // 22 significant bits: the split-precision method of Ootomo & Yokota,
+    // "Recovering single precision accuracy from Tensor Cores", 2022).
+    //   scores^T [64 positions][8 heads] = K [64][HD] . q^T [HD][8]: warp w
+    //     takes positions 16 (w % 4) .. +15 and half w / 4 of the dimensions;
+    //     the two halves are added in the softmax;
+    //   out^T [HD][8 heads] += V^T [HD][64] . P^T [64][8]: warp w takes
+    //     dimensions 16 (w % MTV) .. +15 and positions part w / MTV of the
+    //     chunk; the parts' accumulators are added after the last chunk.
+    // Otherwise fp32 FMA chains on the CUDA cores (fewer registers: the
+    // persistent token kernel inlines this item among its GEMV phases).
+    constexpr uint32_t KSQ = HD / 16;                 // k-steps of 8 dimensions per half
+    constexpr uint32_t MTV = HD / 16, WPV = 8 / MTV;  // m-tiles of out^T, warps per m-tile
+    constexpr uint32_t KSV = 8 / WPV;                 // k-steps of 8 positions per warp
+    const uint32_t g = lane >> 2, t4 = lane & 3;
+    const uint32_t mq = warp & 3, kq = warp >> 2, mv = warp % MTV, kvp = warp / MTV;
+    const uint32_t dd = tid % HD, hs0 = tid / HD;
+    const uint4* qf = qfrag + kq * KSQ * 32 + lane;
+    if constexpr (TC) {
+        // q^T operand fragments, split once per item (read by the first
+        // iteration after its barrier)
+        for (uint32_t e = tid; e < 2 * KSQ * 32; e += kThreads) {
+            const uint32_t ln = e % 32, gg = ln >> 2, d = (e / 32) * 8 + (ln & 3);
+            uint4 f;
+            tf32_split(gg < G ? qs[gg * HD + d] : 0.0f, f.x, f.z);
+            tf32_split(gg < G ? qs[gg * HD + d + 4] : 0.0f, f.y, f.w);
+            qfrag[e] = f;
+        }
+    }
+    float oa[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // TC: out^T (16 mv + g, 2 t4), (.., 2 t4 + 1), (+8, ..), (+8, ..)
+    float o[HPT];                            // CUDA cores: dimension dd of heads hs0 + j HSETS
 #pragma unroll
     for (uint32_t j = 0; j < HPT; j++) o[j] = 0.0f;
-    const uint32_t dd = tid % HD, hs0 = tid / HD;
     // chunks 0 .. NBUF-2 in flight before the loop; each iteration issues
     // chunk c + NBUF - 1 (an empty group past the end) and waits for chunk c
 #pragma unroll
@@ -253,18 +341,40 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
         sync256();
         if (c == 0) at(3);
         const uint32_t c0 = p0 + c * kCh, cnt = p1 - c0 < kCh ? p1 - c0 : kCh;
-        const float* kc = kb + (c % NBUF) * kCh * RS;
-        const float* vc = vb + (c % NBUF) * kCh * RS;
-        // scores: thread t takes position t % 64 and heads t/64, t/64 + 4
-        // (each K row read once for both heads)
-        {
+        const float* kc = kb + (c % NBUF) * kCh * RSK;
+        const float* vc = vb + (c % NBUF) * kCh * RSV;
+        if constexpr (TC) {
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const float* kr = kc + (16 * mq + g) * RSK + kq * (HD / 2) + t4;
+#pragma unroll
+            for (uint32_t j = 0; j < KSQ; j++) {
+                uint32_t ah[4], al[4];
+                tf32_split(kr[8 * j], ah[0], al[0]);
+                tf32_split(kr[8 * RSK + 8 * j], ah[1], al[1]);
+                tf32_split(kr[8 * j + 4], ah[2], al[2]);
+                tf32_split(kr[8 * RSK + 8 * j + 4], ah[3], al[3]);
+                const uint4 f = qf[j * 32];
+                const uint32_t bh[2] = {f.x, f.y}, bl[2] = {f.z, f.w};
+                mma_tf32(acc, al, bh);
+                mma_tf32(acc, ah, bl);
+                mma_tf32(acc, ah, bh);
+            }
+            float* sk = sp + kq * 8 * SPS;
+            const uint32_t r = 16 * mq + g;
+            sk[(2 * t4) * SPS + r] = acc[0];
+            sk[(2 * t4 + 1) * SPS + r] = acc[1];
+            sk[(2 * t4) * SPS + r + 8] = acc[2];
+            sk[(2 * t4 + 1) * SPS + r + 8] = acc[3];
+        } else {
+            // thread t takes position t % 64 and heads t/64, t/64 + 4 (each
+            // K row read once for both heads); scaled scores, masked past cnt
             constexpr uint32_t HSETS_S = kThreads / kCh, HPT_S = (8 + HSETS_S - 1) / HSETS_S;
             const uint32_t r = tid % kCh, h0 = tid / kCh;
             float sc[HPT_S][4];
 #pragma unroll
             for (uint32_t j = 0; j < HPT_S; j++) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
             if (r < cnt) {
-                const float4* k4 = reinterpret_cast<const float4*>(kc + r * RS);
+                const float4* k4 = reinterpret_cast<const float4*>(kc + r * RSK);
 #pragma unroll
                 for (uint32_t d4 = 0; d4 < HD / 4; d4++) {
                     const float4 kk = k4[d4];
@@ -285,7 +395,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
             for (uint32_t j = 0; j < HPT_S; j++) {
                 const uint32_t h = h0 + j * HSETS_S;
                 if (h < G)
-                    sp[h * kCh + r] = r < cnt ? __fmul_rn(__fadd_rn(__fadd_rn(sc[j][0], sc[j][1]),
+                    sp[h * SPS + r] = r < cnt ? __fmul_rn(__fadd_rn(__fadd_rn(sc[j][0], sc[j][1]),
                                                                     __fadd_rn(sc[j][2], sc[j][3])),
                                                           scale)
                                               : -FLT_MAX;
@@ -293,10 +403,19 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
         }
         sync256();
         if (c == 0) at(4);
-        // online softmax: warp h owns head h
+        // online softmax: warp h owns head h; probabilities in the first
+        // score half
         if (warp < G) {
-            float* sh = sp + warp * kCh;
-            const float a0 = sh[lane], a1 = sh[lane + 32];
+            float* sh = sp + warp * SPS;
+            float a0, a1;
+            if constexpr (TC) {
+                const float* sh2 = sh + 8 * SPS;
+                a0 = lane < cnt ? __fmul_rn(__fadd_rn(sh[lane], sh2[lane]), scale) : -FLT_MAX;
+                a1 = lane + 32 < cnt ? __fmul_rn(__fadd_rn(sh[lane + 32], sh2[lane + 32]), scale) : -FLT_MAX;
+            } else {
+                a0 = sh[lane];
+                a1 = sh[lane + 32];
+            }
             float mx = fmaxf(a0, a1);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -314,26 +433,50 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
                 hs_m[warp] = m_new;
                 hs_l[warp] = __fadd_rn(__fmul_rn(hs_l[warp], f), sum);
             }
+        } else if (TC && lane == 0) {
+            hs_f[warp] = 1.0f;  // heads past the group (their columns are discarded)
         }
         sync256();
         if (c == 0) at(5);
-        // P.V: thread t owns dimension t % HD of heads t/HD, t/HD + HSETS,
-        // ...: one chain per head over the positions in order, each V
-        // element read once for all of them
-        {
+        if constexpr (TC) {
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const float* vr = vc + (kvp * KSV * 8 + t4) * RSV + 16 * mv + g;
+            const float* pr = sp + g * SPS + kvp * KSV * 8 + t4;
+#pragma unroll
+            for (uint32_t j = 0; j < KSV; j++) {
+                uint32_t ah[4], al[4], bh[2], bl[2];
+                tf32_split(vr[8 * j * RSV], ah[0], al[0]);
+                tf32_split(vr[8 * j * RSV + 8], ah[1], al[1]);
+                tf32_split(vr[(8 * j + 4) * RSV], ah[2], al[2]);
+                tf32_split(vr[(8 * j + 4) * RSV + 8], ah[3], al[3]);
+                tf32_split(pr[8 * j], bh[0], bl[0]);
+                tf32_split(pr[8 * j + 4], bh[1], bl[1]);
+                mma_tf32(acc, al, bh);
+                mma_tf32(acc, ah, bl);
+                mma_tf32(acc, ah, bh);
+            }
+            const float f0 = hs_f[2 * t4], f1 = hs_f[2 * t4 + 1];
+            oa[0] = __fadd_rn(__fmul_rn(oa[0], f0), acc[0]);
+            oa[1] = __fadd_rn(__fmul_rn(oa[1], f1), acc[1]);
+            oa[2] = __fadd_rn(__fmul_rn(oa[2], f0), acc[2]);
+            oa[3] = __fadd_rn(__fmul_rn(oa[3], f1), acc[3]);
+        } else {
+            // thread t owns dimension t % HD of heads t/HD, t/HD + HSETS, ...:
+            // one chain per head over the positions in order, each V element
+            // read once for all of them
             float pv[HPT];
 #pragma unroll
             for (uint32_t j = 0; j < HPT; j++) pv[j] = 0.0f;
             // four positions at a time: their probabilities as one 16-byte read
             uint32_t r = 0;
             for (; r + 4 <= cnt; r += 4) {
-                const float v0 = vc[r * RS + dd], v1 = vc[(r + 1) * RS + dd], v2 = vc[(r + 2) * RS + dd],
-                            v3 = vc[(r + 3) * RS + dd];
+                const float v0 = vc[r * RSV + dd], v1 = vc[(r + 1) * RSV + dd], v2 = vc[(r + 2) * RSV + dd],
+                            v3 = vc[(r + 3) * RSV + dd];
 #pragma unroll
                 for (uint32_t j = 0; j < HPT; j++) {
                     const uint32_t h = hs0 + j * HSETS;
                     if (h < G) {
-                        const float4 p4 = *reinterpret_cast<const float4*>(sp + h * kCh + r);
+                        const float4 p4 = *reinterpret_cast<const float4*>(sp + h * SPS + r);
                         pv[j] = __fmaf_rn(p4.x, v0, pv[j]);
                         pv[j] = __fmaf_rn(p4.y, v1, pv[j]);
                         pv[j] = __fmaf_rn(p4.z, v2, pv[j]);
@@ -342,11 +485,11 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
                 }
             }
             for (; r < cnt; r++) {
-                const float vv = vc[r * RS + dd];
+                const float vv = vc[r * RSV + dd];
 #pragma unroll
                 for (uint32_t j = 0; j < HPT; j++) {
                     const uint32_t h = hs0 + j * HSETS;
-                    if (h < G) pv[j] = __fmaf_rn(sp[h * kCh + r], vv, pv[j]);
+                    if (h < G) pv[j] = __fmaf_rn(sp[h * SPS + r], vv, pv[j]);
                 }
             }
 #pragma unroll
@@ -358,6 +501,25 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
         sync256();
     }
     cp_wait0();
+    if constexpr (TC) {
+        // out^T parts through shared memory (the K buffers are free): [WPV][8][HD]
+        float* ot = kb + kvp * 8 * HD;
+        const uint32_t d = 16 * mv + g;
+        ot[(2 * t4) * HD + d] = oa[0];
+        ot[(2 * t4 + 1) * HD + d] = oa[1];
+        ot[(2 * t4) * HD + d + 8] = oa[2];
+        ot[(2 * t4 + 1) * HD + d + 8] = oa[3];
+        sync256();
+#pragma unroll
+        for (uint32_t j = 0; j < HPT; j++) {
+            const uint32_t h = hs0 + j * HSETS;
+            if (h < 8) {
+                o[j] = kb[h * HD + dd];
+#pragma unroll
+                for (uint32_t q = 1; q < WPV; q++) o[j] = __fadd_rn(o[j], kb[(q * 8 + h) * HD + dd]);
+            }
+        }
+    }
     at(6);
     mark_dirty();
 
@@ -375,22 +537,22 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
 #pragma unroll
         for (uint32_t j = 0; j < HPT; j++) {
             const uint32_t h = hs0 + j * HSETS;
-            if (h < G) store((size_t)slot * a.out_stride + (size_t)(kvh * G + h) * HD + dd, __fdiv_rn(o[j], hs_l[h]));
+            if (h < G) store((size_t)slot * a.out_stride + (size_t)(kvh * Gf + hlo + h) * HD + dd, __fdiv_rn(o[j], hs_l[h]));
         }
         return;
     }
     // Several splits: publish (unnormalised output, max, sum); the last item
     // to arrive combines all splits in split order.
-    const uint32_t rec = attn_record(G, HD);
+    const uint32_t rec = attn_record(Gf, HD);
     float* part = a.partials + ((size_t)(slot * a.nkv + kvh) * a.max_splits) * rec;
 #pragma unroll
     for (uint32_t j = 0; j < HPT; j++) {
         const uint32_t h = hs0 + j * HSETS;
-        if (h < G) part[(size_t)s * rec + h * HD + dd] = o[j];
+        if (h < G) part[(size_t)s * rec + (hlo + h) * HD + dd] = o[j];
     }
     if (tid < G) {
-        part[(size_t)s * rec + G * HD + tid] = hs_m[tid];
-        part[(size_t)s * rec + G * HD + G + tid] = hs_l[tid];
+        part[(size_t)s * rec + Gf * HD + hlo + tid] = hs_m[tid];
+        part[(size_t)s * rec + Gf * HD + Gf + hlo + tid] = hs_l[tid];
     }
     if (reader_combines) {
         at(7);
@@ -399,14 +561,14 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     __threadfence();
     sync256();
     uint32_t* counter = a.counters + slot * a.nkv + kvh;
-    if (tid == 0) *flag = atomicAdd(counter, 1u) == S - 1 ? 1u : 0u;
+    if (tid == 0) *flag = atomicAdd(counter, 1u) == S * hsplit - 1 ? 1u : 0u;
     sync256();
     const bool last = *flag != 0;
     sync256();  // the flag word is rewritten by the next item
     if (!last) return;
     __threadfence();
-    for (uint32_t idx = tid; idx < G * HD; idx += kThreads)
-        store((size_t)slot * a.out_stride + (size_t)kvh * G * HD + idx, combine<true>(part, S, G, HD, idx));
+    for (uint32_t idx = tid; idx < Gf * HD; idx += kThreads)
+        store((size_t)slot * a.out_stride + (size_t)kvh * Gf * HD + idx, combine<true>(part, S, Gf, HD, idx));
     if (tid == 0) *counter = 0;
 }
 

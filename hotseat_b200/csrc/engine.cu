@@ -219,6 +219,8 @@ struct hs_model {
     bool attn_global = false;     // attention scores in a global buffer (long max_ctx)
     bool attn_split = false;      // split-KV attention (GPU-native paths)
     uint32_t max_splits = 0;
+    uint32_t attn_head_split = 1;  // query-head parts per split-KV attention item
+    uint32_t attn_nbuf = 0;        // K/V chunk buffers per item (0 = by head_dim)
     uint32_t numeric = HS_NUMERIC_REFERENCE;
     TcGemmPlan thead;             // tensor-core LM head
     bool tok = false;             // fast path: one persistent kernel per token (token_fast.cu)
@@ -506,6 +508,9 @@ SplitAttnArgs scratch_attn_args(const hs_scratch* s, const hs_kv* kv) {
     sa.layout = kv->spec.layout;
     sa.page_shift = kv->page_shift;
     sa.max_splits = m->max_splits;
+    sa.head_split = m->attn_head_split;
+    sa.nbuf = m->attn_nbuf;
+    sa.tensor_cores = m->numeric == HS_NUMERIC_TC ? 1u : 0u;
     sa.trace = s->trace;
     return sa;
 }
@@ -842,10 +847,14 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
         // more, so the tensor-core path splits only past 1024 positions per
         // split: no combine at short contexts. Both depend on max_ctx only,
         // never on the batch.
-        m->max_splits = tc ? std::max<uint32_t>(1, (max_ctx + 1023) / 1024) : attn_max_splits(max_ctx);
+        const uint32_t tc_split = std::max<uint32_t>(64, env_u32("HS_TC_SPLIT_POSITIONS", 1024));
+        m->max_splits = tc ? std::min<uint32_t>(128, std::max<uint32_t>(1, (max_ctx + tc_split - 1) / tc_split))
+                           : attn_max_splits(max_ctx);
+        m->attn_head_split = std::max<uint32_t>(1, env_u32("HS_ATTN_HEAD_SPLIT", 1));
+        m->attn_nbuf = env_u32("HS_ATTN_NBUF", 0);
         HS_CUDA_TRY(attn_split_set_smem_limits(optin));
     }
-    m->attn_smem = m->attn_split ? attn_split_smem(hd) : attention_smem(hd, max_ctx);
+    m->attn_smem = m->attn_split ? attn_split_smem(hd, m->attn_nbuf) : attention_smem(hd, max_ctx);
     if (!m->attn_split && m->attn_smem > m->smem_cap) {
         // Long contexts: the scores move to a global buffer (L2-resident per head).
         m->attn_global = true;
@@ -1689,6 +1698,9 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool pref
             sa.layout = b->layout;
             sa.page_shift = b->page_shift;
             sa.max_splits = m->max_splits;
+            sa.head_split = m->attn_head_split;
+            sa.nbuf = m->attn_nbuf;
+            sa.tensor_cores = m->numeric == HS_NUMERIC_TC ? 1u : 0u;
             sa.trace = b->trace;
             sa.trace_slot = *launches;
             if (prefill) {

@@ -170,10 +170,18 @@ struct SplitAttnArgs {
     DevCtl* ctl;             // per-sequence control blocks
     uint32_t layer, nh, nkv, max_ctx, layout, page_shift, max_splits;
     uint32_t mode;           // ATTN_* below
+    uint32_t head_split;     // items per (split, KV head): the group's query heads in this many parts (0 = 1)
+    uint32_t nbuf;           // K/V chunk buffers per item, 2..4 (0 = by head_dim)
+    uint32_t tensor_cores;   // chunk products on the tensor cores (split tf32), else fp32 on the CUDA cores
     uint64_t* trace;
     uint32_t trace_slot;
 };
 enum AttnMode : uint32_t { ATTN_FULL = 0, ATTN_APPEND_ONLY = 1, ATTN_ATTEND_ONLY = 2 };
+// Query-head parts per (split, KV head), at most the group size.
+__host__ __device__ inline uint32_t attn_head_split(const SplitAttnArgs& a) {
+    const uint32_t g = a.nh / a.nkv, h = a.head_split ? a.head_split : 1;
+    return h < g ? h : g;
+}
 // Positions per split for n cached positions: a multiple of 64, so that at
 // most max_splits splits cover n.
 __host__ __device__ inline uint32_t attn_split_len(uint32_t n, uint32_t max_splits) {
@@ -185,7 +193,7 @@ __host__ __device__ inline uint32_t attn_split_len(uint32_t n, uint32_t max_spli
 __host__ __device__ inline uint32_t attn_record(uint32_t groups, uint32_t hd) {
     return (groups * hd + 2 * groups + 3) / 4 * 4;
 }
-size_t attn_split_smem(uint32_t head_dim);
+size_t attn_split_smem(uint32_t head_dim, uint32_t nbufs = 0);
 uint32_t attn_max_splits(uint32_t max_ctx);
 cudaError_t attn_split_set_smem_limits(int optin);
 cudaError_t launch_attn_split(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, cudaStream_t st);

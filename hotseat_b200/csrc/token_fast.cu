@@ -411,6 +411,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
     if (ok) {
         const uint32_t n = pos + 1, Ls = attn_split_len(n, a.attn.max_splits), S = (n + Ls - 1) / Ls;
         const uint32_t G_ = a.nh / nkv, rec = attn_record(G_, a.hd);
+        // attention item i: split i / (nkv * hsp), KV head (i / hsp) % nkv,
+        // query-head part i % hsp
+        const uint32_t hsp = attn_head_split(a.attn), n_items = S * nkv * hsp;
         const bool reader_combines = S > 1 && S <= kReaderCombine &&
                                      ((size_t)nkv * S * rec + a.nh * (S + 1)) * 4 <= attn::item_smem(HD, attn_buf(HD));
         const uint32_t qrows = (a.nh + 2 * nkv) * a.hd;
@@ -429,7 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
                 norm_x(l == 0);
                 // this CTA's first attention item: start loading its cached
                 // K/V rows and RoPE row (written by earlier tokens / constant)
-                if (b < S * nkv) attn::prefetch<HD, attn_buf(HD)>(a.attn, l, b / nkv, b % nkv, 0, pos, att_sm);
+                if (b < n_items)
+                    attn::prefetch<HD, attn_buf(HD)>(a.attn, l, b / (nkv * hsp), (b / hsp) % nkv, 0, pos, att_sm);
                 uint32_t r0, r1;
                 split_range(qrows, G, b, &r0, &r1);
                 pre = tid < r1 - r0 ? lay[l].bqkv[r0 + tid] : 0.0f;
@@ -521,10 +525,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
             if (ph == PH_HEAD) break;
             grid_sync();
             if (ph == PH_QKV) {
-                // attention: item i = s * nkv + kvh for the S splits of this position
+                // attention: the items of the S splits of this position
                 mark(0, tmark ? gtime() : 0);
-                for (uint32_t i = b; i < S * nkv; i += G) {
-                    attn::item<HD, attn_buf(HD)>(a.attn, l, i / nkv, i % nkv, 0, pos, att_sm, i == b, reader_combines,
+                for (uint32_t i = b; i < n_items; i += G) {
+                    attn::item<HD, attn_buf(HD), false>(a.attn, l, i / (nkv * hsp), (i / hsp) % nkv, i % hsp, 0, pos, att_sm,
+                                                 i == b ? 1u : 0u, reader_combines,
                                                  tmark && i == b ? a.phase_ts + 20 * epoch + 12 : nullptr);
                     attn::sync256();
                 }

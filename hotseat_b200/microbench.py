@@ -319,9 +319,15 @@ def bench_token():
                 "arrival_spread_us": float(((latest[sl, i] - earliest[sl, i]) / 1e3).mean()),
                 "last_arrival_to_release_us": float(((body[sl, i, 3] - latest[sl, i]) / 1e3).mean()),
             }
+        # one CTA's first attention item: SM clock at each checkpoint
+        # (the last writer's), cumulative from the item's start
+        probe = body[sl, 1, 12:20].astype(np.int64)
+        item = {name: float(((probe[:, i] - probe[:, 0]) / ghz / 1e3).mean())
+                for i, name in enumerate(["start", "qkv_gathered", "rope_done", "chunk0_ready", "scores_done",
+                                          "softmax_done", "loop_done"]) if i > 0}
         h = flat[5 * L].astype(np.int64)
         print(json.dumps({"bench": "token_kernel", "prompt": 36, "max_tokens": ntok, "kernel_us": float((k[2] - k[0]) / 1e3),
-                          "per_layer": phases, "lm_head_us": float((h[1] - h[0]) / 1e3),
+                          "per_layer": phases, "attention_item_us": item, "lm_head_us": float((h[1] - h[0]) / 1e3),
                           "lm_head_tiles": int(h[5]),
                           "sampler_us": [float((int(t[i][2]) - int(t[i][0])) / 1e3) for i in (1, 2)]}), flush=True)
     s.close()

@@ -196,3 +196,24 @@ def test_tc_migration_between_batches_reproduces_the_transcript(tiny_gguf):
     kv_ref = m.kv()
     hs.Batch(m, 1).run_seqs([kv_ref], [seq(prompts[0], 40, cfg, 8)])
     assert dst.hash(fin[1][1].filled) == kv_ref.hash(fin[1][1].filled)
+
+
+@pytest.mark.parametrize("env", [{"HS_ATTN_HEAD_SPLIT": "2"}, {"HS_ATTN_HEAD_SPLIT": "3", "HS_ATTN_NBUF": "2"},
+                                 {"HS_ATTN_NBUF": "3"}])
+def test_tc_attention_work_split_keeps_the_bits(env, q05_gguf, monkeypatch):
+    """Splitting a (split, KV head) item's query heads over several CTAs, or
+    changing how many K/V chunks load ahead, leaves every head's arithmetic
+    as it was: transcripts, RNG and KV hashes equal the default launch's."""
+    def run():
+        m = load(q05_gguf, 256)
+        g = np.random.default_rng(12)
+        seqs = [seq([int(t) for t in g.integers(0, hs.QWEN05["vocab"], size=70 + 9 * i)], 24,
+                    hs.SamplerCfg.default(temperature=0.8, seed=5 + i), 5 + i) for i in range(3)]
+        kvs = [m.kv() for _ in seqs]
+        out = hs.Batch(m, len(seqs)).run_seqs(kvs, seqs)
+        return [(list(t), list(r.s), kv.hash(st.filled)) for (t, st, r), kv in zip(out, kvs)]
+
+    ref = run()
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    assert run() == ref

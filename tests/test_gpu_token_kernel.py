@@ -92,3 +92,22 @@ def test_token_kernel_reports_bad_input(tiny_gguf, monkeypatch):
     # still usable afterwards
     m.forward(kv, 1, 0, s)
     assert np.all(np.isfinite(s.logits()))
+
+
+def test_token_kernel_head_split_keeps_the_bits(q05_gguf, monkeypatch):
+    """Attention items over parts of a group's query heads (more CTAs per
+    split) give the same logits as whole groups."""
+    rng = np.random.default_rng(8)
+    toks = [int(t) for t in rng.integers(0, hs.QWEN05["vocab"], size=150)]
+    out = []
+    for hsplit in ("1", "2"):
+        monkeypatch.setenv("HS_ATTN_HEAD_SPLIT", hsplit)
+        m = load(q05_gguf, 256, True, monkeypatch)
+        kv, s = m.kv(), m.scratch()
+        rows = []
+        for pos, tok in enumerate(toks):
+            m.forward(kv, tok, pos, s)
+            if pos % 10 == 9:
+                rows.append(s.logits())
+        out.append((np.stack(rows), kv.floats()))
+    assert np.array_equal(out[0][0], out[1][0]) and np.array_equal(out[0][1], out[1][1])
