@@ -44,6 +44,74 @@ __device__ __forceinline__ void cp_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Tagged entries: a value and the tag of the write that produced it in one
+// 8-byte word (value bits low, tag high), stored and loaded as single-copy
+// atomic 8-byte accesses, so a reader that sees the tag it waits for sees
+// that write's value: the data is its own completion flag (no barrier, no
+// separate flag, no fence).
+constexpr uint32_t kPollLimit = 1u << 22;  // polling rounds before a reader gives up
+__device__ __forceinline__ void st_tagged(uint64_t* p, float v, uint32_t tag) {
+    const uint64_t e = ((uint64_t)tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(e) : "memory");
+}
+__device__ __forceinline__ void ld_tagged2(const uint64_t* p, uint64_t& e0, uint64_t& e1) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(e0), "=l"(e1) : "l"(p) : "memory");
+}
+__device__ __forceinline__ float tagged_value(uint64_t e) { return __uint_as_float((uint32_t)e); }
+
+// The 256 consumer threads copy n_pairs pairs of tagged entries into shared
+// memory once both entries of a pair carry `want`: map(i, &src, &dst) gives
+// pair i's source (16-byte aligned) and destination. Each thread takes pairs
+// tid, tid + 256, ..., B at a time, every round's loads in flight together.
+// Returns false (values left unset) after kPollLimit rounds.
+template <uint32_t B, typename Map>
+__device__ bool poll_copy(uint32_t n_pairs, uint32_t want, Map map) {
+    bool ok = true;
+    for (uint32_t base = threadIdx.x; base < n_pairs; base += B * kThreads) {
+        uint32_t pend = 0;
+#pragma unroll
+        for (uint32_t j = 0; j < B; j++)
+            if (base + j * kThreads < n_pairs) pend |= 1u << j;
+        uint32_t rounds = 0;
+        while (pend) {
+            uint64_t e[B][2];
+#pragma unroll
+            for (uint32_t j = 0; j < B; j++)
+                if (pend >> j & 1) {
+                    const uint64_t* src;
+                    float* dst;
+                    map(base + j * kThreads, &src, &dst);
+                    ld_tagged2(src, e[j][0], e[j][1]);
+                }
+#pragma unroll
+            for (uint32_t j = 0; j < B; j++)
+                if ((pend >> j & 1) && (uint32_t)(e[j][0] >> 32) == want && (uint32_t)(e[j][1] >> 32) == want) {
+                    const uint64_t* src;
+                    float* dst;
+                    map(base + j * kThreads, &src, &dst);
+                    dst[0] = tagged_value(e[j][0]);
+                    dst[1] = tagged_value(e[j][1]);
+                    pend &= ~(1u << j);
+                }
+            if (pend && ++rounds > kPollLimit) {
+                ok = false;
+                break;
+            }
+        }
+    }
+    return ok;
+}
+
+// Tagged inputs and outputs of an item inside the persistent token kernel:
+// q/k/v rows awaited with tag `want`, outputs (or, with reader_combines,
+// the split records) written with tag `tag`.
+struct TagIO {
+    const uint64_t* qkv;  // [qkv rows]
+    uint64_t* out;        // [n_heads * head_dim]
+    uint64_t* rec;        // [n_kv][max_splits][attn_record]
+    uint32_t want, tag;
+};
+
 __device__ __forceinline__ void split_f16(float x, uint16_t* hi, uint16_t* lo) {
     const __half h = __float2half_rn(x);
     *hi = __half_as_ushort(h);
@@ -171,7 +239,7 @@ __device__ __forceinline__ void cp_wait_pending(uint32_t n) {
 template <int HD, int NBUF, bool TC>
 __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t hpart, uint32_t slot,
                      uint32_t pos, float* sm, uint32_t npre = 0, bool reader_combines = false,
-                     uint64_t* probe = nullptr) {
+                     uint64_t* probe = nullptr, const TagIO* tio = nullptr) {
     // probe (timing): thread 0 stores clock64() at the item's checkpoints
     auto at = [&](int k) {
         if (probe && threadIdx.x == 0) probe[k] = clock64();
@@ -209,9 +277,19 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     const bool appender = s == 0 && hpart == 0 && append;
     const bool track = appender && tid < 2 && ldv(a.tracking[slot]) != 0;
 
-    // q, k, v of this group; split-K partials in split order, then the bias.
+    // q, k, v of this group; split-K partials in split order, then the bias
+    // (or, tagged, the finished rows once they carry the awaited tag).
     const uint32_t qrow0 = (kvh * Gf + hlo) * HD, krow0 = a.nh * HD + kvh * HD, vrow0 = (a.nh + a.nkv) * HD + kvh * HD;
-    for (uint32_t c = tid; c < (G + 2) * HD / 4; c += kThreads) {
+    if (tio) {
+        const bool got = poll_copy<2>((G + 2) * HD / 2, tio->want, [&](uint32_t i, const uint64_t** src, float** dst) {
+            const uint32_t idx = 2 * i;
+            *src = tio->qkv + (idx < G * HD ? qrow0 + idx
+                                            : (idx < (G + 1) * HD ? krow0 + idx - G * HD : vrow0 + idx - (G + 1) * HD));
+            *dst = idx < G * HD ? qs + idx : (idx < (G + 1) * HD ? kn + idx - G * HD : vn + idx - (G + 1) * HD);
+        });
+        if (!got) atomicOr(&a.ctl[slot].err, ERR_TIMEOUT);
+    }
+    for (uint32_t c = tid; !tio && c < (G + 2) * HD / 4; c += kThreads) {
         const uint32_t idx = 4 * c;
         const uint32_t row = idx < G * HD ? qrow0 + idx : (idx < (G + 1) * HD ? krow0 + idx - G * HD : vrow0 + idx - (G + 1) * HD);
         const float* src = a.qkv + (size_t)slot * a.qkv_rows + row;
@@ -524,7 +602,9 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     mark_dirty();
 
     auto store = [&](size_t at, float v) {
-        if (a.out_f32) {
+        if (tio) {
+            st_tagged(tio->out + at, v, tio->tag);
+        } else if (a.out_f32) {
             a.out_f32[at] = v;
         } else {
             uint16_t hi, lo;
@@ -544,7 +624,22 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     // Several splits: publish (unnormalised output, max, sum); the last item
     // to arrive combines all splits in split order.
     const uint32_t rec = attn_record(Gf, HD);
-    float* part = a.partials + ((size_t)(slot * a.nkv + kvh) * a.max_splits) * rec;
+    const size_t rec0 = (size_t)(slot * a.nkv + kvh) * a.max_splits * rec + (size_t)s * rec;
+    if (tio && reader_combines) {
+        // tagged records: the readers poll them
+#pragma unroll
+        for (uint32_t j = 0; j < HPT; j++) {
+            const uint32_t h = hs0 + j * HSETS;
+            if (h < G) st_tagged(tio->rec + rec0 + (hlo + h) * HD + dd, o[j], tio->tag);
+        }
+        if (tid < G) {
+            st_tagged(tio->rec + rec0 + Gf * HD + hlo + tid, hs_m[tid], tio->tag);
+            st_tagged(tio->rec + rec0 + Gf * HD + Gf + hlo + tid, hs_l[tid], tio->tag);
+        }
+        at(7);
+        return;
+    }
+    float* part = a.partials + rec0 - (size_t)s * rec;
 #pragma unroll
     for (uint32_t j = 0; j < HPT; j++) {
         const uint32_t h = hs0 + j * HSETS;

@@ -925,14 +925,18 @@ __global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs
             }
         }
         __syncthreads();
-        if (tid == 0) {
+        // sampler.rs:135-141: each weight exp((l - max) / T) on its own
+        // thread, then the sums in order on one
+        {
             const float inv_t = __fdiv_rn(1.0f, c->temperature);
             const float mx = key_value(merged[0]);
-            float sum = 0.0f;
-            for (uint32_t i = 0; i < k; i++) {
+            for (uint32_t i = tid; i < k; i += blockDim.x)
                 pk[i] = ref_exp(__fmul_rn(__fsub_rn(key_value(merged[i]), mx), inv_t));
-                sum = __fadd_rn(sum, pk[i]);
-            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float sum = 0.0f;
+            for (uint32_t i = 0; i < k; i++) sum = __fadd_rn(sum, pk[i]);
             uint32_t cut = k;
             if (c->top_p < 1.0f) {
                 const float target = __fmul_rn(c->top_p, sum);

@@ -275,7 +275,9 @@ struct hs_scratch {
     float* att_part = nullptr;      // split-KV attention partials and counters
     uint32_t* att_cnt = nullptr;
     void** kv_tab = nullptr;        // one-entry KV / dirty / tracking tables for split attention
-    uint32_t* tok_bar = nullptr;    // grid barrier counter of the persistent token kernel
+    // persistent token kernel: its launch counter (16 bytes), then its
+    // tagged activations x, qkv, att, hb and attention records
+    uint8_t* tok_mem = nullptr;
     uint64_t* trace = nullptr;      // device, 4 u64 per launch slot (trace mode only)
     uint64_t* trace_init = nullptr; // pinned host template: start=~0, rest 0
     uint32_t trace_slots = 0;
@@ -290,7 +292,7 @@ struct hs_scratch {
         cudaFreeHost(trace_init);
         for (void* p : {(void*)x, (void*)qkv, (void*)att, (void*)hb, (void*)logits, (void*)tokens, (void*)cand,
                         (void*)argbuf, (void*)sc_global, (void*)att_part, (void*)att_cnt, (void*)kv_tab,
-                        (void*)tok_bar})
+                        (void*)tok_mem})
             cudaFree(p);
     }
 };
@@ -515,8 +517,24 @@ SplitAttnArgs scratch_attn_args(const hs_scratch* s, const hs_kv* kv) {
     return sa;
 }
 
-// The fast path's whole token as one persistent kernel (after zeroing its
-// grid barrier counter).
+// Tagged entries of the persistent token kernel's buffers, after its
+// 16-byte launch counter: x, qkv, att, hb, attention records.
+struct TokBufs {
+    size_t x, qkv, att, hb, rec, total;  // offsets and total in entries
+};
+TokBufs tok_bufs(const hs_model* m) {
+    const hs_config& c = m->cfg;
+    TokBufs t{};
+    t.x = 0;
+    t.qkv = t.x + c.d_model;
+    t.att = t.qkv + (size_t)(c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+    t.hb = t.att + (size_t)c.n_heads * c.head_dim;
+    t.rec = t.hb + c.d_ff;
+    t.total = t.rec + (size_t)c.n_kv_heads * m->max_splits * attn_record(c.n_heads / c.n_kv_heads, c.head_dim);
+    return t;
+}
+
+// The fast path's whole token as one persistent kernel.
 int enqueue_token_kernel(hs_scratch* s, const hs_kv* kv) {
     const hs_model* m = s->m;
     const hs_config& c = m->cfg;
@@ -533,23 +551,25 @@ int enqueue_token_kernel(hs_scratch* s, const hs_kv* kv) {
     a.embd = m->embd;
     a.out_norm = m->out_norm;
     a.head_w = m->head_w;
-    a.x = s->x;
-    a.qkv = s->qkv;
-    a.att = s->att;
-    a.hb = s->hb;
+    const TokBufs tb = tok_bufs(m);
+    uint64_t* ent = reinterpret_cast<uint64_t*>(s->tok_mem + 16);
+    a.tx = ent + tb.x;
+    a.tqkv = ent + tb.qkv;
+    a.tatt = ent + tb.att;
+    a.thb = ent + tb.hb;
+    a.trec = ent + tb.rec;
     a.logits = s->logits;
     a.attn = scratch_attn_args(s, kv);
     a.attn.trace = nullptr;
     a.ctl = s->ctl;
-    a.bar = s->tok_bar;
+    a.seq = reinterpret_cast<uint32_t*>(s->tok_mem);
     a.slot_bytes = m->tokp.slot_bytes;
     a.nslot = m->tokp.nslot;
     a.trace = s->trace;
     a.trace_slot = 0;
     // trace slots 0-2: this kernel and the two sampler kernels; then the
-    // timeline, 20 words per barrier interval (5 per layer, then the head)
+    // timeline, 20 words per phase interval (5 per layer, then the head)
     a.phase_ts = s->trace ? s->trace + 3 * 8 : nullptr;
-    HS_CUDA_TRY(cudaMemsetAsync(s->tok_bar, 0, sizeof(uint32_t), s->st));
     HS_CUDA_TRY(launch_token_fast(m->tokp, a, s->st));
     return HS_OK;
 }
@@ -1222,8 +1242,9 @@ int hs_scratch_new(const hs_model* m, hs_scratch** out) {
     HS_CUDA_TRY(cudaMalloc(&s->cand, (size_t)s->n_cta * kSampleSlice * 8));
     HS_CUDA_TRY(cudaMalloc(&s->argbuf, (size_t)s->n_cta * 8));
     if (m->tok) {
-        HS_CUDA_TRY(cudaMalloc(&s->tok_bar, sizeof(uint32_t)));
-        HS_CUDA_TRY(cudaMemset(s->tok_bar, 0, sizeof(uint32_t)));
+        const size_t bytes = 16 + tok_bufs(m).total * 8;
+        HS_CUDA_TRY(cudaMalloc(&s->tok_mem, bytes));
+        HS_CUDA_TRY(cudaMemset(s->tok_mem, 0, bytes));  // counter 0, tags 0 (no launch writes tag 0)
     }
     s->launches_fwd = m->tok ? 1 : c.n_layers * 5 + 1;
     const char* tenv = getenv("HS_TRACE");

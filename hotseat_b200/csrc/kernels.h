@@ -212,15 +212,18 @@ struct TokenArgs {
     const uint16_t* embd;    // [vocab][d]
     const float* out_norm;
     const uint16_t* head_w;  // [vocab][d]
-    float *x, *qkv, *att, *hb, *logits;
-    SplitAttnArgs attn;      // attention items (qkv, att, KV tables, partials, counters)
+    // activations as tagged entries (value, tag of the phase that wrote it)
+    uint64_t *tx, *tqkv, *tatt, *thb;  // [d], [qkv rows], [nh*hd], [ff]
+    uint64_t* trec;          // attention split records [nkv][max_splits][attn_record]
+    float* logits;
+    SplitAttnArgs attn;      // attention items (KV tables, partials, counters)
     DevCtl* ctl;
-    uint32_t* bar;           // grid barrier counter, zero at launch
+    uint32_t* seq;           // launch counter (the tags' high part), advanced by every launch
     uint32_t slot_bytes;     // weight ring: slot size (multiple of 1024) and count
     uint32_t nslot;
     uint64_t* trace;
     uint32_t trace_slot;
-    uint64_t* phase_ts;      // trace mode: %globaltimer at CTA 0's exit of every grid barrier
+    uint64_t* phase_ts;      // trace mode: CTA 0's timeline per phase interval
 };
 struct TokenPlan {
     uint32_t grid = 0, slot_bytes = 0, nslot = 0;

@@ -44,6 +44,11 @@ constexpr uint32_t kMaxLayers = 64;      // layer table copied to shared memory
 __host__ __device__ constexpr uint32_t attn_buf(uint32_t) { return 1; }
 
 __device__ __forceinline__ uint32_t ldv(const uint32_t* p) { return *(const volatile uint32_t*)p; }
+// Bytes of the shared area that holds an attention item or, between
+// attention phases, an input vector of up to xmax tagged entries.
+__host__ __device__ constexpr size_t att_area(uint32_t hd, uint32_t xmax) {
+    return attn::item_smem(hd, attn_buf(hd)) > (size_t)xmax * 8 ? attn::item_smem(hd, attn_buf(hd)) : (size_t)xmax * 8;
+}
 // Exact f16 -> f32 of both halves of a word.
 __device__ __forceinline__ uint64_t widen2(uint32_t v) {
     float a, b;
@@ -61,10 +66,15 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+// Block barrier of the 256 consumer threads that also ORs a predicate.
+__device__ __forceinline__ bool any256(bool p) {
+    uint32_t r;
+    asm volatile(
+        "{ .reg .pred pi, po;\n setp.ne.u32 pi, %1, 0;\n bar.red.or.pred po, 1, 256, pi;\n selp.u32 %0, 1, 0, po; }"
+        : "=r"(r)
+        : "r"((uint32_t)p)
+        : "memory");
+    return r != 0;
 }
 
 // Threads per row for rows of length k: the fast GEMV's rule (a power of two
@@ -77,6 +87,8 @@ __host__ __device__ inline uint32_t row_threads(uint32_t k) {
 }
 
 enum Phase : uint32_t { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DOWN = 3, PH_HEAD = 4 };
+// Writers of tagged entries, in a layer's order (tag(l, TG_*)).
+enum TagPhase : uint32_t { TG_QKV = 0, TG_ATT = 1, TG_O = 2, TG_GU = 3, TG_DOWN = 4 };
 
 // The weights of one phase: `rows` rows of length k, one matrix or the
 // gate/up pair (a slot holds the same rows of both, w0's first).
@@ -259,9 +271,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
     float* red = part + kPart;                                // [64]
     float* xs = red + 64;                                     // [max(d, ff, nh*hd)] input vector
     const uint32_t xn = d > ff ? d : ff;
-    float* att_sm = xs + (xn > a.nh * a.hd ? xn : a.nh * a.hd);  // one attention item
+    const uint32_t xmax = xn > a.nh * a.hd ? xn : a.nh * a.hd;
+    float* att_sm = xs + xmax;  // one attention item, or the staged tagged input
     // the layers' weight pointers (read at every phase start)
-    TokLayer* lay = reinterpret_cast<TokLayer*>(att_sm + attn::item_smem(HD, attn_buf(HD)) / 4);
+    TokLayer* lay = reinterpret_cast<TokLayer*>(att_sm + att_area(HD, xmax) / 4);
     const KTrace tr(a.trace, a.trace_slot);
     tr.enter();
     if (tid == 0) {
@@ -314,24 +327,39 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
     }
 
     // -------------------------------------------------------------- consumers
-    uint32_t epoch = 0;
-    bool gdead = false;
+    // Phases hand their outputs on as tagged entries (attn_body.cuh): the
+    // writes of phase ph of layer l carry tag(l, ph), unique within this
+    // launch and different from the previous launch's (the launch counter),
+    // and every reader polls the entries it needs until they carry the tag
+    // it waits for. Each phase needs all of the previous phase's outputs
+    // (attention only its group's q/k/v rows), so no CTA can overwrite an
+    // entry that another still has to read: the buffers are single.
+    const uint32_t seq = ldv(a.seq);
+    auto tag = [&](uint32_t l, uint32_t t) { return seq * 1024u + l * 5u + t + 1u; };  // t: TG_*
+    bool dead = false;  // a wait ran out (the same in every consumer thread after any256)
+    auto timed_out = [&](bool got) {
+        if (!got && !dead) {
+            dead = true;
+            atomicOr(&ctl->err, ERR_TIMEOUT);
+        }
+    };
+    uint32_t epoch = 0;  // phase interval (trace)
     RowState rs{0, false, 0, 0, 0};
 
-    // Trace mode: per barrier interval (and the LM head after the last), CTA
-    // 0's [input ready, rows done, barrier arrive, barrier exit (%globaltimer
-    // ns), SM cycles waiting for weight tiles, tiles, SM cycles computing
-    // rows, SM cycles in the epilogue], then over all CTAs [~earliest
-    // arrival, latest arrival], 2 words spare, then (attention intervals)
-    // the clock64 checkpoints of CTA 0's first attention item.
+    // Trace mode: per phase interval (5 a layer: QKV, attention, O,
+    // gate/up, down; then the LM head), CTA 0's [input ready, rows done,
+    // outputs written, next phase's input ready (%globaltimer ns), SM cycles
+    // waiting for weight tiles, tiles, SM cycles computing rows, SM cycles
+    // in the epilogue], then over all CTAs [~earliest, latest] outputs
+    // written, 2 words spare, then (attention intervals) the clock64
+    // checkpoints of CTA 0's first attention item.
     const bool tmark = a.phase_ts && b == 0 && tid == 0;
     uint64_t epi_cy = 0;
     auto mark = [&](uint32_t k, uint64_t v) {
         if (tmark) a.phase_ts[20 * epoch + k] = v;
     };
-    // Grid barrier: thread 0 of every CTA arrives once per barrier and waits
-    // (bounded) until all CTAs have; the named barrier releases the others.
-    auto grid_sync = [&]() {
+    // End of a phase interval: trace words, then the next interval.
+    auto phase_end = [&]() {
         attn::sync256();
         if (tid == 0) {
             mark(4, rs.wait_cy);
@@ -339,29 +367,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
             mark(6, rs.comp_cy);
             mark(7, epi_cy);
             mark(2, tmark ? gtime() : 0);
-            if (a.phase_ts) {  // arrival spread over CTAs: latest, and latest of the complements (earliest)
+            if (a.phase_ts) {  // over CTAs: latest, and latest of the complements (earliest)
                 const unsigned long long t = gtime();
                 atomicMax(reinterpret_cast<unsigned long long*>(a.phase_ts + 20 * epoch + 9), t);
                 atomicMax(reinterpret_cast<unsigned long long*>(a.phase_ts + 20 * epoch + 8), ~t);
             }
             rs.wait_cy = rs.tiles = rs.comp_cy = epi_cy = 0;
-            epoch++;
-            // release: this CTA's writes (ordered before this thread by the
-            // block barrier above) become visible with the arrival
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
-            const uint32_t target = epoch * G;
-            uint32_t spins = 0;
-            while (!gdead && ld_acquire(a.bar) < target) {
-                if (++spins > kSpinLimit) {
-                    atomicOr(&ctl->err, ERR_TIMEOUT);
-                    gdead = true;
-                }
-            }
-            if (tmark) a.phase_ts[20 * (epoch - 1) + 3] = gtime();
         }
-        attn::sync256();
+        epoch++;
     };
-    // A phase's RMSNorm gains, loaded before the barrier that precedes it.
+    // A phase's RMSNorm gains, loaded before its input is awaited.
     float gv[kMaxNorm];
     auto load_gain = [&](const float* g) {
 #pragma unroll
@@ -370,20 +385,56 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
             gv[k] = i < d ? g[i] : 0.0f;
         }
     };
-    // RMSNorm of x (of the embedding row at layer 0) with the loaded gains
-    // into xs; the sum of squares by one warp in the fast GEMV's order.
-    auto norm_x = [&](bool embed) {
-        if (embed) {
-            for (uint32_t i = tid; i < d; i += kConsumers) {
-                const float v = h2f(a.embd[(size_t)token * d + i]);
-                xs[i] = v;
-                if (b == 0) a.x[i] = v;
+    // Tagged entries staged in the attention item's shared memory (free
+    // outside attention) once every entry carries `want`: n_runs runs of
+    // `len` entries (even), run r = g * group + j (j < group) from src +
+    // g * group_stride + j * run_stride to stage + r * len; 16-byte
+    // asynchronous copies, re-issued for the pairs not yet tagged, all of a
+    // round in flight together. False after kPollLimit rounds (the staged
+    // values are then whatever arrived).
+    auto stage_tagged = [&](uint64_t* stage, const uint64_t* src, uint32_t n_runs, uint32_t len, uint32_t group,
+                            size_t group_stride, size_t run_stride, uint32_t want) -> bool {
+        const uint32_t per = len / 2, np = n_runs * per;
+        auto from = [&](uint32_t i) {
+            const uint32_t r = i / per;
+            return src + (size_t)(r / group) * group_stride + (size_t)(r % group) * run_stride + 2 * (i % per);
+        };
+        for (uint32_t i = tid; i < np; i += kConsumers) cp_async16(stage + 2 * i, from(i));
+        attn::cp_commit();
+        for (uint32_t round = 0;; round++) {
+            attn::cp_wait0();
+            bool pending = false;
+            for (uint32_t i = tid; i < np; i += kConsumers)
+                if ((uint32_t)(stage[2 * i] >> 32) != want || (uint32_t)(stage[2 * i + 1] >> 32) != want) {
+                    cp_async16(stage + 2 * i, from(i));
+                    pending = true;
+                }
+            attn::cp_commit();
+            if (!pending) return true;
+            if (round >= attn::kPollLimit) {
+                attn::cp_wait0();
+                return false;
             }
-        } else {
-            for (uint32_t i = tid; i < d / 4; i += kConsumers)
-                reinterpret_cast<float4*>(xs)[i] = __ldcg(reinterpret_cast<const float4*>(a.x) + i);
         }
+    };
+    // n tagged entries into xs once they carry `want`.
+    auto await_x = [&](const uint64_t* src, uint32_t n, uint32_t want) {
+        uint64_t* stage = reinterpret_cast<uint64_t*>(att_sm);
+        if (!dead) timed_out(stage_tagged(stage, src, 1, n, 1, 0, 0, want));
+        dead = any256(dead);
+        for (uint32_t i = tid; i < n; i += kConsumers) xs[i] = attn::tagged_value(stage[i]);
         attn::sync256();
+    };
+    // RMSNorm into xs of the embedding row (layer 0) or of x once it
+    // carries `want`, with the loaded gains; the sum of squares by one warp
+    // in the fast GEMV's order.
+    auto norm_x = [&](bool embed, uint32_t want) {
+        if (embed) {
+            for (uint32_t i = tid; i < d; i += kConsumers) xs[i] = h2f(a.embd[(size_t)token * d + i]);
+            attn::sync256();
+        } else {
+            await_x(a.tx, d, want);
+        }
         if (tid < 32) {
             float ss = 0.0f;
             for (uint32_t i = tid; i < d; i += 32) ss = __fmaf_rn(xs[i], xs[i], ss);
@@ -400,25 +451,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
         }
         attn::sync256();
     };
-    // x = n floats (a multiple of 4) from global memory, as asynchronous
-    // 16-byte copies through L2: all in flight at once.
-    auto copy_x = [&](const float* src, uint32_t n) {
-        for (uint32_t i = tid; i < n / 4; i += kConsumers) cp_async16(xs + 4 * i, src + 4 * i);
-        attn::cp_commit();
-        attn::cp_wait0();
-        attn::sync256();
-    };
     if (ok) {
         const uint32_t n = pos + 1, Ls = attn_split_len(n, a.attn.max_splits), S = (n + Ls - 1) / Ls;
         const uint32_t G_ = a.nh / nkv, rec = attn_record(G_, a.hd);
         // attention item i: split i / (nkv * hsp), KV head (i / hsp) % nkv,
         // query-head part i % hsp
         const uint32_t hsp = attn_head_split(a.attn), n_items = S * nkv * hsp;
+        // records of the splits, staged as tagged entries, and the per-head
+        // weights must fit in the attention item's space
+        const uint32_t used = G_ * a.hd + 2 * G_;  // written entries of a record
         const bool reader_combines = S > 1 && S <= kReaderCombine &&
-                                     ((size_t)nkv * S * rec + a.nh * (S + 1)) * 4 <= attn::item_smem(HD, attn_buf(HD));
+                                     (size_t)nkv * S * used * 8 + a.nh * (S + 1) * 4 <= attn::item_smem(HD, attn_buf(HD));
         const uint32_t qrows = (a.nh + 2 * nkv) * a.hd;
         uint32_t dr0, dr1;  // this CTA's rows of d (O and down)
         split_range(d, G, b, &dr0, &dr1);
+        // The residual of row `row` before the O phase of layer l: the
+        // embedding at layer 0, else x as this CTA wrote it in the last down
+        // phase (and before down: as it wrote it in O).
+        auto resid = [&](uint32_t l, uint32_t ph, uint32_t row) -> float {
+            return l == 0 && ph == PH_O ? h2f(a.embd[(size_t)token * d + row]) : attn::tagged_value(a.tx[row]);
+        };
         load_gain(lay[0].attn_norm);
         // The epilogue operand of this thread's first row, read before the
         // phase's tiles: the QKV bias, or the residual row (O, down).
@@ -429,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
             const uint32_t l = step / 4, ph = l < a.n_layers ? step % 4 : (uint32_t)PH_HEAD;
             // ---- input vector
             if (ph == PH_QKV) {
-                norm_x(l == 0);
+                norm_x(l == 0, l > 0 ? tag(l - 1, TG_DOWN) : 0u);
                 // this CTA's first attention item: start loading its cached
                 // K/V rows and RoPE row (written by earlier tokens / constant)
                 if (b < n_items)
@@ -439,55 +491,57 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
                 pre = tid < r1 - r0 ? lay[l].bqkv[r0 + tid] : 0.0f;
             } else if (ph == PH_O) {
                 if (reader_combines) {
-                    // the attention output from the splits' partials, as the
-                    // last split's CTA would combine them: stage them in shared
-                    // memory (the attention item's space), combine in split order
-                    float* ps = att_sm;
-                    const uint32_t per_kvh = S * rec, gh = G_ * a.hd;
-                    for (uint32_t kvh = 0; kvh < nkv; kvh++) {  // 16-byte records: async copies
-                        const float* src = a.attn.partials + (size_t)kvh * a.attn.max_splits * rec;
-                        for (uint32_t i = tid; i < per_kvh / 4; i += kConsumers)
-                            cp_async16(ps + kvh * per_kvh + 4 * i, src + 4 * i);
-                    }
-                    attn::cp_commit();
-                    attn::cp_wait0();
+                    // the attention output from the splits' tagged records,
+                    // as the last split's CTA would combine them: stage them
+                    // in shared memory (the attention item's space), combine
+                    // in split order
+                    // records [kvh][split] of `used` tagged entries (the
+                    // written part of each record, a multiple of 2)
+                    uint64_t* ps = reinterpret_cast<uint64_t*>(att_sm);
+                    const uint32_t gh = G_ * a.hd;
+                    // (record (kvh, q) sits at (kvh * max_splits + q) * rec: runs of
+                    // S records per KV head, so one run per record)
+                    if (!dead)
+                        timed_out(stage_tagged(ps, a.trec, nkv * S, used, S, (size_t)a.attn.max_splits * rec, rec,
+                                               tag(l, TG_ATT)));
                     mark(10, tmark ? gtime() : 0);
                     // per query head: the split weights exp(m_q - M) and the
                     // rescaled sum, then every output element's weighted sum
                     // (the same operations as attn::combine, shared per head)
-                    float* hw = ps + nkv * per_kvh;  // [nh][S + 1]: weights, sum
-                    attn::sync256();
+                    float* hw = reinterpret_cast<float*>(ps + (size_t)nkv * S * used);  // [nh][S + 1]: weights, sum
+                    dead = any256(dead);
+                    auto val = [&](uint32_t kvh, uint32_t q, uint32_t e) {
+                        return attn::tagged_value(ps[(size_t)(kvh * S + q) * used + e]);
+                    };
                     if (tid < a.nh) {
                         const uint32_t kvh = tid / G_, h = tid % G_;
-                        const float* pk = ps + kvh * per_kvh;
                         float M = -FLT_MAX;
-                        for (uint32_t q = 0; q < S; q++) M = fmaxf(M, pk[q * rec + gh + h]);
+                        for (uint32_t q = 0; q < S; q++) M = fmaxf(M, val(kvh, q, gh + h));
                         float den = 0.0f;
                         for (uint32_t q = 0; q < S; q++) {
-                            const float w = __expf(__fsub_rn(pk[q * rec + gh + h], M));
+                            const float w = __expf(__fsub_rn(val(kvh, q, gh + h), M));
                             hw[tid * (S + 1) + q] = w;
-                            den = __fadd_rn(den, __fmul_rn(w, pk[q * rec + gh + G_ + h]));
+                            den = __fadd_rn(den, __fmul_rn(w, val(kvh, q, gh + G_ + h)));
                         }
                         hw[tid * (S + 1) + S] = den;
                     }
                     attn::sync256();
                     mark(11, tmark ? gtime() : 0);
                     for (uint32_t idx = tid; idx < a.nh * a.hd; idx += kConsumers) {
-                        const uint32_t head = idx / a.hd, kvh = head / G_;
-                        const float* pk = ps + kvh * per_kvh + idx - kvh * gh;
+                        const uint32_t head = idx / a.hd, kvh = head / G_, e = idx - kvh * gh;
                         const float* w = hw + head * (S + 1);
                         float num = 0.0f;
-                        for (uint32_t q = 0; q < S; q++) num = __fadd_rn(num, __fmul_rn(w[q], pk[q * rec]));
+                        for (uint32_t q = 0; q < S; q++) num = __fadd_rn(num, __fmul_rn(w[q], val(kvh, q, e)));
                         xs[idx] = __fdiv_rn(num, w[S]);
                     }
                     attn::sync256();
                 } else {
-                    copy_x(a.att, a.nh * a.hd);
+                    await_x(a.tatt, a.nh * a.hd, tag(l, TG_ATT));
                 }
             } else if (ph == PH_DOWN) {
-                copy_x(a.hb, ff);
+                await_x(a.thb, ff, tag(l, TG_GU));
             } else {  // gate/up, head
-                norm_x(false);
+                norm_x(false, ph == PH_GU ? tag(l, TG_O) : tag(a.n_layers - 1, TG_DOWN));
             }
             mark(0, tmark ? gtime() : 0);
             // ---- rows, then the epilogue for this CTA's rows
@@ -510,46 +564,58 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
                     for (uint32_t w = 0; w < WG; w++) u += part[(nrows + i) * WG + w];
                 const uint32_t row = r0 + i;
                 switch (ph) {
-                    case PH_QKV: a.qkv[row] = __fadd_rn(v, i == tid ? pre : bias[row]); break;
-                    case PH_GU: a.hb[row] = __fmul_rn(ref_silu(v), u); break;
+                    case PH_QKV: attn::st_tagged(a.tqkv + row, __fadd_rn(v, i == tid ? pre : bias[row]), tag(l, TG_QKV)); break;
+                    case PH_GU: attn::st_tagged(a.thb + row, __fmul_rn(ref_silu(v), u), tag(l, TG_GU)); break;
                     case PH_HEAD: a.logits[row] = v; break;
-                    default: a.x[row] = __fadd_rn(i == tid ? pre : __ldcg(a.x + row), v); break;  // O, down
+                    default:  // O, down: the residual added
+                        attn::st_tagged(a.tx + row, __fadd_rn(i == tid ? pre : resid(l, ph, row), v),
+                                        tag(l, ph == PH_O ? TG_O : TG_DOWN));
+                        break;
                 }
             }
             if (tmark) epi_cy += clock64() - c2;
-            // ---- operands of the next phase that do not wait for the barrier
+            // ---- operands of the next phase that do not wait for its input
             if (ph == PH_O) load_gain(lay[l].ffn_norm);
-            if (ph == PH_GU) pre = tid < dr1 - dr0 ? __ldcg(a.x + dr0 + tid) : 0.0f;
+            if (ph == PH_GU) pre = tid < dr1 - dr0 ? resid(l, PH_DOWN, dr0 + tid) : 0.0f;
             if (ph == PH_DOWN) load_gain(l + 1 < a.n_layers ? lay[l + 1].attn_norm : a.out_norm);
             mark(1, tmark ? gtime() : 0);
             if (ph == PH_HEAD) break;
-            grid_sync();
+            phase_end();
             if (ph == PH_QKV) {
                 // attention: the items of the S splits of this position
                 mark(0, tmark ? gtime() : 0);
-                for (uint32_t i = b; i < n_items; i += G) {
-                    attn::item<HD, attn_buf(HD), false>(a.attn, l, i / (nkv * hsp), (i / hsp) % nkv, i % hsp, 0, pos, att_sm,
-                                                 i == b ? 1u : 0u, reader_combines,
-                                                 tmark && i == b ? a.phase_ts + 20 * epoch + 12 : nullptr);
+                const attn::TagIO tio{a.tqkv, a.tatt, a.trec, tag(l, TG_QKV), tag(l, TG_ATT)};
+                for (uint32_t i = b; i < n_items && !dead; i += G) {
+                    attn::item<HD, attn_buf(HD), false>(a.attn, l, i / (nkv * hsp), (i / hsp) % nkv, i % hsp, 0, pos,
+                                                        att_sm, i == b ? 1u : 0u, reader_combines,
+                                                        tmark && i == b ? a.phase_ts + 20 * epoch + 12 : nullptr,
+                                                        &tio);
                     attn::sync256();
                 }
-                pre = tid < dr1 - dr0 ? __ldcg(a.x + dr0 + tid) : 0.0f;
+                if (b < n_items && dead) attn::cp_wait0();  // the prefetch of an item not run
+                pre = tid < dr1 - dr0 ? resid(l, PH_O, dr0 + tid) : 0.0f;
                 mark(1, tmark ? gtime() : 0);
-                grid_sync();
+                phase_end();
             }
         }
         mark(4, rs.wait_cy);
         mark(5, rs.tiles);
         mark(6, rs.comp_cy);
         mark(7, epi_cy);
+        // the next launch's tags: after every CTA has read this launch's
+        // counter (each wrote rows this CTA's LM head input needed)
+        if (b == 0 && tid == 0) *a.seq = seq + 1;
+    } else if (b == 0 && tid == 0) {
+        *a.seq = seq + 1;
     }
     __syncthreads();
     tr.exit();
 }
 
 size_t fixed_smem(uint32_t d, uint32_t ff, uint32_t nh, uint32_t hd, uint32_t nslot) {
-    const size_t xs = (size_t)std::max(std::max(d, ff), nh * hd) * 4;
-    return (size_t)2 * nslot * 8 + (kPart + 64) * 4 + xs + attn::item_smem(hd, attn_buf(hd)) + kMaxLayers * sizeof(TokLayer);
+    const uint32_t xmax = std::max(std::max(d, ff), nh * hd);
+    return (size_t)2 * nslot * 8 + (kPart + 64) * 4 + (size_t)xmax * 4 + att_area(hd, xmax) +
+           kMaxLayers * sizeof(TokLayer);
 }
 
 int token_shape(uint32_t hd, uint32_t d, uint32_t ff) {

@@ -303,21 +303,23 @@ def bench_token():
         # timeline words after the 3 launch slots: 20 per barrier interval
         flat = t[3:].reshape(-1)[: 20 * (5 * L + 1)].reshape(5 * L + 1, 20)
         body = flat[: 5 * L].astype(np.int64).reshape(L, 5, 20)
-        prev_exit = np.concatenate([[k[0]], body.reshape(-1, 20)[:-1, 3]]).reshape(L, 5)
+        # per interval: CTA 0's input ready (0), rows done (1), outputs written
+        # (2); over CTAs the earliest (~8) and latest (9) outputs written
+        seq_end = np.concatenate([[k[0]], body.reshape(-1, 20)[:-1, 2]]).reshape(L, 5)
+        latest_prev = np.concatenate([[k[0]], flat[: 5 * L - 1, 9].astype(np.int64)]).reshape(L, 5)
         earliest = (~flat[: 5 * L, 8]).astype(np.int64).reshape(L, 5)
         latest = flat[: 5 * L, 9].astype(np.int64).reshape(L, 5)
         sl = slice(1, L)
         phases = {}
         for i, name in enumerate(["qkv", "attention", "o", "gate_up", "down"]):
             phases[name] = {
-                "input_us": float(((body[sl, i, 0] - prev_exit[sl, i]) / 1e3).mean()),
+                "input_us": float(((body[sl, i, 0] - seq_end[sl, i]) / 1e3).mean()),
+                "detect_us": float(((body[sl, i, 0] - latest_prev[sl, i]) / 1e3).mean()),
                 "rows_us": float(((body[sl, i, 1] - body[sl, i, 0]) / 1e3).mean()),
                 "tiles": float(body[sl, i, 5].mean()),
                 "tile_wait_us": float((body[sl, i, 4] / ghz / 1e3).mean()),
                 "tile_compute_us": float((body[sl, i, 6] / ghz / 1e3).mean()),
-                "barrier_us": float(((body[sl, i, 3] - body[sl, i, 2]) / 1e3).mean()),
-                "arrival_spread_us": float(((latest[sl, i] - earliest[sl, i]) / 1e3).mean()),
-                "last_arrival_to_release_us": float(((body[sl, i, 3] - latest[sl, i]) / 1e3).mean()),
+                "end_spread_us": float(((latest[sl, i] - earliest[sl, i]) / 1e3).mean()),
             }
         # one CTA's first attention item: SM clock at each checkpoint
         # (the last writer's), cumulative from the item's start
@@ -329,7 +331,11 @@ def bench_token():
         print(json.dumps({"bench": "token_kernel", "prompt": 36, "max_tokens": ntok, "kernel_us": float((k[2] - k[0]) / 1e3),
                           "per_layer": phases, "attention_item_us": item, "lm_head_us": float((h[1] - h[0]) / 1e3),
                           "lm_head_tiles": int(h[5]),
-                          "sampler_us": [float((int(t[i][2]) - int(t[i][0])) / 1e3) for i in (1, 2)]}), flush=True)
+                          "sampler_us": [float((int(t[i][2]) - int(t[i][0])) / 1e3) for i in (1, 2)],
+                          # token kernel's end to: candidates' first CTA start, their last exit,
+                          # the final kernel's wait released, its exit
+                          "sampler_path_us": [float((int(x) - int(k[2])) / 1e3)
+                                              for x in (t[1][0], t[1][2], t[2][1], t[2][2])]}), flush=True)
     s.close()
     m.close()
     os.remove(path)
