@@ -1,4 +1,6 @@
-"""The GPU-native numeric path (HS_NUMERIC_FAST) against the CPU restatement.
+"""The GPU-native numeric path (HS_NUMERIC_FAST) against the CPU restatement,
+in both of its forms: the persistent token kernel (tensor-core rows, the
+default where it fits) and the per-kernel launches (HS_TOKEN_KERNEL=0).
 
 Its reductions use fixed GPU shapes instead of the reference's eight serial
 lanes, so the bar is the token loop's: logits within 1e-2 max-abs of the CPU
@@ -16,6 +18,12 @@ pytestmark = pytest.mark.gpu
 
 LOGIT_TOL = 1e-2
 FAST = hs.NUMERIC_FAST
+
+
+@pytest.fixture(autouse=True, params=["token_kernel", "per_kernel"])
+def form(request, monkeypatch):
+    monkeypatch.setenv("HS_TOKEN_KERNEL", "1" if request.param == "token_kernel" else "0")
+    return request.param
 
 
 def load(path, max_ctx):
