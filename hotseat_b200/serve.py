@@ -5,12 +5,13 @@ prompts, 200 decode steps at temperature 0.8; sequence j, homed on GPU
 j // 64, moves to GPU (home + 1) % N once it holds `at_j` positions, at_j
 drawn from the seed in [40, 160]).
 
-    python -m hotseat_b200.serve --gpus N [--seqs 64] [--prompt 64] [--steps 200] [--seed 7]
+    python -m hotseat_b200.serve --gpus N [--seqs 64] [--prompt 64] [--steps 200] [--seed 7] [--round-tokens 8]
 
 One process drives all N GPUs (one model replica, one batch and one worker
 thread per GPU) in lockstep rounds: each round every GPU advances its
-resident sequences by one token (hs_batch_seq_begin / step / end on the
-tensor-core path). The run is made twice from the same seeds: unmigrated
+resident sequences by up to `round_tokens` tokens (hs_batch_seq_begin / step
+/ end on the tensor-core path; the host sees the sequences only between
+rounds). The run is made twice from the same seeds: unmigrated
 (every sequence stays home) and migrated. A migration follows migrate.rs's
 pre-copy: at `at_j` the source KV region is armed and its live bytes copied
 to a region on the destination GPU while the sequence keeps decoding on the
@@ -52,19 +53,19 @@ def _sequences(n_gpus, per_gpu, prompt_len, steps, seed, at_range, vocab):
     return seqs
 
 
-def _round(batch, resident):
-    """One token for every resident sequence of one GPU."""
+def _round(batch, resident, n_tokens):
+    """Up to n_tokens tokens for every resident sequence of one GPU."""
     if not resident:
         return
     batch.begin([q["kv"] for q in resident], resident)
-    batch.step(1)
+    batch.step(n_tokens)
     for q, (toks, st, rng) in zip(resident, batch.end()):
         q["tokens"] = [int(t) for t in toks]
         q["filled"], q["done"], q["done_reason"] = st.filled, st.done, st.done_reason
         q["rng"] = rng
 
 
-def run(models, batches, seqs, migrate, pool):
+def run(models, batches, seqs, migrate, pool, round_tokens):
     n = len(models)
     spec = {g: models[g].kv_spec(hs.TOKEN_MAJOR) for g in range(n)}
     for q in seqs:
@@ -78,7 +79,7 @@ def run(models, batches, seqs, migrate, pool):
         if not live:
             break
         before = {q["j"]: len(q["tokens"]) for q in live}
-        list(pool.map(lambda g: _round(batches[g], [q for q in live if q["gpu"] == g]), range(n)))
+        list(pool.map(lambda g: _round(batches[g], [q for q in live if q["gpu"] == g], round_tokens), range(n)))
         generated += sum(len(q["tokens"]) - before[q["j"]] for q in live)
         if not migrate:
             continue
@@ -124,7 +125,7 @@ def run(models, batches, seqs, migrate, pool):
     return out, generated, seconds, sent
 
 
-def serve(path, n_gpus, per_gpu, prompt, steps, seed, at_range=(40, 160)):
+def serve(path, n_gpus, per_gpu, prompt, steps, seed, at_range=(40, 160), round_tokens=8):
     """Both runs on the GGUF at `path`; returns the result record."""
     max_ctx = prompt + steps + 8
     models = [hs.Model.load(path, max_ctx=max_ctx, device=g, numeric=hs.NUMERIC_TC) for g in range(n_gpus)]
@@ -135,7 +136,7 @@ def serve(path, n_gpus, per_gpu, prompt, steps, seed, at_range=(40, 160)):
         with ThreadPoolExecutor(max_workers=n_gpus) as pool:
             for migrate in (False, True):
                 seqs = _sequences(n_gpus, per_gpu, prompt, steps, seed, at_range, models[0].cfg.vocab)
-                results[migrate] = run(models, batches, seqs, migrate, pool)
+                results[migrate] = run(models, batches, seqs, migrate, pool, round_tokens)
     finally:
         for b in batches:
             b.close()
@@ -145,14 +146,14 @@ def serve(path, n_gpus, per_gpu, prompt, steps, seed, at_range=(40, 160)):
     got, gen1, sec1, sent = results[True]
     return {
         "bench": "serve_migrate", "n_gpus": n_gpus, "sequences": n_gpus * per_gpu, "prompt": prompt,
-        "steps": steps, "numeric": "tc",
+        "steps": steps, "numeric": "tc", "round_tokens": round_tokens,
         "tok_s_migrated": gen1 / sec1, "tok_s_unmigrated": gen0 / sec0, "generated_tokens": gen1,
         "migrations": len(sent.get(0, [])), "precopy_rounds": PRECOPY_ROUNDS,
         "bytes_per_migration_by_round": {str(k): float(np.mean(v)) for k, v in sorted(sent.items())},
         "transcripts_equal": all(got[j][0] == ref[j][0] for j in ref),
         "rng_equal": all(got[j][1:3] == ref[j][1:3] for j in ref),
         "kv_hash_equal": all(got[j][3] == ref[j][3] for j in ref),
-        "timing": "host wall clock over lockstep rounds (begin/step/end per GPU per token)",
+        "timing": "host wall clock over lockstep rounds (begin/step/end per GPU per round)",
     }
 
 
@@ -163,12 +164,13 @@ def main():
     ap.add_argument("--prompt", type=int, default=64)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--seed", type=int, default=7)
+    ap.add_argument("--round-tokens", type=int, default=8, help="tokens per lockstep round")
     args = ap.parse_args()
     td = tempfile.mkdtemp(prefix="hsserve")
     path = os.path.join(td, "q05.gguf")
     hs.write_synthetic_gguf(path, seed=1234, **hs.QWEN05)
     try:
-        rec = serve(path, args.gpus, args.seqs, args.prompt, args.steps, args.seed)
+        rec = serve(path, args.gpus, args.seqs, args.prompt, args.steps, args.seed, round_tokens=args.round_tokens)
     finally:
         os.remove(path)
         os.rmdir(td)

@@ -12,11 +12,12 @@ from conftest import gpu_count
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("n_gpus", [1, 2])
-def test_every_sequence_migrates_and_reproduces_its_transcript(tiny_gguf, n_gpus):
+@pytest.mark.parametrize("n_gpus,round_tokens", [(1, 1), (1, 3), (2, 1), (2, 3)])
+def test_every_sequence_migrates_and_reproduces_its_transcript(tiny_gguf, n_gpus, round_tokens):
     if gpu_count() < n_gpus:
         pytest.skip("needs two GPUs")
-    rec = serve.serve(tiny_gguf, n_gpus, per_gpu=6, prompt=12, steps=30, seed=3, at_range=(14, 30))
+    rec = serve.serve(tiny_gguf, n_gpus, per_gpu=6, prompt=12, steps=30, seed=3, at_range=(14, 30),
+                      round_tokens=round_tokens)
     assert rec["migrations"] == 6 * n_gpus
     assert rec["transcripts_equal"] and rec["rng_equal"] and rec["kv_hash_equal"], rec
     assert rec["bytes_per_migration_by_round"]["0"] > rec["bytes_per_migration_by_round"]["1"] > 0
