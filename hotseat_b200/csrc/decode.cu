@@ -469,9 +469,11 @@ __global__ void __launch_bounds__(256) k_attention(const AttnArgs a) {
 // order), then either finds its first maximum (greedy, sampler.rs:177-187)
 // or orders its slice under cmp_desc and keeps the best kmax keys.
 // Stage 2 (k_sample_final): merges the per-CTA lists into the global top-k
-// and runs the reference's serial tail on one thread: temperature softmax
-// with exp_f32, nucleus cut, one next_f32 draw (sampler.rs:134-166); in
-// sequence mode it then commits the step exactly as seq.rs:273-312 does.
+// (a merge tree of co-rank searches), computes the temperature weights with
+// exp_f32 one per thread, and runs the reference's serial tail on one
+// thread: the sums in order, nucleus cut, one next_f32 draw
+// (sampler.rs:134-166); in sequence mode it then commits the step exactly
+// as seq.rs:273-312 does.
 __device__ __forceinline__ bool seq_needs_sample(const DevCtl* c) {
     if (c->mode == 1) return true;
     return c->active && c->filled + 1 == c->n_tokens;
@@ -899,32 +901,45 @@ __global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs
                 sel_lists[s * k + j] = a.cand[(size_t)sel[s] * a.kmax + j];
             }
             __syncthreads();
-            if (w == 0) {
-                // Warp tournament: lane l owns selected lists l and l + 32.
-                uint32_t ptr0 = 0, ptr1 = 0;
-                uint64_t h0 = lane < n_sel ? sel_lists[lane * k] : ~0ull;
-                uint64_t h1 = lane + 32 < n_sel ? sel_lists[(lane + 32) * k] : ~0ull;
-                for (uint32_t round = 0; round < k; round++) {
-                    const bool first = h0 <= h1;
-                    const uint64_t best = first ? h0 : h1;
-                    const uint32_t hi = (uint32_t)(best >> 32), lo = (uint32_t)best;
-                    const uint32_t mhi = __reduce_min_sync(0xffffffffu, hi);
-                    const uint32_t mlo = __reduce_min_sync(0xffffffffu, hi == mhi ? lo : 0xffffffffu);
-                    const unsigned winners = __ballot_sync(0xffffffffu, hi == mhi && lo == mlo);
-                    if (lane == (uint32_t)(__ffs(winners) - 1)) {
-                        merged[round] = best;
-                        if (first) {
-                            ptr0++;
-                            h0 = ptr0 < k ? sel_lists[lane * k + ptr0] : ~0ull;
-                        } else {
-                            ptr1++;
-                            h1 = ptr1 < k ? sel_lists[(lane + 32) * k + ptr1] : ~0ull;
-                        }
+            tr.mark(1);
+            // Merge tree: pairs of sorted lists merged into the first k of
+            // their union (output p by a co-rank search: i keys of X and
+            // p - i of Y are the p smallest), ping-pong between the two
+            // halves of the list buffer, until one list is left. Keys are
+            // unique, so this is the exact top-k in order.
+            uint64_t* src = sel_lists;
+            uint64_t* dst = sel_lists + 64 * 64;
+            for (uint32_t m = n_sel; m > 1;) {
+                const uint32_t pairs = m / 2, lists = pairs + (m & 1);
+                for (uint32_t idx = tid; idx < lists * k; idx += blockDim.x) {
+                    const uint32_t pr = idx / k, p = idx % k;
+                    const uint64_t* X = src + (size_t)(2 * pr) * k;
+                    if (pr == pairs) {  // the odd list out
+                        dst[(size_t)pr * k + p] = X[p];
+                        continue;
                     }
+                    const uint64_t* Y = X + k;
+                    uint32_t lo = 0, hi = p;
+                    while (lo < hi) {
+                        const uint32_t mid = (lo + hi) >> 1;
+                        if (X[mid] < Y[p - mid - 1])
+                            lo = mid + 1;
+                        else
+                            hi = mid;
+                    }
+                    const uint64_t x = X[lo], y = Y[p - lo];
+                    dst[(size_t)pr * k + p] = x < y ? x : y;
                 }
+                __syncthreads();
+                uint64_t* t = src;
+                src = dst;
+                dst = t;
+                m = lists;
             }
+            for (uint32_t i = tid; i < k; i += blockDim.x) merged[i] = src[i];
         }
         __syncthreads();
+        tr.mark(2);
         // sampler.rs:135-141: each weight exp((l - max) / T) on its own
         // thread, then the sums in order on one
         {
@@ -970,6 +985,7 @@ __global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs
         }
     }
     __syncthreads();
+    tr.mark(3);
     if (tid != 0) return;
     DevCtl* g = a.ctl;
     if (!seq) {
@@ -1117,9 +1133,10 @@ cudaError_t launch_attention(uint32_t head_dim, uint32_t nh, size_t smem, const 
 }
 
 size_t sample_final_smem(uint32_t n_cta, uint32_t kmax) {
-    // Selected lists: at most 64 lists of at most 64 keys (top_k <= 64) when
-    // there are several CTAs; none with one CTA.
-    return n_cta > 1 ? (size_t)64 * 64 * sizeof(uint64_t) : 16;
+    // Selected lists: at most 64 lists of at most 64 keys (top_k <= 64), and
+    // as much again for the merge tree's other half, when there are several
+    // CTAs; none with one CTA.
+    return n_cta > 1 ? (size_t)2 * 64 * 64 * sizeof(uint64_t) : 16;
 }
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st) {

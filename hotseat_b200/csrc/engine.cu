@@ -278,6 +278,7 @@ struct hs_scratch {
     // persistent token kernel: its launch counter (16 bytes), then its
     // tagged activations x, qkv, att, hb and attention records
     uint8_t* tok_mem = nullptr;
+    uint64_t tok_launches = 0;      // token-kernel launches (tag refresh)
     uint64_t* trace = nullptr;      // device, 4 u64 per launch slot (trace mode only)
     uint64_t* trace_init = nullptr; // pinned host template: start=~0, rest 0
     uint32_t trace_slots = 0;
@@ -532,6 +533,19 @@ TokBufs tok_bufs(const hs_model* m) {
     t.rec = t.hb + c.d_ff;
     t.total = t.rec + (size_t)c.n_kv_heads * m->max_splits * attn_record(c.n_heads / c.n_kv_heads, c.head_dim);
     return t;
+}
+
+// Before a launch of the graph holding the token kernel: the kernel's tags
+// are the launch counter x 1024 + (layer, phase), which repeat every 2^22
+// launches; entries not rewritten by every launch (the attention output when
+// the readers combine split records) could then carry a current-looking tag.
+// Clearing the tagged entries every 2^21 launches keeps every entry younger
+// than that.
+int refresh_tags(hs_scratch* s) {
+    if (!s->tok_mem) return HS_OK;
+    if (++s->tok_launches % (1ull << 21) == 0)
+        HS_CUDA_TRY(cudaMemsetAsync(s->tok_mem + 16, 0, tok_bufs(s->m).total * 8, s->st));
+    return HS_OK;
 }
 
 // The fast path's whole token as one persistent kernel.
@@ -1302,6 +1316,7 @@ int hs_forward(const hs_model* m, hs_kv* kv, uint32_t token, uint32_t pos, hs_sc
     h.vocab = m->cfg.vocab;
     h.max_ctx = m->cfg.max_ctx;
     HS_CUDA_TRY(cudaMemcpyAsync(s->ctl, &h, sizeof(DevCtl), cudaMemcpyHostToDevice, s->st));
+    if ((rc = refresh_tags(s))) return rc;
     HS_CUDA_TRY(cudaGraphLaunch(s->g_fwd, s->st));
     if ((rc = sync_ctl(s))) return rc;
     return check_ctl_err(s);
@@ -1456,6 +1471,8 @@ int hs_seq_step(hs_scratch* s, uint32_t n_steps) {
         if (s->trace)
             HS_CUDA_TRY(cudaMemcpyAsync(s->trace, s->trace_init, (size_t)s->trace_slots * 64, cudaMemcpyHostToDevice,
                                         s->st));
+        const int rc = refresh_tags(s);
+        if (rc) return rc;
         HS_CUDA_TRY(cudaGraphLaunch(s->g_step, s->st));
     }
     return HS_OK;

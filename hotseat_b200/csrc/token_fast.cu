@@ -329,9 +329,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
     // -------------------------------------------------------------- consumers
     // Phases hand their outputs on as tagged entries (attn_body.cuh): the
     // writes of phase ph of layer l carry tag(l, ph), unique within this
-    // launch and different from the previous launch's (the launch counter),
-    // and every reader polls the entries it needs until they carry the tag
-    // it waits for. Each phase needs all of the previous phase's outputs
+    // launch and different from earlier launches' (the launch counter; the
+    // host clears the entries every 2^21 launches, before the counter's
+    // part of the tag could repeat), and every reader polls the entries it
+    // needs until they carry the tag it waits for. Each phase needs all of the previous phase's outputs
     // (attention only its group's q/k/v rows), so no CTA can overwrite an
     // entry that another still has to read: the buffers are single.
     const uint32_t seq = ldv(a.seq);

@@ -335,7 +335,11 @@ def bench_token():
                           # token kernel's end to: candidates' first CTA start, their last exit,
                           # the final kernel's wait released, its exit
                           "sampler_path_us": [float((int(x) - int(k[2])) / 1e3)
-                                              for x in (t[1][0], t[1][2], t[2][1], t[2][2])]}), flush=True)
+                                              for x in (t[1][0], t[1][2], t[2][1], t[2][2])],
+                          # the final kernel after its wait: candidate lists loaded, merged,
+                          # token picked, exit (%globaltimer marks, last CTA)
+                          "sampler_final_us": [float((int(t[2][j]) - int(t[2][1])) / 1e3) for j in (4, 5, 6, 2)]}),
+              flush=True)
     s.close()
     m.close()
     os.remove(path)
