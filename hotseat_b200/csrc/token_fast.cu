@@ -352,8 +352,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
     // outputs written, next phase's input ready (%globaltimer ns), SM cycles
     // waiting for weight tiles, tiles, SM cycles computing rows, SM cycles
     // in the epilogue], then over all CTAs [~earliest, latest] outputs
-    // written, 2 words spare, then (attention intervals) the clock64
-    // checkpoints of CTA 0's first attention item.
+    // written, the input staged and transformed (RMSNorm, or the split
+    // combine), then (attention intervals) the clock64 checkpoints of CTA
+    // 0's first attention item.
     const bool tmark = a.phase_ts && b == 0 && tid == 0;
     uint64_t epi_cy = 0;
     auto mark = [&](uint32_t k, uint64_t v) {
@@ -436,6 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
         } else {
             await_x(a.tx, d, want);
         }
+        mark(10, tmark ? gtime() : 0);
         if (tid < 32) {
             float ss = 0.0f;
             for (uint32_t i = tid; i < d; i += 32) ss = __fmaf_rn(xs[i], xs[i], ss);
@@ -451,6 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
             if (i < d) xs[i] = __fmul_rn(__fmul_rn(xs[i], scale), gv[k]);
         }
         attn::sync256();
+        mark(11, tmark ? gtime() : 0);
     };
     if (ok) {
         const uint32_t n = pos + 1, Ls = attn_split_len(n, a.attn.max_splits), S = (n + Ls - 1) / Ls;

@@ -320,6 +320,10 @@ def bench_token():
                 "tile_wait_us": float((body[sl, i, 4] / ghz / 1e3).mean()),
                 "tile_compute_us": float((body[sl, i, 6] / ghz / 1e3).mean()),
                 "end_spread_us": float(((latest[sl, i] - earliest[sl, i]) / 1e3).mean()),
+                # input staged (word 10) and transformed (word 11: RMSNorm, or the
+                # split combine) after the latest previous-phase end (not attention)
+                "staged_us": float(((body[sl, i, 10] - latest_prev[sl, i]) / 1e3).mean()) if i != 1 else 0.0,
+                "transformed_us": float(((body[sl, i, 11] - body[sl, i, 10]) / 1e3).mean()) if i != 1 else 0.0,
             }
         # one CTA's first attention item: SM clock at each checkpoint
         # (the last writer's), cumulative from the item's start
