@@ -179,11 +179,20 @@ def run_reference(args, rank, world):
 
 
 def max_over_ranks(x, world, torch, dist):
+    """The largest x over the ranks (a device tensor under NCCL, a host one
+    under gloo)."""
     if world == 1:
         return x
-    t = torch.tensor([x], device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def weak_value(world, units_per_rank, total_ms):
+    """Whole-job throughput under weak scaling: every rank processed
+    units_per_rank units; total_ms is the slowest rank's time."""
+    return world * units_per_rank / (total_ms / 1000.0)
 
 
 def _copy_rng(hs, r):
@@ -250,7 +259,7 @@ def bench_batch64(hs, torch, dist, path, local, world, args):
     if world > 1:
         dist.barrier()
     ms_per_step = total_ms / args.steps
-    value = world * gen_tokens * args.steps / (total_ms / 1000.0)
+    value = weak_value(world, gen_tokens * args.steps, total_ms)
 
     # end to end through hs_batch_seq_run with host buffers
     e2e_ms = []
@@ -263,7 +272,7 @@ def bench_batch64(hs, torch, dist, path, local, world, args):
         e2e_ms.append(a.elapsed_time(z))
         assert all(list(x[0]) == list(y[0]) for x, y in zip(out, ref))
     e2e_total = max_over_ranks(float(sum(e2e_ms)), world, torch, dist)
-    e2e_value = world * gen_tokens * args.steps / (e2e_total / 1000.0)
+    e2e_value = weak_value(world, gen_tokens * args.steps, e2e_total)
     h2d = sum(len(q["tokens"]) * 4 + CTL_BYTES for q in snap)
     d2h = sum(len(t) * 4 + 2 * CTL_BYTES for t, _, _ in ref)
     launches = b.launches_per_step()
@@ -331,7 +340,7 @@ def bench_batch1(hs, torch, dist, path, local, world, args):
     torch.cuda.synchronize()
     assert list(end()) == list(ref), "decode is not deterministic across steps"
     total_ms = max_over_ranks(float(sum(a.elapsed_time(z) for a, z in evs)), world, torch, dist)
-    value = world * B1_GEN * args.steps / (total_ms / 1000.0)
+    value = weak_value(world, B1_GEN * args.steps, total_ms)
     e2e_ms = []
     for _ in range(args.steps):
         a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -344,7 +353,7 @@ def bench_batch1(hs, torch, dist, path, local, world, args):
         assert list(out) == list(ref)
     e2e_total = max_over_ranks(float(sum(e2e_ms)), world, torch, dist)
     res = dict(value=value, ms_per_step=total_ms / args.steps,
-               e2e_value=world * B1_GEN * args.steps / (e2e_total / 1000.0),
+               e2e_value=weak_value(world, B1_GEN * args.steps, e2e_total),
                gpu_launches=s.launches_per_step() * n_steps * args.steps)
     for o in (s, kv):
         o.close()
