@@ -235,7 +235,8 @@ __device__ __forceinline__ void cp_wait_pending(uint32_t n) {
 // `layer` selects the KV planes (a.layer is not read). TC: the chunk
 // products on the tensor cores, else on the CUDA cores. With
 // `reader_combines`, several splits only publish their partials: the reader
-// of the output combines them (combine()) after a grid-wide barrier.
+// of the output combines them once all are published (the persistent token
+// kernel's O phase, polling the tagged records).
 template <int HD, int NBUF, bool TC>
 __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t hpart, uint32_t slot,
                      uint32_t pos, float* sm, uint32_t npre = 0, bool reader_combines = false,

@@ -1,16 +1,18 @@
 // One decode token of the GPU-native numeric path (HS_NUMERIC_FAST, batch 1)
 // as a single persistent kernel: every layer's five phases (QKV, attention,
-// O, gate/up, down) and the LM head, separated by grid-wide barriers instead
-// of kernel boundaries, with the weight stream running ahead of the compute.
+// O, gate/up, down) and the LM head with no kernel boundary and no grid
+// barrier between them (each phase hands its outputs on as tagged entries
+// that their readers poll), and the weight stream running ahead of the
+// compute.
 //
 //   warp 8 (producer)  streams this CTA's rows of every weight matrix, in
 //                      phase order for the whole token, through a ring of
 //                      shared-memory slots with 1-D bulk copies. It never
 //                      waits for activations, so the weights of the next
 //                      phases arrive while the current phase computes or
-//                      waits at a barrier.
-//   warps 0-7          per phase: build the input vector (RMSNorm of x, the
-//                      attention output or hb), take the weight tiles from
+//                      waits for its input.
+//   warps 0-7          per phase: await and build the input vector (RMSNorm
+//                      of x, the attention output or hb), take the weight tiles from
 //                      the ring, compute their rows and apply the epilogue
 //                      (bias, residual add, SiLU gate); in the attention phase
 //                      they run the split-KV attention items (attn_body.cuh).
