@@ -4,6 +4,7 @@
     python -m hotseat_b200.microbench attention   # GQA decode attention at 1k-32k context
     python -m hotseat_b200.microbench prefill     # 1.5B shape: 16 x 2048-token prefill, 512 greedy steps
     python -m hotseat_b200.microbench token       # batch-1 persistent token kernel: phase timeline
+    python -m hotseat_b200.microbench batch       # batch-64 tensor-core step: per-kernel timeline
 
 dequant: the tensors of the seeded Qwen2.5-0.5B-shape GGUF (ffn_gate 4864x896
 and ffn_down 896x4864 in Q4_K, token_embd 151936x896 in Q6_K) plus the same
@@ -31,8 +32,15 @@ for the GEMMs (the tensor cores execute twice that: f16 hi and lo halves).
 token: the C1 workload (36-token prompt, sampled at temperature 0.8, seed
 99) decoded to 60 and to 120 tokens by the persistent token kernel with the
 trace on; the kernel's timeline of its last step, from CTA 0 (per phase of
-layers 1-23, averaged: input ready, rows done, barrier) and over all CTAs
-(arrival spread, last arrival to release), plus the LM head.
+layers 1-23, averaged: input wait and its parts, rows, tiles) and over all
+CTAs (phase-end spread), plus the LM head and the sampler.
+
+batch: 64 sequences of the 0.5B shape (128-token prompts, 140 tokens at
+temperature 0.8) decoded together on the tensor-core path with the trace
+on; the last step's launch timeline: per kernel role of layers 1-22, the
+time from the previous kernel's last exit to its own last exit, and for the
+four GEMMs their trace marks (latest CTA): dependency wait released, first
+stage landed, MMAs issued, accumulator ready, epilogue done, exit.
 
 Each line printed is one JSON object; peaks are the measured copy bandwidth
 in MEASURED_PEAKS.json when present.
@@ -350,6 +358,51 @@ def bench_token():
     os.rmdir(td)
 
 
+def bench_batch():
+    os.environ["HS_TRACE"] = "1"
+    import hotseat_b200 as hs
+    td = tempfile.mkdtemp(prefix="hsmicro")
+    path = os.path.join(td, "q05.gguf")
+    hs.write_synthetic_gguf(path, seed=1234, **hs.QWEN05)
+    m = hs.Model.load(path, max_ctx=512, numeric=hs.NUMERIC_TC)
+    B = 64
+    b = hs.Batch(m, B)
+    kvs = [m.kv() for _ in range(B)]
+    seqs = []
+    for i in range(B):
+        g = np.random.default_rng(99 + i)
+        p = [int(t) for t in g.integers(0, hs.QWEN05["vocab"], size=128)]
+        seqs.append(dict(tokens=p, prompt_len=128, max_tokens=140, filled=0, rng=hs.Rng.seed(99 + i),
+                         cfg=hs.SamplerCfg.default(temperature=0.8, seed=99 + i)))
+    b.run_seqs(kvs, seqs)
+    n = b.launches_per_step()
+    t = b.trace().astype(np.int64)[:n]
+    names = ["norm", "qkv", "attention", "o", "ffn_norm", "gate_up", "down"]
+    per = {}
+    for j, k in enumerate(names):
+        per[k] = float(np.mean([(t[l * 7 + j, 2] - t[l * 7 + j - 1, 2]) / 1e3 for l in range(1, 23)]))
+    gemm = {}
+    for j, k in [(1, "qkv"), (3, "o"), (5, "gate_up"), (6, "down")]:
+        rows = [t[l * 7 + j] for l in range(1, 23)]
+        prev = [t[l * 7 + j - 1, 2] for l in range(1, 23)]
+        gemm[k] = {
+            "wait_released": float(np.mean([r[1] - p for r, p in zip(rows, prev)]) / 1e3),
+            "first_stage": float(np.mean([r[4] - r[1] for r in rows]) / 1e3),
+            "mmas_issued": float(np.mean([r[5] - r[4] for r in rows]) / 1e3),
+            "accumulator_ready": float(np.mean([r[6] - r[5] for r in rows]) / 1e3),
+            "epilogue_done": float(np.mean([r[7] - r[6] for r in rows]) / 1e3),
+            "exit": float(np.mean([r[2] - r[7] for r in rows]) / 1e3),
+        }
+    print(json.dumps({"bench": "batch_step", "sequences": B, "launches": int(n),
+                      "exit_to_exit_us": per, "layer_us": sum(per.values()), "gemm_marks_us": gemm}), flush=True)
+    for kv in kvs:
+        kv.close()
+    b.close()
+    m.close()
+    os.remove(path)
+    os.rmdir(td)
+
+
 if __name__ == "__main__":
     which = sys.argv[1] if len(sys.argv) > 1 else "all"
     if which in ("dequant", "all"):
@@ -360,3 +413,5 @@ if __name__ == "__main__":
         bench_prefill()
     if which in ("token", "all"):
         bench_token()
+    if which in ("batch", "all"):
+        bench_batch()
