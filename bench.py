@@ -71,8 +71,8 @@ def b1_bytes_per_token():
 
 
 def make_model(path):
-    import hotseat_b200 as hs
-    hs.write_synthetic_gguf(path, seed=MODEL_SEED, **hs.QWEN05)
+    from tests.golden.synth import QWEN05, write_synthetic_gguf
+    write_synthetic_gguf(path, seed=MODEL_SEED, **QWEN05)
 
 
 def b64_prompts():

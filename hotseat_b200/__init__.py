@@ -84,14 +84,6 @@ class SeqState(C.Structure):
                 ("done", C.c_uint32), ("done_reason", C.c_uint32)]
 
 
-class SynthSpec(C.Structure):
-    _fields_ = [("n_layers", C.c_uint32), ("d_model", C.c_uint32), ("n_heads", C.c_uint32),
-                ("n_kv_heads", C.c_uint32), ("d_ff", C.c_uint32), ("vocab", C.c_uint32),
-                ("context_length", C.c_uint32), ("eos", C.c_uint32), ("eps", C.c_float), ("rope_base", C.c_float),
-                ("weight_std", C.c_float), ("bias_std", C.c_float), ("embd_type", C.c_uint32),
-                ("weight_type", C.c_uint32), ("tied", C.c_uint32), ("threads", C.c_uint32), ("seed", C.c_uint64)]
-
-
 _P = C.c_void_p
 _U64P = C.POINTER(C.c_uint64)
 _SIGS = {
@@ -134,7 +126,6 @@ _SIGS = {
     "hs_seq_launches_per_step": (C.c_int, [_P, C.POINTER(C.c_uint32)]),
     "hs_scratch_trace": (C.c_int, [_P, _P, C.c_uint64, _U64P]),
     "hs_dequant_f16": (C.c_int, [C.c_uint32, _P, C.c_uint64, _P, _P]),
-    "hs_synth_write": (C.c_int, [C.c_char_p, C.POINTER(SynthSpec)]),
     "hs_batch_new": (C.c_int, [_P, C.c_uint32, C.POINTER(_P)]),
     "hs_batch_free": (None, [_P]),
     "hs_forward_batch": (C.c_int, [_P, _P, _P, _P, C.c_uint32, _P]),
@@ -490,19 +481,3 @@ def dequant_f16(ggml_type, src_dev_ptr, n, dst_dev_ptr, stream=None):
     _check(_lib.hs_dequant_f16(ggml_type, C.c_void_p(src_dev_ptr), n, C.c_void_p(dst_dev_ptr),
                                C.c_void_p(stream) if stream else None))
 
-
-QWEN05 = dict(n_layers=24, d_model=896, n_heads=14, n_kv_heads=2, d_ff=4864, vocab=151936)
-QWEN15 = dict(n_layers=28, d_model=1536, n_heads=12, n_kv_heads=2, d_ff=8960, vocab=151936)
-
-
-def write_synthetic_gguf(path, n_layers, d_model, n_heads, n_kv_heads, d_ff, vocab, seed, context_length=32768,
-                         eos=None, eps=1e-6, rope_base=1e6, weight_std=0.02, bias_std=0.02, embd_type=14,
-                         weight_type=12, tied=True, threads=0):
-    """Seeded random-init Qwen2-architecture GGUF (no counterpart in hs-engine)."""
-    if eos is None:
-        eos = 151643 if vocab > 151643 else vocab - 1
-    spec = SynthSpec(n_layers, d_model, n_heads, n_kv_heads, d_ff, vocab, context_length, eos, eps, rope_base,
-                     weight_std, bias_std, embd_type, weight_type, 1 if tied else 0, threads or (os.cpu_count() or 1),
-                     seed)
-    _check(_lib.hs_synth_write(os.fsencode(path), C.byref(spec)))
-    return path

@@ -53,6 +53,9 @@ import tempfile
 
 import numpy as np
 
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from tests.golden.synth import QWEN05, QWEN15, write_synthetic_gguf  # noqa: E402  (fixture writer)
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -130,8 +133,8 @@ def bench_dequant(reps=10):
     td = tempfile.mkdtemp(prefix="hsmicro")
     a = os.path.join(td, "q6.gguf")
     b = os.path.join(td, "q4.gguf")
-    hs.write_synthetic_gguf(a, seed=1234, **hs.QWEN05)
-    hs.write_synthetic_gguf(b, seed=1234, embd_type=12, **dict(hs.QWEN05, n_layers=1))
+    write_synthetic_gguf(a, seed=1234, **QWEN05)
+    write_synthetic_gguf(b, seed=1234, embd_type=12, **dict(QWEN05, n_layers=1))
     cases = [(a, "blk.0.ffn_gate.weight", "4864x896"), (a, "blk.0.ffn_down.weight", "896x4864"),
              (b, "token_embd.weight", "151936x896"), (a, "token_embd.weight", "151936x896")]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
@@ -180,7 +183,7 @@ def bench_attention(ctxs=(1024, 4096, 16384, 32767)):
     peak, src = _peak()
     td = tempfile.mkdtemp(prefix="hsmicro")
     path = os.path.join(td, "q05.gguf")
-    hs.write_synthetic_gguf(path, seed=1234, **hs.QWEN05)
+    write_synthetic_gguf(path, seed=1234, **QWEN05)
     max_ctx = max(ctxs) + 8
     layers, row = 24, 2 * 2 * 64 * 4
     for batch, numeric in ((1, hs.NUMERIC_FAST), (64, hs.NUMERIC_TC)):
@@ -230,8 +233,8 @@ def bench_prefill(n_seqs=16, prompt=2048, gen=512):
         tflops, tsrc = 1590.0, "fallback"
     td = tempfile.mkdtemp(prefix="hsmicro")
     path = os.path.join(td, "q15.gguf")
-    hs.write_synthetic_gguf(path, seed=1234, **hs.QWEN15)
-    c = hs.QWEN15
+    write_synthetic_gguf(path, seed=1234, **QWEN15)
+    c = QWEN15
     hd = c["d_model"] // c["n_heads"]
     qrows = (c["n_heads"] + 2 * c["n_kv_heads"]) * hd
     layer_w = c["d_model"] * qrows + c["d_model"] * c["d_model"] + 3 * c["d_model"] * c["d_ff"]
@@ -293,13 +296,13 @@ def bench_token():
     import hotseat_b200 as hs
     td = tempfile.mkdtemp(prefix="hsmicro")
     path = os.path.join(td, "q05.gguf")
-    hs.write_synthetic_gguf(path, seed=1234, **hs.QWEN05)
+    write_synthetic_gguf(path, seed=1234, **QWEN05)
     m = hs.Model.load(path, max_ctx=256, numeric=hs.NUMERIC_FAST)
     s = m.scratch()
     if s.launches_per_step() != 3:
         raise RuntimeError("the persistent token kernel is not in use for this model")
     rng = np.random.default_rng(36)
-    prompt = [int(t) for t in rng.integers(0, hs.QWEN05["vocab"], size=36)]
+    prompt = [int(t) for t in rng.integers(0, QWEN05["vocab"], size=36)]
     cfg = hs.SamplerCfg.default(temperature=0.8, seed=99)
     L, ghz = 24, 1.965
     for ntok in (60, 120):
@@ -363,7 +366,7 @@ def bench_batch():
     import hotseat_b200 as hs
     td = tempfile.mkdtemp(prefix="hsmicro")
     path = os.path.join(td, "q05.gguf")
-    hs.write_synthetic_gguf(path, seed=1234, **hs.QWEN05)
+    write_synthetic_gguf(path, seed=1234, **QWEN05)
     m = hs.Model.load(path, max_ctx=512, numeric=hs.NUMERIC_TC)
     B = 64
     b = hs.Batch(m, B)
@@ -371,7 +374,7 @@ def bench_batch():
     seqs = []
     for i in range(B):
         g = np.random.default_rng(99 + i)
-        p = [int(t) for t in g.integers(0, hs.QWEN05["vocab"], size=128)]
+        p = [int(t) for t in g.integers(0, QWEN05["vocab"], size=128)]
         seqs.append(dict(tokens=p, prompt_len=128, max_tokens=140, filled=0, rng=hs.Rng.seed(99 + i),
                          cfg=hs.SamplerCfg.default(temperature=0.8, seed=99 + i)))
     b.run_seqs(kvs, seqs)

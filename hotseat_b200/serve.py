@@ -30,6 +30,7 @@ destination is a second region on the same GPU.
 import argparse
 import json
 import os
+import sys
 import tempfile
 import time
 from concurrent.futures import ThreadPoolExecutor
@@ -37,6 +38,9 @@ from concurrent.futures import ThreadPoolExecutor
 import numpy as np
 
 import hotseat_b200 as hs
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from tests.golden.synth import QWEN05, write_synthetic_gguf  # noqa: E402  (fixture writer)
 
 PRECOPY_ROUNDS = 3  # rounds the source keeps decoding between the first copy and the hand-over
 
@@ -168,7 +172,7 @@ def main():
     args = ap.parse_args()
     td = tempfile.mkdtemp(prefix="hsserve")
     path = os.path.join(td, "q05.gguf")
-    hs.write_synthetic_gguf(path, seed=1234, **hs.QWEN05)
+    write_synthetic_gguf(path, seed=1234, **QWEN05)
     try:
         rec = serve(path, args.gpus, args.seqs, args.prompt, args.steps, args.seed, round_tokens=args.round_tokens)
     finally:

@@ -258,20 +258,6 @@ int hs_scratch_trace(hs_scratch* s, uint64_t* out, uint64_t n_slots, uint64_t* u
  * into f16 bits at device memory `dst`, on `stream` (cudaStream_t or NULL). */
 int hs_dequant_f16(uint32_t ggml_type, const void* src, uint64_t n, void* dst, void* stream);
 
-/* ---- seeded synthetic GGUF (fixture writer; no counterpart in hs-engine) -- */
-
-typedef struct {
-    uint32_t n_layers, d_model, n_heads, n_kv_heads, d_ff, vocab, context_length, eos;
-    float eps, rope_base, weight_std, bias_std;
-    uint32_t embd_type;   /* ggml type of token_embd.weight (14 = Q6_K) */
-    uint32_t weight_type; /* ggml type of the other 2-D weights (12 = Q4_K) */
-    uint32_t tied;        /* 1: no output.weight (tied LM head) */
-    uint32_t threads;
-    uint64_t seed;
-} hs_synth_spec;
-
-int hs_synth_write(const char* path, const hs_synth_spec* spec);
-
 #ifdef __cplusplus
 }
 #endif

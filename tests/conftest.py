@@ -15,6 +15,8 @@ def pytest_configure(config):
 def _build_all():
     from oracle import ffi as oracle_ffi
     oracle_ffi.build()
+    from tests.golden import synth
+    synth.build()
     import importlib.util
     spec = importlib.util.spec_from_file_location("hs_build", os.path.join(ROOT, "hotseat_b200", "build.py"))
     mod = importlib.util.module_from_spec(spec)
@@ -23,6 +25,8 @@ def _build_all():
 
 
 _build_all()
+
+from tests.golden.synth import QWEN05, QWEN15, write_synthetic_gguf  # noqa: E402
 
 TINY = dict(n_layers=2, d_model=256, n_heads=4, n_kv_heads=2, d_ff=512, vocab=1000, seed=7)
 TINY128 = dict(n_layers=2, d_model=256, n_heads=2, n_kv_heads=1, d_ff=768, vocab=1500, seed=11)
@@ -43,24 +47,21 @@ def fixture_dir(tmp_path_factory):
 
 @pytest.fixture(scope="session")
 def tiny_gguf(fixture_dir):
-    import hotseat_b200 as hs
     p = str(fixture_dir / "tiny.gguf")
-    hs.write_synthetic_gguf(p, **TINY)
+    write_synthetic_gguf(p, **TINY)
     return p
 
 
 @pytest.fixture(scope="session")
 def tiny128_gguf(fixture_dir):
-    import hotseat_b200 as hs
     p = str(fixture_dir / "tiny128.gguf")
-    hs.write_synthetic_gguf(p, **TINY128)
+    write_synthetic_gguf(p, **TINY128)
     return p
 
 
 @pytest.fixture(scope="session")
 def q05_gguf(fixture_dir):
     """The Qwen2.5-0.5B-shape seeded model (Q6_K embedding, Q4_K weights)."""
-    import hotseat_b200 as hs
     p = str(fixture_dir / "qwen05.gguf")
-    hs.write_synthetic_gguf(p, seed=1234, **hs.QWEN05)
+    write_synthetic_gguf(p, seed=1234, **QWEN05)
     return p

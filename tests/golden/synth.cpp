@@ -1,4 +1,5 @@
-// Seeded synthetic Qwen2 GGUF writer.
+// Seeded synthetic Qwen2 GGUF writer (test fixture generator; not part of
+// the product library).
 //
 // Writes a GGUF v3 file with the metadata keys, tokenizer keys and tensor
 // names hotseat's Model::load reads (model.rs:110-185, tok.rs:54-82), with
@@ -10,17 +11,74 @@
 //
 // Every random value is a pure function of (seed, tensor name, element
 // index), so the file is identical for any thread count.
+//
+// Built by tests/golden/synth.py into tests/golden/_build/libhs_synth.so; the
+// tests, the benchmark and the microbenchmarks write their model files with
+// it, so a process that only times the CPU restatement maps no product code.
 #include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <string>
 #include <thread>
 #include <vector>
 
-#include "common.h"
+extern "C" {
+typedef struct {
+    uint32_t n_layers, d_model, n_heads, n_kv_heads, d_ff, vocab, context_length, eos;
+    float eps, rope_base, weight_std, bias_std;
+    uint32_t embd_type;   /* ggml type of token_embd.weight (14 = Q6_K) */
+    uint32_t weight_type; /* ggml type of the other 2-D weights (12 = Q4_K) */
+    uint32_t tied;        /* 1: no output.weight (tied LM head) */
+    uint32_t threads;
+    uint64_t seed;
+} hs_synth_spec;
+}
 
-namespace hs {
+// Status codes: the same values as the library's HS_OK / HS_E_*.
+#define SYN_OK 0
+#define SYN_E_ARG (-1)
+#define SYN_E_IO (-2)
+#define SYN_E_UNSUPPORTED (-6)
+
+namespace synth {
 namespace {
+
+thread_local std::string g_err;
+int fail(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+
+uint32_t f2u(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }
+float u2f(uint32_t u) { float f; std::memcpy(&f, &u, 4); return f; }
+
+// IEEE binary16 -> binary32, exact.
+float h2f_host(uint16_t h) {
+    uint32_t sign = ((uint32_t)h & 0x8000u) << 16;
+    uint32_t exp = ((uint32_t)h >> 10) & 0x1f;
+    uint32_t man = (uint32_t)h & 0x3ff;
+    if (exp == 0) {
+        if (man == 0) return u2f(sign);
+        uint32_t shift = (uint32_t)__builtin_clz(man) - 22;
+        return u2f(sign | ((127 - 15 - shift) << 23) | (((man << (shift + 1)) & 0x3ff) << 13));
+    }
+    if (exp == 0x1f) return u2f(sign | 0x7f800000u | (man << 13));
+    return u2f(sign | ((exp + 112) << 23) | (man << 13));
+}
+
+// ggml type -> (elements per block, bytes per block) for the encodable types.
+bool ggml_block(uint32_t ty, uint64_t* be, uint64_t* bb) {
+    switch (ty) {
+        case 0: *be = 1; *bb = 4; return true;
+        case 1: *be = 1; *bb = 2; return true;
+        case 8: *be = 32; *bb = 34; return true;
+        case 12: *be = 256; *bb = 144; return true;
+        case 14: *be = 256; *bb = 210; return true;
+        default: return false;
+    }
+}
 
 uint64_t mix64(uint64_t z) {
     z += 0x9E3779B97F4A7C15ull;
@@ -220,19 +278,21 @@ class Out {
 };
 
 }  // namespace
-}  // namespace hs
+}  // namespace synth
+
+extern "C" const char* hs_synth_last_error() { return synth::g_err.c_str(); }
 
 extern "C" int hs_synth_write(const char* path, const hs_synth_spec* spec) {
-    using namespace hs;
-    if (!path || !spec) return fail(HS_E_ARG, "null argument");
+    using namespace synth;
+    if (!path || !spec) return fail(SYN_E_ARG, "null argument");
     const hs_synth_spec& sp = *spec;
     uint64_t be, bb;
     for (uint32_t ty : {sp.embd_type, sp.weight_type})
         if (!(ty == 0 || ty == 1 || ty == 8 || ty == 12 || ty == 14))
-            return fail(HS_E_UNSUPPORTED, "synthetic writer encodes F32, F16, Q8_0, Q4_K, Q6_K only");
+            return fail(SYN_E_UNSUPPORTED, "synthetic writer encodes F32, F16, Q8_0, Q4_K, Q6_K only");
     if (!sp.n_layers || !sp.d_model || !sp.n_heads || !sp.n_kv_heads || !sp.d_ff || !sp.vocab ||
         sp.d_model % sp.n_heads || sp.n_heads % sp.n_kv_heads)
-        return fail(HS_E_ARG, "inconsistent model shape");
+        return fail(SYN_E_ARG, "inconsistent model shape");
     uint32_t hd = sp.d_model / sp.n_heads;
     std::vector<Tensor> ts;
     auto w2 = [&](const std::string& n, uint64_t cols, uint64_t rows, uint32_t ty) {
@@ -260,13 +320,13 @@ extern "C" int hs_synth_write(const char* path, const hs_synth_spec* spec) {
     uint64_t off = 0;
     for (auto& t : ts) {
         ggml_block(t.type, &be, &bb);
-        if (elems_of(t) % be) return fail(HS_E_ARG, "tensor " + t.name + " is not a whole number of blocks");
+        if (elems_of(t) % be) return fail(SYN_E_ARG, "tensor " + t.name + " is not a whole number of blocks");
         t.rel_off = off;
         t.bytes = elems_of(t) / be * bb;
         off = (off + t.bytes + 31) / 32 * 32;
     }
     FILE* f = fopen(path, "wb");
-    if (!f) return fail(HS_E_IO, std::string("io: cannot create ") + path);
+    if (!f) return fail(SYN_E_IO, std::string("io: cannot create ") + path);
     Out o(f);
     o.u32(0x46554747u);
     o.u32(3);
@@ -313,6 +373,6 @@ extern "C" int hs_synth_write(const char* path, const hs_synth_spec* spec) {
     }
     bool ok = o.ok();
     ok = (fclose(f) == 0) && ok;
-    if (!ok) return fail(HS_E_IO, std::string("io: write failed for ") + path);
-    return HS_OK;
+    if (!ok) return fail(SYN_E_IO, std::string("io: write failed for ") + path);
+    return SYN_OK;
 }

@@ -11,6 +11,7 @@ import pytest
 
 import hotseat_b200 as hs
 from oracle import ffi
+from tests.golden.synth import write_synthetic_gguf
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -108,8 +109,8 @@ def test_reference_byte_run_cases_on_the_product():
 def test_synthetic_writer_is_deterministic_across_thread_counts(tmp_path):
     a, b = str(tmp_path / "a.gguf"), str(tmp_path / "b.gguf")
     spec = dict(n_layers=1, d_model=128, n_heads=2, n_kv_heads=1, d_ff=256, vocab=300, seed=3)
-    hs.write_synthetic_gguf(a, threads=1, **spec)
-    hs.write_synthetic_gguf(b, threads=7, **spec)
+    write_synthetic_gguf(a, threads=1, **spec)
+    write_synthetic_gguf(b, threads=7, **spec)
     assert open(a, "rb").read() == open(b, "rb").read()
 
 
@@ -124,6 +125,6 @@ def test_synthetic_model_has_the_requested_distribution(tiny_gguf):
 
 
 def test_synthetic_writer_rejects_bad_shapes(tmp_path):
-    with pytest.raises(hs.HotseatError):
-        hs.write_synthetic_gguf(str(tmp_path / "x.gguf"), n_layers=1, d_model=100, n_heads=3, n_kv_heads=1,
+    with pytest.raises(RuntimeError):
+        write_synthetic_gguf(str(tmp_path / "x.gguf"), n_layers=1, d_model=100, n_heads=3, n_kv_heads=1,
                                 d_ff=256, vocab=300, seed=1)

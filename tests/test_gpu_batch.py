@@ -10,6 +10,7 @@ import numpy as np
 import pytest
 
 import hotseat_b200 as hs
+from tests.golden.synth import QWEN05
 from oracle import ffi
 
 from conftest import TINY, TINY128
@@ -32,7 +33,7 @@ def seq(tokens, max_tokens, cfg, seed, **kw):
 @pytest.mark.parametrize("which", ["tiny", "tiny128", "q05"])
 def test_tc_logits_within_tolerance(which, tiny_gguf, tiny128_gguf, q05_gguf):
     path, vocab, n_pos = {"tiny": (tiny_gguf, TINY["vocab"], 40), "tiny128": (tiny128_gguf, TINY128["vocab"], 24),
-                          "q05": (q05_gguf, hs.QWEN05["vocab"], 6)}[which]
+                          "q05": (q05_gguf, QWEN05["vocab"], 6)}[which]
     rng = np.random.default_rng(2)
     toks = [int(t) for t in rng.integers(0, vocab, size=n_pos)]
     m = load(path, 64)
@@ -86,7 +87,7 @@ def test_tc_greedy_tokens_match_the_oracle(q05_gguf):
     """Four greedy sequences (temperature 0, penalty 1.1) of the 0.5B shape
     decoded together; each must pick the CPU path's token at every step."""
     g = np.random.default_rng(36)
-    prompts = [[int(t) for t in g.integers(0, hs.QWEN05["vocab"], size=12 + 4 * i)] for i in range(4)]
+    prompts = [[int(t) for t in g.integers(0, QWEN05["vocab"], size=12 + 4 * i)] for i in range(4)]
     cfg = hs.SamplerCfg.default(temperature=0.0)
     m = load(q05_gguf, 256)
     b = hs.Batch(m, 4)
@@ -100,7 +101,7 @@ def test_tc_greedy_tokens_match_the_oracle(q05_gguf):
 
 def test_tc_sampled_c1_transcript_matches_the_oracle(q05_gguf):
     rng = np.random.default_rng(36)
-    prompt = [int(t) for t in rng.integers(0, hs.QWEN05["vocab"], size=36)]
+    prompt = [int(t) for t in rng.integers(0, QWEN05["vocab"], size=36)]
     cfg = hs.SamplerCfg.default(temperature=0.8, seed=99)
     m = load(q05_gguf, 2048)
     b = hs.Batch(m, 1)
@@ -207,7 +208,7 @@ def test_tc_attention_work_split_keeps_the_bits(env, q05_gguf, monkeypatch):
     def run():
         m = load(q05_gguf, 256)
         g = np.random.default_rng(12)
-        seqs = [seq([int(t) for t in g.integers(0, hs.QWEN05["vocab"], size=70 + 9 * i)], 24,
+        seqs = [seq([int(t) for t in g.integers(0, QWEN05["vocab"], size=70 + 9 * i)], 24,
                     hs.SamplerCfg.default(temperature=0.8, seed=5 + i), 5 + i) for i in range(3)]
         kvs = [m.kv() for _ in seqs]
         out = hs.Batch(m, len(seqs)).run_seqs(kvs, seqs)

@@ -10,6 +10,7 @@ import numpy as np
 import pytest
 
 import hotseat_b200 as hs
+from tests.golden.synth import QWEN05
 from oracle import ffi
 
 from conftest import TINY, TINY128
@@ -33,7 +34,7 @@ def load(path, max_ctx):
 @pytest.mark.parametrize("which", ["tiny", "tiny128", "q05"])
 def test_fast_logits_within_tolerance(which, tiny_gguf, tiny128_gguf, q05_gguf):
     path, vocab, n_pos = {"tiny": (tiny_gguf, TINY["vocab"], 40), "tiny128": (tiny128_gguf, TINY128["vocab"], 24),
-                          "q05": (q05_gguf, hs.QWEN05["vocab"], 6)}[which]
+                          "q05": (q05_gguf, QWEN05["vocab"], 6)}[which]
     rng = np.random.default_rng(2)
     toks = [int(t) for t in rng.integers(0, vocab, size=n_pos)]
     m = load(path, 64)
@@ -71,7 +72,7 @@ def test_fast_greedy_tokens_match_the_oracle(q05_gguf):
     path must pick the CPU path's token at every step. A disagreement is
     reported with the CPU logits' top-1/top-2 margin at that step."""
     rng = np.random.default_rng(36)
-    prompt = [int(t) for t in rng.integers(0, hs.QWEN05["vocab"], size=36)]
+    prompt = [int(t) for t in rng.integers(0, QWEN05["vocab"], size=36)]
     cfg = hs.SamplerCfg.default(temperature=0.0)
     m = load(q05_gguf, 256)
     got = run(m, prompt, 48, cfg, 1)[0]
@@ -92,7 +93,7 @@ def test_fast_greedy_tokens_match_the_oracle(q05_gguf):
 
 def test_fast_sampled_c1_transcript_matches_the_oracle(q05_gguf):
     rng = np.random.default_rng(36)
-    prompt = [int(t) for t in rng.integers(0, hs.QWEN05["vocab"], size=36)]
+    prompt = [int(t) for t in rng.integers(0, QWEN05["vocab"], size=36)]
     cfg = hs.SamplerCfg.default(temperature=0.8, seed=99)
     m = load(q05_gguf, 2048)
     g = run(m, prompt, 120, cfg, 99)

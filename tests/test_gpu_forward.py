@@ -8,6 +8,7 @@ import numpy as np
 import pytest
 
 import hotseat_b200 as hs
+from tests.golden.synth import QWEN05
 from oracle import ffi
 
 from conftest import TINY, TINY128
@@ -51,7 +52,7 @@ def test_long_context_crosses_attention_chunks(tiny_gguf):
 
 
 def test_05b_shape_logits_bit_exact(q05_gguf):
-    compare_run(q05_gguf, hs.QWEN05["vocab"], 5, 64)
+    compare_run(q05_gguf, QWEN05["vocab"], 5, 64)
 
 
 def test_forward_rejects_out_of_range_inputs(tiny_gguf):

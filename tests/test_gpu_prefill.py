@@ -10,6 +10,7 @@ import numpy as np
 import pytest
 
 import hotseat_b200 as hs
+from tests.golden.synth import QWEN05
 from oracle import ffi
 
 from conftest import TINY
@@ -53,7 +54,7 @@ def test_prefill_in_pieces_equals_one_call(tiny_gguf):
 
 def test_prefill_greedy_continuation_matches_the_oracle(q05_gguf):
     g = np.random.default_rng(12)
-    prompt = [int(t) for t in g.integers(0, hs.QWEN05["vocab"], size=80)]
+    prompt = [int(t) for t in g.integers(0, QWEN05["vocab"], size=80)]
     cfg = hs.SamplerCfg.default(temperature=0.0)
     m = hs.Model.load(q05_gguf, max_ctx=256, numeric=TC)
     kv = m.kv()

@@ -6,6 +6,7 @@ import numpy as np
 import pytest
 
 import hotseat_b200 as hs
+from tests.golden.synth import QWEN05
 from oracle import ffi
 
 from conftest import TINY
@@ -111,7 +112,7 @@ def test_random_configs_match_the_oracle_tiny(tiny_scratch, trial):
 def test_random_configs_match_the_oracle_full_vocab(big_scratch, trial):
     m, s = big_scratch
     rng = np.random.default_rng(100 + trial)
-    v = hs.QWEN05["vocab"]
+    v = QWEN05["vocab"]
     logits = (rng.standard_normal(v) * 0.6).astype(np.float32)
     if trial % 2 == 0:
         logits[rng.integers(0, v, 200)] = np.float32(np.sort(logits)[-30])

@@ -7,6 +7,7 @@ import numpy as np
 import pytest
 
 import hotseat_b200 as hs
+from tests.golden.synth import QWEN05
 from oracle import ffi
 
 from conftest import TINY, gpu_count
@@ -178,7 +179,7 @@ def test_c1_transcript_and_kv_hash_match_the_oracle(q05_gguf):
     """The benchmark's batch-1 configuration in full: 36 random prompt ids,
     120 generated tokens at temperature 0.8, seed 99."""
     rng = np.random.default_rng(36)
-    prompt = [int(t) for t in rng.integers(0, hs.QWEN05["vocab"], size=36)]
+    prompt = [int(t) for t in rng.integers(0, QWEN05["vocab"], size=36)]
     cfg = hs.SamplerCfg.default(temperature=0.8, seed=99)
     m = hs.Model.load(q05_gguf, max_ctx=2048)
     g = gpu_run(m, prompt, 120, cfg, 99)

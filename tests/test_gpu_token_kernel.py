@@ -11,6 +11,7 @@ import numpy as np
 import pytest
 
 import hotseat_b200 as hs
+from tests.golden.synth import QWEN05
 
 from conftest import TINY, TINY128
 
@@ -35,7 +36,7 @@ def test_token_kernel_is_one_launch_per_forward(tiny_gguf, monkeypatch):
 def test_token_kernel_forward_is_bit_identical(which, tiny_gguf, tiny128_gguf, q05_gguf, monkeypatch):
     path, vocab, n_pos, max_ctx = {"tiny": (tiny_gguf, TINY["vocab"], 200, 512),
                                    "tiny128": (tiny128_gguf, TINY128["vocab"], 150, 512),
-                                   "q05": (q05_gguf, hs.QWEN05["vocab"], 80, 256)}[which]
+                                   "q05": (q05_gguf, QWEN05["vocab"], 80, 256)}[which]
     rng = np.random.default_rng(5)
     toks = [int(t) for t in rng.integers(0, vocab, size=n_pos)]
     a = load(path, max_ctx, True, monkeypatch)
@@ -52,7 +53,7 @@ def test_token_kernel_forward_is_bit_identical(which, tiny_gguf, tiny128_gguf, q
 
 def test_token_kernel_sampled_sequence_is_bit_identical(q05_gguf, monkeypatch):
     rng = np.random.default_rng(36)
-    prompt = [int(t) for t in rng.integers(0, hs.QWEN05["vocab"], size=24)]
+    prompt = [int(t) for t in rng.integers(0, QWEN05["vocab"], size=24)]
     cfg = hs.SamplerCfg.default(temperature=0.8, seed=99)
     out = []
     for tk in (True, False):
@@ -98,7 +99,7 @@ def test_token_kernel_head_split_keeps_the_bits(q05_gguf, monkeypatch):
     """Attention items over parts of a group's query heads (more CTAs per
     split) give the same logits as whole groups."""
     rng = np.random.default_rng(8)
-    toks = [int(t) for t in rng.integers(0, hs.QWEN05["vocab"], size=150)]
+    toks = [int(t) for t in rng.integers(0, QWEN05["vocab"], size=150)]
     out = []
     for hsplit in ("1", "2"):
         monkeypatch.setenv("HS_ATTN_HEAD_SPLIT", hsplit)

@@ -11,6 +11,7 @@ import pytest
 import torch
 
 import hotseat_b200 as hs
+from tests.golden.synth import QWEN05
 from oracle import ffi
 
 from conftest import TINY, TINY128
@@ -52,7 +53,7 @@ CFGS = {
 @pytest.mark.parametrize("mode", list(CFGS))
 def test_noalloc_matches_hs_sample_twice_in_a_row(which, mode, tiny_gguf, tiny128_gguf, q05_gguf):
     path, vocab = {"tiny": (tiny_gguf, TINY["vocab"]), "tiny128": (tiny128_gguf, TINY128["vocab"]),
-                   "q05": (q05_gguf, hs.QWEN05["vocab"])}[which]
+                   "q05": (q05_gguf, QWEN05["vocab"])}[which]
     kw = dict(CFGS[mode])
     if mode == "plain" and vocab > 1024:
         kw["top_k"] = 64  # any top_k needs a single candidate CTA
