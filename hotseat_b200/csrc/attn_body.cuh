@@ -63,9 +63,9 @@ __device__ __forceinline__ float tagged_value(uint64_t e) { return __uint_as_flo
 // memory once both entries of a pair carry `want`: map(i, &src, &dst) gives
 // pair i's source (16-byte aligned) and destination. Each thread takes pairs
 // tid, tid + 256, ..., B at a time, every round's loads in flight together.
-// Returns false (values left unset) after kPollLimit rounds.
+// Returns false (values left unset) after `limit` rounds.
 template <uint32_t B, typename Map>
-__device__ bool poll_copy(uint32_t n_pairs, uint32_t want, Map map) {
+__device__ bool poll_copy(uint32_t n_pairs, uint32_t want, uint32_t limit, Map map) {
     bool ok = true;
     for (uint32_t base = threadIdx.x; base < n_pairs; base += B * kThreads) {
         uint32_t pend = 0;
@@ -93,7 +93,7 @@ __device__ bool poll_copy(uint32_t n_pairs, uint32_t want, Map map) {
                     dst[1] = tagged_value(e[j][1]);
                     pend &= ~(1u << j);
                 }
-            if (pend && ++rounds > kPollLimit) {
+            if (pend && ++rounds > limit) {
                 ok = false;
                 break;
             }
@@ -110,6 +110,7 @@ struct TagIO {
     uint64_t* out;        // [n_heads * head_dim]
     uint64_t* rec;        // [n_kv][max_splits][attn_record]
     uint32_t want, tag;
+    uint32_t poll_limit;  // polling rounds before the item gives up (ERR_TIMEOUT)
 };
 
 __device__ __forceinline__ void split_f16(float x, uint16_t* hi, uint16_t* lo) {
@@ -282,7 +283,8 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     // (or, tagged, the finished rows once they carry the awaited tag).
     const uint32_t qrow0 = (kvh * Gf + hlo) * HD, krow0 = a.nh * HD + kvh * HD, vrow0 = (a.nh + a.nkv) * HD + kvh * HD;
     if (tio) {
-        const bool got = poll_copy<2>((G + 2) * HD / 2, tio->want, [&](uint32_t i, const uint64_t** src, float** dst) {
+        const bool got = poll_copy<2>((G + 2) * HD / 2, tio->want, tio->poll_limit,
+                                      [&](uint32_t i, const uint64_t** src, float** dst) {
             const uint32_t idx = 2 * i;
             *src = tio->qkv + (idx < G * HD ? qrow0 + idx
                                             : (idx < (G + 1) * HD ? krow0 + idx - G * HD : vrow0 + idx - (G + 1) * HD));

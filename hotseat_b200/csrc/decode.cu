@@ -671,13 +671,19 @@ __global__ void __launch_bounds__(256) k_sample_cand(const SampleArgs a0) {
     tr.exit();
 }
 
-// Candidate kernel for wide slices (a multiple of 1024 logits per CTA, top
+// Candidate kernel for wide slices (a multiple of 256 logits per CTA, top
 // keys kmax <= 64): the same output as k_sample_cand (the CTA's kmax best
 // keys in key order) from an exact radix select instead of sorting. Each
 // thread holds slice/256 keys; 8-bit digits of the 64-bit key, most
 // significant first, narrow the prefix of the kmax-th smallest key until the
 // boundary bin is taken whole; the selected keys (exactly kmax, keys are
 // unique) are then ranked against each other.
+//
+// SORT (sort mode, any top_k): the CTA instead sorts its whole slice of keys
+// (bitonic network in shared memory, padded to a power of two) and writes
+// all `slice` of them in key order; k_sample_rank then finds each key's
+// place among every slice's keys.
+template <bool SORT>
 __global__ void __launch_bounds__(256) k_sample_cand_wide(const SampleArgs a0) {
     const SampleArgs a = slot_args(a0);
     constexpr uint32_t PER = kMaxSlice / 256;
@@ -763,6 +769,33 @@ __global__ void __launch_bounds__(256) k_sample_cand_wide(const SampleArgs a0) {
         const uint32_t e = cta_base + j * 256 + tid;
         key[j] = (j < per && e < a.vocab) ? cand_key(v[j], e) : ~0ull - e;
     }
+    if (SORT) {
+        extern __shared__ uint64_t sk[];  // [n2]
+        uint32_t n2 = 256;
+        while (n2 < slice) n2 <<= 1;
+#pragma unroll
+        for (uint32_t j = 0; j < PER; j++)
+            if (j < per) sk[j * 256 + tid] = key[j];
+        for (uint32_t i = slice + tid; i < n2; i += 256) sk[i] = ~0ull;
+        __syncthreads();
+        for (uint32_t size = 2; size <= n2; size <<= 1) {
+            for (uint32_t j = size >> 1; j > 0; j >>= 1) {
+                for (uint32_t i = tid; i < n2 / 2; i += 256) {
+                    const uint32_t lo = ((i & ~(j - 1)) << 1) | (i & (j - 1)), hi = lo + j;
+                    const bool up = (lo & size) == 0;
+                    const uint64_t x = sk[lo], y = sk[hi];
+                    if ((x > y) == up) {
+                        sk[lo] = y;
+                        sk[hi] = x;
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        for (uint32_t i = tid; i < slice; i += 256) a.cand[(size_t)blockIdx.x * slice + i] = sk[i];
+        tr.exit();
+        return;
+    }
     const uint32_t K = a.kmax;
     uint64_t prefix = 0, mask = 0;  // bits of the K-th key fixed so far
     uint32_t needk = K;              // keys still to take at or below the prefix
@@ -829,6 +862,48 @@ __global__ void __launch_bounds__(256) k_sample_cand_wide(const SampleArgs a0) {
     tr.exit();
 }
 
+// Sort mode, stage 2: the global top-k of each slot in key order. Thread
+// (list l, index j) takes key x = list_l[j] and counts the keys below it in
+// every other list (binary search); keys are unique, so j + those counts is
+// x's rank among all keys, and the keys of rank < k land in wkeys[rank].
+// Only the first min(k, slice) keys of a list can be in the top k, and every
+// key below a top-k key is itself within those prefixes, so the searches run
+// over the prefixes alone.
+__device__ __forceinline__ uint32_t count_below(const uint64_t* list, uint32_t n, uint64_t key) {
+    uint32_t lo = 0, hi = n;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (__ldcg(list + mid) < key)
+            lo = mid + 1;
+        else
+            hi = mid;
+    }
+    return lo;
+}
+
+__global__ void __launch_bounds__(256) k_sample_rank(const SampleArgs a0) {
+    const SampleArgs a = slot_args(a0);
+    pdl_launch_dependents();
+    pdl_wait();
+    const DevCtl* c = a.ctl;
+    const uint32_t mode = __ldcg(&c->mode), active = __ldcg(&c->active);
+    const uint64_t filled = __ldcg((const unsigned long long*)&c->filled);
+    const uint64_t n_tokens = __ldcg((const unsigned long long*)&c->n_tokens);
+    const bool need = mode == 1 || (active && filled + 1 == n_tokens);
+    if (!need || !(__ldcg(&c->temperature) > 0.0f)) return;
+    const uint32_t top_k = __ldcg(&c->top_k);
+    const uint32_t k = top_k == 0 ? a.vocab : min(top_k, a.vocab);
+    const uint32_t slice = a.kmax, L = min(k, slice);
+    const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t l = idx / slice, j = idx % slice;
+    if (l >= a.n_cta || j >= L) return;
+    const uint64_t key = __ldcg(a.cand + (size_t)l * slice + j);
+    uint32_t rank = j;
+    for (uint32_t o = 0; o < a.n_cta; o++)
+        if (o != l) rank += count_below(a.cand + (size_t)o * slice, L, key);
+    if (rank < k) a.wkeys[(size_t)blockIdx.y * a.wide_stride + rank] = key;
+}
+
 constexpr uint32_t kFinalThreads = 256;
 
 __global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs a0) {
@@ -879,6 +954,91 @@ __global__ void __launch_bounds__(kFinalThreads) k_sample_final(const SampleArgs
                 }
             tok_s = fi == 0xffffffffu ? 0u : fi;
         }
+    } else if (need && sample_sort_mode(a.n_cta, a.kmax)) {
+        // Sort mode: the slot's top-k keys are in wkeys in order. The
+        // reference's three passes (sampler.rs:135-166: the sum of the
+        // weights, the nucleus scan `acc += p; if acc >= target`, the sum of
+        // the kept prefix, and the pick scan `acc += p; if r < acc`) all
+        // accumulate the same weights in the same order from zero, so one
+        // serial pass that stores every running sum S_i answers them all:
+        // sum = S_{k-1}; cut = 1 + the first i with S_i >= top_p * sum; the
+        // kept prefix sums to S_{cut-1}; the pick is the first i < cut with
+        // r < S_i. The weights are computed in parallel, the running sums on
+        // one thread, 1024 at a time through shared memory while the other
+        // warps stage the next 1024.
+        const uint32_t k = c->top_k == 0 ? a.vocab : min(c->top_k, a.vocab);
+        const uint64_t* keys = a.wkeys + (size_t)blockIdx.y * a.wide_stride;
+        float* ps = a.wps + (size_t)blockIdx.y * a.wide_stride;
+        float* pb = reinterpret_cast<float*>(merged);  // two 1024-float buffers
+        __shared__ float run_s, cmp_s;
+        __shared__ uint32_t first_s;
+        {
+            const float inv_t = __fdiv_rn(1.0f, c->temperature);
+            const float mx = key_value(__ldcg(keys));
+            for (uint32_t i = tid; i < k; i += blockDim.x)
+                ps[i] = ref_exp(__fmul_rn(__fsub_rn(key_value(__ldcg(keys + i)), mx), inv_t));
+        }
+        __syncthreads();
+        const uint32_t nch = (k + 1023) / 1024;
+        for (uint32_t i = tid; i < min(k, 1024u); i += blockDim.x) pb[i] = __ldcg(ps + i);
+        float run = 0.0f;
+        __syncthreads();
+        for (uint32_t ch = 0; ch < nch; ch++) {
+            float* cur = pb + (ch & 1) * 1024;
+            const uint32_t base = ch * 1024, cnt = min(1024u, k - base);
+            if (tid == 0) {
+                for (uint32_t t = 0; t < cnt; t++) {
+                    run = __fadd_rn(run, cur[t]);
+                    cur[t] = run;
+                }
+            } else if (tid >= 32 && ch + 1 < nch) {
+                float* nxt = pb + ((ch + 1) & 1) * 1024;
+                const uint32_t nb = base + 1024, ncnt = min(1024u, k - nb);
+                for (uint32_t t = tid - 32; t < ncnt; t += blockDim.x - 32) nxt[t] = __ldcg(ps + nb + t);
+            }
+            __syncthreads();
+            for (uint32_t t = tid; t < cnt; t += blockDim.x) ps[base + t] = cur[t];
+            __syncthreads();
+        }
+        if (tid == 0) {
+            run_s = run;
+            first_s = 0xffffffffu;
+            cmp_s = c->top_p < 1.0f ? __fmul_rn(c->top_p, run) : 0.0f;
+        }
+        __syncthreads();
+        uint32_t cut = k;
+        if (c->top_p < 1.0f) {
+            const float target = cmp_s;
+            for (uint32_t i = tid; i < k; i += blockDim.x)
+                if (__ldcg(ps + i) >= target) {
+                    atomicMin(&first_s, i);
+                    break;
+                }
+            __syncthreads();
+            if (first_s != 0xffffffffu) cut = first_s + 1;
+            __syncthreads();
+        }
+        if (tid == 0) {
+            const float sum = c->top_p < 1.0f ? __ldcg(ps + cut - 1) : run_s;
+            uint64_t s4[4] = {c->rng[0], c->rng[1], c->rng[2], c->rng[3]};
+            const float u = __fmul_rn((float)(rng_next(s4) >> 40), 1.0f / 16777216.0f);
+            for (int i = 0; i < 4; i++) c->rng[i] = a.ctl->rng[i] = s4[i];
+            c->draws += 1;
+            a.ctl->draws = c->draws;
+            cmp_s = __fmul_rn(u, sum);
+            first_s = 0xffffffffu;
+        }
+        __syncthreads();
+        {
+            const float r = cmp_s;
+            for (uint32_t i = tid; i < cut; i += blockDim.x)
+                if (r < __ldcg(ps + i)) {
+                    atomicMin(&first_s, i);
+                    break;
+                }
+        }
+        __syncthreads();
+        if (tid == 0) tok_s = (uint32_t)__ldcg(keys + (first_s != 0xffffffffu ? first_s : cut - 1));
     } else if (need) {
         const uint32_t k = c->top_k == 0 ? a.vocab : min(c->top_k, a.vocab);
         if (a.n_cta == 1) {
@@ -1100,6 +1260,7 @@ cudaError_t gemv_set_smem_limits(int optin) {
     if (e == cudaSuccess) e = allow_smem(k_attention<64>, optin);
     if (e == cudaSuccess) e = allow_smem(k_attention<128>, optin);
     if (e == cudaSuccess) e = allow_smem(k_sample_final, optin);
+    if (e == cudaSuccess) e = allow_smem(k_sample_cand_wide<true>, optin);
     return e;
 }
 
@@ -1135,15 +1296,39 @@ cudaError_t launch_attention(uint32_t head_dim, uint32_t nh, size_t smem, const 
 size_t sample_final_smem(uint32_t n_cta, uint32_t kmax) {
     // Selected lists: at most 64 lists of at most 64 keys (top_k <= 64), and
     // as much again for the merge tree's other half, when there are several
-    // CTAs; none with one CTA.
-    return n_cta > 1 ? (size_t)2 * 64 * 64 * sizeof(uint64_t) : 16;
+    // CTAs in list mode; none with one CTA or in sort mode.
+    return n_cta > 1 && !sample_sort_mode(n_cta, kmax) ? (size_t)2 * 64 * 64 * sizeof(uint64_t) : 16;
+}
+
+size_t sample_sort_smem(uint32_t slice) {
+    uint32_t n2 = 256;
+    while (n2 < slice) n2 <<= 1;
+    return (size_t)n2 * sizeof(uint64_t);
 }
 
 cudaError_t launch_sample(const SampleArgs& a, cudaStream_t st) {
     const uint32_t slots = a.slots ? a.slots : 1;
+    const uint32_t slice = a.slice ? a.slice : kSampleSlice;
+    if (sample_sort_mode(a.n_cta, a.kmax)) {
+        // any top_k: every slice sorted whole, ranked across slices, then the final kernel
+        if (slice % 256 || slice > kMaxSlice || a.kmax != slice || !a.wkeys || !a.wps || a.wide_stride < a.vocab ||
+            a.cand_stride < (uint64_t)a.n_cta * slice)
+            return cudaErrorInvalidValue;
+        SampleArgs s = a;
+        s.slice = slice;
+        cudaError_t e = launch_pdl(k_sample_cand_wide<true>, dim3(a.n_cta, slots), dim3(256), sample_sort_smem(slice),
+                                   st, s);
+        if (e != cudaSuccess) return e;
+        SampleArgs r = s;
+        r.trace = nullptr;
+        e = launch_pdl(k_sample_rank, dim3((a.n_cta * slice + 255) / 256, slots), dim3(256), 0, st, r);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(k_sample_final, dim3(1, slots), dim3(kFinalThreads), sample_final_smem(a.n_cta, a.kmax), st,
+                          s);
+    }
     const bool wide = a.slice > kSampleSlice;
     if (wide && (a.slice % 256 || a.slice > kMaxSlice || a.kmax > kMaxTopK)) return cudaErrorInvalidValue;
-    cudaError_t e = wide ? launch_pdl(k_sample_cand_wide, dim3(a.n_cta, slots), dim3(256), 0, st, a)
+    cudaError_t e = wide ? launch_pdl(k_sample_cand_wide<false>, dim3(a.n_cta, slots), dim3(256), 0, st, a)
                          : launch_pdl(k_sample_cand, dim3(a.n_cta, slots), dim3(256), 0, st, a);
     if (e != cudaSuccess) return e;
     return launch_pdl(k_sample_final, dim3(1, slots), dim3(kFinalThreads), sample_final_smem(a.n_cta, a.kmax), st, a);

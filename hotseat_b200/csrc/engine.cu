@@ -267,6 +267,10 @@ struct hs_scratch {
     uint64_t cap = 0;
     uint64_t *cand = nullptr, *argbuf = nullptr;
     uint32_t n_cta = 0, kmax = 0, slice = 0;  // sampler: candidate CTAs, keys kept per CTA, logits per CTA
+    // sampler sort mode (any top_k), allocated at its first use: every
+    // slice's keys in order, the top-k keys in order, their running sums
+    uint64_t *sort_cand = nullptr, *wkeys = nullptr;
+    float* wps = nullptr;
     cudaGraphExec_t g_fwd = nullptr, g_step = nullptr;
     const hs_kv* graph_kv = nullptr;
     uint32_t graph_kmax = 0;
@@ -279,6 +283,9 @@ struct hs_scratch {
     // tagged activations x, qkv, att, hb and attention records
     uint8_t* tok_mem = nullptr;
     uint64_t tok_launches = 0;      // token-kernel launches (tag refresh)
+    // token kernel: polling rounds before a reader of tagged entries gives up
+    // (HS_POLL_LIMIT at creation, a test knob; default 2^22)
+    uint32_t poll_limit = 1u << 22;
     uint64_t* trace = nullptr;      // device, 4 u64 per launch slot (trace mode only)
     uint64_t* trace_init = nullptr; // pinned host template: start=~0, rest 0
     uint32_t trace_slots = 0;
@@ -293,7 +300,7 @@ struct hs_scratch {
         cudaFreeHost(trace_init);
         for (void* p : {(void*)x, (void*)qkv, (void*)att, (void*)hb, (void*)logits, (void*)tokens, (void*)cand,
                         (void*)argbuf, (void*)sc_global, (void*)att_part, (void*)att_cnt, (void*)kv_tab,
-                        (void*)tok_mem})
+                        (void*)tok_mem, (void*)sort_cand, (void*)wkeys, (void*)wps})
             cudaFree(p);
     }
 };
@@ -584,6 +591,7 @@ int enqueue_token_kernel(hs_scratch* s, const hs_kv* kv) {
     // trace slots 0-2: this kernel and the two sampler kernels; then the
     // timeline, 20 words per phase interval (5 per layer, then the head)
     a.phase_ts = s->trace ? s->trace + 3 * 8 : nullptr;
+    a.poll_limit = s->poll_limit;
     HS_CUDA_TRY(launch_token_fast(m->tokp, a, s->st));
     return HS_OK;
 }
@@ -716,6 +724,13 @@ SampleArgs sample_args(hs_scratch* s) {
     a.n_cta = s->n_cta;
     a.kmax = s->kmax;
     a.slice = s->slice;
+    if (sample_sort_mode(s->n_cta, s->kmax)) {
+        a.cand = s->sort_cand;
+        a.cand_stride = (uint64_t)s->n_cta * s->slice;
+        a.wkeys = s->wkeys;
+        a.wps = s->wps;
+        a.wide_stride = s->m->cfg.vocab;
+    }
     a.trace = s->trace;
     a.trace_slot = s->launches_fwd;  // and launches_fwd + 1 for the second kernel
     return a;
@@ -772,7 +787,16 @@ int ctl_err(uint32_t err) {
     return fail(code, "device reported:" + why);
 }
 
-int check_ctl_err(hs_scratch* s) { return ctl_err(s->ctl_h->err); }
+// After a bounded wait ran out, split-attention items may have left their
+// last-CTA counters short; reset them so the next launch starts clean.
+int check_ctl_err(hs_scratch* s) {
+    const uint32_t err = s->ctl_h->err;
+    if ((err & ERR_TIMEOUT) && s->att_cnt) {
+        HS_CUDA_TRY(cudaMemsetAsync(s->att_cnt, 0, s->m->cfg.n_kv_heads * 4, s->st));
+        HS_CUDA_TRY(cudaStreamSynchronize(s->st));
+    }
+    return ctl_err(err);
+}
 
 int sync_ctl(hs_scratch* s) {
     HS_CUDA_TRY(cudaMemcpyAsync(s->ctl_h, s->ctl, sizeof(DevCtl), cudaMemcpyDeviceToHost, s->st));
@@ -780,16 +804,24 @@ int sync_ctl(hs_scratch* s) {
     return HS_OK;
 }
 
-int validate_cfg(const hs_scratch* s, const hs_sampler_cfg* cfg, uint32_t* kmax) {
+// Sampler width for a configuration: one candidate CTA sorts the whole
+// vocabulary (vocab <= 1024, any top_k); with several, top_k <= 64 keeps 64
+// keys per slice (list mode) and a larger top_k (or 0 = all) runs sort mode,
+// whose buffers are allocated here at its first use.
+int validate_cfg(hs_scratch* s, const hs_sampler_cfg* cfg, uint32_t* kmax) {
     const uint32_t vocab = s->m->cfg.vocab;
-    uint32_t k = cfg->top_k == 0 ? vocab : std::min(cfg->top_k, vocab);
-    if (cfg->temperature > 0.0f) {
-        if (k > kSampleSlice || (s->n_cta > 1 && k > kMaxTopK))
-            return fail(HS_E_UNSUPPORTED, "device sampler supports top_k <= " + std::to_string(kMaxTopK) +
-                                              " (or any top_k when vocab <= " + std::to_string(kSampleSlice) + ")");
-    }
+    const uint32_t k = cfg->top_k == 0 ? vocab : std::min(cfg->top_k, vocab);
     *kmax = s->n_cta > 1 ? kMaxTopK : kSampleSlice;
     if (*kmax > vocab) *kmax = std::min<uint32_t>(kSampleSlice, vocab);
+    if (cfg->temperature > 0.0f && s->n_cta > 1 && k > kMaxTopK) {
+        *kmax = s->slice;
+        if (!s->sort_cand) {
+            HS_CUDA_TRY(cudaSetDevice(s->m->device));
+            HS_CUDA_TRY(cudaMalloc(&s->sort_cand, (size_t)s->n_cta * s->slice * 8));
+            HS_CUDA_TRY(cudaMalloc(&s->wkeys, (size_t)vocab * 8));
+            HS_CUDA_TRY(cudaMalloc(&s->wps, (size_t)vocab * 4));
+        }
+    }
     return HS_OK;
 }
 
@@ -1261,6 +1293,8 @@ int hs_scratch_new(const hs_model* m, hs_scratch** out) {
         HS_CUDA_TRY(cudaMemset(s->tok_mem, 0, bytes));  // counter 0, tags 0 (no launch writes tag 0)
     }
     s->launches_fwd = m->tok ? 1 : c.n_layers * 5 + 1;
+    const char* penv = getenv("HS_POLL_LIMIT");
+    if (penv && *penv) s->poll_limit = (uint32_t)std::strtoul(penv, nullptr, 10);
     const char* tenv = getenv("HS_TRACE");
     if (tenv && tenv[0] == '1') {
         s->trace_slots = s->launches_fwd + 2 + (m->tok ? (20 * (5 * c.n_layers + 1) + 7) / 8 : 0);
@@ -1294,7 +1328,7 @@ int hs_scratch_trace(hs_scratch* s, uint64_t* out, uint64_t n_slots, uint64_t* u
 
 int hs_seq_launches_per_step(hs_scratch* s, uint32_t* out) {
     if (!s || !out) return fail(HS_E_ARG, "null argument");
-    *out = s->launches_fwd + 2;
+    *out = s->launches_fwd + (sample_sort_mode(s->n_cta, s->kmax) ? 3 : 2);
     return HS_OK;
 }
 
@@ -1604,6 +1638,10 @@ struct hs_batch {
     void** tab_h = nullptr;        // pinned staging for the three tables
     uint64_t *cand = nullptr, *argbuf = nullptr;
     uint32_t n_cta = 0, kmax_alloc = 0, slice = 0;
+    // sampler sort mode (any top_k), allocated at its first use, per slot:
+    // every slice's keys in order, the top-k keys in order, their running sums
+    uint64_t *sort_cand = nullptr, *wkeys = nullptr;
+    float* wps = nullptr;
     uint32_t* err = nullptr;       // GEMM error word (device)
     uint32_t err_h = 0;
     float* sc_global = nullptr;    // attention scores for long contexts [cap_slots][nh][max_ctx]
@@ -1629,7 +1667,8 @@ struct hs_batch {
         for (void* p : {(void*)x, (void*)part, (void*)logits, (void*)xn_hi, (void*)xn_lo, (void*)att_hi, (void*)att_lo,
                         (void*)hb_hi, (void*)hb_lo, (void*)ctl, (void*)tokens, (void*)tok_tab, (void*)kv_tab,
                         (void*)dirty_tab, (void*)track_tab, (void*)cand, (void*)argbuf, (void*)err,
-                        (void*)sc_global, (void*)att_part, (void*)att_cnt})
+                        (void*)sc_global, (void*)att_part, (void*)att_cnt, (void*)sort_cand, (void*)wkeys,
+                        (void*)wps})
             cudaFree(p);
     }
 };
@@ -1783,6 +1822,12 @@ SampleArgs batch_sample_args(hs_batch* b, uint32_t n, uint32_t kmax) {
     a.cand_stride = (uint64_t)b->n_cta * kmax;
     a.tok_tab = b->tok_tab;
     a.slice = b->slice;
+    if (sample_sort_mode(b->n_cta, kmax)) {
+        a.cand = b->sort_cand;
+        a.wkeys = b->wkeys;
+        a.wps = b->wps;
+        a.wide_stride = b->m->cfg.vocab;
+    }
     return a;
 }
 
@@ -1806,7 +1851,7 @@ int batch_graph(hs_batch* b, uint32_t n, uint32_t kmax, cudaGraphExec_t* out, ui
         sa.trace_slot = *launches;  // and the next slot for the second kernel
         cudaError_t e = launch_sample(sa, b->st);
         if (e != cudaSuccess) rc = fail(HS_E_CUDA, std::string("sampler launch: ") + cudaGetErrorString(e));
-        *launches += 2;
+        *launches += sample_sort_mode(b->n_cta, kmax) ? 3 : 2;
     }
     cudaError_t e = cudaStreamEndCapture(b->st, &g);
     if (rc) {
@@ -2035,12 +2080,17 @@ int hs_batch_seq_begin(hs_batch* b, hs_kv* const* kvs, uint32_t n, uint32_t* con
         for (uint64_t j = 0; j < n_tokens[i]; j++)
             if (tokens[i][j] >= vocab) return fail(HS_E_ARG, who + "token out of range");
         const uint32_t k = cfg[i].top_k == 0 ? vocab : std::min(cfg[i].top_k, vocab);
-        if (cfg[i].temperature > 0.0f && (k > kSampleSlice || (b->n_cta > 1 && k > kMaxTopK)))
-            return fail(HS_E_UNSUPPORTED, who + "device sampler supports top_k <= " + std::to_string(kMaxTopK));
+        if (cfg[i].temperature > 0.0f && b->n_cta > 1 && k > kMaxTopK) kmax = b->slice;  // sort mode
         if (!st[i].done && st[i].filled >= n_tokens[i])
             return fail(HS_E_STATE, who + "nothing to feed at the token boundary");
     }
     HS_CUDA_TRY(cudaSetDevice(m->device));
+    if (sample_sort_mode(b->n_cta, kmax) && !b->sort_cand) {
+        const uint64_t C = b->cap_slots;
+        HS_CUDA_TRY(cudaMalloc(&b->sort_cand, C * b->n_cta * b->slice * 8));
+        HS_CUDA_TRY(cudaMalloc(&b->wkeys, C * vocab * 8));
+        HS_CUDA_TRY(cudaMalloc(&b->wps, C * vocab * 4));
+    }
     int rc = batch_kv_tables(b, kvs, n);
     if (rc) return rc;
     for (uint32_t i = 0; i < n; i++) {

@@ -74,9 +74,17 @@ struct SampleArgs {
     uint32_t slots;
     uint64_t logits_stride, cand_stride;
     uint32_t* const* tok_tab;
-    // Logits per candidate CTA: 0 = kSampleSlice; else a multiple of it up to
-    // kMaxSlice, allowed only when kmax <= 64.
+    // Logits per candidate CTA: 0 = kSampleSlice; else a multiple of 256 up
+    // to kMaxSlice (kmax <= kMaxTopK, or sort mode).
     uint32_t slice;
+    // Sort mode (several candidate CTAs and kmax > kMaxTopK; kmax = the
+    // slice): every candidate CTA writes its whole slice in key order
+    // (cand_stride = n_cta x slice per slot), a rank kernel scatters the
+    // global top-k keys of each slot to wkeys + s*wide_stride in order, and
+    // the final kernel keeps its weights' running sums in wps + s*wide_stride.
+    uint64_t* wkeys;
+    float* wps;
+    uint64_t wide_stride;
 };
 
 int launch_dequant(uint32_t ty, const void* src, uint64_t n, void* dst, cudaStream_t st, int n_sm);
@@ -224,6 +232,9 @@ struct TokenArgs {
     uint64_t* trace;
     uint32_t trace_slot;
     uint64_t* phase_ts;      // trace mode: CTA 0's timeline per phase interval
+    // Polling rounds before a reader of tagged entries gives up and the
+    // launch reports ERR_TIMEOUT (the weight ring's waits are not affected).
+    uint32_t poll_limit;
 };
 struct TokenPlan {
     uint32_t grid = 0, slot_bytes = 0, nslot = 0;
@@ -243,6 +254,10 @@ cudaError_t launch_token_fast(const TokenPlan& p, const TokenArgs& a, cudaStream
 
 constexpr uint32_t kSampleSlice = 1024;  // logits per CTA of the candidate kernel
 constexpr uint32_t kMaxSlice = 4096;     // largest slice a candidate CTA takes
-constexpr uint32_t kMaxTopK = 64;        // top_k supported by the device sampler
+constexpr uint32_t kMaxTopK = 64;        // keys kept per candidate CTA in list mode
+
+// True when a sampler launch runs in sort mode (three kernels: slice sort,
+// rank, final), which serves any top_k, instead of per-slice top-kmax lists.
+__host__ __device__ inline bool sample_sort_mode(uint32_t n_cta, uint32_t kmax) { return n_cta > 1 && kmax > kMaxTopK; }
 
 }  // namespace hs

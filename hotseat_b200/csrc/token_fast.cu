@@ -232,7 +232,9 @@ __device__ __forceinline__ void phase_tiles(const TokenArgs& a, const Mat m, uin
                 tile_pass<T, CM, 2>(st, xp, part, m.k, vr0, vrows, n, r - r0, nrows, tg);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the slot
+        // this warp is done with the slot; after a ring timeout it stops
+        // releasing slots, so the producer stops filling them
+        if (lane == 0 && !dead) mbar_arrive(&empty[s]);
         if (++s == nslot) {
             s = 0;
             parity ^= 1;
@@ -297,8 +299,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
 
     if (warp == kConsumers / 32) {
         // ---------------------------------------------------------- producer
+        uint32_t it = 0;  // tiles put in flight
         if (lane == 0 && ok) {
-            uint32_t it = 0;
             bool dead = false;
             for (uint32_t l = 0; l <= a.n_layers && !dead; l++) {
                 for (uint32_t pi = 0; pi < (l < a.n_layers ? 4u : 1u) && !dead; pi++) {
@@ -324,6 +326,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
             }
         }
         __syncthreads();
+        // Every consumer is past the ring. A fill the consumers stopped
+        // waiting for (after a ring timeout) may still be landing: wait for
+        // the last fill of every slot before the CTA's shared memory goes.
+        if (lane == 0)
+            for (uint32_t s = 0; s < a.nslot && s < it; s++) {
+                const uint32_t last = s + (it - 1 - s) / a.nslot * a.nslot;
+                mbar_wait_bounded(&full[s], (last / a.nslot) & 1, kSpinLimit);
+            }
         tr.exit();
         return;
     }
@@ -394,8 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
     // `len` entries (even), run r = g * group + j (j < group) from src +
     // g * group_stride + j * run_stride to stage + r * len; 16-byte
     // asynchronous copies, re-issued for the pairs not yet tagged, all of a
-    // round in flight together. False after kPollLimit rounds (the staged
-    // values are then whatever arrived).
+    // round in flight together. False after a.poll_limit rounds (the staged
+    // values are then whatever arrived; no copy is left in flight).
     auto stage_tagged = [&](uint64_t* stage, const uint64_t* src, uint32_t n_runs, uint32_t len, uint32_t group,
                             size_t group_stride, size_t run_stride, uint32_t want) -> bool {
         const uint32_t per = len / 2, np = n_runs * per;
@@ -415,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
                 }
             attn::cp_commit();
             if (!pending) return true;
-            if (round >= attn::kPollLimit) {
+            if (round >= a.poll_limit) {
                 attn::cp_wait0();
                 return false;
             }
@@ -590,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
             if (ph == PH_QKV) {
                 // attention: the items of the S splits of this position
                 mark(0, tmark ? gtime() : 0);
-                const attn::TagIO tio{a.tqkv, a.tatt, a.trec, tag(l, TG_QKV), tag(l, TG_ATT)};
+                const attn::TagIO tio{a.tqkv, a.tatt, a.trec, tag(l, TG_QKV), tag(l, TG_ATT), a.poll_limit};
                 for (uint32_t i = b; i < n_items && !dead; i += G) {
                     attn::item<HD, attn_buf(HD), false>(a.attn, l, i / (nkv * hsp), (i / hsp) % nkv, i % hsp, 0, pos,
                                                         att_sm, i == b ? 1u : 0u, reader_combines,

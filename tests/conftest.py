@@ -65,3 +65,12 @@ def q05_gguf(fixture_dir):
     p = str(fixture_dir / "qwen05.gguf")
     write_synthetic_gguf(p, seed=1234, **QWEN05)
     return p
+
+
+@pytest.fixture(scope="session")
+def q15_gguf(fixture_dir):
+    """The Qwen2.5-1.5B-shape seeded model (28 layers, d 1536, 12/2 heads,
+    head_dim 128, ff 8960; Q6_K embedding, Q4_K weights)."""
+    p = str(fixture_dir / "qwen15.gguf")
+    write_synthetic_gguf(p, seed=1234, **QWEN15)
+    return p

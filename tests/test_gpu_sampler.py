@@ -125,9 +125,77 @@ def test_random_configs_match_the_oracle_full_vocab(big_scratch, trial):
         check(s, cfg, logits, hist, seed)
 
 
-def test_unsupported_top_k_is_an_error(big_scratch):
+@pytest.mark.parametrize("top_k", [0, 65, 100, 1000, 4097, 40000, 200000])
+def test_any_top_k_matches_the_oracle_full_vocab(big_scratch, top_k):
+    """top_k beyond the per-slice lists (sort mode): 0 (the whole
+    vocabulary, sampler.rs:120-124), just past 64, across a slice boundary
+    and past the vocabulary; with and without the nucleus cut, with exact
+    ties at the cut, the penalty on."""
     m, s = big_scratch
-    cfg = hs.SamplerCfg.default(top_k=0)
-    with pytest.raises(hs.HotseatError) as e:
-        hs.Sampler(cfg).sample(s, [])
-    assert e.value.code == hs.HS_E_UNSUPPORTED
+    rng = np.random.default_rng(700 + top_k % 997)
+    v = QWEN05["vocab"]
+    for trial in range(3):
+        logits = (rng.standard_normal(v) * float(rng.choice([0.3, 1.0, 3.0]))).astype(np.float32)
+        if trial == 1:
+            logits[rng.integers(0, v, 500)] = np.float32(np.sort(logits)[-max(2, min(top_k or v, v) // 2)])
+        hist = rng.integers(0, v, size=int(rng.integers(1, 300))).astype(np.uint32)
+        cfg = hs.SamplerCfg.default(temperature=float(rng.choice([0.7, 1.0, 1.5])), top_k=top_k,
+                                    top_p=float([0.95, 1.0, 0.5][trial]))
+        check(s, cfg, logits, hist, seed=trial)
+
+
+@pytest.mark.parametrize("top_k", [0, 65, 700, 1500])
+def test_any_top_k_matches_the_oracle_two_slices(tiny128_gguf, top_k):
+    """A 1500-token vocabulary: two 1024-logit candidate CTAs."""
+    m = hs.Model.load(tiny128_gguf, max_ctx=64)
+    s = m.scratch()
+    rng = np.random.default_rng(top_k)
+    v = 1500
+    for trial in range(4):
+        logits = (rng.standard_normal(v) * 2.0).astype(np.float32)
+        if trial % 2:
+            logits[rng.integers(0, v, 40)] = logits.max()
+        hist = rng.integers(0, v, size=20).astype(np.uint32)
+        cfg = hs.SamplerCfg.default(temperature=0.9, top_k=top_k, top_p=float([0.9, 1.0][trial % 2]))
+        check(s, cfg, logits, hist, seed=trial)
+
+
+def test_sequences_with_large_top_k_match_the_oracle(q05_gguf):
+    """Decode loops on the GPU-native path with top_k = 0 and 1000 (sort
+    mode inside the per-token graph): transcripts and RNG states equal the
+    CPU path's."""
+    rng = np.random.default_rng(5)
+    prompt = [int(t) for t in rng.integers(0, QWEN05["vocab"], size=12)]
+    m = hs.Model.load(q05_gguf, max_ctx=128, numeric=hs.NUMERIC_FAST)
+    o = ffi.Model(q05_gguf, max_ctx=128)
+    for top_k in (0, 1000):
+        cfg = hs.SamplerCfg.default(temperature=0.8, top_k=top_k, seed=3)
+        s = m.scratch()
+        toks, st, r = hs.run_seq(m, m.kv(), s, prompt, len(prompt), 10, cfg, hs.Rng.seed(3))
+        assert s.launches_per_step() == 4
+        want, _, orng = o.run_seq(o.new_kv(), prompt, 10, ffi.default_cfg(temperature=0.8, top_k=top_k, seed=3),
+                                  ffi.seeded_rng(3))
+        assert list(toks) == list(want), top_k
+        assert list(r.s) == list(orng.s) and r.draws == orng.draws
+
+
+def test_batch_with_mixed_top_k_matches_the_oracle(q05_gguf):
+    """One tensor-core batch whose sequences sample with top_k 0, 1000 and
+    40 and one greedy: the step graph runs sort mode for all of them; every
+    transcript and RNG state equals the CPU path's."""
+    rng = np.random.default_rng(8)
+    v = QWEN05["vocab"]
+    m = hs.Model.load(q05_gguf, max_ctx=128, numeric=hs.NUMERIC_TC)
+    o = ffi.Model(q05_gguf, max_ctx=128)
+    cases = [(0, 0.8), (1000, 1.0), (40, 0.8), (40, 0.0)]
+    prompts = [[int(t) for t in rng.integers(0, v, size=10 + 3 * i)] for i in range(len(cases))]
+    seqs = [dict(tokens=p, prompt_len=len(p), max_tokens=8, rng=hs.Rng.seed(20 + i),
+                 cfg=hs.SamplerCfg.default(temperature=t, top_k=k, seed=20 + i))
+            for i, (p, (k, t)) in enumerate(zip(prompts, cases))]
+    b = hs.Batch(m, len(seqs))
+    got = b.run_seqs([m.kv() for _ in seqs], seqs)
+    for i, (p, (k, t)) in enumerate(zip(prompts, cases)):
+        want, _, orng = o.run_seq(o.new_kv(), p, 8, ffi.default_cfg(temperature=t, top_k=k, seed=20 + i),
+                                  ffi.seeded_rng(20 + i))
+        assert list(got[i][0]) == list(want), i
+        assert list(got[i][2].s) == list(orng.s) and got[i][2].draws == orng.draws, i
