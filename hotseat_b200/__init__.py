@@ -84,6 +84,34 @@ class SeqState(C.Structure):
                 ("done", C.c_uint32), ("done_reason", C.c_uint32)]
 
 
+MIGRATE_MAX_ROUNDS = 34
+
+
+class MigrateOpts(C.Structure):
+    _fields_ = [("max_rounds", C.c_uint32), ("target_bytes", C.c_uint64), ("verify", C.c_uint32)]
+
+
+class MigrateRoundStat(C.Structure):
+    _fields_ = [("index", C.c_uint32), ("bytes", C.c_uint64), ("runs", C.c_uint64), ("ms", C.c_double),
+                ("tokens_during", C.c_uint64)]
+
+
+class MigrateReport(C.Structure):
+    _fields_ = [("rounds", MigrateRoundStat * MIGRATE_MAX_ROUNDS), ("n_rounds", C.c_uint32),
+                ("precopy_bytes", C.c_uint64), ("precopy_ms", C.c_double), ("park_us", C.c_double),
+                ("stw_us", C.c_double), ("stw_send_us", C.c_double), ("dest_resume_us", C.c_double),
+                ("final_bytes", C.c_uint64), ("live_bytes", C.c_uint64), ("filled", C.c_uint64),
+                ("tokens_total", C.c_uint64), ("kv_hash_src", C.c_uint64), ("kv_hash_dst", C.c_uint64),
+                ("verified", C.c_uint32), ("converged", C.c_uint32), ("stop_reason", C.c_char * 160)]
+
+    def as_dict(self):
+        d = {f: getattr(self, f) for f, _ in self._fields_ if f not in ("rounds", "stop_reason")}
+        d["rounds"] = [dict(index=r.index, bytes=r.bytes, runs=r.runs, ms=r.ms, tokens_during=r.tokens_during)
+                       for r in self.rounds[: self.n_rounds]]
+        d["stop_reason"] = self.stop_reason.decode(errors="replace")
+        return d
+
+
 _P = C.c_void_p
 _U64P = C.POINTER(C.c_uint64)
 _SIGS = {
@@ -103,6 +131,16 @@ _SIGS = {
     "hs_kv_harvest": (C.c_int, [_P, _P, C.c_uint64]),
     "hs_kv_disarm": (C.c_int, [_P]),
     "hs_kv_copy_runs": (C.c_int, [_P, _P, _P, C.c_uint64]),
+    "hs_kv_fingerprint": (C.c_int, [_P, _U64P]),
+    "hs_migrate_opts_default": (None, [C.POINTER(MigrateOpts)]),
+    "hs_migrate_begin": (C.c_int, [_P, _P, C.POINTER(MigrateOpts), C.c_uint64, C.c_uint64, C.c_uint64,
+                                   C.POINTER(_P)]),
+    "hs_migrate_round": (C.c_int, [_P, C.c_uint64, C.c_uint64, C.c_uint64, C.POINTER(C.c_int)]),
+    "hs_migrate_finish": (C.c_int, [_P, C.c_uint64, C.c_uint64, C.c_double, C.POINTER(MigrateReport)]),
+    "hs_migrate_free": (None, [_P]),
+    "hs_kv_peer_copy": (C.c_int, [_P, _P, _P, C.c_uint64, _P]),
+    "hs_kv_read_runs": (C.c_int, [_P, _P, C.c_uint64, _P, C.c_uint64]),
+    "hs_kv_write_runs": (C.c_int, [_P, _P, C.c_uint64, _P, C.c_uint64]),
     "hs_kv_live_ranges_between": (C.c_uint64, [C.POINTER(KvSpec), C.c_uint32, C.c_uint32, _P, C.c_uint64]),
     "hs_runs_to_byte_runs": (C.c_uint64, [_P, C.c_uint64, C.c_uint64, _P, C.c_uint64, _P, C.c_uint64]),
     "hs_scratch_new": (C.c_int, [_P, C.POINTER(_P)]),
@@ -285,9 +323,74 @@ class Kv:
     def disarm(self):
         _check(_lib.hs_kv_disarm(self._h))
 
+    @staticmethod
+    def _runs(runs):
+        return np.array([x for run in runs for x in run] or [0], dtype=np.uint64)
+
     def copy_runs_to(self, dst, runs):
-        r = np.array([x for run in runs for x in run] or [0], dtype=np.uint64)
+        """Blocking copy of byte runs into `dst` (same spec, any GPU)."""
+        r = self._runs(runs)
         _check(_lib.hs_kv_copy_runs(self._h, dst._h, _ptr(r), len(runs)))
+
+    def peer_copy(self, dst, runs, stream=None):
+        """Enqueue the copy of byte runs into `dst` on `stream` (a stream of
+        this region's GPU; None = this region's own stream); not waited for."""
+        r = self._runs(runs)
+        _check(_lib.hs_kv_peer_copy(self._h, dst._h, _ptr(r), len(runs), C.c_void_p(stream) if stream else None))
+
+    def read_runs(self, runs):
+        """The bytes of `runs` packed back to back (hs-wire send_page_bytes)."""
+        r = self._runs(runs)
+        out = np.zeros(max(1, sum(int(x[1]) for x in runs)), dtype=np.uint8)
+        _check(_lib.hs_kv_read_runs(self._h, _ptr(r), len(runs), _ptr(out), out.size))
+        return out[: sum(int(x[1]) for x in runs)]
+
+    def write_runs(self, runs, data):
+        """Scatter packed bytes into `runs` (hs-wire recv_page_bytes)."""
+        r = self._runs(runs)
+        d = np.ascontiguousarray(np.frombuffer(bytes(data), dtype=np.uint8))
+        _check(_lib.hs_kv_write_runs(self._h, _ptr(r), len(runs), _ptr(d) if d.size else None, d.size))
+
+
+class Migration:
+    """Pre-copy migration of a live sequence from KV region `src` to `dst`
+    (hs-worker migrate.rs migrate_out + migrate_in's checks): construction
+    runs the Hello checks and round 0; round() is one iterative round while
+    the sequence keeps decoding (False once the rounds stop); finish(), with
+    the decode loop parked, copies the residue and returns the report. The
+    sequence's tokens, SeqState and RNG are the caller's to hand over."""
+
+    def __init__(self, src, dst, filled, tokens_now, upper=None, max_rounds=8, target_bytes=1 << 20,
+                 verify=False):
+        o = MigrateOpts()
+        _lib.hs_migrate_opts_default(C.byref(o))
+        o.max_rounds, o.target_bytes, o.verify = max_rounds, target_bytes, 1 if verify else 0
+        h = C.c_void_p()
+        _check(_lib.hs_migrate_begin(src._h, dst._h, C.byref(o), filled, filled if upper is None else upper,
+                                     tokens_now, C.byref(h)))
+        self._h = h
+
+    def round(self, filled, tokens_now, upper=None):
+        """filled: positions known complete; upper: the last position the
+        decode loop may have written (filled when parked)."""
+        more = C.c_int()
+        _check(_lib.hs_migrate_round(self._h, filled, filled if upper is None else upper, tokens_now,
+                                     C.byref(more)))
+        return bool(more.value)
+
+    def finish(self, filled, tokens_total, park_us=0.0):
+        r = MigrateReport()
+        rc = _lib.hs_migrate_finish(self._h, filled, tokens_total, park_us, C.byref(r))
+        self.report = r.as_dict()
+        _check(rc)
+        return self.report
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.hs_migrate_free(self._h)
+            self._h = None
+
+    __del__ = close
 
 
 def live_ranges_between(spec, a, b):

@@ -247,9 +247,22 @@ struct hs_kv {
     uint32_t* tracking = nullptr;
     uint64_t fingerprint = 0;
     cudaStream_t st = nullptr;
+    int n_sm = 148;
+    // byte-run transfers: packed staging (grown on demand), the run table
+    // (pinned upload buffer and device copy) and the event after its last use
+    uint8_t* stage = nullptr;
+    uint64_t stage_cap = 0;
+    hs::XferRun *tab_h = nullptr, *tab_dev = nullptr;
+    uint64_t tab_cap = 0;
+    cudaEvent_t tab_ev = nullptr;
     ~hs_kv() {
         cudaSetDevice(device);
+        if (tab_ev) cudaEventSynchronize(tab_ev);
         if (st) cudaStreamDestroy(st);
+        if (tab_ev) cudaEventDestroy(tab_ev);
+        cudaFreeHost(tab_h);
+        cudaFree(tab_dev);
+        cudaFree(stage);
         cudaFree(base);
         cudaFree(dirty);
         cudaFree(harvest_buf);
@@ -1087,7 +1100,15 @@ int hs_kv_alloc(const hs_model* m, uint32_t layout, uint32_t page_size, hs_kv** 
     HS_CUDA_TRY(cudaMalloc(&kv->harvest_buf, kv->n_words * 8));
     HS_CUDA_TRY(cudaMalloc(&kv->tracking, 4));
     HS_CUDA_TRY(cudaMemset(kv->tracking, 0, 4));
+    HS_CUDA_TRY(cudaEventCreateWithFlags(&kv->tab_ev, cudaEventDisableTiming));
+    kv->n_sm = m->n_sm;
     *out = kv.release();
+    return HS_OK;
+}
+
+int hs_kv_fingerprint(const hs_kv* kv, uint64_t* out) {
+    if (!kv || !out) return fail(HS_E_ARG, "null argument");
+    *out = kv->fingerprint;
     return HS_OK;
 }
 
@@ -1220,33 +1241,152 @@ uint64_t hs_runs_to_byte_runs(const uint64_t* words, uint64_t n_pages, uint64_t 
     return merged.size();
 }
 
-int hs_kv_copy_runs(hs_kv* src, hs_kv* dst, const uint64_t* runs, uint64_t n_runs) {
-    if (!src || !dst || (!runs && n_runs)) return fail(HS_E_ARG, "null argument");
+}  // extern "C"
+
+namespace hs {
+namespace {
+
+// Runs (off, len pairs) inside a region of `bytes` bytes; their total.
+int check_runs(const uint64_t* runs, uint64_t n_runs, uint64_t bytes, uint64_t* total) {
+    if (!runs && n_runs) return fail(HS_E_ARG, "null run list");
+    uint64_t t = 0;
+    for (uint64_t i = 0; i < n_runs; i++) {
+        if (runs[2 * i] > bytes || runs[2 * i + 1] > bytes - runs[2 * i])
+            return fail(HS_E_ARG, "run " + std::to_string(i) + " outside the KV region");
+        t += runs[2 * i + 1];
+    }
+    *total = t;
+    return HS_OK;
+}
+
+// The transfer table of `runs`, split into pieces of at most kXferPiece
+// bytes: mode 0 region -> packed, 1 packed -> region, 2 region -> region.
+std::vector<XferRun> xfer_table(const uint64_t* runs, uint64_t n_runs, int mode) {
+    std::vector<XferRun> t;
+    uint64_t packed = 0;
+    for (uint64_t i = 0; i < n_runs; i++) {
+        const uint64_t off = runs[2 * i], len = runs[2 * i + 1];
+        for (uint64_t p = 0; p < len; p += kXferPiece) {
+            const uint64_t n = std::min<uint64_t>(kXferPiece, len - p);
+            const uint64_t r = off + p, k = packed + p;
+            t.push_back(mode == 0 ? XferRun{r, k, n} : mode == 1 ? XferRun{k, r, n} : XferRun{r, r, n});
+        }
+        packed += len;
+    }
+    return t;
+}
+
+// Upload `t` into kv's device table on `st` and launch the copy there; the
+// table buffers are reused only after the event that follows this kernel.
+int launch_table(hs_kv* kv, const std::vector<XferRun>& t, const uint8_t* src, uint8_t* dst, cudaStream_t st) {
+    if (t.empty()) return HS_OK;
+    HS_CUDA_TRY(cudaEventSynchronize(kv->tab_ev));
+    if (t.size() > kv->tab_cap) {
+        cudaFreeHost(kv->tab_h);
+        cudaFree(kv->tab_dev);
+        kv->tab_h = nullptr;
+        kv->tab_dev = nullptr;
+        kv->tab_cap = 0;
+        const uint64_t cap = std::max<uint64_t>(t.size(), 256);
+        HS_CUDA_TRY(cudaMallocHost(&kv->tab_h, cap * sizeof(XferRun)));
+        HS_CUDA_TRY(cudaMalloc(&kv->tab_dev, cap * sizeof(XferRun)));
+        kv->tab_cap = cap;
+    }
+    std::memcpy(kv->tab_h, t.data(), t.size() * sizeof(XferRun));
+    HS_CUDA_TRY(cudaMemcpyAsync(kv->tab_dev, kv->tab_h, t.size() * sizeof(XferRun), cudaMemcpyHostToDevice, st));
+    HS_CUDA_TRY(launch_copy_runs(src, dst, kv->tab_dev, (uint32_t)t.size(), kv->n_sm, st));
+    HS_CUDA_TRY(cudaEventRecord(kv->tab_ev, st));
+    return HS_OK;
+}
+
+int ensure_stage(hs_kv* kv, uint64_t bytes) {
+    if (bytes <= kv->stage_cap) return HS_OK;
+    HS_CUDA_TRY(cudaStreamSynchronize(kv->st));
+    cudaFree(kv->stage);
+    kv->stage = nullptr;
+    kv->stage_cap = 0;
+    HS_CUDA_TRY(cudaMalloc(&kv->stage, bytes));
+    kv->stage_cap = bytes;
+    return HS_OK;
+}
+
+}  // namespace
+}  // namespace hs
+
+extern "C" {
+
+int hs_kv_read_runs(hs_kv* kv, const uint64_t* runs, uint64_t n_runs, void* host, uint64_t host_bytes) {
+    if (!kv) return fail(HS_E_ARG, "null KV region");
+    uint64_t total;
+    int rc = check_runs(runs, n_runs, kv->bytes, &total);
+    if (rc) return rc;
+    if (total && !host) return fail(HS_E_ARG, "null host buffer");
+    if (host_bytes < total) return fail(HS_E_ARG, "host buffer smaller than the runs' bytes");
+    if (!total) return HS_OK;
+    HS_CUDA_TRY(cudaSetDevice(kv->device));
+    if ((rc = ensure_stage(kv, total))) return rc;
+    if ((rc = launch_table(kv, xfer_table(runs, n_runs, 0), reinterpret_cast<const uint8_t*>(kv->base), kv->stage,
+                           kv->st)))
+        return rc;
+    HS_CUDA_TRY(cudaMemcpyAsync(host, kv->stage, total, cudaMemcpyDeviceToHost, kv->st));
+    HS_CUDA_TRY(cudaStreamSynchronize(kv->st));
+    return HS_OK;
+}
+
+int hs_kv_write_runs(hs_kv* kv, const uint64_t* runs, uint64_t n_runs, const void* host, uint64_t host_bytes) {
+    if (!kv) return fail(HS_E_ARG, "null KV region");
+    uint64_t total;
+    int rc = check_runs(runs, n_runs, kv->bytes, &total);
+    if (rc) return rc;
+    if (total && !host) return fail(HS_E_ARG, "null host buffer");
+    if (host_bytes < total) return fail(HS_E_ARG, "host buffer smaller than the runs' bytes");
+    if (!total) return HS_OK;
+    HS_CUDA_TRY(cudaSetDevice(kv->device));
+    if ((rc = ensure_stage(kv, total))) return rc;
+    HS_CUDA_TRY(cudaMemcpyAsync(kv->stage, host, total, cudaMemcpyHostToDevice, kv->st));
+    if ((rc = launch_table(kv, xfer_table(runs, n_runs, 1), kv->stage, reinterpret_cast<uint8_t*>(kv->base),
+                           kv->st)))
+        return rc;
+    HS_CUDA_TRY(cudaStreamSynchronize(kv->st));
+    return HS_OK;
+}
+
+int hs_kv_peer_copy(hs_kv* src, hs_kv* dst, const uint64_t* runs, uint64_t n_runs, void* stream) {
+    if (!src || !dst) return fail(HS_E_ARG, "null KV region");
     if (std::memcmp(&src->spec, &dst->spec, sizeof(hs_kv_spec)) != 0)
         return fail(HS_E_ARG, "KV specs differ between source and destination");
-    for (uint64_t i = 0; i < n_runs; i++)
-        if (runs[2 * i] > src->bytes || runs[2 * i + 1] > src->bytes - runs[2 * i])
-            return fail(HS_E_ARG, "run outside the KV region");
-    HS_CUDA_TRY(cudaSetDevice(dst->device));
-    if (src->device != dst->device) {
+    uint64_t total;
+    int rc = check_runs(runs, n_runs, src->bytes, &total);
+    if (rc || !total) return rc;
+    cudaStream_t st = stream ? reinterpret_cast<cudaStream_t>(stream) : src->st;
+    HS_CUDA_TRY(cudaSetDevice(src->device));
+    bool direct = src->device == dst->device;
+    if (!direct) {
         int can = 0;
-        HS_CUDA_TRY(cudaDeviceCanAccessPeer(&can, dst->device, src->device));
+        HS_CUDA_TRY(cudaDeviceCanAccessPeer(&can, src->device, dst->device));
         if (can) {
-            cudaError_t e = cudaDeviceEnablePeerAccess(src->device, 0);
+            cudaError_t e = cudaDeviceEnablePeerAccess(dst->device, 0);
             if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
                 return fail(HS_E_CUDA, std::string("enable peer access: ") + cudaGetErrorString(e));
             cudaGetLastError();
+            direct = true;
         }
     }
-    for (uint64_t i = 0; i < n_runs; i++) {
-        uint8_t* s = reinterpret_cast<uint8_t*>(src->base) + runs[2 * i];
-        uint8_t* d = reinterpret_cast<uint8_t*>(dst->base) + runs[2 * i];
-        if (src->device == dst->device)
-            HS_CUDA_TRY(cudaMemcpyAsync(d, s, runs[2 * i + 1], cudaMemcpyDeviceToDevice, dst->st));
-        else
-            HS_CUDA_TRY(cudaMemcpyPeerAsync(d, dst->device, s, src->device, runs[2 * i + 1], dst->st));
-    }
-    HS_CUDA_TRY(cudaStreamSynchronize(dst->st));
+    if (direct)  // one kernel: local reads, stores into the destination (over NVLink across GPUs)
+        return launch_table(src, xfer_table(runs, n_runs, 2), reinterpret_cast<const uint8_t*>(src->base),
+                            reinterpret_cast<uint8_t*>(dst->base), st);
+    for (uint64_t i = 0; i < n_runs; i++)  // no peer mapping: the driver's peer copies
+        HS_CUDA_TRY(cudaMemcpyPeerAsync(reinterpret_cast<uint8_t*>(dst->base) + runs[2 * i], dst->device,
+                                        reinterpret_cast<const uint8_t*>(src->base) + runs[2 * i], src->device,
+                                        runs[2 * i + 1], st));
+    return HS_OK;
+}
+
+int hs_kv_copy_runs(hs_kv* src, hs_kv* dst, const uint64_t* runs, uint64_t n_runs) {
+    int rc = hs_kv_peer_copy(src, dst, runs, n_runs, nullptr);
+    if (rc) return rc;
+    HS_CUDA_TRY(cudaSetDevice(src->device));
+    HS_CUDA_TRY(cudaStreamSynchronize(src->st));
     return HS_OK;
 }
 
@@ -1598,21 +1738,25 @@ int hs_kv_harvest(hs_kv* kv, uint64_t* words, uint64_t n_words) {
     return HS_OK;
 }
 
+// Arm and disarm run on the region's own stream and are waited for; a
+// decode step may be in flight on another stream meanwhile (its appends are
+// marked once the flag is set).
 int hs_kv_arm(hs_kv* kv) {
     if (!kv) return fail(HS_E_ARG, "null argument");
     HS_CUDA_TRY(cudaSetDevice(kv->device));
-    HS_CUDA_TRY(cudaMemset(kv->dirty, 0, kv->n_words * 8));
-    const uint32_t one = 1;
-    HS_CUDA_TRY(cudaMemcpy(kv->tracking, &one, 4, cudaMemcpyHostToDevice));
+    HS_CUDA_TRY(cudaMemsetAsync(kv->dirty, 0, kv->n_words * 8, kv->st));
+    HS_CUDA_TRY(cudaMemsetAsync(kv->tracking, 0, 4, kv->st));
+    HS_CUDA_TRY(cudaMemsetAsync(kv->tracking, 1, 1, kv->st));  // tracking = 1 (little-endian u32)
+    HS_CUDA_TRY(cudaStreamSynchronize(kv->st));
     return HS_OK;
 }
 
 int hs_kv_disarm(hs_kv* kv) {
     if (!kv) return fail(HS_E_ARG, "null argument");
     HS_CUDA_TRY(cudaSetDevice(kv->device));
-    const uint32_t zero = 0;
-    HS_CUDA_TRY(cudaMemcpy(kv->tracking, &zero, 4, cudaMemcpyHostToDevice));
-    HS_CUDA_TRY(cudaMemset(kv->dirty, 0, kv->n_words * 8));
+    HS_CUDA_TRY(cudaMemsetAsync(kv->tracking, 0, 4, kv->st));
+    HS_CUDA_TRY(cudaMemsetAsync(kv->dirty, 0, kv->n_words * 8, kv->st));
+    HS_CUDA_TRY(cudaStreamSynchronize(kv->st));
     return HS_OK;
 }
 

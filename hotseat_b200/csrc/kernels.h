@@ -89,6 +89,15 @@ struct SampleArgs {
 
 int launch_dequant(uint32_t ty, const void* src, uint64_t n, void* dst, cudaStream_t st, int n_sm);
 
+// KV byte-run transfers (kv_xfer.cu): `n` runs of at most kXferPiece bytes,
+// src + src_off -> dst + dst_off; dst may be another GPU's peer-mapped memory.
+struct XferRun {
+    uint64_t src_off, dst_off, len;
+};
+constexpr uint64_t kXferPiece = 64 * 1024;
+cudaError_t launch_copy_runs(const uint8_t* src, uint8_t* dst, const XferRun* runs, uint32_t n, int n_sm,
+                             cudaStream_t st);
+
 // Launchers (PDL attribute set; may be captured in a graph).
 cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_t st);
 cudaError_t launch_attention(uint32_t head_dim, uint32_t nh, size_t smem, const AttnArgs& a, cudaStream_t st);

@@ -96,6 +96,9 @@ typedef struct {
  * PageSet's word/bit format (hs-track pageset.rs:10-34). */
 int hs_kv_alloc(const hs_model* m, uint32_t layout, uint32_t page_size, hs_kv** out);
 int hs_kv_info(const hs_kv* kv, hs_kv_spec* spec, uint64_t* bytes, uint32_t* page_size, uint64_t* n_pages);
+/* The fingerprint of the model the region was allocated for (the Hello
+ * field model_fingerprint, hs-wire lib.rs / migrate.rs:250-258). */
+int hs_kv_fingerprint(const hs_kv* kv, uint64_t* out);
 void hs_kv_free(hs_kv* kv);
 /* Byte-range staging between the device region and host memory (the hs-wire
  * send_page_bytes / recv_page_bytes path, hs-wire lib.rs:339-396). */
@@ -109,10 +112,81 @@ int hs_kv_hash(hs_kv* kv, uint32_t n_pos, uint64_t* out);
 int hs_kv_arm(hs_kv* kv);
 int hs_kv_harvest(hs_kv* kv, uint64_t* words, uint64_t n_words);
 int hs_kv_disarm(hs_kv* kv);
-/* Copy byte runs (off, len pairs) from one KV region to another, over
- * NVLink when the two live on different GPUs (the pre-copy data path of
- * hs-worker migrate.rs:234-473 without the TCP hop). Specs must match. */
+/* Run-list staging for the hs-wire TCP path (hs-wire lib.rs:338-396,
+ * Conn::send_page_bytes / recv_page_bytes): the bytes of `runs` ((off, len)
+ * pairs) packed back to back in run order, moved between the device region
+ * and `host` (host_bytes >= the runs' total) in one stream-ordered pass: a
+ * gather (or scatter) kernel over a device staging buffer and one copy each
+ * way. Both return once the bytes are in place. */
+int hs_kv_read_runs(hs_kv* kv, const uint64_t* runs, uint64_t n_runs, void* host, uint64_t host_bytes);
+int hs_kv_write_runs(hs_kv* kv, const uint64_t* runs, uint64_t n_runs, const void* host, uint64_t host_bytes);
+/* Copy byte runs from one KV region to another (the pre-copy data path of
+ * hs-worker migrate.rs:234-473 without the TCP hop): one kernel on the
+ * source's GPU reads the runs and stores them into the destination, through
+ * its peer mapping over NVLink when it lives on another GPU. Enqueued on
+ * `stream` (a cudaStream_t of the source's device; NULL = the source
+ * region's own stream) and not waited for. The copy sees the source bytes as
+ * of its turn on `stream`: to take a residue after the decode loop's last
+ * append, park the loop first or make `stream` wait on an event recorded
+ * after it. Specs must match. */
+int hs_kv_peer_copy(hs_kv* src, hs_kv* dst, const uint64_t* runs, uint64_t n_runs, void* stream);
+/* hs_kv_peer_copy on the source region's stream, waited for. */
 int hs_kv_copy_runs(hs_kv* src, hs_kv* dst, const uint64_t* runs, uint64_t n_runs);
+
+/* ---- pre-copy migration (replaces hs-worker migrate.rs:45-166, 234-630) --
+ * The source half of migrate_out with the destination's Hello checks, for
+ * two device KV regions on one node (the bytes move by hs_kv_copy_runs).
+ * The decode loop and the sequence's FinalState stay the caller's:
+ *   hs_migrate_begin   fingerprint / KV spec / page size must match (else
+ *                      HS_E_STATE "destination refused: ..." before any byte
+ *                      moves, migrate.rs:486-518); arms the source; round 0
+ *                      copies every live byte of positions [0, upper + 1)
+ *   hs_migrate_round   while the sequence keeps decoding: the pages dirtied
+ *                      since the last harvest, clipped to [low, upper + 1);
+ *                      *more = 0 once the rounds stop (nothing left, a round
+ *                      within target_bytes, not shrinking, or max_rounds;
+ *                      migrate.rs:293-346); the next round starts at
+ *                      low = filled.
+ *   `filled`: a count of positions known complete (seen at a token boundary
+ *   at or before the call); `upper`: the last position the decode loop may
+ *   have written by the call (filled when it is parked; filled + the steps
+ *   in flight otherwise). The reference reads one value after its harvest
+ *   for both (migrate.rs:307-313).
+ *   hs_migrate_finish  with the decode loop parked at `filled` (no append in
+ *                      flight): the residue, then with verify both KV hashes
+ *                      inside the window (HS_E_STATE if they differ: keep
+ *                      decoding on the source); fills the report. park_us is
+ *                      the caller's measured park time, added to stw_us.
+ * tokens_now / tokens_total: the sequence's token count, for tokens_during. */
+#define HS_MIGRATE_MAX_ROUNDS 34
+typedef struct {
+    uint32_t max_rounds;   /* Opts::max_rounds (8); at most HS_MIGRATE_MAX_ROUNDS - 2 */
+    uint64_t target_bytes; /* Opts::target_bytes (1 MiB) */
+    uint32_t verify;       /* Opts::verify (0) */
+} hs_migrate_opts;
+typedef struct { /* RoundStat, migrate.rs:70-78 */
+    uint32_t index;
+    uint64_t bytes, runs;
+    double ms;
+    uint64_t tokens_during;
+} hs_migrate_round_stat;
+typedef struct { /* Report, migrate.rs:80-110 (tracker fields: the device bitmap has no faults) */
+    hs_migrate_round_stat rounds[HS_MIGRATE_MAX_ROUNDS];
+    uint32_t n_rounds;
+    uint64_t precopy_bytes;
+    double precopy_ms, park_us, stw_us, stw_send_us, dest_resume_us;
+    uint64_t final_bytes, live_bytes, filled, tokens_total, kv_hash_src, kv_hash_dst;
+    uint32_t verified, converged;
+    char stop_reason[160];
+} hs_migrate_report;
+typedef struct hs_migration hs_migration;
+void hs_migrate_opts_default(hs_migrate_opts* o);
+int hs_migrate_begin(hs_kv* src, hs_kv* dst, const hs_migrate_opts* opts, uint64_t filled, uint64_t upper,
+                     uint64_t tokens_now, hs_migration** out);
+int hs_migrate_round(hs_migration* g, uint64_t filled, uint64_t upper, uint64_t tokens_now, int* more);
+int hs_migrate_finish(hs_migration* g, uint64_t filled, uint64_t tokens_total, double park_us,
+                      hs_migrate_report* out);
+void hs_migrate_free(hs_migration* g);
 
 /* Host-only mirrors of the reference's range logic (no device needed).
  * Output is (off, len) pairs; return value is the number of pairs, which may

@@ -161,41 +161,53 @@ def test_any_top_k_matches_the_oracle_two_slices(tiny128_gguf, top_k):
 
 
 def test_sequences_with_large_top_k_match_the_oracle(q05_gguf):
-    """Decode loops on the GPU-native path with top_k = 0 and 1000 (sort
-    mode inside the per-token graph): transcripts and RNG states equal the
-    CPU path's."""
+    """Decode loops with top_k = 0 and 1000 (sort mode inside the per-token
+    graph) on the bit-exact numeric path: transcripts and RNG states equal
+    the CPU path's. (Over the whole vocabulary the pick depends on running
+    sums of ~150k nearly equal weights, so only bit-identical logits give
+    identical transcripts; the GPU-native paths are held to the sampler's
+    exactness on their own logits by the tests above.)"""
     rng = np.random.default_rng(5)
     prompt = [int(t) for t in rng.integers(0, QWEN05["vocab"], size=12)]
-    m = hs.Model.load(q05_gguf, max_ctx=128, numeric=hs.NUMERIC_FAST)
+    m = hs.Model.load(q05_gguf, max_ctx=128, numeric=hs.NUMERIC_REFERENCE)
     o = ffi.Model(q05_gguf, max_ctx=128)
     for top_k in (0, 1000):
         cfg = hs.SamplerCfg.default(temperature=0.8, top_k=top_k, seed=3)
         s = m.scratch()
         toks, st, r = hs.run_seq(m, m.kv(), s, prompt, len(prompt), 10, cfg, hs.Rng.seed(3))
-        assert s.launches_per_step() == 4
+        assert s.launches_per_step() == 24 * 5 + 1 + 3
         want, _, orng = o.run_seq(o.new_kv(), prompt, 10, ffi.default_cfg(temperature=0.8, top_k=top_k, seed=3),
                                   ffi.seeded_rng(3))
         assert list(toks) == list(want), top_k
         assert list(r.s) == list(orng.s) and r.draws == orng.draws
 
 
-def test_batch_with_mixed_top_k_matches_the_oracle(q05_gguf):
+def test_batch_with_mixed_top_k(q05_gguf):
     """One tensor-core batch whose sequences sample with top_k 0, 1000 and
-    40 and one greedy: the step graph runs sort mode for all of them; every
-    transcript and RNG state equals the CPU path's."""
+    40 and one greedy: the step graph runs sort mode for all of them. Every
+    sequence equals itself decoded alone (tokens, RNG), and the top_k 40 and
+    greedy ones equal the CPU path's transcripts."""
     rng = np.random.default_rng(8)
     v = QWEN05["vocab"]
     m = hs.Model.load(q05_gguf, max_ctx=128, numeric=hs.NUMERIC_TC)
     o = ffi.Model(q05_gguf, max_ctx=128)
     cases = [(0, 0.8), (1000, 1.0), (40, 0.8), (40, 0.0)]
     prompts = [[int(t) for t in rng.integers(0, v, size=10 + 3 * i)] for i in range(len(cases))]
-    seqs = [dict(tokens=p, prompt_len=len(p), max_tokens=8, rng=hs.Rng.seed(20 + i),
-                 cfg=hs.SamplerCfg.default(temperature=t, top_k=k, seed=20 + i))
-            for i, (p, (k, t)) in enumerate(zip(prompts, cases))]
-    b = hs.Batch(m, len(seqs))
-    got = b.run_seqs([m.kv() for _ in seqs], seqs)
-    for i, (p, (k, t)) in enumerate(zip(prompts, cases)):
-        want, _, orng = o.run_seq(o.new_kv(), p, 8, ffi.default_cfg(temperature=t, top_k=k, seed=20 + i),
+
+    def seqs():
+        return [dict(tokens=p, prompt_len=len(p), max_tokens=8, rng=hs.Rng.seed(20 + i),
+                     cfg=hs.SamplerCfg.default(temperature=t, top_k=k, seed=20 + i))
+                for i, (p, (k, t)) in enumerate(zip(prompts, cases))]
+
+    b = hs.Batch(m, len(cases))
+    got = b.run_seqs([m.kv() for _ in cases], seqs())
+    assert b.launches_per_step() == 24 * 7 + 2 + 3
+    for i, q in enumerate(seqs()):
+        alone = hs.Batch(m, 1).run_seqs([m.kv()], [q])[0]
+        assert list(got[i][0]) == list(alone[0]) and list(got[i][2].s) == list(alone[2].s), i
+    for i in (2, 3):
+        k, t = cases[i]
+        want, _, orng = o.run_seq(o.new_kv(), prompts[i], 8, ffi.default_cfg(temperature=t, top_k=k, seed=20 + i),
                                   ffi.seeded_rng(20 + i))
         assert list(got[i][0]) == list(want), i
         assert list(got[i][2].s) == list(orng.s) and got[i][2].draws == orng.draws, i
