@@ -361,6 +361,30 @@ def bench_batch1(hs, torch, dist, path, local, world, args):
     return res
 
 
+def bench_extra(q05_path):
+    """The other configurations, timed on the device (one GPU):
+    c3 - Qwen2.5-1.5B shape, 16 sequences x 2048-token prefill (tensor-core
+         roofline: 2 x weights x tokens FLOPs) then 512 greedy steps at batch
+         16 (HBM roofline);
+    c4 - Q4_K/Q6_K dequantisation of 4864x896, 896x4864 and 151936x896
+         tensors (L2 flushed between launches), and GQA decode attention at
+         1k-32k context, batch 1 and 64 (HBM roofline)."""
+    from hotseat_b200 import microbench as mb
+    out = {}
+    pre, dec = mb.bench_prefill()
+    out["c3"] = {"workload": "qwen2.5-1.5b-shape: 16 x 2048-token prefill, then 512 greedy steps at batch 16",
+                 "prefill": {k: pre[k] for k in ("ms", "tok/s", "gemm_TFLOP/s", "peak_TFLOP/s", "frac", "peak_source",
+                                                 "note")},
+                 "decode": {k: dec[k] for k in ("ms", "tok/s", "GB/s", "frac", "generated", "note")}}
+    out["c4"] = {
+        "dequant": [{k: r[k] for k in ("type", "shape", "us", "GB/s", "frac")} for r in mb.bench_dequant(q05_path=q05_path)],
+        "attention": [{k: r[k] for k in ("batch", "context", "us_per_layer", "GB/s", "frac")}
+                      for r in mb.bench_attention(q05_path=q05_path)],
+        "peak_GB/s": mb._peak()[0],
+    }
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -369,6 +393,8 @@ def main():
     ap.add_argument("--impl", default="hotseat", choices=["hotseat", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch1", action="store_true", help="skip the batch-1 items")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the 1.5B prefill/decode (c3) and kernel microbenchmark (c4) sub-objects")
     ap.add_argument("--profile-step", choices=["batch64", "batch1"],
                     help="reach the post-prompt state, run ONE decode step inside the NVTX range 'decode_step', exit")
     args = ap.parse_args()
@@ -402,6 +428,9 @@ def main():
         if args.profile_step:
             return
         b1 = None if args.no_batch1 else bench_batch1(hs, torch, dist, path, local, world, args)
+        extra = {}
+        if world == 1 and not args.no_extra:
+            extra = bench_extra(path)
         if rank == 0:
             peaks = {}
             try:
@@ -451,6 +480,7 @@ def main():
                                   "e2e": b1["e2e_value"],
                                   "roofline": {"achieved": b1_ach, "peak": peak, "unit": "GB/s",
                                                "frac": b1_ach / peak, "bytes_per_token": b1_bytes_per_token()}}
+            line.update(extra)
             print(json.dumps(line), flush=True)
     finally:
         try:

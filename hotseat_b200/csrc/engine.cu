@@ -2105,7 +2105,7 @@ int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out) {
     HS_CUDA_TRY(cudaMallocHost(&b->tab_h, (size_t)3 * C * sizeof(void*)));
     const char* tenv = getenv("HS_TRACE");
     if (tenv && tenv[0] == '1') {
-        b->trace_slots = c.n_layers * 7 + 4;
+        b->trace_slots = c.n_layers * 8 + 5;  // prefill: 8 launches a layer; decode: 7 + norm, head, sampler
         HS_CUDA_TRY(cudaMalloc(&b->trace, (size_t)b->trace_slots * 64));
         HS_CUDA_TRY(cudaMallocHost(&b->trace_init, (size_t)b->trace_slots * 64));
         for (uint32_t i = 0; i < b->trace_slots; i++) {

@@ -126,15 +126,19 @@ def block_bytes(t):
     return {12: 144, 14: 210, 13: 176, 8: 34, 6: 22}[t]
 
 
-def bench_dequant(reps=10):
+def bench_dequant(reps=10, q05_path=None):
+    """Returns one record per tensor; q05_path: an existing 0.5B-shape file
+    (seed 1234) to read the Q4_K/Q6_K tensors from."""
     import torch
     import hotseat_b200 as hs
     peak, src = _peak()
     td = tempfile.mkdtemp(prefix="hsmicro")
-    a = os.path.join(td, "q6.gguf")
+    a = q05_path or os.path.join(td, "q6.gguf")
     b = os.path.join(td, "q4.gguf")
-    write_synthetic_gguf(a, seed=1234, **QWEN05)
+    if not q05_path:
+        write_synthetic_gguf(a, seed=1234, **QWEN05)
     write_synthetic_gguf(b, seed=1234, embd_type=12, **dict(QWEN05, n_layers=1))
+    out = []
     cases = [(a, "blk.0.ffn_gate.weight", "4864x896"), (a, "blk.0.ffn_down.weight", "896x4864"),
              (b, "token_embd.weight", "151936x896"), (a, "token_embd.weight", "151936x896")]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
@@ -160,12 +164,13 @@ def bench_dequant(reps=10):
         us = 1000.0 * float(np.median(ms))
         moved = nbytes + 2 * n
         gbs = moved / us / 1e3
-        print(json.dumps({"bench": "dequant", "type": {12: "Q4_K", 14: "Q6_K"}[t], "shape": shape,
-                          "bytes": moved, "us": us, "GB/s": gbs, "frac": gbs / peak, "peak": peak,
-                          "peak_source": src, "l2": "flushed between launches"}), flush=True)
-    for p in (a, b):
+        out.append({"bench": "dequant", "type": {12: "Q4_K", 14: "Q6_K"}[t], "shape": shape,
+                    "bytes": moved, "us": us, "GB/s": gbs, "frac": gbs / peak, "peak": peak,
+                    "peak_source": src, "l2": "flushed between launches"})
+    for p in ((b,) if q05_path else (a, b)):
         os.remove(p)
     os.rmdir(td)
+    return out
 
 
 def _att_times(trace, per_layer, att_slot, layers):
@@ -177,13 +182,18 @@ def _att_times(trace, per_layer, att_slot, layers):
     return float(np.mean(out))
 
 
-def bench_attention(ctxs=(1024, 4096, 16384, 32767)):
+def bench_attention(ctxs=(1024, 4096, 16384, 32767), q05_path=None):
+    """Returns one record per (batch, context); tracing is on only for the
+    models this function creates."""
+    old_trace = os.environ.get("HS_TRACE")
     os.environ["HS_TRACE"] = "1"
     import hotseat_b200 as hs
     peak, src = _peak()
     td = tempfile.mkdtemp(prefix="hsmicro")
-    path = os.path.join(td, "q05.gguf")
-    write_synthetic_gguf(path, seed=1234, **QWEN05)
+    path = q05_path or os.path.join(td, "q05.gguf")
+    if not q05_path:
+        write_synthetic_gguf(path, seed=1234, **QWEN05)
+    recs = []
     max_ctx = max(ctxs) + 8
     layers, row = 24, 2 * 2 * 64 * 4
     for batch, numeric in ((1, hs.NUMERIC_FAST), (64, hs.NUMERIC_TC)):
@@ -207,10 +217,10 @@ def bench_attention(ctxs=(1024, 4096, 16384, 32767)):
             us = float(np.median(res[1:]))
             moved = batch * ((p + 1) * row + row)
             gbs = moved / us / 1e3
-            print(json.dumps({"bench": "attention", "batch": batch, "context": p + 1,
-                              "numeric": "fast" if batch == 1 else "tc", "bytes_per_layer": moved,
-                              "us_per_layer": us, "GB/s": gbs, "frac": gbs / peak, "peak": peak,
-                              "peak_source": src}), flush=True)
+            recs.append({"bench": "attention", "batch": batch, "context": p + 1,
+                         "numeric": "fast" if batch == 1 else "tc", "bytes_per_layer": moved,
+                         "us_per_layer": us, "GB/s": gbs, "frac": gbs / peak, "peak": peak,
+                         "peak_source": src})
         for k in kvs:
             k.close()
         if batch == 1:
@@ -218,8 +228,14 @@ def bench_attention(ctxs=(1024, 4096, 16384, 32767)):
         else:
             bt.close()
         m.close()
-    os.remove(path)
+    if not q05_path:
+        os.remove(path)
     os.rmdir(td)
+    if old_trace is None:
+        del os.environ["HS_TRACE"]
+    else:
+        os.environ["HS_TRACE"] = old_trace
+    return recs
 
 
 def bench_prefill(n_seqs=16, prompt=2048, gen=512):
@@ -256,11 +272,10 @@ def bench_prefill(n_seqs=16, prompt=2048, gen=512):
     toks = n_seqs * (prompt - 1)
     flops = 2.0 * c["n_layers"] * layer_w * toks
     tf = flops / (ms / 1000.0) / 1e12
-    print(json.dumps({"bench": "prefill", "model": "qwen2.5-1.5b-shape", "sequences": n_seqs, "prompt": prompt,
-                      "ms": ms, "tok/s": toks / (ms / 1000.0), "gemm_TFLOP/s": tf, "peak_TFLOP/s": tflops,
-                      "frac": tf / tflops, "peak_source": tsrc,
-                      "note": "algorithmic 2*weights*tokens; the tensor cores run twice that (hi/lo halves)"}),
-          flush=True)
+    recs = [{"bench": "prefill", "model": "qwen2.5-1.5b-shape", "sequences": n_seqs, "prompt": prompt,
+             "ms": ms, "tok/s": toks / (ms / 1000.0), "gemm_TFLOP/s": tf, "peak_TFLOP/s": tflops,
+             "frac": tf / tflops, "peak_source": tsrc,
+             "note": "algorithmic 2*weights*tokens; the tensor cores run twice that (hi/lo halves)"}]
     cfg = hs.SamplerCfg.default(temperature=0.0)
     db = hs.Batch(m, n_seqs)
     seqs = [dict(tokens=p, prompt_len=prompt, max_tokens=gen, cfg=cfg, rng=hs.Rng.seed(i), filled=prompt - 1)
@@ -278,10 +293,9 @@ def bench_prefill(n_seqs=16, prompt=2048, gen=512):
     kv_row = c["n_layers"] * 2 * c["n_kv_heads"] * hd * 4
     kv_bytes = n_seqs * kv_row * np.mean([p + 1 for p in range(prompt - 1, prompt + gen - 1)])
     gbs = (step_bytes + kv_bytes) * steps / (ms / 1000.0) / 1e9
-    print(json.dumps({"bench": "decode", "model": "qwen2.5-1.5b-shape", "batch": n_seqs, "context_from": prompt,
-                      "generated": gen_toks, "ms": ms, "tok/s": gen_toks / (ms / 1000.0), "GB/s": gbs,
-                      "frac": gbs / peak_bw, "note": "hs_batch_seq_run end to end, greedy, penalty 1.1"}),
-          flush=True)
+    recs.append({"bench": "decode", "model": "qwen2.5-1.5b-shape", "batch": n_seqs, "context_from": prompt,
+                 "generated": gen_toks, "ms": ms, "tok/s": gen_toks / (ms / 1000.0), "GB/s": gbs,
+                 "frac": gbs / peak_bw, "note": "hs_batch_seq_run end to end, greedy, penalty 1.1"})
     for k in kvs:
         k.close()
     pb.close()
@@ -289,6 +303,7 @@ def bench_prefill(n_seqs=16, prompt=2048, gen=512):
     m.close()
     os.remove(path)
     os.rmdir(td)
+    return recs
 
 
 def bench_token():
@@ -406,15 +421,53 @@ def bench_batch():
     os.rmdir(td)
 
 
+def bench_prefill_trace(prompt=2048, pass_tokens=512):
+    """One prefill pass of the 1.5B shape at the end of a 2048-token prompt
+    (positions prompt-1-pass_tokens .. prompt-2) with the launch timeline:
+    per kernel role of layers 1-26, previous kernel's last exit to its own."""
+    os.environ["HS_TRACE"] = "1"
+    import hotseat_b200 as hs
+    td = tempfile.mkdtemp(prefix="hsmicro")
+    path = os.path.join(td, "q15.gguf")
+    write_synthetic_gguf(path, seed=1234, **QWEN15)
+    c = QWEN15
+    m = hs.Model.load(path, max_ctx=prompt + 8, numeric=hs.NUMERIC_TC)
+    kv = m.kv()
+    toks = [int(t) for t in np.random.default_rng(2048).integers(0, c["vocab"], size=prompt)]
+    b = hs.Batch(m, pass_tokens)
+    head = prompt - 1 - pass_tokens
+    b.prefill(kv, toks[:head])
+    b.prefill(kv, toks[head:prompt - 1], pos0=head)
+    t = b.trace().astype(np.int64)
+    L = c["n_layers"]
+    names = ["norm", "qkv", "append", "attend", "o", "ffn_norm", "gate_up", "down"]
+    per = {}
+    for j, k in enumerate(names):
+        per[k] = float(np.mean([(t[l * 8 + j, 2] - t[l * 8 + j - 1, 2]) / 1e3 for l in range(1, L - 1)]))
+    print(json.dumps({"bench": "prefill_pass", "model": "qwen2.5-1.5b-shape", "positions": [head, prompt - 2],
+                      "exit_to_exit_us": per, "layer_us": sum(per.values()),
+                      "pass_ms": float((t[L * 8 - 1, 2] - t[0, 0]) / 1e6)}), flush=True)
+    kv.close()
+    b.close()
+    m.close()
+    os.remove(path)
+    os.rmdir(td)
+
+
 if __name__ == "__main__":
     which = sys.argv[1] if len(sys.argv) > 1 else "all"
     if which in ("dequant", "all"):
-        bench_dequant()
+        for r in bench_dequant():
+            print(json.dumps(r), flush=True)
     if which in ("attention", "all"):
-        bench_attention()
+        for r in bench_attention():
+            print(json.dumps(r), flush=True)
     if which in ("prefill", "all"):
-        bench_prefill()
+        for r in bench_prefill():
+            print(json.dumps(r), flush=True)
     if which in ("token", "all"):
         bench_token()
     if which in ("batch", "all"):
         bench_batch()
+    if which == "prefill_trace":
+        bench_prefill_trace()
