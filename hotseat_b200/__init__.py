@@ -148,6 +148,8 @@ _SIGS = {
     "hs_forward": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P]),
     "hs_scratch_logits": (C.c_int, [_P, _P, C.c_uint64]),
     "hs_scratch_set_logits": (C.c_int, [_P, _P, C.c_uint64]),
+    "hs_scratch_nll": (C.c_int, [_P, C.c_uint32, C.POINTER(C.c_double)]),
+    "hs_batch_nll": (C.c_int, [_P, _P, C.c_uint32, _P]),
     "hs_sampler_cfg_default": (None, [C.POINTER(SamplerCfg)]),
     "hs_rng_seed": (None, [C.c_uint64, C.POINTER(Rng)]),
     "hs_sample": (C.c_int, [_P, C.POINTER(SamplerCfg), C.POINTER(Rng), _P, C.c_uint64, C.POINTER(C.c_uint32)]),
@@ -434,6 +436,12 @@ class Scratch:
         a = np.ascontiguousarray(logits, dtype=np.float32)
         _check(_lib.hs_scratch_set_logits(self._h, _ptr(a), a.size))
 
+    def nll(self, next_token):
+        """examples/ppl.rs's score of next_token under the current logits."""
+        out = C.c_double()
+        _check(_lib.hs_scratch_nll(self._h, next_token, C.byref(out)))
+        return out.value
+
     @property
     def stream(self):
         return _lib.hs_scratch_stream(self._h)
@@ -524,6 +532,13 @@ class Batch:
         out = np.zeros(self.model.cfg.vocab, dtype=np.float32)
         _check(_lib.hs_batch_logits(self._h, slot, _ptr(out), out.size))
         return out
+
+    def nll(self, next_tokens):
+        """examples/ppl.rs's score per slot of the last forward."""
+        t = np.ascontiguousarray(next_tokens, dtype=np.uint32)
+        out = np.zeros(max(1, t.size), dtype=np.float64)
+        _check(_lib.hs_batch_nll(self._h, _ptr(t), t.size, _ptr(out)))
+        return out[: t.size]
 
     @property
     def stream(self):

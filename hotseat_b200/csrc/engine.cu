@@ -284,6 +284,8 @@ struct hs_scratch {
     // slice's keys in order, the top-k keys in order, their running sums
     uint64_t *sort_cand = nullptr, *wkeys = nullptr;
     float* wps = nullptr;
+    double* nll = nullptr;          // perplexity score of the last forward (hs_scratch_nll)
+    uint32_t* nll_next = nullptr;
     cudaGraphExec_t g_fwd = nullptr, g_step = nullptr;
     const hs_kv* graph_kv = nullptr;
     uint32_t graph_kmax = 0;
@@ -313,7 +315,7 @@ struct hs_scratch {
         cudaFreeHost(trace_init);
         for (void* p : {(void*)x, (void*)qkv, (void*)att, (void*)hb, (void*)logits, (void*)tokens, (void*)cand,
                         (void*)argbuf, (void*)sc_global, (void*)att_part, (void*)att_cnt, (void*)kv_tab,
-                        (void*)tok_mem, (void*)sort_cand, (void*)wkeys, (void*)wps})
+                        (void*)tok_mem, (void*)sort_cand, (void*)wkeys, (void*)wps, (void*)nll, (void*)nll_next})
             cudaFree(p);
     }
 };
@@ -1505,6 +1507,21 @@ int hs_scratch_logits(hs_scratch* s, float* host, uint64_t n) {
     return HS_OK;
 }
 
+int hs_scratch_nll(hs_scratch* s, uint32_t next, double* out) {
+    if (!s || !out) return fail(HS_E_ARG, "null argument");
+    if (next >= s->m->cfg.vocab) return fail(HS_E_ARG, "token out of range");
+    HS_CUDA_TRY(cudaSetDevice(s->m->device));
+    if (!s->nll) {
+        HS_CUDA_TRY(cudaMalloc(&s->nll, 8));
+        HS_CUDA_TRY(cudaMalloc(&s->nll_next, 4));
+    }
+    HS_CUDA_TRY(cudaMemcpyAsync(s->nll_next, &next, 4, cudaMemcpyHostToDevice, s->st));
+    HS_CUDA_TRY(launch_logits_nll(s->logits, s->m->cfg.vocab, s->nll_next, 1, s->m->cfg.vocab, s->nll, s->st));
+    HS_CUDA_TRY(cudaMemcpyAsync(out, s->nll, 8, cudaMemcpyDeviceToHost, s->st));
+    HS_CUDA_TRY(cudaStreamSynchronize(s->st));
+    return HS_OK;
+}
+
 int hs_scratch_set_logits(hs_scratch* s, const float* host, uint64_t n) {
     if (!s || !host) return fail(HS_E_ARG, "null argument");
     if (n != s->m->cfg.vocab) return fail(HS_E_ARG, "expected exactly vocab logits");
@@ -1786,6 +1803,8 @@ struct hs_batch {
     // every slice's keys in order, the top-k keys in order, their running sums
     uint64_t *sort_cand = nullptr, *wkeys = nullptr;
     float* wps = nullptr;
+    double* nll = nullptr;         // perplexity scores of the last forward (hs_batch_nll) [cap_slots]
+    uint32_t* nll_next = nullptr;
     uint32_t* err = nullptr;       // GEMM error word (device)
     uint32_t err_h = 0;
     float* sc_global = nullptr;    // attention scores for long contexts [cap_slots][nh][max_ctx]
@@ -1812,7 +1831,7 @@ struct hs_batch {
                         (void*)hb_hi, (void*)hb_lo, (void*)ctl, (void*)tokens, (void*)tok_tab, (void*)kv_tab,
                         (void*)dirty_tab, (void*)track_tab, (void*)cand, (void*)argbuf, (void*)err,
                         (void*)sc_global, (void*)att_part, (void*)att_cnt, (void*)sort_cand, (void*)wkeys,
-                        (void*)wps})
+                        (void*)wps, (void*)nll, (void*)nll_next})
             cudaFree(p);
     }
 };
@@ -2195,6 +2214,25 @@ int hs_prefill(const hs_model* m, hs_kv* kv, const uint32_t* tokens, uint32_t n,
         HS_CUDA_TRY(cudaGraphLaunch(g, b->st));
         if ((rc = batch_sync(b, cnt))) return rc;
     }
+    return HS_OK;
+}
+
+int hs_batch_nll(hs_batch* b, const uint32_t* next, uint32_t n, double* out) {
+    if (!b || (!next && n) || (!out && n)) return fail(HS_E_ARG, "null argument");
+    if (n > b->cap_slots) return fail(HS_E_ARG, "more rows than the batch holds");
+    const uint32_t vocab = b->m->cfg.vocab;
+    for (uint32_t i = 0; i < n; i++)
+        if (next[i] >= vocab) return fail(HS_E_ARG, "token out of range");
+    if (!n) return HS_OK;
+    HS_CUDA_TRY(cudaSetDevice(b->m->device));
+    if (!b->nll) {
+        HS_CUDA_TRY(cudaMalloc(&b->nll, (size_t)b->cap_slots * 8));
+        HS_CUDA_TRY(cudaMalloc(&b->nll_next, (size_t)b->cap_slots * 4));
+    }
+    HS_CUDA_TRY(cudaMemcpyAsync(b->nll_next, next, (size_t)n * 4, cudaMemcpyHostToDevice, b->st));
+    HS_CUDA_TRY(launch_logits_nll(b->logits, vocab, b->nll_next, n, vocab, b->nll, b->st));
+    HS_CUDA_TRY(cudaMemcpyAsync(out, b->nll, (size_t)n * 8, cudaMemcpyDeviceToHost, b->st));
+    HS_CUDA_TRY(cudaStreamSynchronize(b->st));
     return HS_OK;
 }
 

@@ -98,6 +98,10 @@ constexpr uint64_t kXferPiece = 64 * 1024;
 cudaError_t launch_copy_runs(const uint8_t* src, uint8_t* dst, const XferRun* runs, uint32_t n, int n_sm,
                              cudaStream_t st);
 
+// Perplexity score (nll.cu): out[r] = NLL of next[r] under logits row r.
+cudaError_t launch_logits_nll(const float* logits, uint64_t stride, const uint32_t* next, uint32_t rows,
+                              uint32_t vocab, double* out, cudaStream_t st);
+
 // Launchers (PDL attribute set; may be captured in a graph).
 cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, cudaStream_t st);
 cudaError_t launch_attention(uint32_t head_dim, uint32_t nh, size_t smem, const AttnArgs& a, cudaStream_t st);

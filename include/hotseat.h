@@ -207,6 +207,10 @@ int hs_scratch_logits(hs_scratch* s, float* host, uint64_t n);
 /* Overwrite Scratch::logits from the host (the field is public in the
  * reference, so a caller may sample from logits it supplies). */
 int hs_scratch_set_logits(hs_scratch* s, const float* host, uint64_t n);
+/* The perplexity harness's score (hs-engine examples/ppl.rs:35-43) of the
+ * scratch's logits: -((l[next] - max) - ln(sum of exp_f32(l - max))), the
+ * sum in f64 (in a fixed tree order on the device). */
+int hs_scratch_nll(hs_scratch* s, uint32_t next, double* out);
 
 /* ---- sampling (replaces sampler.rs:12-187, seq.rs:321-330) ------------- */
 
@@ -294,6 +298,9 @@ int hs_forward_batch(const hs_model* m, hs_kv* const* kvs, const uint32_t* token
 int hs_prefill(const hs_model* m, hs_kv* kv, const uint32_t* tokens, uint32_t n, uint32_t pos0, hs_batch* b);
 /* Logits of sequence `slot` from the last hs_forward_batch. */
 int hs_batch_logits(hs_batch* b, uint32_t slot, float* host, uint64_t n);
+/* hs_scratch_nll for slots 0..n-1 of the last hs_forward_batch: out[i] =
+ * the score of next[i] under slot i's logits. */
+int hs_batch_nll(hs_batch* b, const uint32_t* next, uint32_t n, double* out);
 /* hs_seq_run for n sequences at once: sequence i uses kvs[i], its history
  * tokens[i] (n_tokens[i] valid, capacity cap each), st[i], cfg[i], rng[i];
  * all advance until each stops (or reaches stop_at_filled, 0 = never). */

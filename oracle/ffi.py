@@ -77,6 +77,7 @@ def lib():
         "hso_sample": (C.c_uint32, [C.POINTER(SamplerCfg), C.POINTER(Rng), P, C.c_size_t, P, C.c_size_t]),
         "hso_argmax": (C.c_uint32, [P, C.c_size_t]),
         "hso_penalised_argmax": (C.c_uint32, [C.POINTER(SamplerCfg), P, C.c_size_t, P, C.c_size_t]),
+        "hso_nll": (C.c_double, [P, C.c_size_t, C.c_uint32]),
         "hso_split": (None, [C.c_size_t, C.c_size_t, C.c_size_t, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
         "hso_kv_row_off": (C.c_uint64, [C.POINTER(KvSpec), C.c_uint64, C.c_int, C.c_uint64, C.c_uint64]),
         "hso_kv_written_ranges": (C.c_size_t, [C.POINTER(KvSpec), C.c_uint64, P, C.c_size_t]),

@@ -1081,6 +1081,16 @@ float hso_dot_f16(const uint16_t* w, const float* x, size_t n) { return dot_f16(
 float hso_dot_f32(const float* a, const float* b, size_t n) { return dot_f32(a, b, n); }
 void hso_rmsnorm(float* out, const float* x, const float* g, size_t n, float eps) { rmsnorm(out, x, g, n, eps); }
 void hso_softmax(float* x, size_t n) { softmax(x, n); }
+// examples/ppl.rs:35-43: the negative log-likelihood of `next` under the
+// logits, max-shifted: max by f32::max from -inf, then the exponentials
+// (exp_f32 of the f32 difference) summed in f64 in order, natural log in f64.
+double hso_nll(const float* logits, size_t n, uint32_t next) {
+    float mx = -INFINITY;
+    for (size_t i = 0; i < n; i++) mx = std::fmax(mx, logits[i]);
+    double sum = 0.0;
+    for (size_t i = 0; i < n; i++) sum += (double)exp_f32(logits[i] - mx);
+    return -((double)(logits[next] - mx) - std::log(sum));
+}
 int hso_dequant_f16(uint32_t ty, const uint8_t* src, size_t n, uint16_t* dst) {
     return dequant_to_f16(ty, src, n, dst);
 }

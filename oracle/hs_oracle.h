@@ -38,6 +38,7 @@ float hso_dot_f16(const uint16_t* w, const float* x, size_t n);
 float hso_dot_f32(const float* a, const float* b, size_t n);
 void hso_rmsnorm(float* out, const float* x, const float* g, size_t n, float eps);
 void hso_softmax(float* x, size_t n);
+double hso_nll(const float* logits, size_t n, uint32_t next); /* examples/ppl.rs:35-43 */
 
 /* quant.rs: ggml type ids 0,1,6,8,12,13,14. Returns 0, or -1 on unknown type. */
 int hso_dequant_f16(uint32_t ggml_type, const uint8_t* src, size_t n, uint16_t* dst);
