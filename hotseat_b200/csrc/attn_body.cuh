@@ -175,6 +175,71 @@ __device__ __forceinline__ float combine(const float* part, uint32_t S, uint32_t
     return __fdiv_rn(num, den);
 }
 
+// combine<true> for every output element of the group at once, by the
+// CTA's 256 threads, with the same operations in the same split order (the
+// same bits): the S splits' maxima and sums are staged into shared memory
+// `st` (the item's space, free by now) with parallel loads, the weights
+// exp(m_q - M) computed once per (split, head), then the outputs kCombTile
+// splits at a time, each element accumulating its splits one after another.
+// Needs (3 * S * G + 19 + kCombTile * G * hd) floats of `st` (16-byte
+// aligned), S <= 128, G <= 8.
+constexpr uint32_t kCombTile = 16;
+template <typename Store>
+__device__ void combine_staged(const float* part, uint32_t S, uint32_t G, uint32_t hd, float* st, Store store) {
+    const uint32_t rec = attn_record(G, hd), gh = G * hd, tid = threadIdx.x;
+    float* ms = st;            // [S][G] maxima
+    float* ls = ms + S * G;    // [S][G] sums
+    float* ws = ls + S * G;    // [S][G] weights
+    float* mx = ws + S * G;    // [8]
+    float* den = mx + 8;       // [8]
+    float* tile = st + ((3 * S * G + 16 + 3) & ~3u);  // [kCombTile][gh], 16-byte aligned for the float4 stores
+    for (uint32_t i = tid; i < S * G; i += kThreads) {
+        const uint32_t q = i / G, h = i % G;
+        ms[i] = __ldcg(part + (size_t)q * rec + gh + h);
+        ls[i] = __ldcg(part + (size_t)q * rec + gh + G + h);
+    }
+    sync256();
+    if (tid < G) {
+        float M = -FLT_MAX;
+        for (uint32_t q = 0; q < S; q++) M = fmaxf(M, ms[q * G + tid]);
+        mx[tid] = M;
+    }
+    sync256();
+    for (uint32_t i = tid; i < S * G; i += kThreads) ws[i] = __expf(__fsub_rn(ms[i], mx[i % G]));
+    sync256();
+    if (tid < G) {
+        float d = 0.0f;
+        for (uint32_t q = 0; q < S; q++) d = __fadd_rn(d, __fmul_rn(ws[q * G + tid], ls[q * G + tid]));
+        den[tid] = d;
+    }
+    constexpr uint32_t NPT = 4;  // outputs per thread: gh <= 8 * 128
+    float num[NPT] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (uint32_t q0 = 0; q0 < S; q0 += kCombTile) {
+        const uint32_t cnt = S - q0 < kCombTile ? S - q0 : kCombTile;
+        sync256();  // the previous tile is consumed (and den is written)
+        for (uint32_t i = tid; i < cnt * (gh / 4); i += kThreads) {
+            const uint32_t t = i / (gh / 4), c4 = i % (gh / 4);
+            reinterpret_cast<float4*>(tile + t * gh)[c4] =
+                __ldcg(reinterpret_cast<const float4*>(part + (size_t)(q0 + t) * rec) + c4);
+        }
+        sync256();
+#pragma unroll
+        for (uint32_t j = 0; j < NPT; j++) {
+            const uint32_t idx = tid + j * kThreads;
+            if (idx < gh) {
+                const uint32_t h = idx / hd;
+                for (uint32_t t = 0; t < cnt; t++)
+                    num[j] = __fadd_rn(num[j], __fmul_rn(ws[(q0 + t) * G + h], tile[t * gh + idx]));
+            }
+        }
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < NPT; j++) {
+        const uint32_t idx = tid + j * kThreads;
+        if (idx < gh) store(idx, __fdiv_rn(num[j], den[idx / hd]));
+    }
+}
+
 __device__ __forceinline__ uint64_t kv_row_off(const SplitAttnArgs& a, uint32_t layer, uint32_t kvh, uint32_t hd,
                                                uint32_t p, uint32_t is_v) {
     const uint64_t plane = (uint64_t)a.max_ctx * a.nkv * hd;
@@ -665,8 +730,14 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     sync256();  // the flag word is rewritten by the next item
     if (!last) return;
     __threadfence();
-    for (uint32_t idx = tid; idx < Gf * HD; idx += kThreads)
-        store((size_t)slot * a.out_stride + (size_t)kvh * Gf * HD + idx, combine<true>(part, S, Gf, HD, idx));
+    if (a.unstaged_combine) {
+        for (uint32_t idx = tid; idx < Gf * HD; idx += kThreads)
+            store((size_t)slot * a.out_stride + (size_t)kvh * Gf * HD + idx, combine<true>(part, S, Gf, HD, idx));
+    } else {
+        combine_staged(part, S, Gf, HD, sm, [&](uint32_t idx, float v) {
+            store((size_t)slot * a.out_stride + (size_t)kvh * Gf * HD + idx, v);
+        });
+    }
     if (tid == 0) *counter = 0;
 }
 

@@ -221,6 +221,7 @@ struct hs_model {
     uint32_t max_splits = 0;
     uint32_t attn_head_split = 1;  // query-head parts per split-KV attention item
     uint32_t attn_nbuf = 0;        // K/V chunk buffers per item (0 = by head_dim)
+    uint32_t attn_unstaged = 0;    // HS_ATTN_UNSTAGED_COMBINE=1: the per-element combine (same bits; measurement)
     uint32_t numeric = HS_NUMERIC_REFERENCE;
     TcGemmPlan thead;             // tensor-core LM head
     bool tok = false;             // fast path: one persistent kernel per token (token_fast.cu)
@@ -536,6 +537,7 @@ SplitAttnArgs scratch_attn_args(const hs_scratch* s, const hs_kv* kv) {
     sa.head_split = m->attn_head_split;
     sa.nbuf = m->attn_nbuf;
     sa.tensor_cores = m->numeric == HS_NUMERIC_TC ? 1u : 0u;
+    sa.unstaged_combine = m->attn_unstaged;
     sa.trace = s->trace;
     return sa;
 }
@@ -933,6 +935,7 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
                            : attn_max_splits(max_ctx);
         m->attn_head_split = std::max<uint32_t>(1, env_u32("HS_ATTN_HEAD_SPLIT", 1));
         m->attn_nbuf = env_u32("HS_ATTN_NBUF", 0);
+        m->attn_unstaged = env_u32("HS_ATTN_UNSTAGED_COMBINE", 0);
         HS_CUDA_TRY(attn_split_set_smem_limits(optin));
     }
     m->attn_smem = m->attn_split ? attn_split_smem(hd, m->attn_nbuf) : attention_smem(hd, max_ctx);
@@ -1940,6 +1943,7 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool pref
             sa.max_splits = m->max_splits;
             sa.head_split = m->attn_head_split;
             sa.nbuf = m->attn_nbuf;
+            sa.unstaged_combine = m->attn_unstaged;
             sa.tensor_cores = m->numeric == HS_NUMERIC_TC ? 1u : 0u;
             sa.trace = b->trace;
             sa.trace_slot = *launches;
