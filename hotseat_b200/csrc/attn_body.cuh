@@ -247,6 +247,77 @@ __device__ __forceinline__ uint64_t kv_row_off(const SplitAttnArgs& a, uint32_t 
     return (uint64_t)layer * 2 * plane + (is_v ? plane : 0) + within;
 }
 
+// Warp-split attend (SplitAttnArgs::warp_split): each of the 8 warps takes
+// the blocks of WB positions b = w, w + 8, ... of the item's range and keeps
+// WBUF of its blocks in flight in its own part of the chunk buffers.
+template <int HD, int NBUF>
+struct WsGeom {
+    static constexpr uint32_t WB = 8, RW = HD + 4;
+    static constexpr uint32_t AREA = NBUF * kCh * (k_stride(HD) + v_stride(HD)) + 2 * 8 * SPS;  // floats from kb on
+    static constexpr uint32_t WONE = 2 * WB * RW;                                                 // one block's K and V rows
+    static constexpr uint32_t QP = 8 * RW;  // q rows padded to RW (the head pairs' rows in distinct banks)
+    static constexpr uint32_t FIT = AREA > QP ? ((AREA - QP) / 8 - 8 * WB - 8) / WONE : 0;
+    static constexpr uint32_t WBUF = FIT > 4 ? 4 : (FIT < 1 ? 1 : FIT);
+    static constexpr uint32_t WS = WBUF * WONE + 8 * WB + 8;                                      // floats of a warp's area
+    static constexpr bool OK = 8 * WS + QP <= AREA && 8 * 8 * HD + 3 * 64 <= AREA;  // fits this item's buffers
+};
+
+// Stages block b of warp `warp` (local block index b / 8 picks the buffer)
+// of the range [p0, p1) into its area: every cached row with 16-byte
+// asynchronous copies, the row at `pos` from kn / vn when `fill_pos` (the
+// item appends it and it is not in memory yet) or left out when `skip_pos`
+// (a prefetch before kn / vn exist). One commit group per call, empty past
+// the range's end.
+template <int HD, int NBUF>
+__device__ __forceinline__ void ws_stage(const SplitAttnArgs& a, const float* kv, uint32_t layer, uint32_t kvh,
+                                         float* kb, uint32_t warp, uint32_t lane, uint32_t b, uint32_t p0,
+                                         uint32_t p1, uint32_t pos, bool fill_pos, bool skip_pos, const float* kn,
+                                         const float* vn) {
+    using W = WsGeom<HD, NBUF>;
+    const uint32_t nb = (p1 - p0 + W::WB - 1) / W::WB;
+    if (b < nb) {
+        const uint32_t pb = p0 + b * W::WB, cnt = p1 - pb < W::WB ? p1 - pb : W::WB;
+        float* wk = kb + warp * W::WS + ((b / 8) % W::WBUF) * W::WONE;
+        float* wv = wk + W::WB * W::RW;
+        for (uint32_t i = lane; i < cnt * (HD / 4); i += 32) {
+            const uint32_t rr = i / (HD / 4), c4 = i % (HD / 4);
+            if (pb + rr == pos && (fill_pos || skip_pos)) {
+                if (fill_pos) {
+                    *reinterpret_cast<float4*>(wk + rr * W::RW + 4 * c4) = *reinterpret_cast<const float4*>(kn + 4 * c4);
+                    *reinterpret_cast<float4*>(wv + rr * W::RW + 4 * c4) = *reinterpret_cast<const float4*>(vn + 4 * c4);
+                }
+            } else {
+                cp_async16(wk + rr * W::RW + 4 * c4, kv + kv_row_off(a, layer, kvh, HD, pb + rr, 0) + 4 * c4);
+                cp_async16(wv + rr * W::RW + 4 * c4, kv + kv_row_off(a, layer, kvh, HD, pb + rr, 1) + 4 * c4);
+            }
+        }
+    }
+    cp_commit();
+}
+
+// The warp-split counterpart of prefetch(): the RoPE row of `pos` and each
+// warp's first WBUF blocks (all but the row at `pos`), WBUF commit groups
+// per thread (the first with the RoPE row). Returns WBUF.
+template <int HD, int NBUF>
+__device__ uint32_t ws_prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t slot,
+                                uint32_t pos, float* sm) {
+    using W = WsGeom<HD, NBUF>;
+    static_assert(W::OK, "warp-split staging must fit the item's chunk buffers");
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.min_split);
+    const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n;
+    float* rope = sm + item_rope_off(HD, NBUF);
+    if (threadIdx.x < HD / 4) {
+        const uint32_t i = threadIdx.x % (HD / 8), half = threadIdx.x / (HD / 8);
+        const float* src = (half ? a.rope_sin : a.rope_cos) + (size_t)pos * (HD / 2) + 4 * i;
+        cp_async16(rope + half * (HD / 2) + 4 * i, src);
+    }
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint32_t i = 0; i < W::WBUF; i++)
+        ws_stage<HD, NBUF>(a, a.kv[slot], layer, kvh, sm + 10 * HD, warp, lane, warp + 8 * i, p0, p1, pos, false, true,
+                           nullptr, nullptr);
+    return W::WBUF;
+}
+
 // Issues the asynchronous loads of the RoPE row and of the cached rows of
 // an item's first `nch` chunks (at most NBUF), all but `pos`, into its
 // buffers, one commit group per chunk (the RoPE row with the first): those
@@ -259,7 +330,7 @@ __device__ uint32_t prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s,
     constexpr uint32_t RSK = k_stride(HD), RSV = v_stride(HD);
     float* kb = sm + 10 * HD;
     float* vb = kb + NBUF * kCh * RSK;
-    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits);
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.min_split);
     const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n, have = (p1 - p0 + kCh - 1) / kCh;
     if (nch > have) nch = have;
     const float* kv = a.kv[slot];
@@ -331,7 +402,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     uint32_t* flag = reinterpret_cast<uint32_t*>(hs_l + 8);
     uint4* qfrag = reinterpret_cast<uint4*>(hs_l + 12);  // [2][HD/16][32]
     const float* rope = sm + item_rope_off(HD, NBUF);
-    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits), S = (n + L - 1) / L;
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.min_split), S = (n + L - 1) / L;
     // Prefill runs append (every token's k, v) and attend (reading all rows
     // from memory) as two launches, so tokens of one sequence in one batch
     // see each other's rows.
@@ -416,6 +487,199 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
         return;
     }
 
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+    const uint32_t dd = tid % HD, hs0 = tid / HD;
+    float o[HPT];  // dimension dd of heads hs0 + j HSETS (both paths end here)
+#pragma unroll
+    for (uint32_t j = 0; j < HPT; j++) o[j] = 0.0f;
+    // (the warp-split form exists only where its staging fits this item's buffers)
+    bool use_ws = false;
+    if constexpr (WsGeom<HD, NBUF>::OK) use_ws = a.warp_split != 0;
+    if (use_ws) {
+      if constexpr (WsGeom<HD, NBUF>::OK) {
+        // Warp-split attend: warp w takes the blocks of WB positions b = w,
+        // w + 8, w + 16, ... of [p0, p1) and keeps its own online softmax per
+        // head, with no block barrier inside the loop (each warp stages its
+        // blocks' K and V rows itself, WBUF blocks in flight); the warps'
+        // states merge in warp order at the end. Scores on the CUDA cores in
+        // fp32 (lane: position b*WB + lane % WB, heads 2 (lane / WB) and +1),
+        // P.V on the CUDA cores (lane: dimensions DPL lane .. +DPL-1).
+        using W = WsGeom<HD, NBUF>;
+        constexpr uint32_t WB = W::WB, DPL = HD / 32, RW = W::RW, WBUF = W::WBUF, WS = W::WS, WONE = W::WONE;
+        float* wa = kb + warp * WS;
+        float* wp = wa + WBUF * WONE;  // [WB][8 heads] probabilities of the block
+        float* wf = wp + 8 * WB;       // [8] rescale of the running sums
+        float* qp = kb + 8 * WS;       // [8][RW] q rows, padded
+        for (uint32_t i = tid; i < G * (HD / 4); i += kThreads)
+            reinterpret_cast<float4*>(qp + (i / (HD / 4)) * RW)[i % (HD / 4)] = reinterpret_cast<const float4*>(qs)[i];
+        sync256();
+        const uint32_t nr = p1 - p0, nb = (nr + WB - 1) / WB;
+        const uint32_t r = lane % WB, hq = lane / WB, h0 = 2 * hq, h1 = 2 * hq + 1;
+        // blocks of this warp staged so far: WBUF when ws_prefetch() ran
+        // (the row at pos left out: filled here once kn / vn exist)
+        uint32_t issued = npre > 0 ? WBUF : 0;
+        if (npre > 0 && append && pos >= p0 && pos < p1) {
+            const uint32_t bp = (pos - p0) / WB;
+            if (bp % 8 == warp && bp / 8 < WBUF) {
+                float* wk = wa + ((bp / 8) % WBUF) * WONE;
+                const uint32_t rr = (pos - p0) % WB;
+                for (uint32_t c4 = lane; c4 < HD / 4; c4 += 32) {
+                    reinterpret_cast<float4*>(wk + rr * RW)[c4] = reinterpret_cast<const float4*>(kn)[c4];
+                    reinterpret_cast<float4*>(wk + WB * RW + rr * RW)[c4] = reinterpret_cast<const float4*>(vn)[c4];
+                }
+            }
+        }
+        auto stage = [&](uint32_t i) {  // this warp's local block i
+            ws_stage<HD, NBUF>(a, kv, layer, kvh, kb, warp, lane, warp + 8 * i, p0, p1, pos, append, false, kn, vn);
+        };
+        float rm0 = -FLT_MAX, rm1 = -FLT_MAX, rl0 = 0.0f, rl1 = 0.0f;  // running max / sum of heads h0, h1
+        float acc[8][DPL];
+#pragma unroll
+        for (uint32_t h = 0; h < 8; h++)
+#pragma unroll
+            for (uint32_t k = 0; k < DPL; k++) acc[h][k] = 0.0f;
+        for (; issued + 1 < WBUF; issued++) stage(issued);
+        for (uint32_t b = warp; b < nb; b += 8) {
+            for (; issued < b / 8 + WBUF; issued++) stage(issued);
+            cp_wait<WBUF - 1>();  // this block's group: exactly WBUF - 1 younger ones are committed
+            __syncwarp();
+            if (b == warp) at(3);  // warp 0's first block ready
+            const uint32_t pb = p0 + b * WB, cnt = p1 - pb < WB ? p1 - pb : WB;
+            const float* wk = wa + ((b / 8) % WBUF) * WONE;
+            const float* wv = wk + WB * RW;
+            float s0 = -FLT_MAX, s1 = -FLT_MAX;
+            if (r < cnt) {
+                float a0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, a1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                const float4* k4 = reinterpret_cast<const float4*>(wk + r * RW);
+                const float4* q0 = reinterpret_cast<const float4*>(qp + (h0 < G ? h0 : 0) * RW);
+                const float4* q1 = reinterpret_cast<const float4*>(qp + (h1 < G ? h1 : 0) * RW);
+#pragma unroll 8
+                for (uint32_t d4 = 0; d4 < HD / 4; d4++) {
+                    const float4 kk = k4[d4], x = q0[d4], y = q1[d4];
+                    a0[0] = __fmaf_rn(x.x, kk.x, a0[0]);
+                    a0[1] = __fmaf_rn(x.y, kk.y, a0[1]);
+                    a0[2] = __fmaf_rn(x.z, kk.z, a0[2]);
+                    a0[3] = __fmaf_rn(x.w, kk.w, a0[3]);
+                    a1[0] = __fmaf_rn(y.x, kk.x, a1[0]);
+                    a1[1] = __fmaf_rn(y.y, kk.y, a1[1]);
+                    a1[2] = __fmaf_rn(y.z, kk.z, a1[2]);
+                    a1[3] = __fmaf_rn(y.w, kk.w, a1[3]);
+                }
+                if (h0 < G) s0 = __fmul_rn(__fadd_rn(__fadd_rn(a0[0], a0[1]), __fadd_rn(a0[2], a0[3])), scale);
+                if (h1 < G) s1 = __fmul_rn(__fadd_rn(__fadd_rn(a1[0], a1[1]), __fadd_rn(a1[2], a1[3])), scale);
+            }
+            // the block's maximum and sum per head over the WB lanes of the group
+            float mx0 = s0, mx1 = s1;
+#pragma unroll
+            for (uint32_t off = 1; off < WB; off <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+            }
+            const float n0 = fmaxf(rm0, mx0), n1 = fmaxf(rm1, mx1);
+            const float e0 = r < cnt && h0 < G ? __expf(__fsub_rn(s0, n0)) : 0.0f;
+            const float e1 = r < cnt && h1 < G ? __expf(__fsub_rn(s1, n1)) : 0.0f;
+            float sm0 = e0, sm1 = e1;
+#pragma unroll
+            for (uint32_t off = 1; off < WB; off <<= 1) {
+                sm0 = __fadd_rn(sm0, __shfl_xor_sync(0xffffffffu, sm0, off));
+                sm1 = __fadd_rn(sm1, __shfl_xor_sync(0xffffffffu, sm1, off));
+            }
+            const float f0 = rm0 == -FLT_MAX ? 0.0f : __expf(__fsub_rn(rm0, n0));
+            const float f1 = rm1 == -FLT_MAX ? 0.0f : __expf(__fsub_rn(rm1, n1));
+            rl0 = __fadd_rn(__fmul_rn(rl0, f0), sm0);
+            rl1 = __fadd_rn(__fmul_rn(rl1, f1), sm1);
+            rm0 = n0;
+            rm1 = n1;
+            wp[r * 8 + h0] = e0;
+            wp[r * 8 + h1] = e1;
+            if (r == 0) {
+                wf[h0] = f0;
+                wf[h1] = f1;
+            }
+            __syncwarp();
+            // each position's V slice and all heads' probabilities read once
+            float pv[8][DPL];
+#pragma unroll
+            for (uint32_t h = 0; h < 8; h++)
+#pragma unroll
+                for (uint32_t k = 0; k < DPL; k++) pv[h][k] = 0.0f;
+            for (uint32_t rr = 0; rr < cnt; rr++) {
+                const float4 pa = *reinterpret_cast<const float4*>(wp + rr * 8);
+                const float4 pb = *reinterpret_cast<const float4*>(wp + rr * 8 + 4);
+                const float pr[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+                float vv[DPL];
+                if constexpr (DPL == 2) {
+                    const float2 t = *reinterpret_cast<const float2*>(wv + rr * RW + 2 * lane);
+                    vv[0] = t.x;
+                    vv[1] = t.y;
+                } else {
+                    const float4 t = *reinterpret_cast<const float4*>(wv + rr * RW + 4 * lane);
+                    vv[0] = t.x;
+                    vv[1] = t.y;
+                    vv[2] = t.z;
+                    vv[3] = t.w;
+                }
+#pragma unroll
+                for (uint32_t h = 0; h < 8; h++)
+                    if (h < G)
+#pragma unroll
+                        for (uint32_t k = 0; k < DPL; k++) pv[h][k] = __fmaf_rn(pr[h], vv[k], pv[h][k]);
+            }
+#pragma unroll
+            for (uint32_t h = 0; h < 8; h++) {
+                if (h < G) {
+                    const float f = wf[h];
+#pragma unroll
+                    for (uint32_t k = 0; k < DPL; k++) acc[h][k] = __fadd_rn(__fmul_rn(acc[h][k], f), pv[h][k]);
+                }
+            }
+            __syncwarp();  // the block's buffers and probabilities are reused
+        }
+        cp_wait0();
+        sync256();
+        // merge: warp w's maxima, sums and outputs, then per head the weights
+        // exp(m_w - M) and the sums in warp order
+        float* mm = kb;               // [8 warps][8 heads]
+        float* ll = mm + 64;          // [8][8]
+        float* wt = ll + 64;          // [8][8] weights
+        float* ao = wt + 64;          // [8 warps][8 heads][HD]
+        if (r == 0) {
+            mm[warp * 8 + h0] = rm0;
+            mm[warp * 8 + h1] = rm1;
+            ll[warp * 8 + h0] = rl0;
+            ll[warp * 8 + h1] = rl1;
+        }
+#pragma unroll
+        for (uint32_t h = 0; h < 8; h++)
+            if (h < G)
+#pragma unroll
+                for (uint32_t k = 0; k < DPL; k++) ao[(warp * 8 + h) * HD + DPL * lane + k] = acc[h][k];
+        sync256();
+        if (tid < G) {
+            float M = -FLT_MAX;
+            for (uint32_t w = 0; w < 8; w++) M = fmaxf(M, mm[w * 8 + tid]);
+            float l = 0.0f;
+            for (uint32_t w = 0; w < 8; w++) {
+                const float m_w = mm[w * 8 + tid];
+                const float x = m_w == -FLT_MAX ? 0.0f : __expf(__fsub_rn(m_w, M));
+                wt[w * 8 + tid] = x;
+                l = __fadd_rn(l, __fmul_rn(x, ll[w * 8 + tid]));
+            }
+            hs_m[tid] = M;
+            hs_l[tid] = l;
+        }
+        sync256();
+#pragma unroll
+        for (uint32_t j = 0; j < HPT; j++) {
+            const uint32_t h = hs0 + j * HSETS;
+            if (h < G) {
+                float v = 0.0f;
+                for (uint32_t w = 0; w < 8; w++) v = __fadd_rn(v, __fmul_rn(wt[w * 8 + h], ao[(w * 8 + h) * HD + dd]));
+                o[j] = v;
+            }
+        }
+      }
+    } else {
     const uint32_t nch = (p1 - p0 + kCh - 1) / kCh;
     auto issue = [&](uint32_t c) {
         if (c < nch) {
@@ -442,7 +706,6 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
         }
         if (c >= npre) cp_commit();  // a prefetched chunk's group is committed already
     };
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
     // TC: both products of a chunk on the tensor cores (mma.sync m16n8k8,
     // tf32 operands split hi + lo so that lo*hi + hi*lo + hi*hi keeps about
     // 22 significant bits: the split-precision method of Ootomo & Yokota,
@@ -460,7 +723,6 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     constexpr uint32_t KSV = 8 / WPV;                 // k-steps of 8 positions per warp
     const uint32_t g = lane >> 2, t4 = lane & 3;
     const uint32_t mq = warp & 3, kq = warp >> 2, mv = warp % MTV, kvp = warp / MTV;
-    const uint32_t dd = tid % HD, hs0 = tid / HD;
     const uint4* qf = qfrag + kq * KSQ * 32 + lane;
     if constexpr (TC) {
         // q^T operand fragments, split once per item (read by the first
@@ -474,9 +736,6 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
         }
     }
     float oa[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // TC: out^T (16 mv + g, 2 t4), (.., 2 t4 + 1), (+8, ..), (+8, ..)
-    float o[HPT];                            // CUDA cores: dimension dd of heads hs0 + j HSETS
-#pragma unroll
-    for (uint32_t j = 0; j < HPT; j++) o[j] = 0.0f;
     // chunks 0 .. NBUF-2 in flight before the loop; each iteration issues
     // chunk c + NBUF - 1 (an empty group past the end) and waits for chunk c
 #pragma unroll
@@ -666,6 +925,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
             }
         }
     }
+    }  // chunked attend
     at(6);
     mark_dirty();
 

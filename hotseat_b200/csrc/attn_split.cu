@@ -50,10 +50,11 @@ __global__ void __launch_bounds__(attn::kThreads, 2) k_attn_split(const SplitAtt
     // The cached rows (all but pos) and the RoPE row do not depend on the
     // kernels this launch overlaps: with a whole item (append and attend),
     // start loading the first chunks before waiting for the QKV product.
-    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits), S = (n + L - 1) / L;
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.min_split), S = (n + L - 1) / L;
     uint32_t npre = 0;
     if (a.mode == ATTN_FULL && active && pos < a.max_ctx && s < S)
-        npre = attn::prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm, NB - 1 > 0 ? NB - 1 : 1);
+        npre = a.warp_split ? attn::ws_prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm)
+                            : attn::prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm, NB - 1 > 0 ? NB - 1 : 1);
     pdl_wait();
     if (!active) return;
     if (pos >= a.max_ctx) {

@@ -195,6 +195,8 @@ struct SplitAttnArgs {
     uint32_t nbuf;           // K/V chunk buffers per item, 2..4 (0 = by head_dim)
     uint32_t tensor_cores;   // chunk products on the tensor cores (split tf32), else fp32 on the CUDA cores
     uint32_t unstaged_combine;  // measurement knob: the last CTA's combine reads the splits through L2 per element
+    uint32_t warp_split;     // attend with the warps on separate blocks of positions (one merge at the end)
+    uint32_t min_split;      // positions per split at least this (a multiple of 64; 0 = 64)
     uint64_t* trace;
     uint32_t trace_slot;
 };
@@ -206,9 +208,12 @@ __host__ __device__ inline uint32_t attn_head_split(const SplitAttnArgs& a) {
 }
 // Positions per split for n cached positions: a multiple of 64, so that at
 // most max_splits splits cover n.
-__host__ __device__ inline uint32_t attn_split_len(uint32_t n, uint32_t max_splits) {
+// Positions per split: a multiple of 64 covering n in at most max_splits
+// splits, and at least min_len (0: 64).
+__host__ __device__ inline uint32_t attn_split_len(uint32_t n, uint32_t max_splits, uint32_t min_len) {
     const uint32_t chunks = (n + 63) / 64;
-    return (chunks + max_splits - 1) / max_splits * 64;
+    const uint32_t L = (chunks + max_splits - 1) / max_splits * 64;
+    return L > min_len ? L : (min_len > 64 ? min_len : 64);
 }
 // Floats per published split of one (sequence, KV head): the group's
 // unnormalised outputs [G][hd], maxima [G], sums [G], padded to 16 bytes.

@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
         mark(11, tmark ? gtime() : 0);
     };
     if (ok) {
-        const uint32_t n = pos + 1, Ls = attn_split_len(n, a.attn.max_splits), S = (n + Ls - 1) / Ls;
+        const uint32_t n = pos + 1, Ls = attn_split_len(n, a.attn.max_splits, a.attn.min_split), S = (n + Ls - 1) / Ls;
         const uint32_t G_ = a.nh / nkv, rec = attn_record(G_, a.hd);
         // attention item i: split i / (nkv * hsp), KV head (i / hsp) % nkv,
         // query-head part i % hsp
@@ -500,8 +500,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
                 norm_x(l == 0, l > 0 ? tag(l - 1, TG_DOWN) : 0u);
                 // this CTA's first attention item: start loading its cached
                 // K/V rows and RoPE row (written by earlier tokens / constant)
-                if (b < n_items)
-                    attn::prefetch<HD, attn_buf(HD)>(a.attn, l, b / (nkv * hsp), (b / hsp) % nkv, 0, pos, att_sm);
+                if (b < n_items) {
+                    bool ws = false;
+                    if constexpr (attn::WsGeom<HD, attn_buf(HD)>::OK) {
+                        ws = a.attn.warp_split != 0;
+                        if (ws) attn::ws_prefetch<HD, attn_buf(HD)>(a.attn, l, b / (nkv * hsp), (b / hsp) % nkv, 0, pos, att_sm);
+                    }
+                    if (!ws)
+                        attn::prefetch<HD, attn_buf(HD)>(a.attn, l, b / (nkv * hsp), (b / hsp) % nkv, 0, pos, att_sm);
+                }
                 uint32_t r0, r1;
                 split_range(qrows, G, b, &r0, &r1);
                 pre = tid < r1 - r0 ? lay[l].bqkv[r0 + tid] : 0.0f;

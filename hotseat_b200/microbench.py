@@ -411,8 +411,15 @@ def bench_batch():
             "epilogue_done": float(np.mean([r[7] - r[6] for r in rows]) / 1e3),
             "exit": float(np.mean([r[2] - r[7] for r in rows]) / 1e3),
         }
+    # attention item checkpoints (SM cycles from the item's start, maximum over
+    # CTAs): RoPE done, first chunk (or warp 0's first block) ready, the
+    # positions done, the item's end
+    att = [t[l * 7 + 2] for l in range(1, 23)]
+    item = {k: float(np.mean([r[4 + i] for r in att]) / 1965.0) for i, k in
+            enumerate(["rope_done", "first_ready", "positions_done", "end"])}
     print(json.dumps({"bench": "batch_step", "sequences": B, "launches": int(n),
-                      "exit_to_exit_us": per, "layer_us": sum(per.values()), "gemm_marks_us": gemm}), flush=True)
+                      "exit_to_exit_us": per, "layer_us": sum(per.values()), "gemm_marks_us": gemm,
+                      "attention_item_us": item}), flush=True)
     for kv in kvs:
         kv.close()
     b.close()
