@@ -50,10 +50,10 @@ __global__ void __launch_bounds__(attn::kThreads, 2) k_attn_split(const SplitAtt
     // The cached rows (all but pos) and the RoPE row do not depend on the
     // kernels this launch overlaps: with a whole item (append and attend),
     // start loading the first chunks before waiting for the QKV product.
-    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.min_split), S = (n + L - 1) / L;
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from), S = (n + L - 1) / L;
     uint32_t npre = 0;
     if (a.mode == ATTN_FULL && active && pos < a.max_ctx && s < S)
-        npre = a.warp_split ? attn::ws_prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm)
+        npre = attn_use_ws(n, a.ws_from) ? attn::ws_prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm)
                             : attn::prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm, NB - 1 > 0 ? NB - 1 : 1);
     pdl_wait();
     if (!active) return;
@@ -83,6 +83,20 @@ __global__ void __launch_bounds__(attn::kThreads, 2) k_attn_split(const SplitAtt
 
 size_t attn_split_smem(uint32_t head_dim, uint32_t nbufs) {
     return attn::item_smem(head_dim, buffers(head_dim, nbufs));
+}
+
+bool attn_ws_fits(uint32_t hd, uint32_t nbufs) {
+    switch (hd * 8 + nbufs) {
+        case 64 * 8 + 1: return attn::WsGeom<64, 1>::OK;
+        case 64 * 8 + 2: return attn::WsGeom<64, 2>::OK;
+        case 64 * 8 + 3: return attn::WsGeom<64, 3>::OK;
+        case 64 * 8 + 4: return attn::WsGeom<64, 4>::OK;
+        case 128 * 8 + 1: return attn::WsGeom<128, 1>::OK;
+        case 128 * 8 + 2: return attn::WsGeom<128, 2>::OK;
+        case 128 * 8 + 3: return attn::WsGeom<128, 3>::OK;
+        case 128 * 8 + 4: return attn::WsGeom<128, 4>::OK;
+        default: return false;
+    }
 }
 
 uint32_t attn_max_splits(uint32_t max_ctx) {

@@ -222,8 +222,7 @@ struct hs_model {
     uint32_t attn_head_split = 1;  // query-head parts per split-KV attention item
     uint32_t attn_nbuf = 0;        // K/V chunk buffers per item (0 = by head_dim)
     uint32_t attn_unstaged = 0;    // HS_ATTN_UNSTAGED_COMBINE=1: the per-element combine (same bits; measurement)
-    uint32_t attn_warp_split = 0;  // attend with warp-split blocks (HS_ATTN_WARP_SPLIT=0: the chunked form)
-    uint32_t attn_min_split = 0;   // positions per split at least (batch 1; HS_ATTN_MIN_SPLIT)
+    uint32_t attn_ws_from = 0;     // warp-split item form from this many positions on (0: never)
     uint32_t numeric = HS_NUMERIC_REFERENCE;
     TcGemmPlan thead;             // tensor-core LM head
     bool tok = false;             // fast path: one persistent kernel per token (token_fast.cu)
@@ -540,8 +539,7 @@ SplitAttnArgs scratch_attn_args(const hs_scratch* s, const hs_kv* kv) {
     sa.nbuf = m->attn_nbuf;
     sa.tensor_cores = m->numeric == HS_NUMERIC_TC ? 1u : 0u;
     sa.unstaged_combine = m->attn_unstaged;
-    sa.warp_split = m->attn_warp_split;
-    sa.min_split = m->attn_min_split;
+    sa.ws_from = m->attn_ws_from;
     sa.trace = s->trace;
     return sa;
 }
@@ -940,10 +938,15 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
         m->attn_head_split = std::max<uint32_t>(1, env_u32("HS_ATTN_HEAD_SPLIT", 1));
         m->attn_nbuf = env_u32("HS_ATTN_NBUF", 0);
         m->attn_unstaged = env_u32("HS_ATTN_UNSTAGED_COMBINE", 0);
-        m->attn_warp_split = env_u32("HS_ATTN_WARP_SPLIT", 1) != 0 ? 1u : 0u;
-        // batch 1 with warp-split items: one item per KV head up to 512
-        // positions (the O phase then reads finished outputs, no split combine)
-        m->attn_min_split = tc ? 0u : env_u32("HS_ATTN_MIN_SPLIT", m->attn_warp_split ? 512 : 0) / 64 * 64;
+        // The GPU-native path's persistent token kernel runs its items with one
+        // chunk buffer, and its per-kernel form must run the same arithmetic:
+        // warp-split only where the one-buffer item holds it.
+        // Measured: the warp-split form is faster at batch 1 from about 8k
+        // positions (512-position items, several blocks per warp) and slower
+        // below and on the batched path, where the chunked form stays.
+        // HS_ATTN_WS_FROM overrides (positions; 0 = never).
+        m->attn_ws_from = env_u32("HS_ATTN_WS_FROM", tc ? 0u : 8192u);
+        if (!tc && !attn_ws_fits(hd, 1)) m->attn_ws_from = 0;
         HS_CUDA_TRY(attn_split_set_smem_limits(optin));
     }
     m->attn_smem = m->attn_split ? attn_split_smem(hd, m->attn_nbuf) : attention_smem(hd, max_ctx);
@@ -1952,8 +1955,7 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool pref
             sa.head_split = m->attn_head_split;
             sa.nbuf = m->attn_nbuf;
             sa.unstaged_combine = m->attn_unstaged;
-            sa.warp_split = m->attn_warp_split;
-            sa.min_split = m->attn_min_split;
+            sa.ws_from = m->attn_ws_from;
             sa.tensor_cores = m->numeric == HS_NUMERIC_TC ? 1u : 0u;
             sa.trace = b->trace;
             sa.trace_slot = *launches;

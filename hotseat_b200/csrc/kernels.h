@@ -195,8 +195,7 @@ struct SplitAttnArgs {
     uint32_t nbuf;           // K/V chunk buffers per item, 2..4 (0 = by head_dim)
     uint32_t tensor_cores;   // chunk products on the tensor cores (split tf32), else fp32 on the CUDA cores
     uint32_t unstaged_combine;  // measurement knob: the last CTA's combine reads the splits through L2 per element
-    uint32_t warp_split;     // attend with the warps on separate blocks of positions (one merge at the end)
-    uint32_t min_split;      // positions per split at least this (a multiple of 64; 0 = 64)
+    uint32_t ws_from;        // from this many positions on, the warp-split item form (0: never)
     uint64_t* trace;
     uint32_t trace_slot;
 };
@@ -208,12 +207,17 @@ __host__ __device__ inline uint32_t attn_head_split(const SplitAttnArgs& a) {
 }
 // Positions per split for n cached positions: a multiple of 64, so that at
 // most max_splits splits cover n.
+// The item form for n positions: warp-split blocks from ws_from positions
+// on (0: never), the chunked form below.
+__host__ __device__ inline bool attn_use_ws(uint32_t n, uint32_t ws_from) { return ws_from && n >= ws_from; }
 // Positions per split: a multiple of 64 covering n in at most max_splits
-// splits, and at least min_len (0: 64).
-__host__ __device__ inline uint32_t attn_split_len(uint32_t n, uint32_t max_splits, uint32_t min_len) {
+// splits; at least 512 where the warp-split form runs (fewer, longer items
+// whose warps each take several blocks).
+__host__ __device__ inline uint32_t attn_split_len(uint32_t n, uint32_t max_splits, uint32_t ws_from) {
     const uint32_t chunks = (n + 63) / 64;
     const uint32_t L = (chunks + max_splits - 1) / max_splits * 64;
-    return L > min_len ? L : (min_len > 64 ? min_len : 64);
+    const uint32_t min_len = attn_use_ws(n, ws_from) ? 512 : 64;
+    return L > min_len ? L : min_len;
 }
 // Floats per published split of one (sequence, KV head): the group's
 // unnormalised outputs [G][hd], maxima [G], sums [G], padded to 16 bytes.
@@ -222,6 +226,8 @@ __host__ __device__ inline uint32_t attn_record(uint32_t groups, uint32_t hd) {
 }
 size_t attn_split_smem(uint32_t head_dim, uint32_t nbufs = 0);
 uint32_t attn_max_splits(uint32_t max_ctx);
+// The warp-split attend fits an item with `nbufs` chunk buffers at head_dim hd.
+bool attn_ws_fits(uint32_t hd, uint32_t nbufs);
 cudaError_t attn_split_set_smem_limits(int optin);
 cudaError_t launch_attn_split(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, cudaStream_t st);
 

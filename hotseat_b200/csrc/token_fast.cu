@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
         mark(11, tmark ? gtime() : 0);
     };
     if (ok) {
-        const uint32_t n = pos + 1, Ls = attn_split_len(n, a.attn.max_splits, a.attn.min_split), S = (n + Ls - 1) / Ls;
+        const uint32_t n = pos + 1, Ls = attn_split_len(n, a.attn.max_splits, a.attn.ws_from), S = (n + Ls - 1) / Ls;
         const uint32_t G_ = a.nh / nkv, rec = attn_record(G_, a.hd);
         // attention item i: split i / (nkv * hsp), KV head (i / hsp) % nkv,
         // query-head part i % hsp
@@ -503,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_token_fast(const __grid_constan
                 if (b < n_items) {
                     bool ws = false;
                     if constexpr (attn::WsGeom<HD, attn_buf(HD)>::OK) {
-                        ws = a.attn.warp_split != 0;
+                        ws = attn_use_ws(pos + 1, a.attn.ws_from);
                         if (ws) attn::ws_prefetch<HD, attn_buf(HD)>(a.attn, l, b / (nkv * hsp), (b / hsp) % nkv, 0, pos, att_sm);
                     }
                     if (!ws)
