@@ -385,6 +385,24 @@ def bench_extra(q05_path):
     return out
 
 
+def bench_c5(path, rank, world, local, dist):
+    """c5 - serving with live migration on the job's GPUs: 64 sequences per
+    GPU, 64-token prompts, 200 steps at temperature 0.8; every sequence is
+    migrated once, at a seeded position in [40, 160], to the next rank's GPU
+    (pre-copy into a region that rank owns, mapped by CUDA IPC; with one GPU
+    a second region on it), then the same run without migrations: aggregate
+    tok/s of both, the hand-overs' stop-the-world window, and whether every
+    transcript, RNG state and KV hash is unchanged. Host-driven lockstep
+    rounds of 8 tokens, so the rate is below the graph-driven headline."""
+    from hotseat_b200 import serve_dist
+    eng = serve_dist.GpuEngine(path, local, 64 + 200 + 8, 128)
+    try:
+        return serve_dist.serve_dist(eng, dist if world > 1 else serve_dist.Solo, rank, world, per=64,
+                                     prompt_len=64, steps=200, seed=7, round_tokens=8)
+    finally:
+        eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -431,6 +449,10 @@ def main():
         extra = {}
         if world == 1 and not args.no_extra:
             extra = bench_extra(path)
+        if not args.no_extra:
+            c5 = bench_c5(path, rank, world, local, dist)
+            if rank == 0:
+                extra["c5"] = c5
         if rank == 0:
             peaks = {}
             try:

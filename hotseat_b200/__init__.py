@@ -132,6 +132,8 @@ _SIGS = {
     "hs_kv_disarm": (C.c_int, [_P]),
     "hs_kv_copy_runs": (C.c_int, [_P, _P, _P, C.c_uint64]),
     "hs_kv_fingerprint": (C.c_int, [_P, _U64P]),
+    "hs_kv_ipc_handle": (C.c_int, [_P, _P, C.c_uint64]),
+    "hs_kv_open_ipc": (C.c_int, [_P, C.c_char_p, C.c_uint32, C.c_uint32, C.POINTER(_P)]),
     "hs_migrate_opts_default": (None, [C.POINTER(MigrateOpts)]),
     "hs_migrate_begin": (C.c_int, [_P, _P, C.POINTER(MigrateOpts), C.c_uint64, C.c_uint64, C.c_uint64,
                                    C.POINTER(_P)]),
@@ -288,6 +290,20 @@ class Kv:
     def alloc(cls, model, layout=TOKEN_MAJOR, page_size=4096):
         h = C.c_void_p()
         _check(_lib.hs_kv_alloc(model._h, layout, page_size, C.byref(h)))
+        return cls(h, model)
+
+    def ipc_handle(self):
+        """The region's CUDA IPC handle (bytes) for another process's open_ipc."""
+        buf = C.create_string_buffer(64)
+        _check(_lib.hs_kv_ipc_handle(self._h, buf, 64))
+        return buf.raw
+
+    @classmethod
+    def open_ipc(cls, model, handle, layout=TOKEN_MAJOR, page_size=4096):
+        """Map another process's region (same spec) on `model`'s GPU as a
+        hand-over destination."""
+        h = C.c_void_p()
+        _check(_lib.hs_kv_open_ipc(model._h, bytes(handle), layout, page_size, C.byref(h)))
         return cls(h, model)
 
     def close(self):

@@ -257,6 +257,7 @@ struct hs_kv {
     hs::XferRun *tab_h = nullptr, *tab_dev = nullptr;
     uint64_t tab_cap = 0;
     cudaEvent_t tab_ev = nullptr;
+    bool ipc_view = false;  // `base` maps another process's region (hs_kv_open_ipc)
     ~hs_kv() {
         cudaSetDevice(device);
         if (tab_ev) cudaEventSynchronize(tab_ev);
@@ -265,7 +266,10 @@ struct hs_kv {
         cudaFreeHost(tab_h);
         cudaFree(tab_dev);
         cudaFree(stage);
-        cudaFree(base);
+        if (ipc_view)
+            cudaIpcCloseMemHandle(base);
+        else
+            cudaFree(base);
         cudaFree(dirty);
         cudaFree(harvest_buf);
         cudaFree(tracking);
@@ -1111,6 +1115,51 @@ int hs_kv_alloc(const hs_model* m, uint32_t layout, uint32_t page_size, hs_kv** 
     HS_CUDA_TRY(cudaStreamCreateWithFlags(&kv->st, cudaStreamNonBlocking));
     HS_CUDA_TRY(cudaMalloc(&kv->base, kv->bytes));
     HS_CUDA_TRY(cudaMemset(kv->base, 0, kv->bytes));
+    HS_CUDA_TRY(cudaMalloc(&kv->dirty, kv->n_words * 8));
+    HS_CUDA_TRY(cudaMemset(kv->dirty, 0, kv->n_words * 8));
+    HS_CUDA_TRY(cudaMalloc(&kv->harvest_buf, kv->n_words * 8));
+    HS_CUDA_TRY(cudaMalloc(&kv->tracking, 4));
+    HS_CUDA_TRY(cudaMemset(kv->tracking, 0, 4));
+    HS_CUDA_TRY(cudaEventCreateWithFlags(&kv->tab_ev, cudaEventDisableTiming));
+    kv->n_sm = m->n_sm;
+    *out = kv.release();
+    return HS_OK;
+}
+
+int hs_kv_ipc_handle(hs_kv* kv, void* out, uint64_t out_bytes) {
+    if (!kv || !out) return fail(HS_E_ARG, "null argument");
+    if (out_bytes < sizeof(cudaIpcMemHandle_t)) return fail(HS_E_ARG, "handle buffer smaller than HS_IPC_HANDLE_BYTES");
+    if (kv->ipc_view) return fail(HS_E_ARG, "the region belongs to another process");
+    HS_CUDA_TRY(cudaSetDevice(kv->device));
+    cudaIpcMemHandle_t h;
+    HS_CUDA_TRY(cudaIpcGetMemHandle(&h, kv->base));
+    std::memcpy(out, &h, sizeof h);
+    return HS_OK;
+}
+
+int hs_kv_open_ipc(const hs_model* m, const void* handle, uint32_t layout, uint32_t page_size, hs_kv** out) {
+    if (!m || !handle || !out) return fail(HS_E_ARG, "null argument");
+    if (layout > 1) return fail(HS_E_ARG, "unknown KV layout");
+    if (page_size < 256 || (page_size & (page_size - 1))) return fail(HS_E_ARG, "page_size must be a power of two >= 256");
+    HS_CUDA_TRY(cudaSetDevice(m->device));
+    auto kv = std::make_unique<hs_kv>();
+    kv->device = m->device;
+    kv->spec = hs_kv_spec{m->cfg.n_layers, m->cfg.n_kv_heads, m->cfg.head_dim, m->cfg.max_ctx, layout};
+    kv->bytes = (uint64_t)kv->spec.n_layers * 2 * kv->spec.max_ctx * kv->spec.n_kv_heads * kv->spec.head_dim * 4;
+    kv->page_size = page_size;
+    kv->page_shift = (uint32_t)__builtin_ctz(page_size);
+    kv->n_pages = (kv->bytes + page_size - 1) / page_size;
+    kv->n_words = (kv->n_pages + 63) / 64;
+    kv->fingerprint = m->cfg.fingerprint;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof h);
+    void* p = nullptr;
+    HS_CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    kv->base = static_cast<float*>(p);
+    kv->ipc_view = true;
+    HS_CUDA_TRY(cudaStreamCreateWithFlags(&kv->st, cudaStreamNonBlocking));
+    // the view is written and read, never decoded into: its own page bits
+    // exist only so that every region has them
     HS_CUDA_TRY(cudaMalloc(&kv->dirty, kv->n_words * 8));
     HS_CUDA_TRY(cudaMemset(kv->dirty, 0, kv->n_words * 8));
     HS_CUDA_TRY(cudaMalloc(&kv->harvest_buf, kv->n_words * 8));

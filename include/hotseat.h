@@ -96,6 +96,18 @@ typedef struct {
  * PageSet's word/bit format (hs-track pageset.rs:10-34). */
 int hs_kv_alloc(const hs_model* m, uint32_t layout, uint32_t page_size, hs_kv** out);
 int hs_kv_info(const hs_kv* kv, hs_kv_spec* spec, uint64_t* bytes, uint32_t* page_size, uint64_t* n_pages);
+/* Cross-process hand-over on one node (the destination worker is another
+ * process, e.g. one rank per GPU): the owner exports its region with
+ * hs_kv_ipc_handle (a CUDA IPC handle, HS_IPC_HANDLE_BYTES bytes); the source
+ * process opens it with hs_kv_open_ipc on its own model and GPU, which maps
+ * the remote region for hs_kv_peer_copy / hs_kv_copy_runs / hs_migrate_* as
+ * a destination (stores over NVLink). A view is never decoded into; the
+ * owner must keep its region alive until the view is freed (hs_kv_free). No
+ * counterpart in the reference, whose hand-over crosses a TCP socket
+ * (hs-wire lib.rs:338-396). */
+#define HS_IPC_HANDLE_BYTES 64
+int hs_kv_ipc_handle(hs_kv* kv, void* out, uint64_t out_bytes);
+int hs_kv_open_ipc(const hs_model* m, const void* handle, uint32_t layout, uint32_t page_size, hs_kv** out);
 /* The fingerprint of the model the region was allocated for (the Hello
  * field model_fingerprint, hs-wire lib.rs / migrate.rs:250-258). */
 int hs_kv_fingerprint(const hs_kv* kv, uint64_t* out);
