@@ -24,7 +24,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC,-ffp-contract=off,-fno-fast-math",
           "-I" + os.path.join(HERE, "..", "include")]
-SOURCES = ["engine.cu", "decode.cu", "decode_fast.cu", "batch_tc.cu", "batch_ops.cu", "attn_split.cu", "token_fast.cu", "dequant.cu", "sample_noalloc.cu", "kv_xfer.cu", "migrate.cpp", "nll.cu", "gguf.cpp", "hostmath.cpp"]
+SOURCES = ["engine.cu", "decode.cu", "decode_fast.cu", "batch_tc.cu", "batch_ops.cu", "attn_split.cu", "attn_prefill.cu", "token_fast.cu", "dequant.cu", "sample_noalloc.cu", "kv_xfer.cu", "migrate.cpp", "nll.cu", "gguf.cpp", "hostmath.cpp"]
 HEADERS = ["common.h", "device.cuh", "kernels.h", "gguf.h", "attn_body.cuh"]
 
 

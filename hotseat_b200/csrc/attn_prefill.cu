@@ -1,0 +1,414 @@
+// Query-block causal GQA attention for prompt prefill on the tensor-core
+// path (hs_prefill): model.rs:259-305 for a pass of consecutive prompt
+// tokens of one sequence, whose k, v rows the append launch has already
+// written to the KV region.
+//
+// The per-token split-KV item (attn_split.cu) streams a token's whole prefix
+// of K/V for every token; here one CTA takes kRows = 64 query rows (the G
+// heads of one KV head for floor(64 / G) consecutive tokens) and one
+// segment of `seg` cached positions, so every K/V chunk it loads serves 64
+// rows. Segments are fixed in absolute positions ([s seg, (s+1) seg), seg
+// from max_ctx only), chunks of 64 positions run from the segment's start,
+// and each row's products, running maximum, sum and output are its own, so
+// a token's bits depend on its position and the KV contents only: never on
+// which tokens share its block, on the pass it is in or on the batch. A
+// token with one segment (pos < seg) is written normalised by the attend
+// kernel; otherwise each segment writes (unnormalised output, max, sum) and
+// the combine kernel merges the token's pos / seg + 1 segments in segment
+// order (attn::combine_staged, the split items' combine).
+//
+// Products: fp32 FMA chains on the CUDA cores, register-tiled. Scores: a
+// thread holds a 4 (rows) x 4 (positions) tile, q and K read from shared
+// memory as float4 along head_dim (q broadcast in the warp, K rows
+// swizzled so that a warp's 16 rows hit distinct banks). Online softmax per
+// row over the chunk (the 16 lanes holding a row reduce by shuffles).
+// P.V: the same thread holds the same 4 rows x head_dim/16 dimensions; P is
+// stored transposed [position][row] (swizzled) and read as float4 per
+// position, V rows as float4 per 16 lanes.
+//
+// Pipeline per chunk: K(c) and V(c) are separate commit groups; K(c+1)
+// loads while the softmax and P.V of chunk c run, V(c+1) while the scores of
+// chunk c+1 run. Shared memory (head_dim 128): q 32 KB + K 32 KB + V 32 KB +
+// P 16 KB = 112 KB, two CTAs per SM.
+#include <cfloat>
+
+#include "attn_body.cuh"
+#include "common.h"
+#include "kernels.h"
+
+namespace hs {
+namespace {
+
+constexpr uint32_t kRows = 64;  // query rows per CTA
+constexpr uint32_t kPCh = 64;   // positions per chunk
+constexpr uint32_t kPThreads = 256;
+
+template <int HD>
+struct PfGeom {
+    static constexpr uint32_t Q = kRows * HD, K = kPCh * HD, V = kPCh * HD, P = kPCh * kRows;
+    static constexpr size_t bytes = (size_t)(Q + K + V + P) * sizeof(float);
+};
+
+// float4 slot of dimension group k4 in row r of the q and K buffers
+__device__ __forceinline__ uint32_t swz(uint32_t k4, uint32_t r) { return k4 ^ (r & 7u); }
+
+__device__ __forceinline__ void store_out(const SplitAttnArgs& a, size_t at, float v) {
+    if (a.out_f32) {
+        a.out_f32[at] = v;
+    } else {
+        uint16_t hi, lo;
+        attn::split_f16(v, &hi, &lo);
+        a.out_hi[at] = hi;
+        a.out_lo[at] = lo;
+    }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kPThreads, 2)
+    k_prefill_attend(const SplitAttnArgs a, uint32_t slots, uint32_t qb_tokens, uint32_t seg) {
+    using Geo = PfGeom<HD>;
+    constexpr uint32_t NK4 = HD / 4, HALF = HD / 2, DJ = HD / 64;  // float4 groups of V per lane
+    extern __shared__ __align__(16) float sm[];
+    float* Qs = sm;
+    float* Ks = Qs + Geo::Q;
+    float* Vs = Ks + Geo::K;
+    float* Ps = Vs + Geo::V;
+    __shared__ uint32_t s_lim[kRows];  // per token of the block: pos + 1, or 0 (no such token)
+    __shared__ uint32_t s_max;
+    const uint32_t s = blockIdx.x, qb = blockIdx.y, kvh = blockIdx.z, tid = threadIdx.x;
+    const uint32_t Gf = a.nh / a.nkv, t0 = qb * qb_tokens;
+    const KTrace tr(a.trace, a.trace_slot);
+    tr.enter();
+    pdl_launch_dependents();
+    if (tid < kRows) {  // control blocks are host-written before the launch
+        uint32_t lim = 0;
+        if (tid < qb_tokens && t0 + tid < slots) {
+            const DevCtl* c = a.ctl + t0 + tid;
+            const uint32_t pos = attn::ldv(&c->pos);
+            if (attn::ldv(&c->active) != 0 && pos < a.max_ctx) lim = pos + 1;
+        }
+        s_lim[tid] = lim;
+    }
+    __syncthreads();
+    if (tid < 32) {
+        uint32_t m = s_lim[tid] > s_lim[tid + 32] ? s_lim[tid] : s_lim[tid + 32];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const uint32_t o = __shfl_xor_sync(0xffffffffu, m, off);
+            m = o > m ? o : m;
+        }
+        if (tid == 0) s_max = m;
+    }
+    __syncthreads();
+    const uint32_t lim_max = s_max, p_begin = s * seg;
+    if (lim_max <= p_begin) {  // no token of the block reaches this segment
+        tr.exit();
+        return;
+    }
+    const uint32_t p_end = p_begin + seg < lim_max ? p_begin + seg : lim_max;
+    const uint32_t nch = (p_end - p_begin + kPCh - 1) / kPCh;
+    const float* kv = a.kv[t0];
+    const uint32_t layer = a.layer;
+    auto load_k = [&](uint32_t c) {
+        if (c < nch) {
+            const uint32_t c0 = p_begin + c * kPCh, cnt = p_end - c0 < kPCh ? p_end - c0 : kPCh;
+            for (uint32_t i = tid; i < cnt * NK4; i += kPThreads) {
+                const uint32_t rr = i / NK4, k4 = i % NK4;
+                cp_async16(Ks + rr * HD + 4 * swz(k4, rr), kv + attn::kv_row_off(a, layer, kvh, HD, c0 + rr, 0) + 4 * k4);
+            }
+        }
+        attn::cp_commit();
+    };
+    auto load_v = [&](uint32_t c) {
+        if (c < nch) {
+            const uint32_t c0 = p_begin + c * kPCh, cnt = p_end - c0 < kPCh ? p_end - c0 : kPCh;
+            for (uint32_t i = tid; i < cnt * NK4; i += kPThreads) {
+                const uint32_t rr = i / NK4, k4 = i % NK4;
+                cp_async16(Vs + rr * HD + 4 * k4, kv + attn::kv_row_off(a, layer, kvh, HD, c0 + rr, 1) + 4 * k4);
+            }
+            // rows past the chunk's end: zero (their probabilities are 0,
+            // and 0 times a stale non-finite value would not be)
+            for (uint32_t i = cnt * NK4 + tid; i < kPCh * NK4; i += kPThreads)
+                reinterpret_cast<float4*>(Vs)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        attn::cp_commit();
+    };
+
+    // The QKV product and the appended rows come from the previous launches.
+    pdl_wait();
+    load_k(0);
+    load_v(0);
+
+    // q rows of the block: split-K partials in split order, then the bias,
+    // then RoPE at the token's position (model.rs:365-373); zero for rows
+    // without a token. Job = (row, dimension group k4 < HD/8): the float4
+    // pair (k4, k4 + HD/8) that RoPE rotates together.
+    for (uint32_t j = tid; j < kRows * (HD / 8); j += kPThreads) {
+        const uint32_t r = j / (HD / 8), k4 = j % (HD / 8), t = r / Gf, h = r % Gf;
+        float4 x0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), x1 = x0;
+        const uint32_t lim = r < qb_tokens * Gf ? s_lim[t] : 0u;
+        if (lim) {
+            const uint32_t pos = lim - 1, row = (kvh * Gf + h) * HD + 4 * k4;
+            const float* src = a.qkv + (size_t)(t0 + t) * a.qkv_rows + row;
+            for (uint32_t q = 0; q < a.n_part; q++) {
+                x0 = attn::f4add(x0, __ldcg(reinterpret_cast<const float4*>(src + q * a.part_stride)));
+                x1 = attn::f4add(x1, __ldcg(reinterpret_cast<const float4*>(src + q * a.part_stride + HALF)));
+            }
+            if (a.bias) {
+                x0 = attn::f4add(x0, *reinterpret_cast<const float4*>(a.bias + row));
+                x1 = attn::f4add(x1, *reinterpret_cast<const float4*>(a.bias + row + HALF));
+            }
+            const float4 c = *reinterpret_cast<const float4*>(a.rope_cos + (size_t)pos * HALF + 4 * k4);
+            const float4 sn = *reinterpret_cast<const float4*>(a.rope_sin + (size_t)pos * HALF + 4 * k4);
+            auto rot = [](float& u, float& w, float cc, float ss) {
+                const float u0 = u, w0 = w;
+                u = __fsub_rn(__fmul_rn(u0, cc), __fmul_rn(w0, ss));
+                w = __fadd_rn(__fmul_rn(u0, ss), __fmul_rn(w0, cc));
+            };
+            rot(x0.x, x1.x, c.x, sn.x);
+            rot(x0.y, x1.y, c.y, sn.y);
+            rot(x0.z, x1.z, c.z, sn.z);
+            rot(x0.w, x1.w, c.w, sn.w);
+        }
+        reinterpret_cast<float4*>(Qs + r * HD)[swz(k4, r)] = x0;
+        reinterpret_cast<float4*>(Qs + r * HD)[swz(k4 + HD / 8, r)] = x1;
+    }
+
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+    const uint32_t warp = tid >> 5, lane = tid & 31, rl = lane >> 4, cl = lane & 15;
+    const uint32_t r0 = warp * 8 + rl * 4, rg = r0 / 4;  // this thread's 4 rows, their float4 slot in P
+    uint32_t rlim[4];  // positions < rlim are this row's (0: no token)
+#pragma unroll
+    for (uint32_t ii = 0; ii < 4; ii++) {
+        const uint32_t r = r0 + ii;
+        rlim[ii] = r < qb_tokens * Gf ? s_lim[r / Gf] : 0u;
+    }
+    float m[4], l[4], acc[4][4 * DJ];
+#pragma unroll
+    for (uint32_t ii = 0; ii < 4; ii++) {
+        m[ii] = -FLT_MAX;
+        l[ii] = 0.0f;
+#pragma unroll
+        for (uint32_t d = 0; d < 4 * DJ; d++) acc[ii][d] = 0.0f;
+    }
+
+    for (uint32_t c = 0; c < nch; c++) {
+        const uint32_t c0 = p_begin + c * kPCh, cnt = p_end - c0 < kPCh ? p_end - c0 : kPCh;
+        attn::cp_wait<1>();  // K(c) (V(c) may still be in flight)
+        __syncthreads();
+        if (c == 0) tr.mark(1);
+        float sc[4][4];
+#pragma unroll
+        for (uint32_t ii = 0; ii < 4; ii++)
+#pragma unroll
+            for (uint32_t i = 0; i < 4; i++) sc[ii][i] = 0.0f;
+#pragma unroll 4
+        for (uint32_t k4 = 0; k4 < NK4; k4++) {
+            float4 q[4], k[4];
+#pragma unroll
+            for (uint32_t ii = 0; ii < 4; ii++) q[ii] = reinterpret_cast<const float4*>(Qs + (r0 + ii) * HD)[swz(k4, r0 + ii)];
+#pragma unroll
+            for (uint32_t i = 0; i < 4; i++) k[i] = reinterpret_cast<const float4*>(Ks + (cl + 16 * i) * HD)[swz(k4, cl)];
+#pragma unroll
+            for (uint32_t ii = 0; ii < 4; ii++)
+#pragma unroll
+                for (uint32_t i = 0; i < 4; i++) {
+                    float v = sc[ii][i];
+                    v = __fmaf_rn(q[ii].x, k[i].x, v);
+                    v = __fmaf_rn(q[ii].y, k[i].y, v);
+                    v = __fmaf_rn(q[ii].z, k[i].z, v);
+                    v = __fmaf_rn(q[ii].w, k[i].w, v);
+                    sc[ii][i] = v;
+                }
+        }
+        __syncthreads();  // K(c) consumed
+        load_k(c + 1);
+        // online softmax of the chunk per row; masked: past the chunk, past
+        // the row's position, rows without a token
+        float f[4];
+#pragma unroll
+        for (uint32_t ii = 0; ii < 4; ii++) {
+            float mx = -FLT_MAX;
+#pragma unroll
+            for (uint32_t i = 0; i < 4; i++) {
+                const uint32_t rr = cl + 16 * i;
+                const bool ok = rr < cnt && c0 + rr < rlim[ii];
+                sc[ii][i] = ok ? __fmul_rn(sc[ii][i], scale) : -FLT_MAX;
+                mx = fmaxf(mx, sc[ii][i]);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            // nothing of this row in the chunk: an exact no-op (f = 1, all
+            // probabilities 0, m and l kept). Selects, not a branch: both
+            // half-warps (different rows) take every shuffle.
+            const bool none = mx == -FLT_MAX;
+            const float mn = none ? m[ii] : fmaxf(m[ii], mx);
+            float sum = 0.0f;
+#pragma unroll
+            for (uint32_t i = 0; i < 4; i++) {
+                const float e = sc[ii][i] == -FLT_MAX ? 0.0f : __expf(__fsub_rn(sc[ii][i], mn));
+                sc[ii][i] = e;
+                sum = __fadd_rn(sum, e);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
+            f[ii] = none ? 1.0f : (m[ii] == -FLT_MAX ? 0.0f : __expf(__fsub_rn(m[ii], mn)));
+            l[ii] = none ? l[ii] : __fadd_rn(__fmul_rn(l[ii], f[ii]), sum);
+            m[ii] = mn;
+        }
+#pragma unroll
+        for (uint32_t i = 0; i < 4; i++) {
+            const uint32_t col = cl + 16 * i;
+            reinterpret_cast<float4*>(Ps + col * kRows)[rg ^ (col & 15u)] =
+                make_float4(sc[0][i], sc[1][i], sc[2][i], sc[3][i]);
+        }
+        attn::cp_wait<1>();  // V(c) (K(c+1) may still be in flight)
+        __syncthreads();
+#pragma unroll
+        for (uint32_t ii = 0; ii < 4; ii++)
+#pragma unroll
+            for (uint32_t d = 0; d < 4 * DJ; d++) acc[ii][d] = __fmul_rn(acc[ii][d], f[ii]);
+#pragma unroll 4
+        for (uint32_t j = 0; j < cnt; j++) {
+            const float4 p = reinterpret_cast<const float4*>(Ps + j * kRows)[rg ^ (j & 15u)];
+            const float pr[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+            for (uint32_t dj = 0; dj < DJ; dj++) {
+                const float4 v = reinterpret_cast<const float4*>(Vs + j * HD)[cl + 16 * dj];
+#pragma unroll
+                for (uint32_t ii = 0; ii < 4; ii++) {
+                    acc[ii][4 * dj + 0] = __fmaf_rn(pr[ii], v.x, acc[ii][4 * dj + 0]);
+                    acc[ii][4 * dj + 1] = __fmaf_rn(pr[ii], v.y, acc[ii][4 * dj + 1]);
+                    acc[ii][4 * dj + 2] = __fmaf_rn(pr[ii], v.z, acc[ii][4 * dj + 2]);
+                    acc[ii][4 * dj + 3] = __fmaf_rn(pr[ii], v.w, acc[ii][4 * dj + 3]);
+                }
+            }
+        }
+        __syncthreads();  // V(c) and P consumed
+        load_v(c + 1);
+    }
+    attn::cp_wait0();
+    tr.mark(2);
+
+    // rows of a token with one segment: the normalised output; otherwise this
+    // segment's record (rows whose token does not reach it write nothing)
+    const uint32_t rec = attn_record(Gf, HD);
+#pragma unroll
+    for (uint32_t ii = 0; ii < 4; ii++) {
+        const uint32_t r = r0 + ii;
+        if (rlim[ii] <= p_begin) continue;
+        const uint32_t slot = t0 + r / Gf, h = r % Gf;
+        if (rlim[ii] <= seg) {
+            const size_t o = (size_t)slot * a.out_stride + (size_t)(kvh * Gf + h) * HD;
+#pragma unroll
+            for (uint32_t dj = 0; dj < DJ; dj++)
+#pragma unroll
+                for (uint32_t e = 0; e < 4; e++)
+                    store_out(a, o + 4 * (cl + 16 * dj) + e, __fdiv_rn(acc[ii][4 * dj + e], l[ii]));
+        } else {
+            float* part = a.partials + ((size_t)(slot * a.nkv + kvh) * a.max_splits + s) * rec;
+#pragma unroll
+            for (uint32_t dj = 0; dj < DJ; dj++)
+                reinterpret_cast<float4*>(part + h * HD)[cl + 16 * dj] =
+                    make_float4(acc[ii][4 * dj], acc[ii][4 * dj + 1], acc[ii][4 * dj + 2], acc[ii][4 * dj + 3]);
+            if (cl == 0) {
+                part[Gf * HD + h] = m[ii];
+                part[Gf * HD + Gf + h] = l[ii];
+            }
+        }
+    }
+    tr.exit();
+}
+
+// Merge of a token's segments (pos / seg + 1 of them, when more than one),
+// one CTA per (KV head, token).
+template <int HD>
+__global__ void __launch_bounds__(kPThreads) k_prefill_combine(const SplitAttnArgs a, uint32_t seg) {
+    extern __shared__ __align__(16) float sm[];
+    const uint32_t kvh = blockIdx.x, slot = blockIdx.y;
+    const KTrace tr(a.trace, a.trace_slot);
+    tr.enter();
+    const DevCtl* c = a.ctl + slot;
+    const bool active = attn::ldv(&c->active) != 0;
+    const uint32_t pos = attn::ldv(&c->pos);
+    pdl_launch_dependents();
+    pdl_wait();
+    if (active && pos < a.max_ctx && pos >= seg) {
+        const uint32_t S = pos / seg + 1, Gf = a.nh / a.nkv;
+        const float* part = a.partials + (size_t)(slot * a.nkv + kvh) * a.max_splits * attn_record(Gf, HD);
+        const size_t o = (size_t)slot * a.out_stride + (size_t)kvh * Gf * HD;
+        attn::combine_staged(part, S, Gf, HD, sm, [&](uint32_t idx, float v) { store_out(a, o + idx, v); });
+    }
+    tr.exit();
+}
+
+size_t combine_smem(uint32_t hd, uint32_t nseg, uint32_t G) {
+    return ((size_t)3 * nseg * G + 20 + (size_t)attn::kCombTile * G * hd) * sizeof(float);
+}
+
+}  // namespace
+
+uint32_t attn_prefill_seg(uint32_t max_ctx) {
+    const uint32_t chunks = (max_ctx + kPCh - 1) / kPCh;
+    const uint32_t seg = (chunks + kPrefillMaxSegs - 1) / kPrefillMaxSegs * kPCh;
+    return seg > 256 ? seg : 256;
+}
+
+uint32_t attn_prefill_segs(uint32_t max_ctx) {
+    const uint32_t seg = attn_prefill_seg(max_ctx);
+    return (max_ctx + seg - 1) / seg;
+}
+
+bool attn_prefill_supported(uint32_t head_dim, uint32_t nh, uint32_t nkv) {
+    return (head_dim == 64 || head_dim == 128) && nkv && nh % nkv == 0 && nh / nkv <= 8;
+}
+
+cudaError_t attn_prefill_set_smem_limits(int optin) {
+    const void* fa[] = {(const void*)k_prefill_attend<64>, (const void*)k_prefill_attend<128>};
+    const size_t na[] = {PfGeom<64>::bytes, PfGeom<128>::bytes};
+    for (int i = 0; i < 2; i++) {
+        if (na[i] > (size_t)optin) continue;
+        const cudaError_t e = cudaFuncSetAttribute(fa[i], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)na[i]);
+        if (e != cudaSuccess) return e;
+    }
+    const void* fc[] = {(const void*)k_prefill_combine<64>, (const void*)k_prefill_combine<128>};
+    const uint32_t hds[] = {64, 128};
+    for (int i = 0; i < 2; i++) {
+        const size_t need = combine_smem(hds[i], kPrefillMaxSegs, 8);
+        const cudaError_t e = cudaFuncSetAttribute(fc[i], cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)(need < (size_t)optin ? need : (size_t)optin));
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+cudaError_t launch_attn_prefill(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, uint32_t seg,
+                                cudaStream_t st, uint32_t trace_slot) {
+    if (!attn_prefill_supported(head_dim, a.nh, a.nkv) || seg == 0 || slots == 0 || (!a.out_f32 && !a.out_hi))
+        return cudaErrorInvalidValue;
+    const uint32_t G = a.nh / a.nkv, qb_tokens = kRows / G;
+    const uint32_t nseg = (a.max_ctx + seg - 1) / seg;
+    if (nseg > a.max_splits || nseg > kPrefillMaxSegs) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(nseg, (slots + qb_tokens - 1) / qb_tokens, a.nkv);
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = head_dim == 64 ? PfGeom<64>::bytes : PfGeom<128>::bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    SplitAttnArgs b = a;
+    b.trace_slot = trace_slot;
+    cudaError_t e = head_dim == 64 ? cudaLaunchKernelEx(&cfg, k_prefill_attend<64>, b, slots, qb_tokens, seg)
+                                   : cudaLaunchKernelEx(&cfg, k_prefill_attend<128>, b, slots, qb_tokens, seg);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(a.nkv, slots, 1);
+    cfg.dynamicSmemBytes = combine_smem(head_dim, nseg, G);
+    b.trace_slot = trace_slot + 1;
+    return head_dim == 64 ? cudaLaunchKernelEx(&cfg, k_prefill_combine<64>, b, seg)
+                          : cudaLaunchKernelEx(&cfg, k_prefill_combine<128>, b, seg);
+}
+
+}  // namespace hs

@@ -223,6 +223,8 @@ struct hs_model {
     uint32_t attn_nbuf = 0;        // K/V chunk buffers per item (0 = by head_dim)
     uint32_t attn_unstaged = 0;    // HS_ATTN_UNSTAGED_COMBINE=1: the per-element combine (same bits; measurement)
     uint32_t attn_ws_from = 0;     // warp-split item form from this many positions on (0: never)
+    bool pf_qblock = false;        // prefill attends by query blocks (attn_prefill.cu)
+    uint32_t pf_seg = 0, pf_nseg = 0;  // its segment length and segments per token at most
     uint32_t numeric = HS_NUMERIC_REFERENCE;
     TcGemmPlan thead;             // tensor-core LM head
     bool tok = false;             // fast path: one persistent kernel per token (token_fast.cu)
@@ -952,6 +954,14 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
         m->attn_ws_from = env_u32("HS_ATTN_WS_FROM", tc ? 0u : 8192u);
         if (!tc && !attn_ws_fits(hd, 1)) m->attn_ws_from = 0;
         HS_CUDA_TRY(attn_split_set_smem_limits(optin));
+        // Prefill attends by query blocks (64 rows share each K/V chunk);
+        // HS_PREFILL_ATTN=0 keeps the per-token split items (measurement).
+        if (tc && attn_prefill_supported(hd, n_heads, n_kv) && env_u32("HS_PREFILL_ATTN", 1) != 0) {
+            m->pf_qblock = true;
+            m->pf_seg = attn_prefill_seg(max_ctx);
+            m->pf_nseg = attn_prefill_segs(max_ctx);
+            HS_CUDA_TRY(attn_prefill_set_smem_limits(optin));
+        }
     }
     m->attn_smem = m->attn_split ? attn_split_smem(hd, m->attn_nbuf) : attention_smem(hd, max_ctx);
     if (!m->attn_split && m->attn_smem > m->smem_cap) {
@@ -1873,6 +1883,7 @@ struct hs_batch {
     float* sc_global = nullptr;    // attention scores for long contexts [cap_slots][nh][max_ctx]
     float* att_part = nullptr;     // split-KV attention partials [cap_slots][nkv][max_splits][record]
     uint32_t* att_cnt = nullptr;   // [cap_slots][nkv]
+    float* pf_part = nullptr;      // prefill segment records [cap_slots][nkv][pf_nseg][record], at first prefill
     uint64_t* trace = nullptr;     // launch timeline (HS_TRACE=1 at creation): 8 u64 per launch
     uint64_t* trace_init = nullptr;
     uint32_t trace_slots = 0;
@@ -1894,7 +1905,7 @@ struct hs_batch {
                         (void*)hb_hi, (void*)hb_lo, (void*)ctl, (void*)tokens, (void*)tok_tab, (void*)kv_tab,
                         (void*)dirty_tab, (void*)track_tab, (void*)cand, (void*)argbuf, (void*)err,
                         (void*)sc_global, (void*)att_part, (void*)att_cnt, (void*)sort_cand, (void*)wkeys,
-                        (void*)wps, (void*)nll, (void*)nll_next})
+                        (void*)wps, (void*)nll, (void*)nll_next, (void*)pf_part})
             cudaFree(p);
     }
 };
@@ -2017,7 +2028,15 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool pref
                 sa.mode = ATTN_ATTEND_ONLY;
                 sa.trace_slot = *launches;
             }
-            e = launch_attn_split(hd, sa, n, b->st);
+            if (prefill && m->pf_qblock) {
+                // query blocks over fixed segments, then the segments' merge
+                sa.partials = b->pf_part;
+                sa.max_splits = m->pf_nseg;
+                e = launch_attn_prefill(hd, sa, n, m->pf_seg, b->st, *launches);
+                if (e == cudaSuccess) (*launches)++;
+            } else {
+                e = launch_attn_split(hd, sa, n, b->st);
+            }
         } else {
             return fail(HS_E_STATE, "internal: tensor-core model without split attention");
         }
@@ -2189,7 +2208,7 @@ int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out) {
     HS_CUDA_TRY(cudaMallocHost(&b->tab_h, (size_t)3 * C * sizeof(void*)));
     const char* tenv = getenv("HS_TRACE");
     if (tenv && tenv[0] == '1') {
-        b->trace_slots = c.n_layers * 8 + 5;  // prefill: 8 launches a layer; decode: 7 + norm, head, sampler
+        b->trace_slots = c.n_layers * 9 + 5;  // prefill: 9 launches a layer; decode: 7 + norm, head, sampler
         HS_CUDA_TRY(cudaMalloc(&b->trace, (size_t)b->trace_slots * 64));
         HS_CUDA_TRY(cudaMallocHost(&b->trace_init, (size_t)b->trace_slots * 64));
         for (uint32_t i = 0; i < b->trace_slots; i++) {
@@ -2255,6 +2274,9 @@ int hs_prefill(const hs_model* m, hs_kv* kv, const uint32_t* tokens, uint32_t n,
         if (tokens[i] >= m->cfg.vocab) return fail(HS_E_ARG, "token " + std::to_string(tokens[i]) + " out of range");
     HS_CUDA_TRY(cudaSetDevice(m->device));
     const uint32_t C = b->cap_slots;
+    if (m->pf_qblock && !b->pf_part)
+        HS_CUDA_TRY(cudaMalloc(&b->pf_part, (size_t)C * m->cfg.n_kv_heads * m->pf_nseg *
+                                                attn_record(m->cfg.n_heads / m->cfg.n_kv_heads, m->cfg.head_dim) * 4));
     std::vector<hs_kv*> same(std::min(C, std::max(n, 1u)), kv);
     for (uint32_t off = 0; off < n; off += C) {
         const uint32_t cnt = std::min(C, n - off);

@@ -231,6 +231,20 @@ bool attn_ws_fits(uint32_t hd, uint32_t nbufs);
 cudaError_t attn_split_set_smem_limits(int optin);
 cudaError_t launch_attn_split(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, cudaStream_t st);
 
+// Prompt prefill attention by query blocks (attn_prefill.cu): the ATTEND_ONLY
+// half of a prefill pass (every slot one token of the same sequence, whose
+// k, v rows are appended), over segments of attn_prefill_seg(max_ctx)
+// positions with their records in a.partials [slots][nkv][a.max_splits]
+// [attn_record] (a.max_splits >= attn_prefill_segs(max_ctx)), then their
+// merge: two launches, trace slots trace_slot and trace_slot + 1.
+constexpr uint32_t kPrefillMaxSegs = 32;
+uint32_t attn_prefill_seg(uint32_t max_ctx);
+uint32_t attn_prefill_segs(uint32_t max_ctx);
+bool attn_prefill_supported(uint32_t head_dim, uint32_t nh, uint32_t nkv);
+cudaError_t attn_prefill_set_smem_limits(int optin);
+cudaError_t launch_attn_prefill(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, uint32_t seg,
+                                cudaStream_t st, uint32_t trace_slot);
+
 cudaError_t launch_tc_norm(const TcNormArgs& a, uint32_t slots, cudaStream_t st);
 
 // One decode token of the fast path as one persistent kernel (token_fast.cu).

@@ -448,12 +448,15 @@ def bench_prefill_trace(prompt=2048, pass_tokens=512):
     t = b.trace().astype(np.int64)
     L = c["n_layers"]
     names = ["norm", "qkv", "append", "attend", "o", "ffn_norm", "gate_up", "down"]
+    if os.environ.get("HS_PREFILL_ATTN", "1") != "0":  # query-block attend, then the segments' merge
+        names.insert(4, "combine")
+    P = len(names)
     per = {}
     for j, k in enumerate(names):
-        per[k] = float(np.mean([(t[l * 8 + j, 2] - t[l * 8 + j - 1, 2]) / 1e3 for l in range(1, L - 1)]))
+        per[k] = float(np.mean([(t[l * P + j, 2] - t[l * P + j - 1, 2]) / 1e3 for l in range(1, L - 1)]))
     print(json.dumps({"bench": "prefill_pass", "model": "qwen2.5-1.5b-shape", "positions": [head, prompt - 2],
                       "exit_to_exit_us": per, "layer_us": sum(per.values()),
-                      "pass_ms": float((t[L * 8 - 1, 2] - t[0, 0]) / 1e6)}), flush=True)
+                      "pass_ms": float((t[L * P - 1, 2] - t[0, 0]) / 1e6)}), flush=True)
     kv.close()
     b.close()
     m.close()

@@ -5,7 +5,14 @@ Prefill GEMMs use wide weight tiles and no K split (the prompt's tokens
 give the parallelism), so their sums are ordered differently from the decode
 steps': the KV rows match token-by-token decoding within the path's
 tolerance, greedy continuations are identical, prefill in pieces is
-bit-identical to one call, and the greedy tokens match the CPU path."""
+bit-identical to one call, and the greedy tokens match the CPU path.
+
+Prefill attention runs by query blocks over fixed segments of cached
+positions (attn_prefill.cu); HS_PREFILL_ATTN=0 at model load keeps the
+per-token split items. The two agree within tolerance on prompts that span
+several segments, and a token's bits do not depend on the pass it is in."""
+import os
+
 import numpy as np
 import pytest
 
@@ -13,7 +20,7 @@ import hotseat_b200 as hs
 from tests.golden.synth import QWEN05
 from oracle import ffi
 
-from conftest import TINY
+from conftest import TINY, TINY128
 
 pytestmark = pytest.mark.gpu
 
@@ -75,3 +82,63 @@ def test_prefill_rejects_bad_input(tiny_gguf):
         b.prefill(kv, [1, 2, TINY["vocab"]])
     with pytest.raises(hs.HotseatError):
         b.prefill(kv, [1, 2], pos0=63)
+
+
+def _load(path, max_ctx, qblock):
+    old = os.environ.get("HS_PREFILL_ATTN")
+    os.environ["HS_PREFILL_ATTN"] = "1" if qblock else "0"
+    try:
+        return hs.Model.load(path, max_ctx=max_ctx, numeric=TC)
+    finally:
+        if old is None:
+            del os.environ["HS_PREFILL_ATTN"]
+        else:
+            os.environ["HS_PREFILL_ATTN"] = old
+
+
+@pytest.mark.parametrize("shape,n", [("tiny", 700), ("tiny128", 700), ("q05", 600), ("tiny128", 200)])
+def test_query_block_prefill_matches_the_per_token_items(shape, n, request):
+    """Several 256-position segments (and one, at 200): the same KV rows and
+    next-token logits as the per-token split items within tolerance."""
+    path, vocab = {"tiny": ("tiny_gguf", TINY["vocab"]), "tiny128": ("tiny128_gguf", TINY128["vocab"]),
+                   "q05": ("q05_gguf", QWEN05["vocab"])}[shape]
+    path = request.getfixturevalue(path)
+    prompt = [int(t) for t in np.random.default_rng(n).integers(0, vocab, size=n)]
+    got = []
+    for qblock in (True, False):
+        m = _load(path, 1024, qblock)
+        kv = m.kv()
+        hs.Batch(m, 256).prefill(kv, prompt[:-1])
+        b = hs.Batch(m, 1)
+        b.forward([kv], [prompt[-1]], [n - 1])
+        got.append((kv.floats(), b.logits(0)))
+    kv_err = float(np.max(np.abs(got[0][0] - got[1][0])))
+    logit_err = float(np.max(np.abs(got[0][1] - got[1][1])))
+    print(f"{shape}, {n - 1} prompt tokens: KV {kv_err:.3g}, logits {logit_err:.3g}")
+    assert kv_err <= 1e-3 and logit_err <= 1e-2
+
+
+def test_query_block_prefill_in_pieces_equals_one_call_across_segments(tiny128_gguf):
+    """Passes cut at 301 and at multiples of 128 put the tokens in different
+    query blocks: the KV region is bit-identical."""
+    m = hs.Model.load(tiny128_gguf, max_ctx=1024, numeric=TC)
+    prompt = [int(t) for t in np.random.default_rng(31).integers(0, TINY128["vocab"], size=700)]
+    b = hs.Batch(m, 128)
+    one, two = m.kv(), m.kv()
+    b.prefill(one, prompt)
+    b.prefill(two, prompt[:301])
+    b.prefill(two, prompt[301:], pos0=301)
+    assert one.hash(700) == two.hash(700)
+
+
+def test_query_block_prefill_then_decode_matches_token_by_token(tiny128_gguf):
+    m = hs.Model.load(tiny128_gguf, max_ctx=1024, numeric=TC)
+    prompt = [int(t) for t in np.random.default_rng(5).integers(0, TINY128["vocab"], size=600)]
+    cfg = hs.SamplerCfg.default(temperature=0.0)
+    kv_a = m.kv()
+    ref = hs.Batch(m, 1).run_seqs([kv_a], [state(prompt, 600, 16, cfg, 2)])[0]
+    kv_b = m.kv()
+    hs.Batch(m, 512).prefill(kv_b, prompt[:-1])
+    got = hs.Batch(m, 1).run_seqs([kv_b], [state(prompt, 600, 16, cfg, 2, filled=599)])[0]
+    assert list(got[0]) == list(ref[0])
+    assert float(np.max(np.abs(kv_a.floats() - kv_b.floats()))) <= 1e-3
