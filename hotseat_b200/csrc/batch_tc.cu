@@ -175,7 +175,11 @@ constexpr uint32_t kXchgStride = 33;  // floats per slot row of the hi/lo exchan
 // epilogue the B operand stacks the gate tile over the up tile (N = 2*nt).
 //
 // Work unit = (weight-row tile of n_tile rows, K split). A CTA takes units
-// blockIdx.x, +gridDim.x, ...; blockIdx.y picks the 64-slot group.
+// blockIdx.x, +gridDim.x, ...; blockIdx.y picks the 64-slot group. With
+// m_loop (prompt passes: many 64-slot groups) the grid is one row and a CTA
+// walks items = (unit, group) i = blockIdx.x, +gridDim.x, ... (unit i %
+// units, group i / units), so the CTAs sweep the groups together and each
+// item's epilogue overlaps the next item's MMAs.
 // Shared memory: [nst stages: A hi | A lo | W0 (| W1)][xchg][barriers][tmem slot].
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -208,17 +212,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tr.enter();
 
     const uint32_t kt_n = a.K / 64, S = a.splits, n_units = a.n_tiles * S;
-    const uint32_t m0 = blockIdx.y * 64;
-    const TcAcc acc = tc_acc(NMAT, nt, n_units > gridDim.x);
+    const uint32_t n_items = a.m_loop ? n_units * ((a.slots + 63) / 64) : n_units;
+    auto item_m0 = [&](uint32_t i) -> uint32_t { return a.m_loop ? i / n_units * 64 : blockIdx.y * 64; };
+    const TcAcc acc = tc_acc(NMAT, nt, n_items > gridDim.x);
     const uint32_t buf_cols = acc.nacc * N;
     auto k_range = [&](uint32_t split, uint32_t* k0, uint32_t* k1) {
         *k0 = split * kt_n / S;
         *k1 = (split + 1) * kt_n / S;
     };
     uint32_t total_its = 0;
-    for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+    for (uint32_t i = blockIdx.x; i < n_items; i += gridDim.x) {
         uint32_t k0, k1;
-        k_range(u % S, &k0, &k1);
+        k_range(i % n_units % S, &k0, &k1);
         total_its += k1 - k0;
     }
 
@@ -254,9 +259,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (NMAT == 2) prefetch_tmap(&tm_w1);
             prefetch_tmap(&tm_ahi);
             prefetch_tmap(&tm_alo);
-            uint32_t it = 0, deferred[kMaxStages];
+            uint32_t it = 0, deferred[kMaxStages], deferred_m[kMaxStages];
             bool waited = false;
-            auto a_load = [&](uint32_t s, uint32_t kt) {
+            auto a_load = [&](uint32_t s, uint32_t kt, uint32_t m0) {
                 uint8_t* st = smem + s * stage_bytes;
                 tma_load_2d(st, &tm_ahi, (int)(kt * 64), (int)m0, &full[s]);
                 tma_load_2d(st + a_half, &tm_alo, (int)(kt * 64), (int)m0, &full[s]);
@@ -284,13 +289,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             break;
                         }
                         mbar_expect_tx(&full[s], stage_bytes);
-                        a_load(s, kt);
+                        a_load(s, kt, item_m0(u));
                     }
                 }
                 waited = true;
             }
-            for (uint32_t u = blockIdx.x; u < n_units && ok && !wres; u += gridDim.x) {
-                const uint32_t tile = u / S;
+            for (uint32_t i = blockIdx.x; i < n_items && ok && !wres; i += gridDim.x) {
+                const uint32_t u = i % n_units, tile = u / S, m0 = item_m0(i);
                 uint32_t k0, k1;
                 k_range(u % S, &k0, &k1);
                 for (uint32_t kt = k0; kt < k1; kt++, it++) {
@@ -304,14 +309,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tma_load_2d(st, &tm_w0, (int)(kt * 64), (int)(tile * nt), &full[s]);
                     if (NMAT == 2) tma_load_2d(st + w_bytes, &tm_w1, (int)(kt * 64), (int)(tile * nt), &full[s]);
                     if (waited) {
-                        a_load(s, kt);
+                        a_load(s, kt, m0);
                     } else {
                         deferred[it] = kt;
+                        deferred_m[it] = m0;
                         if (it + 1 == nst || it + 1 == total_its) {
                             pdl_wait();
                             if (a.trace && blockIdx.x == 0 && blockIdx.y == 0) a.trace[8 * a.trace_slot + 1] = gtime();
                             waited = true;
-                            for (uint32_t i = 0; i <= it; i++) a_load(i, deferred[i]);
+                            for (uint32_t j = 0; j <= it; j++) a_load(j, deferred[j], deferred_m[j]);
                         }
                     }
                 }
@@ -324,7 +330,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t idesc = tc_idesc(128, N);
             uint32_t it = 0, t = 0;
             if (wres && blockIdx.x < n_units && !mbar_wait_bounded(wfull, 0, kLimit)) ok = false;
-            for (uint32_t u = blockIdx.x; u < n_units && ok; u += gridDim.x, t++) {
+            for (uint32_t i = blockIdx.x; i < n_items && ok; i += gridDim.x, t++) {
+                const uint32_t u = i % n_units;
                 const uint32_t b = t % acc.nbuf, use = t / acc.nbuf;
                 if (use > 0 && !mbar_wait_bounded(&tempty[b], (use - 1) & 1, kLimit)) {
                     ok = false;
@@ -366,11 +373,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         pdl_wait();
         const bool hi_warp = warp < 2;
         const uint32_t sl = (warp & 1) * 32 + lane;  // slot within the 64-slot group
-        const uint32_t slot = m0 + sl;
-        const bool live = slot < a.slots;
         const bool vec = (a.ld & 3) == 0;
         uint32_t t = 0;
-        for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x, t++) {
+        for (uint32_t i = blockIdx.x; i < n_items; i += gridDim.x, t++) {
+            const uint32_t u = i % n_units, slot = item_m0(i) + sl;
+            const bool live = slot < a.slots;
             const uint32_t b = t % acc.nbuf, use = t / acc.nbuf;
             // One thread waits; the named barrier makes the outcome (and the
             // accumulator) visible to all four warps, which then leave or
@@ -506,7 +513,8 @@ cudaError_t launch_tc_gemm(const TcGemmPlan& p, const CUtensorMap& ahi, const CU
     if (p.nst == 0 || p.nst > kMaxStages || !tc_tile_ok(p.n_tile, silu) || p.K % 64 || p.splits == 0 ||
         p.splits > p.K / 64 || (silu && p.splits != 1) || a.n_tile != p.n_tile || a.splits != p.splits ||
         a.nst != p.nst || a.K != p.K || a.wres != (p.wres ? 1u : 0u) ||
-        (p.wres && p.n_tiles * p.splits > p.grid))  // weights resident: one unit per CTA
+        (p.wres && p.n_tiles * p.splits > p.grid) ||  // weights resident: one unit per CTA
+        a.m_loop != (p.m_loop ? 1u : 0u) || (p.m_loop && (p.wres || p.m_tiles != 1)))
         return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(p.grid, p.m_tiles);

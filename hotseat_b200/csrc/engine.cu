@@ -452,11 +452,31 @@ int plan_tc(TcGemmPlan* p, int epi, uint32_t rows, uint32_t K, const uint16_t* w
     p->rows = rows;
     p->splits = 1;
     if (prefill) {
-        // Prompt passes bring many 64-token M tiles: wide weight tiles, one
-        // K split, parallelism from the M dimension.
-        uint32_t nt = silu ? 64 : 128;
+        // Prompt passes bring many 64-token groups. These GEMMs are bound by
+        // the latency of each k-block's loads, not by bandwidth (measured: L2
+        // and tensor pipes both under a quarter busy), so the widest weight
+        // tiles (N = 256: twice the MMA work per k-block of 128) and CTAs
+        // that walk (tile, group) items; the partial-sum GEMMs add a K split
+        // fixed per model, the one with the fewest k-blocks on the busiest
+        // CTA over a 1024-token pass (a token's bits then depend on the
+        // model only, never on the pass).
+        uint32_t nt = silu ? env_u32("HS_TC_PREFILL_SILU_TILE", 128) : env_u32("HS_TC_PREFILL_TILE", 256);
         while (nt > 16 && nt / 2 >= rows) nt /= 2;
         p->n_tile = nt;
+        p->m_loop = env_u32("HS_TC_PREFILL_MLOOP", 1) != 0;
+        if (epi == TC_PART && p->m_loop) {
+            const uint32_t tiles = (rows + nt - 1) / nt, groups = 1024 / 64;
+            const uint32_t max_s = std::min<uint32_t>(env_u32("HS_TC_PREFILL_MAX_SPLITS", 8), std::max<uint32_t>(1, kt_n / 4));
+            uint64_t best = ~0ull;
+            for (uint32_t S = 1; S <= max_s; S++) {
+                const uint64_t items = (uint64_t)tiles * groups * S, rounds = (items + sm - 1) / sm;
+                const uint64_t cost = rounds * ((kt_n + S - 1) / S);
+                if (cost < best) {
+                    best = cost;
+                    p->splits = S;
+                }
+            }
+        }
     } else if (silu) {
         uint32_t nt = 8;
         while (nt < 128 && (rows + nt - 1) / nt > sm) nt += 8;
@@ -492,7 +512,7 @@ int plan_tc(TcGemmPlan* p, int epi, uint32_t rows, uint32_t K, const uint16_t* w
     const uint32_t units = p->n_tiles * p->splits;
     p->grid = std::min<uint32_t>(units, sm);
     p->m_tiles = 1;
-    const uint32_t per_cta = (units + p->grid - 1) / p->grid * ((kt_n + p->splits - 1) / p->splits);
+    const uint32_t per_cta = (p->m_loop ? 16 : (units + p->grid - 1) / p->grid) * ((kt_n + p->splits - 1) / p->splits);
     uint32_t nst = std::min<uint32_t>(16, per_cta);
     // A smaller budget lets the next kernel's CTA share the SM and start its
     // weight prefetch (programmatic dependent launch) while this one drains.
@@ -503,7 +523,7 @@ int plan_tc(TcGemmPlan* p, int epi, uint32_t rows, uint32_t K, const uint16_t* w
     // One unit per CTA: keep all its weight boxes in shared memory, loaded
     // before the dependency wait, and stream only the activations after it
     // (HS_TC_WRES=0 keeps weights and activations in the same stages).
-    if (units <= p->grid && env_u32("HS_TC_WRES", 1) != 0) {
+    if (units <= p->grid && !p->m_loop && env_u32("HS_TC_WRES", 1) != 0) {
         const uint32_t kw = (kt_n + p->splits - 1) / p->splits;
         uint32_t na = std::min<uint32_t>(16, kw);
         while (na > 1 && tc_gemm_smem_wres(p->n_tile, na, silu, kw) > smem_cap) na--;
@@ -1927,6 +1947,10 @@ int batch_gemm(hs_batch* b, const TcGemmPlan& p, const uint16_t* a_hi, const uin
     if (rc) return rc;
     TcGemmPlan q = p;
     q.m_tiles = (n + 63) / 64;
+    if (p.m_loop) {  // one grid row of at most one CTA per SM walking all (unit, group) items
+        q.grid = std::min<uint32_t>(p.n_tiles * p.splits * q.m_tiles, (uint32_t)b->m->n_sm);
+        q.m_tiles = 1;
+    }
     TcGemmArgs a{};
     a.K = p.K;
     a.rows = p.rows;
@@ -1936,6 +1960,7 @@ int batch_gemm(hs_batch* b, const TcGemmPlan& p, const uint16_t* a_hi, const uin
     a.slots = n;
     a.nst = p.nst;
     a.wres = p.wres ? 1u : 0u;
+    a.m_loop = p.m_loop ? 1u : 0u;
     a.ld = ld;
     a.part_stride = (uint64_t)b->cap_slots * p.rows;
     a.out = out;

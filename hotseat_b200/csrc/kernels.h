@@ -129,6 +129,7 @@ struct TcGemmArgs {
     uint32_t wres;           // 1: the CTA's one unit keeps all its weight boxes in shared memory,
                              //    loaded before the dependency wait; only activations stream
     uint32_t ld;             // row stride (elements) of the outputs
+    uint32_t m_loop;         // 1: one grid row; a CTA walks (unit, 64-slot group) items
     uint64_t part_stride;    // TC_PART: elements between splits
     float* out;              // TC_STORE: out = D; TC_PART: out[split] = partial D
     uint16_t* out_hi;        // TC_SILU: f16 pair of silu(gate) * up
@@ -142,6 +143,7 @@ struct TcGemmPlan {
     int epi = TC_STORE;
     uint32_t K = 0, rows = 0, n_tile = 0, n_tiles = 0, splits = 1, nst = 0, grid = 0, m_tiles = 1;
     bool wres = false;       // weights resident (see TcGemmArgs::wres)
+    bool m_loop = false;     // CTAs walk the 64-slot groups (see TcGemmArgs::m_loop); grid set per launch
     size_t smem = 0;
     CUtensorMap tm0{}, tm1{};  // weight boxes {64 columns, n_tile rows}
 };

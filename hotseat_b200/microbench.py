@@ -238,7 +238,7 @@ def bench_attention(ctxs=(1024, 4096, 16384, 32767), q05_path=None):
     return recs
 
 
-def bench_prefill(n_seqs=16, prompt=2048, gen=512):
+def bench_prefill(n_seqs=16, prompt=2048, gen=512, pass_tokens=1024):
     import torch
     import hotseat_b200 as hs
     peak_bw, _ = _peak()
@@ -258,9 +258,9 @@ def bench_prefill(n_seqs=16, prompt=2048, gen=512):
     kvs = [m.kv() for _ in range(n_seqs)]
     prompts = [[int(t) for t in np.random.default_rng(2048 + i).integers(0, c["vocab"], size=prompt)]
                for i in range(n_seqs)]
-    pb = hs.Batch(m, 512)
+    pb = hs.Batch(m, pass_tokens)
     stream = torch.cuda.ExternalStream(pb.stream)
-    pb.prefill(kvs[0], prompts[0][:512])  # warm-up (graphs)
+    pb.prefill(kvs[0], prompts[0][:pass_tokens])  # warm-up (graphs)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record(stream)
@@ -273,7 +273,8 @@ def bench_prefill(n_seqs=16, prompt=2048, gen=512):
     flops = 2.0 * c["n_layers"] * layer_w * toks
     tf = flops / (ms / 1000.0) / 1e12
     recs = [{"bench": "prefill", "model": "qwen2.5-1.5b-shape", "sequences": n_seqs, "prompt": prompt,
-             "ms": ms, "tok/s": toks / (ms / 1000.0), "gemm_TFLOP/s": tf, "peak_TFLOP/s": tflops,
+             "pass_tokens": pass_tokens, "ms": ms, "tok/s": toks / (ms / 1000.0), "gemm_TFLOP/s": tf,
+             "peak_TFLOP/s": tflops,
              "frac": tf / tflops, "peak_source": tsrc,
              "note": "algorithmic 2*weights*tokens; the tensor cores run twice that (hi/lo halves)"}]
     cfg = hs.SamplerCfg.default(temperature=0.0)
@@ -428,7 +429,7 @@ def bench_batch():
     os.rmdir(td)
 
 
-def bench_prefill_trace(prompt=2048, pass_tokens=512):
+def bench_prefill_trace(prompt=2048, pass_tokens=1024):
     """One prefill pass of the 1.5B shape at the end of a 2048-token prompt
     (positions prompt-1-pass_tokens .. prompt-2) with the launch timeline:
     per kernel role of layers 1-26, previous kernel's last exit to its own."""
@@ -473,11 +474,11 @@ if __name__ == "__main__":
         for r in bench_attention():
             print(json.dumps(r), flush=True)
     if which in ("prefill", "all"):
-        for r in bench_prefill():
+        for r in bench_prefill(pass_tokens=int(sys.argv[2]) if which == "prefill" and len(sys.argv) > 2 else 1024):
             print(json.dumps(r), flush=True)
     if which in ("token", "all"):
         bench_token()
     if which in ("batch", "all"):
         bench_batch()
     if which == "prefill_trace":
-        bench_prefill_trace()
+        bench_prefill_trace(pass_tokens=int(sys.argv[2]) if len(sys.argv) > 2 else 1024)
