@@ -342,6 +342,69 @@ __global__ void __launch_bounds__(kPThreads) k_prefill_combine(const SplitAttnAr
     tr.exit();
 }
 
+// The append half of a prefill pass (model.rs:268-275): one warp per
+// (token, KV head) rebuilds the token's k and v from the QKV product
+// (split-K partials in split order, then the bias: the split items' order,
+// so the rows have the same bits), applies RoPE to k (model.rs:365-373),
+// writes both rows and, when the region tracks writes, marks their pages
+// dirty once the rows are visible.
+template <int HD>
+__global__ void __launch_bounds__(kPThreads) k_prefill_append(const SplitAttnArgs a, uint32_t slots) {
+    constexpr uint32_t HALF = HD / 2;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t item = blockIdx.x * (kPThreads / 32) + warp;
+    const KTrace tr(a.trace, a.trace_slot);
+    tr.enter();
+    pdl_launch_dependents();
+    const bool in = item < slots * a.nkv;
+    const uint32_t slot = in ? item / a.nkv : 0, kvh = in ? item % a.nkv : 0;
+    DevCtl* ctl = a.ctl + slot;
+    const bool active = in && attn::ldv(&ctl->active) != 0;
+    const uint32_t pos = in ? attn::ldv(&ctl->pos) : 0;
+    pdl_wait();
+    if (active && pos >= a.max_ctx && lane == 0 && kvh == 0) atomicOr(&ctl->err, ERR_POS);
+    if (active && pos < a.max_ctx) {
+        float* kv = a.kv[slot];
+        const float* src = a.qkv + (size_t)slot * a.qkv_rows;
+        const uint32_t krow = a.nh * HD + kvh * HD, vrow = (a.nh + a.nkv) * HD + kvh * HD;
+        auto row = [&](uint32_t r) {  // float4 at row offset r: partials in split order, then the bias
+            float4 p = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (uint32_t q = 0; q < a.n_part; q++)
+                p = attn::f4add(p, __ldcg(reinterpret_cast<const float4*>(src + q * a.part_stride + r)));
+            if (a.bias) p = attn::f4add(p, *reinterpret_cast<const float4*>(a.bias + r));
+            return p;
+        };
+        if (lane < HALF / 4) {  // k: the float4 pair (lane, lane + HALF/4) that RoPE rotates together
+            float4 x0 = row(krow + 4 * lane), x1 = row(krow + HALF + 4 * lane);
+            const float4 c = *reinterpret_cast<const float4*>(a.rope_cos + (size_t)pos * HALF + 4 * lane);
+            const float4 sn = *reinterpret_cast<const float4*>(a.rope_sin + (size_t)pos * HALF + 4 * lane);
+            auto rot = [](float& u, float& w, float cc, float ss) {
+                const float u0 = u, w0 = w;
+                u = __fsub_rn(__fmul_rn(u0, cc), __fmul_rn(w0, ss));
+                w = __fadd_rn(__fmul_rn(u0, ss), __fmul_rn(w0, cc));
+            };
+            rot(x0.x, x1.x, c.x, sn.x);
+            rot(x0.y, x1.y, c.y, sn.y);
+            rot(x0.z, x1.z, c.z, sn.z);
+            rot(x0.w, x1.w, c.w, sn.w);
+            float* kd = kv + attn::kv_row_off(a, a.layer, kvh, HD, pos, 0);
+            reinterpret_cast<float4*>(kd)[lane] = x0;
+            reinterpret_cast<float4*>(kd + HALF)[lane] = x1;
+        }
+        if (lane < HD / 4)
+            reinterpret_cast<float4*>(kv + attn::kv_row_off(a, a.layer, kvh, HD, pos, 1))[lane] = row(vrow + 4 * lane);
+        __syncwarp();
+        if (lane < 2 && attn::ldv(a.tracking[slot]) != 0) {  // lane 0: the k row's pages, lane 1: the v row's
+            __threadfence();
+            const uint64_t off = attn::kv_row_off(a, a.layer, kvh, HD, pos, lane) * 4, last = off + HD * 4 - 1;
+            uint64_t* dirty = a.dirty[slot];
+            for (uint64_t pg = off >> a.page_shift; pg <= (last >> a.page_shift); pg++)
+                atomicOr(reinterpret_cast<unsigned long long*>(&dirty[pg >> 6]), 1ull << (pg & 63));
+        }
+    }
+    tr.exit();
+}
+
 size_t combine_smem(uint32_t hd, uint32_t nseg, uint32_t G) {
     return ((size_t)3 * nseg * G + 20 + (size_t)attn::kCombTile * G * hd) * sizeof(float);
 }
@@ -380,6 +443,21 @@ cudaError_t attn_prefill_set_smem_limits(int optin) {
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+cudaError_t launch_prefill_append(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, cudaStream_t st) {
+    if (!attn_prefill_supported(head_dim, a.nh, a.nkv) || slots == 0) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((slots * a.nkv + kPThreads / 32 - 1) / (kPThreads / 32));
+    cfg.blockDim = dim3(kPThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return head_dim == 64 ? cudaLaunchKernelEx(&cfg, k_prefill_append<64>, a, slots)
+                          : cudaLaunchKernelEx(&cfg, k_prefill_append<128>, a, slots);
 }
 
 cudaError_t launch_attn_prefill(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, uint32_t seg,

@@ -34,11 +34,11 @@ constexpr uint32_t kMaxParts = 32;      // split-K partials a consumer adds
 __device__ __forceinline__ float4 f4add(float4 a, float4 b) {
     return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
 }
-// Sum of `n` split partials of one float4 chunk, in split order; all the
-// loads (up to 24) are issued before the first add so they overlap in one
-// round trip.
+// Sum of `n` split partials of one float4 chunk, in split order; the loads
+// of B partials at a time (up to 24) are issued before the first add so they
+// overlap in one round trip.
+template <uint32_t B>
 __device__ __forceinline__ float4 sum_parts(const float* base, uint64_t stride, uint32_t n) {
-    constexpr uint32_t B = 24;
     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (uint32_t s0 = 0; s0 < n; s0 += B) {
         float4 v[B];
@@ -53,7 +53,10 @@ __device__ __forceinline__ float4 sum_parts(const float* base, uint64_t stride, 
 }
 
 // ---------------------------------------------------------------- RMSNorm
-// Thread t owns the float4 chunks t and t + 256 of the row.
+// Thread t owns the float4 chunks t and t + 256 of the row. B: partials
+// loaded per round (24 for the many-split decode GEMMs; 8 keeps a CTA small
+// enough for several per SM when a prompt pass launches one per token).
+template <uint32_t B>
 __global__ void __launch_bounds__(kNormThreads) k_tc_norm(const TcNormArgs a) {
     __shared__ float red[kNormThreads / 32];
     const uint32_t slot = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -83,7 +86,7 @@ __global__ void __launch_bounds__(kNormThreads) k_tc_norm(const TcNormArgs a) {
             x = make_float4(h2f(e.x & 0xffff), h2f(e.x >> 16), h2f(e.y & 0xffff), h2f(e.y >> 16));
         } else {
             x = *reinterpret_cast<const float4*>(a.x + (size_t)slot * a.d + 4 * c);
-            if (a.n_part) x = f4add(x, sum_parts(a.part + (size_t)slot * a.d + 4 * c, a.part_stride, a.n_part));
+            if (a.n_part) x = f4add(x, sum_parts<B>(a.part + (size_t)slot * a.d + 4 * c, a.part_stride, a.n_part));
         }
         if (a.embd || a.n_part) *reinterpret_cast<float4*>(a.x + (size_t)slot * a.d + 4 * c) = x;
         v[j] = x;
@@ -138,7 +141,8 @@ cudaError_t launch_tc_norm(const TcNormArgs& a, uint32_t slots, cudaStream_t st)
     if (a.d % 4 || a.d > kNormThreads * kNormMaxChunks * 4 || a.n_part > kMaxParts) return cudaErrorInvalidValue;
     TcNormArgs c = a;
     void* args[] = {&c};
-    return launch_pdl(reinterpret_cast<const void*>(k_tc_norm), dim3(slots), dim3(kNormThreads), 0, st, args);
+    const void* fn = a.n_part > 8 ? reinterpret_cast<const void*>(k_tc_norm<24>) : reinterpret_cast<const void*>(k_tc_norm<8>);
+    return launch_pdl(fn, dim3(slots), dim3(kNormThreads), 0, st, args);
 }
 
 }  // namespace hs

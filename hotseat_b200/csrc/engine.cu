@@ -2047,7 +2047,7 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool pref
             if (prefill) {
                 // tokens of one sequence: every k, v appended before any attends
                 sa.mode = ATTN_APPEND_ONLY;
-                e = launch_attn_split(hd, sa, n, b->st);
+                e = m->pf_qblock ? launch_prefill_append(hd, sa, n, b->st) : launch_attn_split(hd, sa, n, b->st);
                 if (e != cudaSuccess) return fail(HS_E_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
                 (*launches)++;
                 sa.mode = ATTN_ATTEND_ONLY;

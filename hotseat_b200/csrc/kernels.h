@@ -246,6 +246,9 @@ bool attn_prefill_supported(uint32_t head_dim, uint32_t nh, uint32_t nkv);
 cudaError_t attn_prefill_set_smem_limits(int optin);
 cudaError_t launch_attn_prefill(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, uint32_t seg,
                                 cudaStream_t st, uint32_t trace_slot);
+// The append half of a prefill pass (every slot's k, v rows written and their
+// pages marked), the same rows as ATTN_APPEND_ONLY's items: one launch.
+cudaError_t launch_prefill_append(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, cudaStream_t st);
 
 cudaError_t launch_tc_norm(const TcNormArgs& a, uint32_t slots, cudaStream_t st);
 

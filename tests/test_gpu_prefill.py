@@ -142,3 +142,30 @@ def test_query_block_prefill_then_decode_matches_token_by_token(tiny128_gguf):
     got = hs.Batch(m, 1).run_seqs([kv_b], [state(prompt, 600, 16, cfg, 2, filled=599)])[0]
     assert list(got[0]) == list(ref[0])
     assert float(np.max(np.abs(kv_a.floats() - kv_b.floats()))) <= 1e-3
+
+
+@pytest.mark.parametrize("layout", [hs.TOKEN_MAJOR, hs.HEAD_MAJOR])
+def test_prefill_marks_exactly_the_pages_it_writes(tiny128_gguf, layout):
+    """An armed region: the prefill append marks the pages of every k, v row
+    it writes, the same bits as the per-token items."""
+    prompt = [int(t) for t in np.random.default_rng(9).integers(0, TINY128["vocab"], size=300)]
+    got = []
+    for qblock in (True, False):
+        m = _load(tiny128_gguf, 1024, qblock)
+        kv = m.kv(layout=layout, page_size=4096)
+        kv.arm()
+        hs.Batch(m, 128).prefill(kv, prompt, pos0=0)
+        got.append(kv.harvest())
+        kv.disarm()
+    c = m.cfg
+    hd, nkv, T = c.head_dim, c.n_kv_heads, c.max_ctx
+    want = np.zeros_like(got[0])
+    for layer in range(c.n_layers):
+        for is_v in (0, 1):
+            for kvh in range(nkv):
+                for p in range(len(prompt)):
+                    within = (p * nkv + kvh) * hd if layout == hs.TOKEN_MAJOR else (kvh * T + p) * hd
+                    off = ((layer * 2 + is_v) * T * nkv * hd + within) * 4
+                    for pg in range(off // 4096, (off + hd * 4 - 1) // 4096 + 1):
+                        want[pg >> 6] |= np.uint64(1) << np.uint64(pg & 63)
+    assert np.array_equal(got[0], want) and np.array_equal(got[1], want)
