@@ -342,6 +342,324 @@ __global__ void __launch_bounds__(kPThreads) k_prefill_combine(const SplitAttnAr
     tr.exit();
 }
 
+// ---------------------------------------------------------------- tensor cores
+// The same query blocks, segments and records with both products on the
+// tensor cores (mma.sync m16n8k16, f16 operands, f32 accumulate), every
+// operand carried as an f16 pair hi = f16(x), lo = f16(x - hi) and every
+// product as lo*hi + hi*lo + hi*hi into the same f32 accumulator (about 22
+// significant bits of each operand; the f16 range, as the tensor-core GEMMs'
+// activation pairs). One CTA: kTcRows = 128 query rows (floor(128 / G)
+// tokens), 8 warps of 16 rows; a warp computes its rows' scores for the
+// whole 64-position chunk (8 n-tiles), their online softmax, and P.V for all
+// head_dim columns, with the probabilities kept in registers (the score
+// accumulator layout of two n-tiles is the A-operand layout of one 16-wide
+// k-step). Each row's arithmetic is its own, so a token's bits depend on its
+// position and the KV contents only.
+//
+// Per chunk: the f32 K and V rows land by cp.async in staging buffers; all
+// threads convert them once into f16 hi/lo K [position][dim] and V^T
+// [dim][position] (rows padded by 8 halves: the fragment loads of a warp hit
+// 32 distinct banks); the next chunk's rows then load while the warps run
+// the products. Shared memory at head_dim 128: q pairs 68 KB + K pairs 34 KB
+// + V pairs 36 KB + staging 66 KB = 204 KB, one CTA per SM.
+constexpr uint32_t kTcRows = 128;
+
+template <int HD>
+struct PfTcGeom {
+    static constexpr uint32_t QS = HD + 8, KS = HD + 8, VS = kPCh + 8, SS = HD + 4;  // row strides (halves / floats)
+    static constexpr uint32_t Q = kTcRows * QS, K = kPCh * KS, V = HD * VS;        // halves per hi or lo buffer
+    static constexpr uint32_t STG = kPCh * SS;                                      // floats per staging buffer
+    static constexpr size_t bytes = (size_t)2 * (Q + K + V) * 2 + (size_t)2 * STG * 4;
+};
+
+__device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(__fsub_rn(x0, hf.x), __fsub_rn(x1, hf.y));
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+__device__ __forceinline__ void mma_h16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t ld_h2(const uint16_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+template <int HD>
+__global__ void __launch_bounds__(kPThreads, 1)
+    k_prefill_attend_tc(const SplitAttnArgs a, uint32_t slots, uint32_t qb_tokens, uint32_t seg) {
+    using Geo = PfTcGeom<HD>;
+    constexpr uint32_t NK4 = HD / 4, HALF = HD / 2, NT = HD / 8, QS = Geo::QS, KS = Geo::KS, VS = Geo::VS,
+                       SS = Geo::SS;
+    extern __shared__ __align__(16) uint16_t smh[];
+    uint16_t* Qh = smh;
+    uint16_t* Ql = Qh + Geo::Q;
+    uint16_t* Kh = Ql + Geo::Q;
+    uint16_t* Kl = Kh + Geo::K;
+    uint16_t* Vh = Kl + Geo::K;  // V^T [dim][position]
+    uint16_t* Vl = Vh + Geo::V;
+    float* Ks = reinterpret_cast<float*>(Vl + Geo::V);  // staging [position][SS]
+    float* Vs = Ks + Geo::STG;
+    __shared__ uint32_t s_lim[kTcRows];
+    __shared__ uint32_t s_max;
+    const uint32_t s = blockIdx.x, qb = blockIdx.y, kvh = blockIdx.z, tid = threadIdx.x;
+    const uint32_t Gf = a.nh / a.nkv, t0 = qb * qb_tokens;
+    const KTrace tr(a.trace, a.trace_slot);
+    tr.enter();
+    pdl_launch_dependents();
+    if (tid < kTcRows) {
+        uint32_t lim = 0;
+        if (tid < qb_tokens && t0 + tid < slots) {
+            const DevCtl* c = a.ctl + t0 + tid;
+            const uint32_t pos = attn::ldv(&c->pos);
+            if (attn::ldv(&c->active) != 0 && pos < a.max_ctx) lim = pos + 1;
+        }
+        s_lim[tid] = lim;
+    }
+    __syncthreads();
+    if (tid < 32) {
+        uint32_t m = 0;
+        for (uint32_t i = tid; i < kTcRows; i += 32) m = s_lim[i] > m ? s_lim[i] : m;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const uint32_t o = __shfl_xor_sync(0xffffffffu, m, off);
+            m = o > m ? o : m;
+        }
+        if (tid == 0) s_max = m;
+    }
+    __syncthreads();
+    const uint32_t lim_max = s_max, p_begin = s * seg;
+    if (lim_max <= p_begin) {
+        tr.exit();
+        return;
+    }
+    const uint32_t p_end = p_begin + seg < lim_max ? p_begin + seg : lim_max;
+    const uint32_t nch = (p_end - p_begin + kPCh - 1) / kPCh;
+    const float* kv = a.kv[t0];
+    const uint32_t layer = a.layer;
+    auto stage = [&](uint32_t c) {  // chunk c's cached rows into the staging buffers, one commit group
+        const uint32_t c0 = p_begin + c * kPCh, cnt = p_end - c0 < kPCh ? p_end - c0 : kPCh;
+        for (uint32_t i = tid; i < cnt * NK4; i += kPThreads) {
+            const uint32_t rr = i / NK4, k4 = i % NK4;
+            cp_async16(Ks + rr * SS + 4 * k4, kv + attn::kv_row_off(a, layer, kvh, HD, c0 + rr, 0) + 4 * k4);
+            cp_async16(Vs + rr * SS + 4 * k4, kv + attn::kv_row_off(a, layer, kvh, HD, c0 + rr, 1) + 4 * k4);
+        }
+        attn::cp_commit();
+    };
+
+    pdl_wait();
+    stage(0);
+
+    // q rows: partials in split order, the bias, RoPE (as k_prefill_attend),
+    // then the f16 pairs; zero for rows without a token
+    for (uint32_t j = tid; j < kTcRows * (HD / 8); j += kPThreads) {
+        const uint32_t r = j / (HD / 8), k4 = j % (HD / 8), t = r / Gf, h = r % Gf;
+        float4 x0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), x1 = x0;
+        const uint32_t lim = r < qb_tokens * Gf ? s_lim[t] : 0u;
+        if (lim) {
+            const uint32_t pos = lim - 1, row = (kvh * Gf + h) * HD + 4 * k4;
+            const float* src = a.qkv + (size_t)(t0 + t) * a.qkv_rows + row;
+            for (uint32_t q = 0; q < a.n_part; q++) {
+                x0 = attn::f4add(x0, __ldcg(reinterpret_cast<const float4*>(src + q * a.part_stride)));
+                x1 = attn::f4add(x1, __ldcg(reinterpret_cast<const float4*>(src + q * a.part_stride + HALF)));
+            }
+            if (a.bias) {
+                x0 = attn::f4add(x0, *reinterpret_cast<const float4*>(a.bias + row));
+                x1 = attn::f4add(x1, *reinterpret_cast<const float4*>(a.bias + row + HALF));
+            }
+            const float4 c = *reinterpret_cast<const float4*>(a.rope_cos + (size_t)pos * HALF + 4 * k4);
+            const float4 sn = *reinterpret_cast<const float4*>(a.rope_sin + (size_t)pos * HALF + 4 * k4);
+            auto rot = [](float& u, float& w, float cc, float ss) {
+                const float u0 = u, w0 = w;
+                u = __fsub_rn(__fmul_rn(u0, cc), __fmul_rn(w0, ss));
+                w = __fadd_rn(__fmul_rn(u0, ss), __fmul_rn(w0, cc));
+            };
+            rot(x0.x, x1.x, c.x, sn.x);
+            rot(x0.y, x1.y, c.y, sn.y);
+            rot(x0.z, x1.z, c.z, sn.z);
+            rot(x0.w, x1.w, c.w, sn.w);
+        }
+        uint2 h0, l0, h1, l1;
+        split_h2(x0.x, x0.y, h0.x, l0.x);
+        split_h2(x0.z, x0.w, h0.y, l0.y);
+        split_h2(x1.x, x1.y, h1.x, l1.x);
+        split_h2(x1.z, x1.w, h1.y, l1.y);
+        *reinterpret_cast<uint2*>(Qh + r * QS + 4 * k4) = h0;
+        *reinterpret_cast<uint2*>(Ql + r * QS + 4 * k4) = l0;
+        *reinterpret_cast<uint2*>(Qh + r * QS + HALF + 4 * k4) = h1;
+        *reinterpret_cast<uint2*>(Ql + r * QS + HALF + 4 * k4) = l1;
+    }
+
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+    const uint32_t warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    const uint32_t ra = warp * 16 + g, rb = ra + 8;  // this thread's two rows
+    const uint32_t lima = ra < qb_tokens * Gf ? s_lim[ra / Gf] : 0u;
+    const uint32_t limb = rb < qb_tokens * Gf ? s_lim[rb / Gf] : 0u;
+    float ma = -FLT_MAX, mb = -FLT_MAX, la = 0.0f, lb = 0.0f;
+    float O[NT][4];
+#pragma unroll
+    for (uint32_t n = 0; n < NT; n++) O[n][0] = O[n][1] = O[n][2] = O[n][3] = 0.0f;
+
+    for (uint32_t c = 0; c < nch; c++) {
+        const uint32_t c0 = p_begin + c * kPCh, cnt = p_end - c0 < kPCh ? p_end - c0 : kPCh;
+        attn::cp_wait0();
+        __syncthreads();  // staging holds chunk c; the previous chunk's pairs are consumed
+        if (c == 0) tr.mark(1);
+        // staging -> f16 pairs: K [position][dim]; V^T [dim][position] with
+        // positions past the chunk's end zero (their probabilities are 0, and
+        // 0 times a stale non-finite value would not be)
+        for (uint32_t i = tid; i < kPCh * NK4; i += kPThreads) {
+            const uint32_t rr = i / NK4, k4 = i % NK4;
+            float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (rr < cnt) x = *reinterpret_cast<const float4*>(Ks + rr * SS + 4 * k4);
+            uint2 h, l;
+            split_h2(x.x, x.y, h.x, l.x);
+            split_h2(x.z, x.w, h.y, l.y);
+            *reinterpret_cast<uint2*>(Kh + rr * KS + 4 * k4) = h;
+            *reinterpret_cast<uint2*>(Kl + rr * KS + 4 * k4) = l;
+        }
+        for (uint32_t i = tid; i < kPCh * NK4; i += kPThreads) {
+            const uint32_t rr = i % kPCh, k4 = i / kPCh;  // lanes along positions: the V^T writes are contiguous
+            float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (rr < cnt) x = *reinterpret_cast<const float4*>(Vs + rr * SS + 4 * k4);
+            const float xv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (uint32_t e = 0; e < 4; e++) {
+                const __half h = __float2half_rn(xv[e]);
+                Vh[(4 * k4 + e) * VS + rr] = __half_as_ushort(h);
+                Vl[(4 * k4 + e) * VS + rr] = __half_as_ushort(__float2half_rn(__fsub_rn(xv[e], __half2float(h))));
+            }
+        }
+        __syncthreads();  // pairs ready; staging free
+        if (c + 1 < nch) stage(c + 1);
+
+        // scores: 16 rows x 64 positions per warp
+        float S[8][4];
+#pragma unroll
+        for (uint32_t j = 0; j < 8; j++) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
+#pragma unroll
+        for (uint32_t k0 = 0; k0 < HD; k0 += 16) {
+            uint32_t ah[4], al[4];
+            ah[0] = ld_h2(Qh + ra * QS + k0 + 2 * t4);
+            ah[1] = ld_h2(Qh + rb * QS + k0 + 2 * t4);
+            ah[2] = ld_h2(Qh + ra * QS + k0 + 2 * t4 + 8);
+            ah[3] = ld_h2(Qh + rb * QS + k0 + 2 * t4 + 8);
+            al[0] = ld_h2(Ql + ra * QS + k0 + 2 * t4);
+            al[1] = ld_h2(Ql + rb * QS + k0 + 2 * t4);
+            al[2] = ld_h2(Ql + ra * QS + k0 + 2 * t4 + 8);
+            al[3] = ld_h2(Ql + rb * QS + k0 + 2 * t4 + 8);
+#pragma unroll
+            for (uint32_t j = 0; j < 8; j++) {
+                const uint32_t kr = (8 * j + g) * KS + k0 + 2 * t4;
+                const uint32_t bh0 = ld_h2(Kh + kr), bh1 = ld_h2(Kh + kr + 8);
+                const uint32_t bl0 = ld_h2(Kl + kr), bl1 = ld_h2(Kl + kr + 8);
+                mma_h16(S[j], al, bh0, bh1);
+                mma_h16(S[j], ah, bl0, bl1);
+                mma_h16(S[j], ah, bh0, bh1);
+            }
+        }
+        // online softmax per row (row a: S[j][0..1], row b: S[j][2..3];
+        // positions 8 j + 2 t4 + e); the 4 lanes of a row reduce by shuffles.
+        // Selects, not branches: every lane takes every shuffle.
+        float mxa = -FLT_MAX, mxb = -FLT_MAX;
+#pragma unroll
+        for (uint32_t j = 0; j < 8; j++)
+#pragma unroll
+            for (uint32_t e = 0; e < 2; e++) {
+                const uint32_t col = 8 * j + 2 * t4 + e;
+                const bool in = col < cnt;
+                S[j][e] = in && c0 + col < lima ? __fmul_rn(S[j][e], scale) : -FLT_MAX;
+                S[j][2 + e] = in && c0 + col < limb ? __fmul_rn(S[j][2 + e], scale) : -FLT_MAX;
+                mxa = fmaxf(mxa, S[j][e]);
+                mxb = fmaxf(mxb, S[j][2 + e]);
+            }
+#pragma unroll
+        for (int off = 1; off < 4; off <<= 1) {
+            mxa = fmaxf(mxa, __shfl_xor_sync(0xffffffffu, mxa, off));
+            mxb = fmaxf(mxb, __shfl_xor_sync(0xffffffffu, mxb, off));
+        }
+        const bool nonea = mxa == -FLT_MAX, noneb = mxb == -FLT_MAX;
+        const float mna = nonea ? ma : fmaxf(ma, mxa), mnb = noneb ? mb : fmaxf(mb, mxb);
+        float suma = 0.0f, sumb = 0.0f;
+#pragma unroll
+        for (uint32_t j = 0; j < 8; j++)
+#pragma unroll
+            for (uint32_t e = 0; e < 2; e++) {
+                S[j][e] = S[j][e] == -FLT_MAX ? 0.0f : __expf(__fsub_rn(S[j][e], mna));
+                S[j][2 + e] = S[j][2 + e] == -FLT_MAX ? 0.0f : __expf(__fsub_rn(S[j][2 + e], mnb));
+                suma = __fadd_rn(suma, S[j][e]);
+                sumb = __fadd_rn(sumb, S[j][2 + e]);
+            }
+#pragma unroll
+        for (int off = 1; off < 4; off <<= 1) {
+            suma = __fadd_rn(suma, __shfl_xor_sync(0xffffffffu, suma, off));
+            sumb = __fadd_rn(sumb, __shfl_xor_sync(0xffffffffu, sumb, off));
+        }
+        const float fa = nonea ? 1.0f : (ma == -FLT_MAX ? 0.0f : __expf(__fsub_rn(ma, mna)));
+        const float fb = noneb ? 1.0f : (mb == -FLT_MAX ? 0.0f : __expf(__fsub_rn(mb, mnb)));
+        la = nonea ? la : __fadd_rn(__fmul_rn(la, fa), suma);
+        lb = noneb ? lb : __fadd_rn(__fmul_rn(lb, fb), sumb);
+        ma = mna;
+        mb = mnb;
+#pragma unroll
+        for (uint32_t n = 0; n < NT; n++) {
+            O[n][0] = __fmul_rn(O[n][0], fa);
+            O[n][1] = __fmul_rn(O[n][1], fa);
+            O[n][2] = __fmul_rn(O[n][2], fb);
+            O[n][3] = __fmul_rn(O[n][3], fb);
+        }
+        // P.V: the 16-position slab k = positions 16 q .. +15 is score
+        // n-tiles 2q and 2q + 1
+#pragma unroll
+        for (uint32_t q = 0; q < kPCh / 16; q++) {
+            uint32_t ph[4], pl[4];
+            split_h2(S[2 * q][0], S[2 * q][1], ph[0], pl[0]);
+            split_h2(S[2 * q][2], S[2 * q][3], ph[1], pl[1]);
+            split_h2(S[2 * q + 1][0], S[2 * q + 1][1], ph[2], pl[2]);
+            split_h2(S[2 * q + 1][2], S[2 * q + 1][3], ph[3], pl[3]);
+#pragma unroll
+            for (uint32_t n = 0; n < NT; n++) {
+                const uint32_t vr = (8 * n + g) * VS + 16 * q + 2 * t4;
+                const uint32_t bh0 = ld_h2(Vh + vr), bh1 = ld_h2(Vh + vr + 8);
+                const uint32_t bl0 = ld_h2(Vl + vr), bl1 = ld_h2(Vl + vr + 8);
+                mma_h16(O[n], pl, bh0, bh1);
+                mma_h16(O[n], ph, bl0, bl1);
+                mma_h16(O[n], ph, bh0, bh1);
+            }
+        }
+    }
+    attn::cp_wait0();
+    tr.mark(2);
+
+    const uint32_t rec = attn_record(Gf, HD);
+#pragma unroll
+    for (uint32_t side = 0; side < 2; side++) {
+        const uint32_t r = side ? rb : ra, lim = side ? limb : lima;
+        const float m = side ? mb : ma, l = side ? lb : la;
+        if (lim <= p_begin) continue;
+        const uint32_t slot = t0 + r / Gf, h = r % Gf;
+        if (lim <= seg) {
+            const size_t o = (size_t)slot * a.out_stride + (size_t)(kvh * Gf + h) * HD;
+#pragma unroll
+            for (uint32_t n = 0; n < NT; n++) {
+                store_out(a, o + 8 * n + 2 * t4, __fdiv_rn(O[n][2 * side], l));
+                store_out(a, o + 8 * n + 2 * t4 + 1, __fdiv_rn(O[n][2 * side + 1], l));
+            }
+        } else {
+            float* part = a.partials + ((size_t)(slot * a.nkv + kvh) * a.max_splits + s) * rec;
+#pragma unroll
+            for (uint32_t n = 0; n < NT; n++)
+                *reinterpret_cast<float2*>(part + h * HD + 8 * n + 2 * t4) = make_float2(O[n][2 * side], O[n][2 * side + 1]);
+            if (t4 == 0) {
+                part[Gf * HD + h] = m;
+                part[Gf * HD + Gf + h] = l;
+            }
+        }
+    }
+    tr.exit();
+}
+
 // The append half of a prefill pass (model.rs:268-275): one warp per
 // (token, KV head) rebuilds the token's k and v from the QKV product
 // (split-K partials in split order, then the bias: the split items' order,
@@ -427,9 +745,10 @@ bool attn_prefill_supported(uint32_t head_dim, uint32_t nh, uint32_t nkv) {
 }
 
 cudaError_t attn_prefill_set_smem_limits(int optin) {
-    const void* fa[] = {(const void*)k_prefill_attend<64>, (const void*)k_prefill_attend<128>};
-    const size_t na[] = {PfGeom<64>::bytes, PfGeom<128>::bytes};
-    for (int i = 0; i < 2; i++) {
+    const void* fa[] = {(const void*)k_prefill_attend<64>, (const void*)k_prefill_attend<128>,
+                        (const void*)k_prefill_attend_tc<64>, (const void*)k_prefill_attend_tc<128>};
+    const size_t na[] = {PfGeom<64>::bytes, PfGeom<128>::bytes, PfTcGeom<64>::bytes, PfTcGeom<128>::bytes};
+    for (int i = 0; i < 4; i++) {
         if (na[i] > (size_t)optin) continue;
         const cudaError_t e = cudaFuncSetAttribute(fa[i], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)na[i]);
         if (e != cudaSuccess) return e;
@@ -460,17 +779,22 @@ cudaError_t launch_prefill_append(uint32_t head_dim, const SplitAttnArgs& a, uin
                           : cudaLaunchKernelEx(&cfg, k_prefill_append<128>, a, slots);
 }
 
+size_t attn_prefill_smem(uint32_t head_dim, bool tensor_cores) {
+    if (tensor_cores) return head_dim == 64 ? PfTcGeom<64>::bytes : PfTcGeom<128>::bytes;
+    return head_dim == 64 ? PfGeom<64>::bytes : PfGeom<128>::bytes;
+}
+
 cudaError_t launch_attn_prefill(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, uint32_t seg,
-                                cudaStream_t st, uint32_t trace_slot) {
+                                cudaStream_t st, uint32_t trace_slot, bool tensor_cores) {
     if (!attn_prefill_supported(head_dim, a.nh, a.nkv) || seg == 0 || slots == 0 || (!a.out_f32 && !a.out_hi))
         return cudaErrorInvalidValue;
-    const uint32_t G = a.nh / a.nkv, qb_tokens = kRows / G;
+    const uint32_t G = a.nh / a.nkv, qb_tokens = (tensor_cores ? kTcRows : kRows) / G;
     const uint32_t nseg = (a.max_ctx + seg - 1) / seg;
     if (nseg > a.max_splits || nseg > kPrefillMaxSegs) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(nseg, (slots + qb_tokens - 1) / qb_tokens, a.nkv);
     cfg.blockDim = dim3(kPThreads);
-    cfg.dynamicSmemBytes = head_dim == 64 ? PfGeom<64>::bytes : PfGeom<128>::bytes;
+    cfg.dynamicSmemBytes = attn_prefill_smem(head_dim, tensor_cores);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -479,8 +803,13 @@ cudaError_t launch_attn_prefill(uint32_t head_dim, const SplitAttnArgs& a, uint3
     cfg.numAttrs = 1;
     SplitAttnArgs b = a;
     b.trace_slot = trace_slot;
-    cudaError_t e = head_dim == 64 ? cudaLaunchKernelEx(&cfg, k_prefill_attend<64>, b, slots, qb_tokens, seg)
-                                   : cudaLaunchKernelEx(&cfg, k_prefill_attend<128>, b, slots, qb_tokens, seg);
+    cudaError_t e;
+    if (tensor_cores)
+        e = head_dim == 64 ? cudaLaunchKernelEx(&cfg, k_prefill_attend_tc<64>, b, slots, qb_tokens, seg)
+                           : cudaLaunchKernelEx(&cfg, k_prefill_attend_tc<128>, b, slots, qb_tokens, seg);
+    else
+        e = head_dim == 64 ? cudaLaunchKernelEx(&cfg, k_prefill_attend<64>, b, slots, qb_tokens, seg)
+                           : cudaLaunchKernelEx(&cfg, k_prefill_attend<128>, b, slots, qb_tokens, seg);
     if (e != cudaSuccess) return e;
     cfg.gridDim = dim3(a.nkv, slots, 1);
     cfg.dynamicSmemBytes = combine_smem(head_dim, nseg, G);

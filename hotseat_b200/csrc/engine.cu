@@ -224,6 +224,7 @@ struct hs_model {
     uint32_t attn_unstaged = 0;    // HS_ATTN_UNSTAGED_COMBINE=1: the per-element combine (same bits; measurement)
     uint32_t attn_ws_from = 0;     // warp-split item form from this many positions on (0: never)
     bool pf_qblock = false;        // prefill attends by query blocks (attn_prefill.cu)
+    bool pf_tc = false;            // ... with the products on the tensor cores
     uint32_t pf_seg = 0, pf_nseg = 0;  // its segment length and segments per token at most
     uint32_t numeric = HS_NUMERIC_REFERENCE;
     TcGemmPlan thead;             // tensor-core LM head
@@ -974,10 +975,14 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
         m->attn_ws_from = env_u32("HS_ATTN_WS_FROM", tc ? 0u : 8192u);
         if (!tc && !attn_ws_fits(hd, 1)) m->attn_ws_from = 0;
         HS_CUDA_TRY(attn_split_set_smem_limits(optin));
-        // Prefill attends by query blocks (64 rows share each K/V chunk);
-        // HS_PREFILL_ATTN=0 keeps the per-token split items (measurement).
-        if (tc && attn_prefill_supported(hd, n_heads, n_kv) && env_u32("HS_PREFILL_ATTN", 1) != 0) {
+        // Prefill attends by query blocks (128 rows share each K/V chunk,
+        // products on the tensor cores); HS_PREFILL_ATTN=1 runs 64-row blocks
+        // on the CUDA cores, 0 the per-token split items (measurement).
+        const uint32_t pf_mode = env_u32("HS_PREFILL_ATTN", 2);
+        if (tc && attn_prefill_supported(hd, n_heads, n_kv) && pf_mode != 0 &&
+            attn_prefill_smem(hd, pf_mode >= 2) <= (size_t)optin) {
             m->pf_qblock = true;
+            m->pf_tc = pf_mode >= 2;
             m->pf_seg = attn_prefill_seg(max_ctx);
             m->pf_nseg = attn_prefill_segs(max_ctx);
             HS_CUDA_TRY(attn_prefill_set_smem_limits(optin));
@@ -2057,7 +2062,7 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool pref
                 // query blocks over fixed segments, then the segments' merge
                 sa.partials = b->pf_part;
                 sa.max_splits = m->pf_nseg;
-                e = launch_attn_prefill(hd, sa, n, m->pf_seg, b->st, *launches);
+                e = launch_attn_prefill(hd, sa, n, m->pf_seg, b->st, *launches, m->pf_tc);
                 if (e == cudaSuccess) (*launches)++;
             } else {
                 e = launch_attn_split(hd, sa, n, b->st);

@@ -244,8 +244,11 @@ uint32_t attn_prefill_seg(uint32_t max_ctx);
 uint32_t attn_prefill_segs(uint32_t max_ctx);
 bool attn_prefill_supported(uint32_t head_dim, uint32_t nh, uint32_t nkv);
 cudaError_t attn_prefill_set_smem_limits(int optin);
+// tensor_cores: the products on mma.sync with f16 hi/lo operands (128-row
+// blocks), else fp32 FMA chains on the CUDA cores (64-row blocks).
 cudaError_t launch_attn_prefill(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, uint32_t seg,
-                                cudaStream_t st, uint32_t trace_slot);
+                                cudaStream_t st, uint32_t trace_slot, bool tensor_cores);
+size_t attn_prefill_smem(uint32_t head_dim, bool tensor_cores);
 // The append half of a prefill pass (every slot's k, v rows written and their
 // pages marked), the same rows as ATTN_APPEND_ONLY's items: one launch.
 cudaError_t launch_prefill_append(uint32_t head_dim, const SplitAttnArgs& a, uint32_t slots, cudaStream_t st);

@@ -8,9 +8,11 @@ tolerance, greedy continuations are identical, prefill in pieces is
 bit-identical to one call, and the greedy tokens match the CPU path.
 
 Prefill attention runs by query blocks over fixed segments of cached
-positions (attn_prefill.cu); HS_PREFILL_ATTN=0 at model load keeps the
-per-token split items. The two agree within tolerance on prompts that span
-several segments, and a token's bits do not depend on the pass it is in."""
+positions (attn_prefill.cu), its products on the tensor cores (f16 hi/lo
+operands); HS_PREFILL_ATTN=1 at model load runs the blocks on the CUDA cores
+and 0 the per-token split items. All three agree within tolerance on prompts
+that span several segments, and a token's bits do not depend on the pass it
+is in."""
 import os
 
 import numpy as np
@@ -84,9 +86,12 @@ def test_prefill_rejects_bad_input(tiny_gguf):
         b.prefill(kv, [1, 2], pos0=63)
 
 
-def _load(path, max_ctx, qblock):
+QBLOCK_TC, QBLOCK_CUDA_CORES, PER_TOKEN = "2", "1", "0"
+
+
+def _load(path, max_ctx, mode):
     old = os.environ.get("HS_PREFILL_ATTN")
-    os.environ["HS_PREFILL_ATTN"] = "1" if qblock else "0"
+    os.environ["HS_PREFILL_ATTN"] = mode
     try:
         return hs.Model.load(path, max_ctx=max_ctx, numeric=TC)
     finally:
@@ -96,8 +101,9 @@ def _load(path, max_ctx, qblock):
             os.environ["HS_PREFILL_ATTN"] = old
 
 
+@pytest.mark.parametrize("mode", [QBLOCK_TC, QBLOCK_CUDA_CORES])
 @pytest.mark.parametrize("shape,n", [("tiny", 700), ("tiny128", 700), ("q05", 600), ("tiny128", 200)])
-def test_query_block_prefill_matches_the_per_token_items(shape, n, request):
+def test_query_block_prefill_matches_the_per_token_items(shape, n, mode, request):
     """Several 256-position segments (and one, at 200): the same KV rows and
     next-token logits as the per-token split items within tolerance."""
     path, vocab = {"tiny": ("tiny_gguf", TINY["vocab"]), "tiny128": ("tiny128_gguf", TINY128["vocab"]),
@@ -105,8 +111,8 @@ def test_query_block_prefill_matches_the_per_token_items(shape, n, request):
     path = request.getfixturevalue(path)
     prompt = [int(t) for t in np.random.default_rng(n).integers(0, vocab, size=n)]
     got = []
-    for qblock in (True, False):
-        m = _load(path, 1024, qblock)
+    for md in (mode, PER_TOKEN):
+        m = _load(path, 1024, md)
         kv = m.kv()
         hs.Batch(m, 256).prefill(kv, prompt[:-1])
         b = hs.Batch(m, 1)
@@ -114,14 +120,15 @@ def test_query_block_prefill_matches_the_per_token_items(shape, n, request):
         got.append((kv.floats(), b.logits(0)))
     kv_err = float(np.max(np.abs(got[0][0] - got[1][0])))
     logit_err = float(np.max(np.abs(got[0][1] - got[1][1])))
-    print(f"{shape}, {n - 1} prompt tokens: KV {kv_err:.3g}, logits {logit_err:.3g}")
+    print(f"{shape}, {n - 1} prompt tokens, mode {mode}: KV {kv_err:.3g}, logits {logit_err:.3g}")
     assert kv_err <= 1e-3 and logit_err <= 1e-2
 
 
-def test_query_block_prefill_in_pieces_equals_one_call_across_segments(tiny128_gguf):
+@pytest.mark.parametrize("mode", [QBLOCK_TC, QBLOCK_CUDA_CORES])
+def test_query_block_prefill_in_pieces_equals_one_call_across_segments(tiny128_gguf, mode):
     """Passes cut at 301 and at multiples of 128 put the tokens in different
     query blocks: the KV region is bit-identical."""
-    m = hs.Model.load(tiny128_gguf, max_ctx=1024, numeric=TC)
+    m = _load(tiny128_gguf, 1024, mode)
     prompt = [int(t) for t in np.random.default_rng(31).integers(0, TINY128["vocab"], size=700)]
     b = hs.Batch(m, 128)
     one, two = m.kv(), m.kv()
@@ -150,8 +157,8 @@ def test_prefill_marks_exactly_the_pages_it_writes(tiny128_gguf, layout):
     it writes, the same bits as the per-token items."""
     prompt = [int(t) for t in np.random.default_rng(9).integers(0, TINY128["vocab"], size=300)]
     got = []
-    for qblock in (True, False):
-        m = _load(tiny128_gguf, 1024, qblock)
+    for md in (QBLOCK_TC, PER_TOKEN):
+        m = _load(tiny128_gguf, 1024, md)
         kv = m.kv(layout=layout, page_size=4096)
         kv.arm()
         hs.Batch(m, 128).prefill(kv, prompt, pos0=0)
