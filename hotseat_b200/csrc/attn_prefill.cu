@@ -549,14 +549,26 @@ __global__ void __launch_bounds__(kPThreads, 1)
             al[1] = ld_h2(Ql + rb * QS + k0 + 2 * t4);
             al[2] = ld_h2(Ql + ra * QS + k0 + 2 * t4 + 8);
             al[3] = ld_h2(Ql + rb * QS + k0 + 2 * t4 + 8);
+            // four n-tiles at a time, each accumulator's three products in
+            // the same order, the tiles interleaved (independent MMAs between
+            // dependent ones)
 #pragma unroll
-            for (uint32_t j = 0; j < 8; j++) {
-                const uint32_t kr = (8 * j + g) * KS + k0 + 2 * t4;
-                const uint32_t bh0 = ld_h2(Kh + kr), bh1 = ld_h2(Kh + kr + 8);
-                const uint32_t bl0 = ld_h2(Kl + kr), bl1 = ld_h2(Kl + kr + 8);
-                mma_h16(S[j], al, bh0, bh1);
-                mma_h16(S[j], ah, bl0, bl1);
-                mma_h16(S[j], ah, bh0, bh1);
+            for (uint32_t j0 = 0; j0 < 8; j0 += 4) {
+                uint32_t bh[4][2], bl[4][2];
+#pragma unroll
+                for (uint32_t u = 0; u < 4; u++) {
+                    const uint32_t kr = (8 * (j0 + u) + g) * KS + k0 + 2 * t4;
+                    bh[u][0] = ld_h2(Kh + kr);
+                    bh[u][1] = ld_h2(Kh + kr + 8);
+                    bl[u][0] = ld_h2(Kl + kr);
+                    bl[u][1] = ld_h2(Kl + kr + 8);
+                }
+#pragma unroll
+                for (uint32_t u = 0; u < 4; u++) mma_h16(S[j0 + u], al, bh[u][0], bh[u][1]);
+#pragma unroll
+                for (uint32_t u = 0; u < 4; u++) mma_h16(S[j0 + u], ah, bl[u][0], bl[u][1]);
+#pragma unroll
+                for (uint32_t u = 0; u < 4; u++) mma_h16(S[j0 + u], ah, bh[u][0], bh[u][1]);
             }
         }
         // online softmax per row (row a: S[j][0..1], row b: S[j][2..3];
@@ -619,13 +631,22 @@ __global__ void __launch_bounds__(kPThreads, 1)
             split_h2(S[2 * q + 1][0], S[2 * q + 1][1], ph[2], pl[2]);
             split_h2(S[2 * q + 1][2], S[2 * q + 1][3], ph[3], pl[3]);
 #pragma unroll
-            for (uint32_t n = 0; n < NT; n++) {
-                const uint32_t vr = (8 * n + g) * VS + 16 * q + 2 * t4;
-                const uint32_t bh0 = ld_h2(Vh + vr), bh1 = ld_h2(Vh + vr + 8);
-                const uint32_t bl0 = ld_h2(Vl + vr), bl1 = ld_h2(Vl + vr + 8);
-                mma_h16(O[n], pl, bh0, bh1);
-                mma_h16(O[n], ph, bl0, bl1);
-                mma_h16(O[n], ph, bh0, bh1);
+            for (uint32_t n0 = 0; n0 < NT; n0 += 4) {
+                uint32_t bh[4][2], bl[4][2];
+#pragma unroll
+                for (uint32_t u = 0; u < 4; u++) {
+                    const uint32_t vr = (8 * (n0 + u) + g) * VS + 16 * q + 2 * t4;
+                    bh[u][0] = ld_h2(Vh + vr);
+                    bh[u][1] = ld_h2(Vh + vr + 8);
+                    bl[u][0] = ld_h2(Vl + vr);
+                    bl[u][1] = ld_h2(Vl + vr + 8);
+                }
+#pragma unroll
+                for (uint32_t u = 0; u < 4; u++) mma_h16(O[n0 + u], pl, bh[u][0], bh[u][1]);
+#pragma unroll
+                for (uint32_t u = 0; u < 4; u++) mma_h16(O[n0 + u], ph, bl[u][0], bl[u][1]);
+#pragma unroll
+                for (uint32_t u = 0; u < 4; u++) mma_h16(O[n0 + u], ph, bh[u][0], bh[u][1]);
             }
         }
     }
@@ -723,8 +744,11 @@ __global__ void __launch_bounds__(kPThreads) k_prefill_append(const SplitAttnArg
     tr.exit();
 }
 
+// combine_staged's space for at most nseg segments: maxima, sums, weights
+// and a tile of min(kCombTile, nseg) segment outputs.
 size_t combine_smem(uint32_t hd, uint32_t nseg, uint32_t G) {
-    return ((size_t)3 * nseg * G + 20 + (size_t)attn::kCombTile * G * hd) * sizeof(float);
+    const uint32_t rows = nseg < attn::kCombTile ? nseg : attn::kCombTile;
+    return ((size_t)3 * nseg * G + 20 + (size_t)rows * G * hd) * sizeof(float);
 }
 
 }  // namespace
