@@ -57,7 +57,7 @@ __device__ __forceinline__ float4 sum_parts(const float* base, uint64_t stride, 
 // loaded per round (24 for the many-split decode GEMMs; 8 keeps a CTA small
 // enough for several per SM when a prompt pass launches one per token).
 template <uint32_t B>
-__global__ void __launch_bounds__(kNormThreads) k_tc_norm(const TcNormArgs a) {
+__global__ void __launch_bounds__(kNormThreads, B <= 8 ? 4 : 1) k_tc_norm(const TcNormArgs a) {
     __shared__ float red[kNormThreads / 32];
     const uint32_t slot = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const KTrace tr(a.trace, a.trace_slot);

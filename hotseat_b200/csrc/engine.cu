@@ -984,7 +984,11 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
             m->pf_qblock = true;
             m->pf_tc = pf_mode >= 2;
             m->pf_seg = attn_prefill_seg(max_ctx);
-            m->pf_nseg = attn_prefill_segs(max_ctx);
+            // HS_PREFILL_SEG (a multiple of 64, at least the default, at most
+            // 32 segments): longer segments, for measurement
+            const uint32_t want = env_u32("HS_PREFILL_SEG", 0);
+            if (want % 64 == 0 && want > m->pf_seg) m->pf_seg = want;
+            m->pf_nseg = (max_ctx + m->pf_seg - 1) / m->pf_seg;
             HS_CUDA_TRY(attn_prefill_set_smem_limits(optin));
         }
     }

@@ -104,7 +104,7 @@ def _load(path, max_ctx, mode):
 @pytest.mark.parametrize("mode", [QBLOCK_TC, QBLOCK_CUDA_CORES])
 @pytest.mark.parametrize("shape,n", [("tiny", 700), ("tiny128", 700), ("q05", 600), ("tiny128", 200)])
 def test_query_block_prefill_matches_the_per_token_items(shape, n, mode, request):
-    """Several 256-position segments (and one, at 200): the same KV rows and
+    """Several 384-position segments (and one, at 200): the same KV rows and
     next-token logits as the per-token split items within tolerance."""
     path, vocab = {"tiny": ("tiny_gguf", TINY["vocab"]), "tiny128": ("tiny128_gguf", TINY128["vocab"]),
                    "q05": ("q05_gguf", QWEN05["vocab"])}[shape]
