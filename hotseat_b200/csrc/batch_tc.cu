@@ -214,7 +214,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t kt_n = a.K / 64, S = a.splits, n_units = a.n_tiles * S;
     const uint32_t n_items = a.m_loop ? n_units * ((a.slots + 63) / 64) : n_units;
     auto item_m0 = [&](uint32_t i) -> uint32_t { return a.m_loop ? i / n_units * 64 : blockIdx.y * 64; };
-    const TcAcc acc = tc_acc(NMAT, nt, n_items > gridDim.x);
+    // The accumulator arrangement sets the order of a tile's sums, so it must
+    // not depend on the pass: walking CTAs always take the several-items form.
+    const TcAcc acc = tc_acc(NMAT, nt, a.m_loop ? true : n_items > gridDim.x);
     const uint32_t buf_cols = acc.nacc * N;
     auto k_range = [&](uint32_t split, uint32_t* k0, uint32_t* k1) {
         *k0 = split * kt_n / S;

@@ -984,10 +984,10 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
             m->pf_qblock = true;
             m->pf_tc = pf_mode >= 2;
             m->pf_seg = attn_prefill_seg(max_ctx);
-            // HS_PREFILL_SEG (a multiple of 64, at least the default, at most
-            // 32 segments): longer segments, for measurement
+            // HS_PREFILL_SEG (a multiple of 64 giving at most 32 segments):
+            // another segment length, for measurement
             const uint32_t want = env_u32("HS_PREFILL_SEG", 0);
-            if (want % 64 == 0 && want > m->pf_seg) m->pf_seg = want;
+            if (want >= 64 && want % 64 == 0 && (max_ctx + want - 1) / want <= kPrefillMaxSegs) m->pf_seg = want;
             m->pf_nseg = (max_ctx + m->pf_seg - 1) / m->pf_seg;
             HS_CUDA_TRY(attn_prefill_set_smem_limits(optin));
         }
@@ -2196,7 +2196,7 @@ extern "C" {
 int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out) {
     if (!m || !out) return fail(HS_E_ARG, "null argument");
     if (m->numeric != HS_NUMERIC_TC) return fail(HS_E_UNSUPPORTED, "hs_batch needs a model loaded with HS_NUMERIC_TC");
-    if (max_seqs == 0 || max_seqs > 1024) return fail(HS_E_ARG, "max_seqs must be 1..1024");
+    if (max_seqs == 0 || max_seqs > 4096) return fail(HS_E_ARG, "max_seqs must be 1..4096");
     HS_CUDA_TRY(cudaSetDevice(m->device));
     auto b = std::make_unique<hs_batch>();
     b->m = m;

@@ -238,7 +238,7 @@ def bench_attention(ctxs=(1024, 4096, 16384, 32767), q05_path=None):
     return recs
 
 
-def bench_prefill(n_seqs=16, prompt=2048, gen=512, pass_tokens=1024):
+def bench_prefill(n_seqs=16, prompt=2048, gen=512, pass_tokens=2048):
     import torch
     import hotseat_b200 as hs
     peak_bw, _ = _peak()
@@ -474,7 +474,7 @@ if __name__ == "__main__":
         for r in bench_attention():
             print(json.dumps(r), flush=True)
     if which in ("prefill", "all"):
-        for r in bench_prefill(pass_tokens=int(sys.argv[2]) if which == "prefill" and len(sys.argv) > 2 else 1024):
+        for r in bench_prefill(pass_tokens=int(sys.argv[2]) if which == "prefill" and len(sys.argv) > 2 else 2048):
             print(json.dumps(r), flush=True)
     if which in ("token", "all"):
         bench_token()

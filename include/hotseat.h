@@ -293,7 +293,7 @@ int hs_seq_end(hs_scratch* s, uint32_t* tokens, uint64_t* n_tokens, uint64_t cap
  * region, history, SeqState, sampler config and RNG. No counterpart type in
  * the reference. */
 typedef struct hs_batch hs_batch;
-int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out); /* max_seqs 1..1024 */
+int hs_batch_new(const hs_model* m, uint32_t max_seqs, hs_batch** out); /* max_seqs 1..4096 (sequences, or prompt tokens per prefill pass) */
 void hs_batch_free(hs_batch* b);
 /* One Model::forward for each of n sequences: tokens[i] at pos[i], appending
  * to kvs[i] (all regions of one layout and page size). Blocks until done. */

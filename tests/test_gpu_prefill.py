@@ -176,3 +176,14 @@ def test_prefill_marks_exactly_the_pages_it_writes(tiny128_gguf, layout):
                     for pg in range(off // 4096, (off + hd * 4 - 1) // 4096 + 1):
                         want[pg >> 6] |= np.uint64(1) << np.uint64(pg & 63)
     assert np.array_equal(got[0], want) and np.array_equal(got[1], want)
+
+
+def test_one_2048_token_pass_equals_128_token_passes(tiny128_gguf):
+    """A batch of 2,048 slots prefills a 2,000-token prompt in one pass; the
+    KV region is bit-identical to passes of 128 tokens."""
+    m = hs.Model.load(tiny128_gguf, max_ctx=2048, numeric=TC)
+    prompt = [int(t) for t in np.random.default_rng(41).integers(0, TINY128["vocab"], size=2000)]
+    one, many = m.kv(), m.kv()
+    hs.Batch(m, 2048).prefill(one, prompt)
+    hs.Batch(m, 128).prefill(many, prompt)
+    assert one.hash(2000) == many.hash(2000)
