@@ -136,6 +136,28 @@ def test_tc_batched_transcripts_equal_single_runs(tiny_gguf):
         assert kvs[i].hash(together[i][1].filled) == kv1.hash(alone[1].filled)
 
 
+def test_tc_batch_of_more_than_1024_sequences_equals_single_runs(tiny_gguf):
+    """1,100 sequences in one batch (a capacity of 1,152 slots: 18 groups of
+    64): sampled transcripts, RNG and KV hashes of the first, a middle and the
+    last sequence equal each one run alone."""
+    m = load(tiny_gguf, 32)
+    g = np.random.default_rng(11)
+    n = 1100
+    seqs = [seq([int(t) for t in g.integers(0, TINY["vocab"], size=4 + i % 5)], 6,
+                hs.SamplerCfg.default(temperature=0.8, top_k=40), 500 + i) for i in range(n)]
+    kvs = [m.kv() for _ in range(n)]
+    together = hs.Batch(m, n).run_seqs(kvs, seqs)
+    for i in (0, 517, n - 1):
+        q2 = dict(seqs[i], rng=hs.Rng.seed(500 + i))
+        kv1 = m.kv()
+        alone = hs.Batch(m, 1).run_seqs([kv1], [q2])[0]
+        assert list(together[i][0]) == list(alone[0]), i
+        assert list(together[i][2].s) == list(alone[2].s)
+        assert kvs[i].hash(together[i][1].filled) == kv1.hash(alone[1].filled)
+    for kv in kvs:
+        kv.close()
+
+
 def test_tc_batch_marks_exactly_the_written_pages(tiny_gguf):
     m = load(tiny_gguf, 96)
     b = hs.Batch(m, 3)
