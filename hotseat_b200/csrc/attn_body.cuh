@@ -354,6 +354,94 @@ __device__ uint32_t prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s,
     return nch > 0 ? nch : 1;
 }
 
+// Tensor-core warp-split attend (SplitAttnArgs::tcw; tensor-core path,
+// head_dim 64): warp w takes the blocks of 16 positions b = w, w + 8, ... of
+// the item's range, staged by cp.async into its own two buffers (K rows
+// padded to 72 floats, V rows to 68: the fragment loads of a warp hit
+// distinct banks), and runs scores and P.V on mma.sync m16n8k16 with every
+// operand an f16 pair hi = f16(x), lo = f16(x - hi) and every product
+// lo*hi + hi*lo + hi*hi into the same f32 accumulator; rows are the group's
+// query heads (16-row tile, rows past the group zero), each warp keeps its
+// own online softmax, and the warps merge in warp order at the end.
+template <int NBUF>
+struct TcwGeom {
+    static constexpr uint32_t HD = 64, PB = 16, KS = 72, VS = 68;
+    static constexpr uint32_t BUF = PB * KS + PB * VS;  // floats of one block buffer (K then V)
+    static constexpr uint32_t WS = 2 * BUF;             // floats of a warp's area
+    static constexpr uint32_t AREA = NBUF * kCh * (k_stride(HD) + v_stride(HD)) + 2 * 8 * SPS;
+    static constexpr bool OK = 8 * WS <= AREA && 3 * 64 + 8 * 8 * HD <= AREA;
+};
+
+__device__ __forceinline__ void h2split(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(__fsub_rn(x0, hf.x), __fsub_rn(x1, hf.y));
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Stages block b of warp `warp` (local block b / 8 picks buffer (b / 8) % 2)
+// of the range [p0, p1): every cached row with 16-byte cp.async copies, the
+// row at `pos` from kn / vn when `fill_pos` or left out when `skip_pos` (a
+// prefetch before kn / vn exist); V rows past the range's end zero (their
+// probabilities are 0, and 0 times a stale non-finite value would not be).
+// One commit group per call, empty past the range's end.
+template <int NBUF>
+__device__ __forceinline__ void tcw_stage(const SplitAttnArgs& a, const float* kv, uint32_t layer, uint32_t kvh,
+                                          float* area, uint32_t warp, uint32_t lane, uint32_t b, uint32_t p0,
+                                          uint32_t p1, uint32_t pos, bool fill_pos, bool skip_pos, const float* kn,
+                                          const float* vn) {
+    using T = TcwGeom<NBUF>;
+    const uint32_t nb = (p1 - p0 + T::PB - 1) / T::PB;
+    if (b < nb) {
+        const uint32_t pb = p0 + b * T::PB, cnt = p1 - pb < T::PB ? p1 - pb : T::PB;
+        float* kd = area + warp * T::WS + ((b / 8) % 2) * T::BUF;
+        float* vd = kd + T::PB * T::KS;
+        for (uint32_t i = lane; i < T::PB * (T::HD / 4); i += 32) {
+            const uint32_t rr = i / (T::HD / 4), c4 = i % (T::HD / 4);
+            if (rr >= cnt) {
+                *reinterpret_cast<float4*>(vd + rr * T::VS + 4 * c4) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            } else if (pb + rr == pos && (fill_pos || skip_pos)) {
+                if (fill_pos) {
+                    *reinterpret_cast<float4*>(kd + rr * T::KS + 4 * c4) = *reinterpret_cast<const float4*>(kn + 4 * c4);
+                    *reinterpret_cast<float4*>(vd + rr * T::VS + 4 * c4) = *reinterpret_cast<const float4*>(vn + 4 * c4);
+                }
+            } else {
+                cp_async16(kd + rr * T::KS + 4 * c4, kv + kv_row_off(a, layer, kvh, T::HD, pb + rr, 0) + 4 * c4);
+                cp_async16(vd + rr * T::VS + 4 * c4, kv + kv_row_off(a, layer, kvh, T::HD, pb + rr, 1) + 4 * c4);
+            }
+        }
+    }
+    cp_commit();
+}
+
+// The tensor-core warp-split counterpart of prefetch(): the RoPE row of
+// `pos` and each warp's first block (all but the row at `pos`), one commit
+// group per thread. Returns 1.
+template <int NBUF>
+__device__ uint32_t tcw_prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t slot,
+                                 uint32_t pos, float* sm) {
+    using T = TcwGeom<NBUF>;
+    static_assert(T::OK, "tensor-core warp-split staging must fit the item's chunk buffers");
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from);
+    const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n;
+    float* rope = sm + item_rope_off(T::HD, NBUF);
+    if (threadIdx.x < T::HD / 4) {
+        const uint32_t i = threadIdx.x % (T::HD / 8), half = threadIdx.x / (T::HD / 8);
+        const float* src = (half ? a.rope_sin : a.rope_cos) + (size_t)pos * (T::HD / 2) + 4 * i;
+        cp_async16(rope + half * (T::HD / 2) + 4 * i, src);
+    }
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    tcw_stage<NBUF>(a, a.kv[slot], layer, kvh, sm + 10 * T::HD, warp, lane, warp, p0, p1, pos, false, true, nullptr,
+                    nullptr);
+    return 1;
+}
+
 // Waits until at most n (0..3) commit groups are pending.
 __device__ __forceinline__ void cp_wait_pending(uint32_t n) {
     switch (n) {
@@ -493,9 +581,157 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
 #pragma unroll
     for (uint32_t j = 0; j < HPT; j++) o[j] = 0.0f;
     // (the warp-split form exists only where its staging fits this item's buffers)
-    bool use_ws = false;
-    if constexpr (WsGeom<HD, NBUF>::OK) use_ws = attn_use_ws(n, a.ws_from);
-    if (use_ws) {
+    bool use_ws = false, use_tcw = false;
+    if constexpr (TC && HD == 64 && TcwGeom<NBUF>::OK) use_tcw = a.tcw != 0;
+    if constexpr (WsGeom<HD, NBUF>::OK) use_ws = !use_tcw && attn_use_ws(n, a.ws_from);
+    if (use_tcw) {
+      if constexpr (TC && HD == 64 && TcwGeom<NBUF>::OK) {
+        using T = TcwGeom<NBUF>;
+        constexpr uint32_t PB = T::PB, KS = T::KS, VS = T::VS;
+        const uint32_t g = lane >> 2, t4 = lane & 3;
+        const uint32_t nb = (p1 - p0 + PB - 1) / PB;
+        float* area = kb;
+        // q as A fragments: row g = query head g of the part (zero past G),
+        // rows 8-15 zero; split into f16 pairs once
+        uint32_t qh[4][4], ql[4][4];
+        const bool live = g < G;
+#pragma unroll
+        for (uint32_t kk = 0; kk < 4; kk++) {
+            const float* qr = qs + g * HD + 16 * kk + 2 * t4;
+            h2split(live ? qr[0] : 0.0f, live ? qr[1] : 0.0f, qh[kk][0], ql[kk][0]);
+            h2split(live ? qr[8] : 0.0f, live ? qr[9] : 0.0f, qh[kk][2], ql[kk][2]);
+            qh[kk][1] = ql[kk][1] = qh[kk][3] = ql[kk][3] = 0u;
+        }
+        // block 0 of every warp was staged by tcw_prefetch() without the row
+        // at pos: the warp that holds it fills it from kn / vn now
+        if (npre > 0 && pos >= p0 && pos < p1 && (pos - p0) / PB == warp) {
+            float* kd = area + warp * T::WS;
+            float* vd = kd + PB * KS;
+            const uint32_t rr = (pos - p0) % PB;
+            for (uint32_t c4 = lane; c4 < HD / 4; c4 += 32) {
+                *reinterpret_cast<float4*>(kd + rr * KS + 4 * c4) = *reinterpret_cast<const float4*>(kn + 4 * c4);
+                *reinterpret_cast<float4*>(vd + rr * VS + 4 * c4) = *reinterpret_cast<const float4*>(vn + 4 * c4);
+            }
+        }
+        auto stage = [&](uint32_t i) {  // this warp's local block i
+            tcw_stage<NBUF>(a, kv, layer, kvh, area, warp, lane, warp + 8 * i, p0, p1, pos, append, false, kn, vn);
+        };
+        if (npre == 0) stage(0);
+        float rm = -FLT_MAX, rl = 0.0f;  // running max / sum of row g
+        float O[HD / 8][4];
+#pragma unroll
+        for (uint32_t d = 0; d < HD / 8; d++) O[d][0] = O[d][1] = O[d][2] = O[d][3] = 0.0f;
+        const uint32_t nloc = nb > warp ? (nb - warp + 7) / 8 : 0;
+        for (uint32_t i = 0; i < nloc; i++) {
+            stage(i + 1);  // an empty group past this warp's last block
+            cp_wait<1>();  // block i landed
+            __syncwarp();
+            if (i == 0 && warp == 0) at(3);
+            const uint32_t pb = p0 + (warp + 8 * i) * PB, cnt = p1 - pb < PB ? p1 - pb : PB;
+            const float* kd = area + warp * T::WS + (i % 2) * T::BUF;
+            const float* vd = kd + PB * KS;
+            float S[2][4];
+#pragma unroll
+            for (uint32_t j = 0; j < 2; j++) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
+#pragma unroll
+            for (uint32_t kk = 0; kk < 4; kk++) {
+#pragma unroll
+                for (uint32_t j = 0; j < 2; j++) {
+                    const float* kr = kd + (8 * j + g) * KS + 16 * kk + 2 * t4;
+                    const float2 x0 = *reinterpret_cast<const float2*>(kr);
+                    const float2 x1 = *reinterpret_cast<const float2*>(kr + 8);
+                    uint32_t bh0, bl0, bh1, bl1;
+                    h2split(x0.x, x0.y, bh0, bl0);
+                    h2split(x1.x, x1.y, bh1, bl1);
+                    mma16816(S[j], ql[kk], bh0, bh1);
+                    mma16816(S[j], qh[kk], bl0, bl1);
+                    mma16816(S[j], qh[kk], bh0, bh1);
+                }
+            }
+            // online softmax of row g over the block's positions 8 j + 2 t4 + e;
+            // selects, not branches: every lane takes every shuffle
+            float sv[4] = {S[0][0], S[0][1], S[1][0], S[1][1]};
+            float mx = -FLT_MAX;
+#pragma unroll
+            for (uint32_t e = 0; e < 4; e++) {
+                const uint32_t col = (e >> 1) * 8 + 2 * t4 + (e & 1);
+                sv[e] = live && col < cnt ? __fmul_rn(sv[e], scale) : -FLT_MAX;
+                mx = fmaxf(mx, sv[e]);
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            const bool none = mx == -FLT_MAX;
+            const float mn = none ? rm : fmaxf(rm, mx);
+            float sum = 0.0f;
+#pragma unroll
+            for (uint32_t e = 0; e < 4; e++) {
+                sv[e] = sv[e] == -FLT_MAX ? 0.0f : __expf(__fsub_rn(sv[e], mn));
+                sum = __fadd_rn(sum, sv[e]);
+            }
+            sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
+            sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
+            const float f = none ? 1.0f : (rm == -FLT_MAX ? 0.0f : __expf(__fsub_rn(rm, mn)));
+            rl = none ? rl : __fadd_rn(__fmul_rn(rl, f), sum);
+            rm = mn;
+            uint32_t ph[4], pl[4];
+            h2split(sv[0], sv[1], ph[0], pl[0]);
+            h2split(sv[2], sv[3], ph[2], pl[2]);
+            ph[1] = pl[1] = ph[3] = pl[3] = 0u;
+#pragma unroll
+            for (uint32_t d = 0; d < HD / 8; d++) {
+                O[d][0] = __fmul_rn(O[d][0], f);
+                O[d][1] = __fmul_rn(O[d][1], f);
+                const float* vr = vd + 2 * t4 * VS + 8 * d + g;
+                uint32_t bh0, bl0, bh1, bl1;
+                h2split(vr[0], vr[VS], bh0, bl0);
+                h2split(vr[8 * VS], vr[9 * VS], bh1, bl1);
+                mma16816(O[d], pl, bh0, bh1);
+                mma16816(O[d], ph, bl0, bl1);
+                mma16816(O[d], ph, bh0, bh1);
+            }
+            __syncwarp();  // this buffer is restaged two blocks on
+        }
+        cp_wait0();
+        sync256();  // every warp is done with its area: the merge reuses it
+        // merge: warp w's maxima, sums and outputs of rows 0-7, then per head
+        // the weights exp(m_w - M) and the sums in warp order
+        float* mm = kb;          // [8 warps][8 heads]
+        float* ll = mm + 64;     // [8][8]
+        float* wt = ll + 64;     // [8][8] weights
+        float* ao = wt + 64;     // [8 warps][8 heads][HD]
+        if (t4 == 0) {
+            mm[warp * 8 + g] = rm;
+            ll[warp * 8 + g] = rl;
+        }
+#pragma unroll
+        for (uint32_t d = 0; d < HD / 8; d++)
+            *reinterpret_cast<float2*>(ao + (warp * 8 + g) * HD + 8 * d + 2 * t4) = make_float2(O[d][0], O[d][1]);
+        sync256();
+        if (tid < G) {
+            float M = -FLT_MAX;
+            for (uint32_t w = 0; w < 8; w++) M = fmaxf(M, mm[w * 8 + tid]);
+            float l = 0.0f;
+            for (uint32_t w = 0; w < 8; w++) {
+                const float m_w = mm[w * 8 + tid];
+                const float x = m_w == -FLT_MAX ? 0.0f : __expf(__fsub_rn(m_w, M));
+                wt[w * 8 + tid] = x;
+                l = __fadd_rn(l, __fmul_rn(x, ll[w * 8 + tid]));
+            }
+            hs_m[tid] = M;
+            hs_l[tid] = l;
+        }
+        sync256();
+#pragma unroll
+        for (uint32_t j = 0; j < HPT; j++) {
+            const uint32_t h = hs0 + j * HSETS;
+            if (h < G) {
+                float v = 0.0f;
+                for (uint32_t w = 0; w < 8; w++) v = __fadd_rn(v, __fmul_rn(wt[w * 8 + h], ao[(w * 8 + h) * HD + dd]));
+                o[j] = v;
+            }
+        }
+      }
+    } else if (use_ws) {
       if constexpr (WsGeom<HD, NBUF>::OK) {
         // Warp-split attend: warp w takes the blocks of WB positions b = w,
         // w + 8, w + 16, ... of [p0, p1) and keeps its own online softmax per

@@ -52,9 +52,17 @@ __global__ void __launch_bounds__(attn::kThreads, 2) k_attn_split(const SplitAtt
     // start loading the first chunks before waiting for the QKV product.
     const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from), S = (n + L - 1) / L;
     uint32_t npre = 0;
-    if (a.mode == ATTN_FULL && active && pos < a.max_ctx && s < S)
-        npre = attn_use_ws(n, a.ws_from) ? attn::ws_prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm)
-                            : attn::prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm, NB - 1 > 0 ? NB - 1 : 1);
+    if (a.mode == ATTN_FULL && active && pos < a.max_ctx && s < S) {
+        bool tcw = false;  // the same choice as attn::item's
+        if constexpr (TC && HD == 64 && attn::TcwGeom<NB>::OK) tcw = a.tcw != 0;
+        if (tcw) {
+            if constexpr (TC && HD == 64 && attn::TcwGeom<NB>::OK)
+                npre = attn::tcw_prefetch<NB>(a, a.layer, s, kvh, slot, pos, sm);
+        } else {
+            npre = attn_use_ws(n, a.ws_from) ? attn::ws_prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm)
+                                : attn::prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm, NB - 1 > 0 ? NB - 1 : 1);
+        }
+    }
     pdl_wait();
     if (!active) return;
     if (pos >= a.max_ctx) {

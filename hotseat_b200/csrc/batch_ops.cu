@@ -57,7 +57,7 @@ __device__ __forceinline__ float4 sum_parts(const float* base, uint64_t stride, 
 // loaded per round (24 for the many-split decode GEMMs; 8 keeps a CTA small
 // enough for several per SM when a prompt pass launches one per token).
 template <uint32_t B>
-__global__ void __launch_bounds__(kNormThreads, B <= 8 ? 4 : 1) k_tc_norm(const TcNormArgs a) {
+__device__ __forceinline__ void tc_norm_body(const TcNormArgs a) {
     __shared__ float red[kNormThreads / 32];
     const uint32_t slot = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const KTrace tr(a.trace, a.trace_slot);
@@ -121,6 +121,12 @@ __global__ void __launch_bounds__(kNormThreads, B <= 8 ? 4 : 1) k_tc_norm(const 
     tr.exit();
 }
 
+// The decode path's many-split consumers (one CTA per sequence, few CTAs),
+// and the prompt pass's few-split ones held to 64 registers (four CTAs per SM
+// for one CTA per token).
+__global__ void __launch_bounds__(kNormThreads) k_tc_norm24(const TcNormArgs a) { tc_norm_body<24>(a); }
+__global__ void __launch_bounds__(kNormThreads, 4) k_tc_norm8(const TcNormArgs a) { tc_norm_body<8>(a); }
+
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
@@ -141,7 +147,7 @@ cudaError_t launch_tc_norm(const TcNormArgs& a, uint32_t slots, cudaStream_t st)
     if (a.d % 4 || a.d > kNormThreads * kNormMaxChunks * 4 || a.n_part > kMaxParts) return cudaErrorInvalidValue;
     TcNormArgs c = a;
     void* args[] = {&c};
-    const void* fn = a.n_part > 8 ? reinterpret_cast<const void*>(k_tc_norm<24>) : reinterpret_cast<const void*>(k_tc_norm<8>);
+    const void* fn = a.n_part > 8 ? reinterpret_cast<const void*>(k_tc_norm24) : reinterpret_cast<const void*>(k_tc_norm8);
     return launch_pdl(fn, dim3(slots), dim3(kNormThreads), 0, st, args);
 }
 

@@ -223,6 +223,7 @@ struct hs_model {
     uint32_t attn_nbuf = 0;        // K/V chunk buffers per item (0 = by head_dim)
     uint32_t attn_unstaged = 0;    // HS_ATTN_UNSTAGED_COMBINE=1: the per-element combine (same bits; measurement)
     uint32_t attn_ws_from = 0;     // warp-split item form from this many positions on (0: never)
+    uint32_t attn_tcw = 0;         // tensor-core path, head_dim 64: the tensor-core warp-split item form
     bool pf_qblock = false;        // prefill attends by query blocks (attn_prefill.cu)
     bool pf_tc = false;            // ... with the products on the tensor cores
     uint32_t pf_seg = 0, pf_nseg = 0;  // its segment length and segments per token at most
@@ -973,6 +974,12 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
         // below and on the batched path, where the chunked form stays.
         // HS_ATTN_WS_FROM overrides (positions; 0 = never).
         m->attn_ws_from = env_u32("HS_ATTN_WS_FROM", tc ? 0u : 8192u);
+        // Tensor-core path at head_dim 64 with four chunk buffers: the items'
+        // products on mma.sync with f16 hi/lo operands, positions split over
+        // the 8 warps (HS_ATTN_TCW=0 keeps the chunked tf32 form).
+        // The form stages its own blocks, so the chunk-buffer knob does not
+        // apply to it: its launches always take the four-buffer item space.
+        m->attn_tcw = tc && hd == 64 && env_u32("HS_ATTN_TCW", 1) != 0 ? 1u : 0u;
         if (!tc && !attn_ws_fits(hd, 1)) m->attn_ws_from = 0;
         HS_CUDA_TRY(attn_split_set_smem_limits(optin));
         // Prefill attends by query blocks (128 rows share each K/V chunk,
@@ -2047,9 +2054,10 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool pref
             sa.page_shift = b->page_shift;
             sa.max_splits = m->max_splits;
             sa.head_split = m->attn_head_split;
-            sa.nbuf = m->attn_nbuf;
+            sa.nbuf = m->attn_tcw ? 4u : m->attn_nbuf;
             sa.unstaged_combine = m->attn_unstaged;
             sa.ws_from = m->attn_ws_from;
+            sa.tcw = m->attn_tcw;
             sa.tensor_cores = m->numeric == HS_NUMERIC_TC ? 1u : 0u;
             sa.trace = b->trace;
             sa.trace_slot = *launches;

@@ -198,6 +198,7 @@ struct SplitAttnArgs {
     uint32_t tensor_cores;   // chunk products on the tensor cores (split tf32), else fp32 on the CUDA cores
     uint32_t unstaged_combine;  // measurement knob: the last CTA's combine reads the splits through L2 per element
     uint32_t ws_from;        // from this many positions on, the warp-split item form (0: never)
+    uint32_t tcw;            // tensor-core path, head_dim 64: the tensor-core warp-split item form
     uint64_t* trace;
     uint32_t trace_slot;
 };

@@ -222,11 +222,13 @@ def test_tc_migration_between_batches_reproduces_the_transcript(tiny_gguf):
 
 
 @pytest.mark.parametrize("env", [{"HS_ATTN_HEAD_SPLIT": "2"}, {"HS_ATTN_HEAD_SPLIT": "3", "HS_ATTN_NBUF": "2"},
-                                 {"HS_ATTN_NBUF": "3"}])
+                                 {"HS_ATTN_NBUF": "3"}, {"HS_ATTN_HEAD_SPLIT": "7"}])
 def test_tc_attention_work_split_keeps_the_bits(env, q05_gguf, monkeypatch):
     """Splitting a (split, KV head) item's query heads over several CTAs, or
     changing how many K/V chunks load ahead, leaves every head's arithmetic
-    as it was: transcripts, RNG and KV hashes equal the default launch's."""
+    as it was: transcripts, RNG and KV hashes equal the default launch's.
+    (At head_dim 64 the default is the tensor-core warp-split form, which
+    stages its own blocks: the chunk-buffer count does not reach it.)"""
     def run():
         m = load(q05_gguf, 256)
         g = np.random.default_rng(12)
