@@ -354,22 +354,26 @@ __device__ uint32_t prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s,
     return nch > 0 ? nch : 1;
 }
 
-// Tensor-core warp-split attend (SplitAttnArgs::tcw; tensor-core path,
-// head_dim 64): warp w takes the blocks of 16 positions b = w, w + 8, ... of
-// the item's range, staged by cp.async into its own two buffers (K rows
-// padded to 72 floats, V rows to 68: the fragment loads of a warp hit
-// distinct banks), and runs scores and P.V on mma.sync m16n8k16 with every
+// Tensor-core warp-split attend (SplitAttnArgs::tcw; tensor-core path):
+// warp w < NW takes the blocks of 16 positions b = w, w + NW, ... of the
+// item's range, staged by cp.async into its own two buffers (K rows padded
+// by 8 floats, V rows by 4: the fragment loads of a warp hit distinct
+// banks); NW = 8 at head_dim 64, 6 at 128 (the buffers that fit the item's
+// space; the other warps take no block), and runs scores and P.V on
+// mma.sync m16n8k16 with every
 // operand an f16 pair hi = f16(x), lo = f16(x - hi) and every product
 // lo*hi + hi*lo + hi*hi into the same f32 accumulator; rows are the group's
 // query heads (16-row tile, rows past the group zero), each warp keeps its
 // own online softmax, and the warps merge in warp order at the end.
-template <int NBUF>
+template <int HD_, int NBUF>
 struct TcwGeom {
-    static constexpr uint32_t HD = 64, PB = 16, KS = 72, VS = 68;
+    static constexpr uint32_t HD = HD_, PB = 16, KS = HD + 8, VS = HD + 4;
     static constexpr uint32_t BUF = PB * KS + PB * VS;  // floats of one block buffer (K then V)
     static constexpr uint32_t WS = 2 * BUF;             // floats of a warp's area
     static constexpr uint32_t AREA = NBUF * kCh * (k_stride(HD) + v_stride(HD)) + 2 * 8 * SPS;
-    static constexpr bool OK = 8 * WS <= AREA && 3 * 64 + 8 * 8 * HD <= AREA;
+    static constexpr uint32_t FIT = AREA / WS;
+    static constexpr uint32_t NW = FIT > 8 ? 8 : FIT;  // warps that take blocks
+    static constexpr bool OK = (HD == 64 || HD == 128) && NW >= 4 && 3 * 64 + 8 * 8 * HD <= AREA;
 };
 
 __device__ __forceinline__ void h2split(float x0, float x1, uint32_t& hi, uint32_t& lo) {
@@ -385,22 +389,22 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Stages block b of warp `warp` (local block b / 8 picks buffer (b / 8) % 2)
+// Stages block b of warp `warp` (local block b / NW picks buffer (b / NW) % 2)
 // of the range [p0, p1): every cached row with 16-byte cp.async copies, the
 // row at `pos` from kn / vn when `fill_pos` or left out when `skip_pos` (a
 // prefetch before kn / vn exist); V rows past the range's end zero (their
 // probabilities are 0, and 0 times a stale non-finite value would not be).
 // One commit group per call, empty past the range's end.
-template <int NBUF>
+template <int HD, int NBUF>
 __device__ __forceinline__ void tcw_stage(const SplitAttnArgs& a, const float* kv, uint32_t layer, uint32_t kvh,
                                           float* area, uint32_t warp, uint32_t lane, uint32_t b, uint32_t p0,
                                           uint32_t p1, uint32_t pos, bool fill_pos, bool skip_pos, const float* kn,
                                           const float* vn) {
-    using T = TcwGeom<NBUF>;
+    using T = TcwGeom<HD, NBUF>;
     const uint32_t nb = (p1 - p0 + T::PB - 1) / T::PB;
-    if (b < nb) {
+    if (warp < T::NW && b < nb) {
         const uint32_t pb = p0 + b * T::PB, cnt = p1 - pb < T::PB ? p1 - pb : T::PB;
-        float* kd = area + warp * T::WS + ((b / 8) % 2) * T::BUF;
+        float* kd = area + warp * T::WS + ((b / T::NW) % 2) * T::BUF;
         float* vd = kd + T::PB * T::KS;
         for (uint32_t i = lane; i < T::PB * (T::HD / 4); i += 32) {
             const uint32_t rr = i / (T::HD / 4), c4 = i % (T::HD / 4);
@@ -423,10 +427,10 @@ __device__ __forceinline__ void tcw_stage(const SplitAttnArgs& a, const float* k
 // The tensor-core warp-split counterpart of prefetch(): the RoPE row of
 // `pos` and each warp's first block (all but the row at `pos`), one commit
 // group per thread. Returns 1.
-template <int NBUF>
+template <int HD, int NBUF>
 __device__ uint32_t tcw_prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_t kvh, uint32_t slot,
                                  uint32_t pos, float* sm) {
-    using T = TcwGeom<NBUF>;
+    using T = TcwGeom<HD, NBUF>;
     static_assert(T::OK, "tensor-core warp-split staging must fit the item's chunk buffers");
     const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from);
     const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n;
@@ -437,8 +441,8 @@ __device__ uint32_t tcw_prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_
         cp_async16(rope + half * (T::HD / 2) + 4 * i, src);
     }
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    tcw_stage<NBUF>(a, a.kv[slot], layer, kvh, sm + 10 * T::HD, warp, lane, warp, p0, p1, pos, false, true, nullptr,
-                    nullptr);
+    tcw_stage<HD, NBUF>(a, a.kv[slot], layer, kvh, sm + 10 * T::HD, warp, lane, warp, p0, p1, pos, false, true,
+                        nullptr, nullptr);
     return 1;
 }
 
@@ -582,29 +586,28 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     for (uint32_t j = 0; j < HPT; j++) o[j] = 0.0f;
     // (the warp-split form exists only where its staging fits this item's buffers)
     bool use_ws = false, use_tcw = false;
-    if constexpr (TC && HD == 64 && TcwGeom<NBUF>::OK) use_tcw = a.tcw != 0;
+    if constexpr (TC && TcwGeom<HD, NBUF>::OK) use_tcw = a.tcw != 0;
     if constexpr (WsGeom<HD, NBUF>::OK) use_ws = !use_tcw && attn_use_ws(n, a.ws_from);
     if (use_tcw) {
-      if constexpr (TC && HD == 64 && TcwGeom<NBUF>::OK) {
-        using T = TcwGeom<NBUF>;
-        constexpr uint32_t PB = T::PB, KS = T::KS, VS = T::VS;
+      if constexpr (TC && TcwGeom<HD, NBUF>::OK) {
+        using T = TcwGeom<HD, NBUF>;
+        constexpr uint32_t PB = T::PB, KS = T::KS, VS = T::VS, NW = T::NW, KK = HD / 16, ND = HD / 8;
         const uint32_t g = lane >> 2, t4 = lane & 3;
         const uint32_t nb = (p1 - p0 + PB - 1) / PB;
         float* area = kb;
         // q as A fragments: row g = query head g of the part (zero past G),
         // rows 8-15 zero; split into f16 pairs once
-        uint32_t qh[4][4], ql[4][4];
+        uint32_t qh[KK][2], ql[KK][2];
         const bool live = g < G;
 #pragma unroll
-        for (uint32_t kk = 0; kk < 4; kk++) {
+        for (uint32_t kk = 0; kk < KK; kk++) {
             const float* qr = qs + g * HD + 16 * kk + 2 * t4;
             h2split(live ? qr[0] : 0.0f, live ? qr[1] : 0.0f, qh[kk][0], ql[kk][0]);
-            h2split(live ? qr[8] : 0.0f, live ? qr[9] : 0.0f, qh[kk][2], ql[kk][2]);
-            qh[kk][1] = ql[kk][1] = qh[kk][3] = ql[kk][3] = 0u;
+            h2split(live ? qr[8] : 0.0f, live ? qr[9] : 0.0f, qh[kk][1], ql[kk][1]);
         }
-        // block 0 of every warp was staged by tcw_prefetch() without the row
-        // at pos: the warp that holds it fills it from kn / vn now
-        if (npre > 0 && pos >= p0 && pos < p1 && (pos - p0) / PB == warp) {
+        // block 0 of every block-taking warp was staged by tcw_prefetch()
+        // without the row at pos: the warp that holds it fills it now
+        if (npre > 0 && pos >= p0 && pos < p1 && (pos - p0) / PB == warp && warp < NW) {
             float* kd = area + warp * T::WS;
             float* vd = kd + PB * KS;
             const uint32_t rr = (pos - p0) % PB;
@@ -614,27 +617,29 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
             }
         }
         auto stage = [&](uint32_t i) {  // this warp's local block i
-            tcw_stage<NBUF>(a, kv, layer, kvh, area, warp, lane, warp + 8 * i, p0, p1, pos, append, false, kn, vn);
+            tcw_stage<HD, NBUF>(a, kv, layer, kvh, area, warp, lane, warp + NW * i, p0, p1, pos, append, false, kn,
+                                vn);
         };
         if (npre == 0) stage(0);
         float rm = -FLT_MAX, rl = 0.0f;  // running max / sum of row g
-        float O[HD / 8][4];
+        float O[ND][2];                  // row g's output, dimensions 8 d + 2 t4 (+1)
 #pragma unroll
-        for (uint32_t d = 0; d < HD / 8; d++) O[d][0] = O[d][1] = O[d][2] = O[d][3] = 0.0f;
-        const uint32_t nloc = nb > warp ? (nb - warp + 7) / 8 : 0;
+        for (uint32_t d = 0; d < ND; d++) O[d][0] = O[d][1] = 0.0f;
+        const uint32_t nloc = warp < NW && nb > warp ? (nb - warp + NW - 1) / NW : 0;
         for (uint32_t i = 0; i < nloc; i++) {
             stage(i + 1);  // an empty group past this warp's last block
             cp_wait<1>();  // block i landed
             __syncwarp();
             if (i == 0 && warp == 0) at(3);
-            const uint32_t pb = p0 + (warp + 8 * i) * PB, cnt = p1 - pb < PB ? p1 - pb : PB;
+            const uint32_t pb = p0 + (warp + NW * i) * PB, cnt = p1 - pb < PB ? p1 - pb : PB;
             const float* kd = area + warp * T::WS + (i % 2) * T::BUF;
             const float* vd = kd + PB * KS;
             float S[2][4];
 #pragma unroll
             for (uint32_t j = 0; j < 2; j++) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
 #pragma unroll
-            for (uint32_t kk = 0; kk < 4; kk++) {
+            for (uint32_t kk = 0; kk < KK; kk++) {
+                const uint32_t ah[4] = {qh[kk][0], 0u, qh[kk][1], 0u}, al[4] = {ql[kk][0], 0u, ql[kk][1], 0u};
 #pragma unroll
                 for (uint32_t j = 0; j < 2; j++) {
                     const float* kr = kd + (8 * j + g) * KS + 16 * kk + 2 * t4;
@@ -643,9 +648,9 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
                     uint32_t bh0, bl0, bh1, bl1;
                     h2split(x0.x, x0.y, bh0, bl0);
                     h2split(x1.x, x1.y, bh1, bl1);
-                    mma16816(S[j], ql[kk], bh0, bh1);
-                    mma16816(S[j], qh[kk], bl0, bl1);
-                    mma16816(S[j], qh[kk], bh0, bh1);
+                    mma16816(S[j], al, bh0, bh1);
+                    mma16816(S[j], ah, bl0, bl1);
+                    mma16816(S[j], ah, bh0, bh1);
                 }
             }
             // online softmax of row g over the block's positions 8 j + 2 t4 + e;
@@ -678,23 +683,27 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
             h2split(sv[2], sv[3], ph[2], pl[2]);
             ph[1] = pl[1] = ph[3] = pl[3] = 0u;
 #pragma unroll
-            for (uint32_t d = 0; d < HD / 8; d++) {
-                O[d][0] = __fmul_rn(O[d][0], f);
-                O[d][1] = __fmul_rn(O[d][1], f);
+            for (uint32_t d = 0; d < ND; d++) {
+                // rows 8-15 of P are zero, so their outputs stay zero: fresh
+                // zeros stand in for them
+                float acc[4] = {__fmul_rn(O[d][0], f), __fmul_rn(O[d][1], f), 0.0f, 0.0f};
                 const float* vr = vd + 2 * t4 * VS + 8 * d + g;
                 uint32_t bh0, bl0, bh1, bl1;
                 h2split(vr[0], vr[VS], bh0, bl0);
                 h2split(vr[8 * VS], vr[9 * VS], bh1, bl1);
-                mma16816(O[d], pl, bh0, bh1);
-                mma16816(O[d], ph, bl0, bl1);
-                mma16816(O[d], ph, bh0, bh1);
+                mma16816(acc, pl, bh0, bh1);
+                mma16816(acc, ph, bl0, bl1);
+                mma16816(acc, ph, bh0, bh1);
+                O[d][0] = acc[0];
+                O[d][1] = acc[1];
             }
             __syncwarp();  // this buffer is restaged two blocks on
         }
         cp_wait0();
         sync256();  // every warp is done with its area: the merge reuses it
-        // merge: warp w's maxima, sums and outputs of rows 0-7, then per head
-        // the weights exp(m_w - M) and the sums in warp order
+        // merge: warp w's maxima, sums and outputs of rows 0-7 (warps past NW:
+        // no block, weight 0), then per head the weights exp(m_w - M) and the
+        // sums in warp order
         float* mm = kb;          // [8 warps][8 heads]
         float* ll = mm + 64;     // [8][8]
         float* wt = ll + 64;     // [8][8] weights
@@ -704,7 +713,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
             ll[warp * 8 + g] = rl;
         }
 #pragma unroll
-        for (uint32_t d = 0; d < HD / 8; d++)
+        for (uint32_t d = 0; d < ND; d++)
             *reinterpret_cast<float2*>(ao + (warp * 8 + g) * HD + 8 * d + 2 * t4) = make_float2(O[d][0], O[d][1]);
         sync256();
         if (tid < G) {

@@ -36,8 +36,10 @@ namespace {
 __host__ __device__ constexpr int nbuf(int hd) { return hd == 64 ? 4 : 3; }
 uint32_t buffers(uint32_t hd, uint32_t want) { return want >= 2 && want <= 4 ? want : nbuf((int)hd); }
 
+// Two CTAs per SM where the item's space allows it (head_dim 64); at 128 the
+// item takes most of an SM's shared memory, so one CTA may use every register.
 template <int HD, int NB, bool TC>
-__global__ void __launch_bounds__(attn::kThreads, 2) k_attn_split(const SplitAttnArgs a) {
+__global__ void __launch_bounds__(attn::kThreads, HD == 64 ? 2 : 1) k_attn_split(const SplitAttnArgs a) {
     extern __shared__ __align__(16) float sm[];
     const uint32_t hsplit = attn_head_split(a);
     const uint32_t s = blockIdx.x / hsplit, hpart = blockIdx.x % hsplit, kvh = blockIdx.y, slot = blockIdx.z;
@@ -54,10 +56,10 @@ __global__ void __launch_bounds__(attn::kThreads, 2) k_attn_split(const SplitAtt
     uint32_t npre = 0;
     if (a.mode == ATTN_FULL && active && pos < a.max_ctx && s < S) {
         bool tcw = false;  // the same choice as attn::item's
-        if constexpr (TC && HD == 64 && attn::TcwGeom<NB>::OK) tcw = a.tcw != 0;
+        if constexpr (TC && attn::TcwGeom<HD, NB>::OK) tcw = a.tcw != 0;
         if (tcw) {
-            if constexpr (TC && HD == 64 && attn::TcwGeom<NB>::OK)
-                npre = attn::tcw_prefetch<NB>(a, a.layer, s, kvh, slot, pos, sm);
+            if constexpr (TC && attn::TcwGeom<HD, NB>::OK)
+                npre = attn::tcw_prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm);
         } else {
             npre = attn_use_ws(n, a.ws_from) ? attn::ws_prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm)
                                 : attn::prefetch<HD, NB>(a, a.layer, s, kvh, slot, pos, sm, NB - 1 > 0 ? NB - 1 : 1);

@@ -960,7 +960,12 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
         // more, so the tensor-core path splits only past 1024 positions per
         // split: no combine at short contexts. Both depend on max_ctx only,
         // never on the batch.
-        const uint32_t tc_split = std::max<uint32_t>(64, env_u32("HS_TC_SPLIT_POSITIONS", 1024));
+        // At head_dim 128 an item holds most of an SM's shared memory (one CTA
+        // per SM), so its splits are shorter: measured on the 1.5B shape at
+        // batch 16 and 2-2.5k positions (4 splits, one wave of 128 items),
+        // attention 35.4 µs per layer at 704 positions against 41.6 at 1024
+        // and 45.6 at 640 (two waves).
+        const uint32_t tc_split = std::max<uint32_t>(64, env_u32("HS_TC_SPLIT_POSITIONS", hd == 128 ? 704 : 1024));
         m->max_splits = tc ? std::min<uint32_t>(128, std::max<uint32_t>(1, (max_ctx + tc_split - 1) / tc_split))
                            : attn_max_splits(max_ctx);
         m->attn_head_split = std::max<uint32_t>(1, env_u32("HS_ATTN_HEAD_SPLIT", 1));
@@ -978,8 +983,9 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
         // products on mma.sync with f16 hi/lo operands, positions split over
         // the 8 warps (HS_ATTN_TCW=0 keeps the chunked tf32 form).
         // The form stages its own blocks, so the chunk-buffer knob does not
-        // apply to it: its launches always take the four-buffer item space.
-        m->attn_tcw = tc && hd == 64 && env_u32("HS_ATTN_TCW", 1) != 0 ? 1u : 0u;
+        // apply to it: its launches always take the default item space (four
+        // buffers at head_dim 64, three at 128), which fixes its warp count.
+        m->attn_tcw = tc && (hd == 64 || hd == 128) && env_u32("HS_ATTN_TCW", 1) != 0 ? 1u : 0u;
         if (!tc && !attn_ws_fits(hd, 1)) m->attn_ws_from = 0;
         HS_CUDA_TRY(attn_split_set_smem_limits(optin));
         // Prefill attends by query blocks (128 rows share each K/V chunk,
@@ -2054,7 +2060,7 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool pref
             sa.page_shift = b->page_shift;
             sa.max_splits = m->max_splits;
             sa.head_split = m->attn_head_split;
-            sa.nbuf = m->attn_tcw ? 4u : m->attn_nbuf;
+            sa.nbuf = m->attn_tcw ? (hd == 64 ? 4u : 3u) : m->attn_nbuf;
             sa.unstaged_combine = m->attn_unstaged;
             sa.ws_from = m->attn_ws_from;
             sa.tcw = m->attn_tcw;

@@ -377,33 +377,46 @@ def bench_token():
     os.rmdir(td)
 
 
-def bench_batch():
+def bench_batch(shape="q05"):
+    """The last decode step's launch timeline: q05 = the C2 workload (64
+    sequences of the 0.5B shape, 128-token prompts, 140 tokens); q15 = the C3
+    decode (16 sequences of the 1.5B shape after a 2,047-token prefill, 16
+    tokens)."""
     os.environ["HS_TRACE"] = "1"
     import hotseat_b200 as hs
     td = tempfile.mkdtemp(prefix="hsmicro")
-    path = os.path.join(td, "q05.gguf")
-    write_synthetic_gguf(path, seed=1234, **QWEN05)
-    m = hs.Model.load(path, max_ctx=512, numeric=hs.NUMERIC_TC)
-    B = 64
+    c = QWEN05 if shape == "q05" else QWEN15
+    path = os.path.join(td, shape + ".gguf")
+    write_synthetic_gguf(path, seed=1234, **c)
+    B, prompt, gen, max_ctx = (64, 128, 140, 512) if shape == "q05" else (16, 2048, 16, 2568)
+    m = hs.Model.load(path, max_ctx=max_ctx, numeric=hs.NUMERIC_TC)
     b = hs.Batch(m, B)
     kvs = [m.kv() for _ in range(B)]
     seqs = []
+    pb = hs.Batch(m, prompt) if shape != "q05" else None
     for i in range(B):
         g = np.random.default_rng(99 + i)
-        p = [int(t) for t in g.integers(0, QWEN05["vocab"], size=128)]
-        seqs.append(dict(tokens=p, prompt_len=128, max_tokens=140, filled=0, rng=hs.Rng.seed(99 + i),
+        p = [int(t) for t in g.integers(0, c["vocab"], size=prompt)]
+        filled = 0
+        if pb is not None:
+            pb.prefill(kvs[i], p[:-1])
+            filled = prompt - 1
+        seqs.append(dict(tokens=p, prompt_len=prompt, max_tokens=gen, filled=filled, rng=hs.Rng.seed(99 + i),
                          cfg=hs.SamplerCfg.default(temperature=0.8, seed=99 + i)))
+    if pb is not None:
+        pb.close()
     b.run_seqs(kvs, seqs)
     n = b.launches_per_step()
     t = b.trace().astype(np.int64)[:n]
+    L = c["n_layers"]
     names = ["norm", "qkv", "attention", "o", "ffn_norm", "gate_up", "down"]
     per = {}
     for j, k in enumerate(names):
-        per[k] = float(np.mean([(t[l * 7 + j, 2] - t[l * 7 + j - 1, 2]) / 1e3 for l in range(1, 23)]))
+        per[k] = float(np.mean([(t[l * 7 + j, 2] - t[l * 7 + j - 1, 2]) / 1e3 for l in range(1, L - 1)]))
     gemm = {}
     for j, k in [(1, "qkv"), (3, "o"), (5, "gate_up"), (6, "down")]:
-        rows = [t[l * 7 + j] for l in range(1, 23)]
-        prev = [t[l * 7 + j - 1, 2] for l in range(1, 23)]
+        rows = [t[l * 7 + j] for l in range(1, L - 1)]
+        prev = [t[l * 7 + j - 1, 2] for l in range(1, L - 1)]
         gemm[k] = {
             "wait_released": float(np.mean([r[1] - p for r, p in zip(rows, prev)]) / 1e3),
             "first_stage": float(np.mean([r[4] - r[1] for r in rows]) / 1e3),
@@ -415,10 +428,10 @@ def bench_batch():
     # attention item checkpoints (SM cycles from the item's start, maximum over
     # CTAs): RoPE done, first chunk (or warp 0's first block) ready, the
     # positions done, the item's end
-    att = [t[l * 7 + 2] for l in range(1, 23)]
+    att = [t[l * 7 + 2] for l in range(1, L - 1)]
     item = {k: float(np.mean([r[4 + i] for r in att]) / 1965.0) for i, k in
             enumerate(["rope_done", "first_ready", "positions_done", "end"])}
-    print(json.dumps({"bench": "batch_step", "sequences": B, "launches": int(n),
+    print(json.dumps({"bench": "batch_step", "model": shape, "sequences": B, "launches": int(n),
                       "exit_to_exit_us": per, "layer_us": sum(per.values()), "gemm_marks_us": gemm,
                       "attention_item_us": item}), flush=True)
     for kv in kvs:
@@ -480,5 +493,7 @@ if __name__ == "__main__":
         bench_token()
     if which in ("batch", "all"):
         bench_batch()
+    if which == "batch15":
+        bench_batch("q15")
     if which == "prefill_trace":
         bench_prefill_trace(pass_tokens=int(sys.argv[2]) if len(sys.argv) > 2 else 1024)
