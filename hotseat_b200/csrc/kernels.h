@@ -196,7 +196,7 @@ struct SplitAttnArgs {
     uint32_t head_split;     // items per (split, KV head): the group's query heads in this many parts (0 = 1)
     uint32_t nbuf;           // K/V chunk buffers per item, 2..4 (0 = by head_dim)
     uint32_t tensor_cores;   // chunk products on the tensor cores (split tf32), else fp32 on the CUDA cores
-    uint32_t unstaged_combine;  // measurement knob: the last CTA's combine reads the splits through L2 per element
+    uint32_t unstaged_combine;  // the last CTA's combine reads the splits through L2 per element (always at <= 8 splits)
     uint32_t ws_from;        // from this many positions on, the warp-split item form (0: never)
     uint32_t tcw;            // tensor-core path, head_dim 64: the tensor-core warp-split item form
     uint64_t* trace;
