@@ -356,10 +356,13 @@ __device__ uint32_t prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s,
 
 // Tensor-core warp-split attend (SplitAttnArgs::tcw; tensor-core path):
 // warp w < NW takes the blocks of 16 positions b = w, w + NW, ... of the
-// item's range, staged by cp.async into its own two buffers (K rows padded
-// by 8 floats, V rows by 4: the fragment loads of a warp hit distinct
-// banks); NW = 8 at head_dim 64, 6 at 128 (the buffers that fit the item's
-// space; the other warps take no block), and runs scores and P.V on
+// item's range, staged by cp.async into its own WB = 2 buffers, one block
+// ahead (K rows padded by 8 floats, V rows by 4: the fragment loads of a
+// warp hit distinct banks); NW = 8 warps at head_dim 64, 6 at 128 (the
+// buffers that fit the item's space; the other warps take no block; 4 warps
+// x 3 buffers at 128 measured slower, 34.5 vs 31.2 µs per layer at batch
+// 16, 2k positions: the warps' compute matters more than the extra block in
+// flight), and runs scores and P.V on
 // mma.sync m16n8k16 with every
 // operand an f16 pair hi = f16(x), lo = f16(x - hi) and every product
 // lo*hi + hi*lo + hi*hi into the same f32 accumulator; rows are the group's
@@ -369,7 +372,8 @@ template <int HD_, int NBUF>
 struct TcwGeom {
     static constexpr uint32_t HD = HD_, PB = 16, KS = HD + 8, VS = HD + 4;
     static constexpr uint32_t BUF = PB * KS + PB * VS;  // floats of one block buffer (K then V)
-    static constexpr uint32_t WS = 2 * BUF;             // floats of a warp's area
+    static constexpr uint32_t WB = 2;                   // buffers per warp
+    static constexpr uint32_t WS = WB * BUF;            // floats of a warp's area
     static constexpr uint32_t AREA = NBUF * kCh * (k_stride(HD) + v_stride(HD)) + 2 * 8 * SPS;
     static constexpr uint32_t FIT = AREA / WS;
     static constexpr uint32_t NW = FIT > 8 ? 8 : FIT;  // warps that take blocks
@@ -389,7 +393,7 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Stages block b of warp `warp` (local block b / NW picks buffer (b / NW) % 2)
+// Stages block b of warp `warp` (local block b / NW picks buffer (b / NW) % WB)
 // of the range [p0, p1): every cached row with 16-byte cp.async copies, the
 // row at `pos` from kn / vn when `fill_pos` or left out when `skip_pos` (a
 // prefetch before kn / vn exist); V rows past the range's end zero (their
@@ -404,7 +408,7 @@ __device__ __forceinline__ void tcw_stage(const SplitAttnArgs& a, const float* k
     const uint32_t nb = (p1 - p0 + T::PB - 1) / T::PB;
     if (warp < T::NW && b < nb) {
         const uint32_t pb = p0 + b * T::PB, cnt = p1 - pb < T::PB ? p1 - pb : T::PB;
-        float* kd = area + warp * T::WS + ((b / T::NW) % 2) * T::BUF;
+        float* kd = area + warp * T::WS + ((b / T::NW) % T::WB) * T::BUF;
         float* vd = kd + T::PB * T::KS;
         for (uint32_t i = lane; i < T::PB * (T::HD / 4); i += 32) {
             const uint32_t rr = i / (T::HD / 4), c4 = i % (T::HD / 4);
@@ -591,7 +595,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     if (use_tcw) {
       if constexpr (TC && TcwGeom<HD, NBUF>::OK) {
         using T = TcwGeom<HD, NBUF>;
-        constexpr uint32_t PB = T::PB, KS = T::KS, VS = T::VS, NW = T::NW, KK = HD / 16, ND = HD / 8;
+        constexpr uint32_t PB = T::PB, KS = T::KS, VS = T::VS, NW = T::NW, WB = T::WB, KK = HD / 16, ND = HD / 8;
         const uint32_t g = lane >> 2, t4 = lane & 3;
         const uint32_t nb = (p1 - p0 + PB - 1) / PB;
         float* area = kb;
@@ -620,19 +624,22 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
             tcw_stage<HD, NBUF>(a, kv, layer, kvh, area, warp, lane, warp + NW * i, p0, p1, pos, append, false, kn,
                                 vn);
         };
-        if (npre == 0) stage(0);
+        // local blocks 0 .. WB-2 in flight before the loop (block 0 from
+        // tcw_prefetch() when it ran); each iteration issues block i + WB - 1
+        // (an empty group past the end) and waits for block i
+        for (uint32_t i = npre > 0 ? 1u : 0u; i + 1 < WB; i++) stage(i);
         float rm = -FLT_MAX, rl = 0.0f;  // running max / sum of row g
         float O[ND][2];                  // row g's output, dimensions 8 d + 2 t4 (+1)
 #pragma unroll
         for (uint32_t d = 0; d < ND; d++) O[d][0] = O[d][1] = 0.0f;
         const uint32_t nloc = warp < NW && nb > warp ? (nb - warp + NW - 1) / NW : 0;
         for (uint32_t i = 0; i < nloc; i++) {
-            stage(i + 1);  // an empty group past this warp's last block
-            cp_wait<1>();  // block i landed
+            stage(i + WB - 1);
+            cp_wait<WB - 1>();  // block i landed
             __syncwarp();
             if (i == 0 && warp == 0) at(3);
             const uint32_t pb = p0 + (warp + NW * i) * PB, cnt = p1 - pb < PB ? p1 - pb : PB;
-            const float* kd = area + warp * T::WS + (i % 2) * T::BUF;
+            const float* kd = area + warp * T::WS + (i % WB) * T::BUF;
             const float* vd = kd + PB * KS;
             float S[2][4];
 #pragma unroll
@@ -697,7 +704,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
                 O[d][0] = acc[0];
                 O[d][1] = acc[1];
             }
-            __syncwarp();  // this buffer is restaged two blocks on
+            __syncwarp();  // this buffer is restaged WB blocks on
         }
         cp_wait0();
         sync256();  // every warp is done with its area: the merge reuses it
