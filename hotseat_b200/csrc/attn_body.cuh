@@ -303,7 +303,7 @@ __device__ uint32_t ws_prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t
                                 uint32_t pos, float* sm) {
     using W = WsGeom<HD, NBUF>;
     static_assert(W::OK, "warp-split staging must fit the item's chunk buffers");
-    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from);
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from, a.min_split);
     const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n;
     float* rope = sm + item_rope_off(HD, NBUF);
     if (threadIdx.x < HD / 4) {
@@ -330,7 +330,7 @@ __device__ uint32_t prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_t s,
     constexpr uint32_t RSK = k_stride(HD), RSV = v_stride(HD);
     float* kb = sm + 10 * HD;
     float* vb = kb + NBUF * kCh * RSK;
-    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from);
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from, a.min_split);
     const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n, have = (p1 - p0 + kCh - 1) / kCh;
     if (nch > have) nch = have;
     const float* kv = a.kv[slot];
@@ -436,7 +436,7 @@ __device__ uint32_t tcw_prefetch(const SplitAttnArgs& a, uint32_t layer, uint32_
                                  uint32_t pos, float* sm) {
     using T = TcwGeom<HD, NBUF>;
     static_assert(T::OK, "tensor-core warp-split staging must fit the item's chunk buffers");
-    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from);
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from, a.min_split);
     const uint32_t p0 = s * L, p1 = p0 + L < n ? p0 + L : n;
     float* rope = sm + item_rope_off(T::HD, NBUF);
     if (threadIdx.x < T::HD / 4) {
@@ -498,7 +498,7 @@ __device__ void item(const SplitAttnArgs& a, uint32_t layer, uint32_t s, uint32_
     uint32_t* flag = reinterpret_cast<uint32_t*>(hs_l + 8);
     uint4* qfrag = reinterpret_cast<uint4*>(hs_l + 12);  // [2][HD/16][32]
     const float* rope = sm + item_rope_off(HD, NBUF);
-    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from), S = (n + L - 1) / L;
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from, a.min_split), S = (n + L - 1) / L;
     // Prefill runs append (every token's k, v) and attend (reading all rows
     // from memory) as two launches, so tokens of one sequence in one batch
     // see each other's rows.

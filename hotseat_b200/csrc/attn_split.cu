@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(attn::kThreads, HD == 64 ? 2 : 1) k_attn_split
     // The cached rows (all but pos) and the RoPE row do not depend on the
     // kernels this launch overlaps: with a whole item (append and attend),
     // start loading the first chunks before waiting for the QKV product.
-    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from), S = (n + L - 1) / L;
+    const uint32_t n = pos + 1, L = attn_split_len(n, a.max_splits, a.ws_from, a.min_split), S = (n + L - 1) / L;
     uint32_t npre = 0;
     if (a.mode == ATTN_FULL && active && pos < a.max_ctx && s < S) {
         bool tcw = false;  // the same choice as attn::item's

@@ -223,7 +223,8 @@ struct hs_model {
     uint32_t attn_nbuf = 0;        // K/V chunk buffers per item (0 = by head_dim)
     uint32_t attn_unstaged = 0;    // HS_ATTN_UNSTAGED_COMBINE=1: the per-element combine (same bits; measurement)
     uint32_t attn_ws_from = 0;     // warp-split item form from this many positions on (0: never)
-    uint32_t attn_tcw = 0;         // tensor-core path, head_dim 64: the tensor-core warp-split item form
+    uint32_t attn_tcw = 0;         // tensor-core path: the tensor-core warp-split item form
+    uint32_t attn_min_split = 0;   // tensor-core path: target positions per split
     bool pf_qblock = false;        // prefill attends by query blocks (attn_prefill.cu)
     bool pf_tc = false;            // ... with the products on the tensor cores
     uint32_t pf_seg = 0, pf_nseg = 0;  // its segment length and segments per token at most
@@ -965,7 +966,12 @@ int hs_model_load_ex(const char* path, uint32_t max_ctx, int device, uint32_t nu
         // batch 16 and 2-2.5k positions (4 splits, one wave of 128 items),
         // attention 35.4 µs per layer at 704 positions against 41.6 at 1024
         // and 45.6 at 640 (two waves).
-        const uint32_t tc_split = std::max<uint32_t>(64, env_u32("HS_TC_SPLIT_POSITIONS", hd == 128 ? 704 : 1024));
+        const uint32_t tc_split =
+            (std::max<uint32_t>(64, env_u32("HS_TC_SPLIT_POSITIONS", hd == 128 ? 704 : 1024)) + 63) / 64 * 64;
+        // ... and n cut into ceil(n / tc_split) equal splits: a 1k context
+        // under a 32k max_ctx is 2 items, not 17 of 64 positions
+        // (HS_TC_MIN_SPLIT=0: spread over max_splits)
+        m->attn_min_split = tc && env_u32("HS_TC_MIN_SPLIT", 1) != 0 ? tc_split : 0u;
         m->max_splits = tc ? std::min<uint32_t>(128, std::max<uint32_t>(1, (max_ctx + tc_split - 1) / tc_split))
                            : attn_max_splits(max_ctx);
         m->attn_head_split = std::max<uint32_t>(1, env_u32("HS_ATTN_HEAD_SPLIT", 1));
@@ -2064,6 +2070,7 @@ int batch_enqueue_forward(hs_batch* b, uint32_t n, uint32_t* launches, bool pref
             sa.unstaged_combine = m->attn_unstaged;
             sa.ws_from = m->attn_ws_from;
             sa.tcw = m->attn_tcw;
+            sa.min_split = m->attn_min_split;
             sa.tensor_cores = m->numeric == HS_NUMERIC_TC ? 1u : 0u;
             sa.trace = b->trace;
             sa.trace_slot = *launches;

@@ -198,7 +198,8 @@ struct SplitAttnArgs {
     uint32_t tensor_cores;   // chunk products on the tensor cores (split tf32), else fp32 on the CUDA cores
     uint32_t unstaged_combine;  // the last CTA's combine reads the splits through L2 per element (always at <= 8 splits)
     uint32_t ws_from;        // from this many positions on, the warp-split item form (0: never)
-    uint32_t tcw;            // tensor-core path, head_dim 64: the tensor-core warp-split item form
+    uint32_t tcw;            // tensor-core path: the tensor-core warp-split item form
+    uint32_t min_split;      // target positions per split (0: spread over max_splits)
     uint64_t* trace;
     uint32_t trace_slot;
 };
@@ -215,10 +216,19 @@ __host__ __device__ inline uint32_t attn_head_split(const SplitAttnArgs& a) {
 __host__ __device__ inline bool attn_use_ws(uint32_t n, uint32_t ws_from) { return ws_from && n >= ws_from; }
 // Positions per split: a multiple of 64 covering n in at most max_splits
 // splits; at least 512 where the warp-split form runs (fewer, longer items
-// whose warps each take several blocks).
-__host__ __device__ inline uint32_t attn_split_len(uint32_t n, uint32_t max_splits, uint32_t ws_from) {
+// whose warps each take several blocks). With a target length (the
+// tensor-core path: the length max_splits was sized for) n is cut into
+// ceil(n / target) splits (at most max_splits) of equal length, so a short
+// context under a long max_ctx is not cut into 64-position items.
+__host__ __device__ inline uint32_t attn_split_len(uint32_t n, uint32_t max_splits, uint32_t ws_from,
+                                                   uint32_t target = 0) {
     const uint32_t chunks = (n + 63) / 64;
-    const uint32_t L = (chunks + max_splits - 1) / max_splits * 64;
+    uint32_t splits = max_splits;
+    if (target) {
+        const uint32_t want = (n + target - 1) / target;
+        if (want < splits) splits = want;
+    }
+    const uint32_t L = (chunks + splits - 1) / splits * 64;
     const uint32_t min_len = attn_use_ws(n, ws_from) ? 512 : 64;
     return L > min_len ? L : min_len;
 }
