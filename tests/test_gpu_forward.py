@@ -3,7 +3,7 @@
 The batch-1 kernels keep the reference's accumulation order, so the bar here
 is bit equality of logits and of the KV bytes. The tolerance the token loop is
 held to (logits within 1e-2 max-abs of the CPU path) is asserted as well, so a
-deliberate change of numeric path would still be judged by it."""
+deliberate change of numeric path would still be checked against it."""
 import numpy as np
 import pytest
 
