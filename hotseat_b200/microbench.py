@@ -29,7 +29,7 @@ up to 512 per pass), then the 16 decoded together for 512 greedy tokens
 (temperature 0, penalty 1.1). FLOPs = 2 x (non-embedding weights) per token
 for the GEMMs (the tensor cores execute twice that: f16 hi and lo halves).
 
-token: the C1 workload (36-token prompt, sampled at temperature 0.8, seed
+token: one sequence of the 0.5B shape (36-token prompt, sampled at temperature 0.8, seed
 99) decoded to 60 and to 120 tokens by the persistent token kernel with the
 trace on; the kernel's timeline of its last step, from CTA 0 (per phase of
 layers 1-23, averaged: input wait and its parts, rows, tiles) and over all
@@ -378,10 +378,9 @@ def bench_token():
 
 
 def bench_batch(shape="q05"):
-    """The last decode step's launch timeline: q05 = the C2 workload (64
-    sequences of the 0.5B shape, 128-token prompts, 140 tokens); q15 = the C3
-    decode (16 sequences of the 1.5B shape after a 2,047-token prefill, 16
-    tokens)."""
+    """The last decode step's launch timeline: q05 = 64 sequences of the 0.5B
+    shape (128-token prompts, 140 tokens); q15 = 16 sequences of the 1.5B
+    shape decoding after a 2,047-token prefill (16 tokens)."""
     os.environ["HS_TRACE"] = "1"
     import hotseat_b200 as hs
     td = tempfile.mkdtemp(prefix="hsmicro")
